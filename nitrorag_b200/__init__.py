@@ -1,0 +1,11 @@
+"""B200 engine for the Q8_0 prefill/decode step of NitroRAG's inference server.
+
+The product is ``libnitro_engine.so`` (C ABI in ``include/nitro_engine.h``); this package
+is its Python face (``engine.NitroEngine``), the build recipe and the seeded synthetic
+model/workload generators.  Importing the package does not require a GPU; creating a
+GPU engine does, and fails loudly when the library or the device is missing."""
+from .engine import (FNV_OFFSET_BASIS, NR_Q8_FAITHFUL, NR_Q8_FIXED, EngineConfig, NitroEngine, NrError,
+                     StepResult, argmax, hash_block_state)
+
+__all__ = ["NitroEngine", "EngineConfig", "StepResult", "NrError", "hash_block_state", "argmax",
+           "NR_Q8_FIXED", "NR_Q8_FAITHFUL", "FNV_OFFSET_BASIS"]

@@ -1,0 +1,363 @@
+// Paged attention over the fp32 KV pools, decode and causal prefill.
+//
+// The pools are laid out [page][layer][kv_head][16][head_dim], so one (page, layer,
+// kv_head) is a contiguous 16 x head_dim tile (4 KB at head_dim 64).  Every tile a CTA
+// needs is fetched with one bulk asynchronous copy (cp.async.bulk, the TMA engine's
+// non-tensor form) into shared memory and signalled on an mbarrier, so the SMs issue a
+// handful of instructions per 4 KB and keep many tiles in flight.
+//
+// Scores and the softmax are fp32.  Inside a warp two lanes share one key row (each takes
+// half of head_dim; their partial dots are joined with one shuffle), the 16 keys of a page
+// are processed at once, and the softmax is the online (running max / running sum) form
+// in the exp2 domain.  The reference computes decode scores, then a two-pass softmax
+// (src/model_q8.cpp:625-662, :142-159), and prefill with a single-pass online softmax
+// (:485-523); both equal softmax(q.k/sqrt(head)) . V up to fp32 rounding.
+//
+// Decode work is split ("flash-decoding"): each CTA takes one (sequence, head, chunk of
+// up to chunk_pages pages); a sequence whose context spans several chunks has its partial
+// (max, sum, unnormalised output) merged by whichever CTA finishes last, found with a
+// per-(sequence, head) arrival counter that the merging CTA resets to zero.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nitro {
+
+void count_launch();
+
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Running softmax state of one query inside a warp.  Lane l owns output dims
+// [l*DPL, l*DPL + DPL) with DPL = head_dim / 32.
+template <int HD>
+struct QState {
+    static constexpr int DPL = HD / 32;
+    float m;  // running max (log2 domain)
+    float l;  // running sum of exp2(s - m)
+    float o[DPL];
+    __device__ void init() {
+        m = -INFINITY;
+        l = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) o[i] = 0.0f;
+    }
+};
+
+// Fold the 16 rows of one K/V page tile (in shared memory) into a query's state.
+// qs: the query (head_dim floats, shared memory, pre-scaled by log2(e)/sqrt(head_dim));
+// n_valid: how many leading rows of the page are attended (1..16).
+template <int HD>
+__device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, const float* Kt, const float* Vt,
+                                            int n_valid, int lane) {
+    constexpr int HALF4 = HD / 8;  // float4s per half row
+    const int t = lane >> 1, half = lane & 1;
+    const float4* krow = reinterpret_cast<const float4*>(Kt + t * HD + half * (HD / 2));
+    const float4* qrow = reinterpret_cast<const float4*>(qs + half * (HD / 2));
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < HALF4; j++) {
+        // rotate the float4 index with the lane so the 8 lanes of each shared-memory
+        // phase hit 8 different bank groups
+        const int jj = (j + lane) & (HALF4 - 1);
+        float4 kv = krow[jj];
+        float4 qv = qrow[jj];
+        s = fmaf(qv.x, kv.x, s);
+        s = fmaf(qv.y, kv.y, s);
+        s = fmaf(qv.z, kv.z, s);
+        s = fmaf(qv.w, kv.w, s);
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (t >= n_valid) s = -INFINITY;
+    float mp = s;
+#pragma unroll
+    for (int o = 2; o < 32; o <<= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, o));
+    const float m_new = fmaxf(st.m, mp);
+    const float corr = exp2f(st.m - m_new);
+    const float p = exp2f(s - m_new);
+    float ps = half == 0 ? p : 0.0f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    st.l = st.l * corr + ps;
+    st.m = m_new;
+#pragma unroll
+    for (int i = 0; i < QState<HD>::DPL; i++) st.o[i] *= corr;
+    const float* vbase = Vt + lane * QState<HD>::DPL;
+#pragma unroll
+    for (int tt = 0; tt < kPage; tt++) {
+        const float pt = __shfl_sync(0xffffffffu, p, 2 * tt);
+        if (QState<HD>::DPL == 2) {
+            float2 v = *reinterpret_cast<const float2*>(vbase + tt * HD);
+            st.o[0] = fmaf(pt, v.x, st.o[0]);
+            st.o[1] = fmaf(pt, v.y, st.o[1]);
+        } else {
+            float4 v = *reinterpret_cast<const float4*>(vbase + tt * HD);
+            st.o[0] = fmaf(pt, v.x, st.o[0]);
+            st.o[1] = fmaf(pt, v.y, st.o[1]);
+            st.o[2] = fmaf(pt, v.z, st.o[2]);
+            st.o[3] = fmaf(pt, v.w, st.o[3]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ decode
+template <int HD>
+__global__ void __launch_bounds__(kAttnWarps * 32) decode_attn_kernel(DecodeAttnArgs a) {
+    constexpr int TILE = kPage * HD;  // floats per K (or V) tile
+    constexpr int DPL = HD / 32;
+    extern __shared__ __align__(128) float smem[];  // [chunk][2][TILE]
+    __shared__ uint64_t bars[16];
+    __shared__ __align__(16) float qs[HD];
+    __shared__ float red_m[kAttnWarps], red_l[kAttnWarps];
+    __shared__ __align__(16) float red_o[kAttnWarps][HD];
+    __shared__ int is_last;
+
+    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int ctx = a.ctx_lens[b];
+    const int n_pages = (ctx + kPage - 1) / kPage;
+    const int nsplit = (n_pages + a.chunk_pages - 1) / a.chunk_pages;
+    if (split >= nsplit) return;
+    const int p0 = split * a.chunk_pages;
+    const int np = min(a.chunk_pages, n_pages - p0);
+    const int kvh = h / (a.n_heads / a.geom.n_kv_heads);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < np; i++) mbar_init(&bars[i], 1);
+        fence_barrier_init();
+        const int* bt = a.block_tables + (int64_t)b * a.max_pages;
+        for (int i = 0; i < np; i++) {
+            const int64_t off = a.geom.tile_offset(bt[p0 + i], a.layer, kvh);
+            mbar_arrive_expect_tx(&bars[i], 2u * TILE * 4u);
+            bulk_g2s(smem + (2 * i) * TILE, a.kpool + off, TILE * 4, &bars[i]);
+            bulk_g2s(smem + (2 * i + 1) * TILE, a.vpool + off, TILE * 4, &bars[i]);
+        }
+    }
+    const float qscale = kLog2e / sqrtf((float)HD);
+    for (int d = threadIdx.x; d < HD; d += blockDim.x)
+        qs[d] = a.q[((int64_t)b * a.n_heads + h) * HD + d] * qscale;
+    __syncthreads();
+
+    QState<HD> st;
+    st.init();
+    bool ok = true;
+    for (int i = warp; i < np; i += kAttnWarps) {
+        if (!mbar_wait(&bars[i], 0, a.err)) { ok = false; break; }
+        const int first = (p0 + i) * kPage;
+        const int n_valid = min(kPage, ctx - first);
+        attend_page<HD>(st, qs, smem + (2 * i) * TILE, smem + (2 * i + 1) * TILE, n_valid, lane);
+    }
+    if (!ok) st.init();
+    // combine the warps of this CTA
+    if (lane == 0) { red_m[warp] = st.m; red_l[warp] = st.l; }
+#pragma unroll
+    for (int i = 0; i < DPL; i++) red_o[warp][lane * DPL + i] = st.o[i];
+    __syncthreads();
+    if (warp != 0) return;
+    float M = red_m[0];
+#pragma unroll
+    for (int w = 1; w < kAttnWarps; w++) M = fmaxf(M, red_m[w]);
+    float L = 0.0f, O[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) O[i] = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) {
+        const float c = (red_m[w] == -INFINITY) ? 0.0f : exp2f(red_m[w] - M);
+        L += red_l[w] * c;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) O[i] += red_o[w][lane * DPL + i] * c;
+    }
+    float* out = a.out + ((int64_t)b * a.n_heads + h) * HD + lane * DPL;
+    if (nsplit == 1) {
+        const float inv = 1.0f / L;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) out[i] = O[i] * inv;
+        return;
+    }
+    // publish this chunk's partial, then let the last-arriving CTA merge
+    const int64_t bh = (int64_t)b * a.n_heads + h;
+    float* po = a.part_o + (bh * a.max_splits + split) * HD + lane * DPL;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) po[i] = O[i];
+    if (lane == 0) {
+        a.part_ml[(bh * a.max_splits + split) * 2] = M;
+        a.part_ml[(bh * a.max_splits + split) * 2 + 1] = L;
+    }
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) {
+        const int prev = atomicAdd(a.counters + bh, 1);
+        is_last = (prev == nsplit - 1);
+    }
+    __syncwarp();
+    if (!is_last) return;
+    __threadfence();
+    float GM = -INFINITY;
+    for (int s = 0; s < nsplit; s++) GM = fmaxf(GM, __ldcg(a.part_ml + (bh * a.max_splits + s) * 2));
+    float GL = 0.0f, GO[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) GO[i] = 0.0f;
+    for (int s = 0; s < nsplit; s++) {
+        const float ms = __ldcg(a.part_ml + (bh * a.max_splits + s) * 2);
+        const float ls = __ldcg(a.part_ml + (bh * a.max_splits + s) * 2 + 1);
+        const float c = (ms == -INFINITY) ? 0.0f : exp2f(ms - GM);
+        GL += ls * c;
+        const float* ps = a.part_o + (bh * a.max_splits + s) * HD + lane * DPL;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) GO[i] += __ldcg(ps + i) * c;
+    }
+    const float inv = 1.0f / GL;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) out[i] = GO[i] * inv;
+    if (lane == 0) a.counters[bh] = 0;
+}
+
+// ------------------------------------------------------------------ prefill
+// One CTA per (16-query tile, head).  Pages 0..last of the sequence stream through
+// kStages shared-memory stages; each warp carries the softmax state of 4 queries.
+constexpr int kPrefillQ = 16;
+constexpr int kStages = 4;
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAttnArgs a) {
+    constexpr int TILE = kPage * HD;
+    constexpr int QPW = kPrefillQ / kAttnWarps;  // queries per warp
+    constexpr int DPL = HD / 32;
+    extern __shared__ __align__(128) float smem[];  // [kStages][2][TILE] then q [kPrefillQ][HD]
+    __shared__ uint64_t full[kStages];
+    float* qs = smem + kStages * 2 * TILE;
+
+    const int qt = blockIdx.x, h = blockIdx.y;
+    const int t0 = qt * kPrefillQ;
+    const int nq = min(kPrefillQ, a.T - t0);
+    const int last_pos = a.start_pos + t0 + nq - 1;
+    const int n_pages = last_pos / kPage + 1;
+    const int kvh = h / (a.n_heads / a.geom.n_kv_heads);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    auto issue = [&](int page_idx) {
+        const int s = page_idx % kStages;
+        const int64_t off = a.geom.tile_offset(a.block_table[page_idx], a.layer, kvh);
+        mbar_arrive_expect_tx(&full[s], 2u * TILE * 4u);
+        bulk_g2s(smem + (2 * s) * TILE, a.kpool + off, TILE * 4, &full[s]);
+        bulk_g2s(smem + (2 * s + 1) * TILE, a.vpool + off, TILE * 4, &full[s]);
+    };
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
+        fence_barrier_init();
+        for (int i = 0; i < kStages && i < n_pages; i++) issue(i);
+    }
+    const float qscale = kLog2e / sqrtf((float)HD);
+    for (int i = threadIdx.x; i < kPrefillQ * HD; i += blockDim.x) {
+        const int qi = i / HD, d = i % HD;
+        qs[i] = qi < nq ? a.q[((int64_t)(t0 + qi) * a.n_heads + h) * HD + d] * qscale : 0.0f;
+    }
+    __syncthreads();
+
+    QState<HD> st[QPW];
+#pragma unroll
+    for (int j = 0; j < QPW; j++) st[j].init();
+    bool ok = true;
+    for (int p = 0; p < n_pages; p++) {
+        const int s = p % kStages;
+        if (ok && !mbar_wait(&full[s], (p / kStages) & 1, a.err)) ok = false;
+        if (ok) {
+#pragma unroll
+            for (int j = 0; j < QPW; j++) {
+                const int qi = warp + j * kAttnWarps;
+                const int pos = a.start_pos + t0 + qi;
+                const int n_valid = min(kPage, pos - p * kPage + 1);
+                if (qi < nq && n_valid > 0)
+                    attend_page<HD>(st[j], qs + qi * HD, smem + (2 * s) * TILE, smem + (2 * s + 1) * TILE,
+                                    n_valid, lane);
+            }
+        }
+        // CTA-uniform: every thread leaves together if any wait gave up
+        if (!__syncthreads_and(ok)) { ok = false; break; }
+        if (threadIdx.x == 0 && p + kStages < n_pages) issue(p + kStages);
+    }
+    if (!ok) return;
+#pragma unroll
+    for (int j = 0; j < QPW; j++) {
+        const int qi = warp + j * kAttnWarps;
+        if (qi >= nq) continue;
+        float* out = a.out + ((int64_t)(t0 + qi) * a.n_heads + h) * HD + lane * DPL;
+        const float inv = 1.0f / st[j].l;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) out[i] = st[j].o[i] * inv;
+    }
+}
+
+// cudaFuncSetAttribute is per device: remember which devices have been configured.
+template <class K>
+void ensure_smem(K kernel, int bytes) {
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        done[dev] = true;
+    }
+}
+
+}  // namespace
+
+int decode_attn_chunk_pages(int head_dim) { return head_dim <= 64 ? 8 : 4; }
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+size_t decode_attn_workspace_bytes(int B, int n_heads, int head_dim, int max_pages) {
+    const int cp = decode_attn_chunk_pages(head_dim);
+    const int ms = (max_pages + cp - 1) / cp;
+    size_t o = align_up((size_t)B * n_heads * ms * head_dim * 4, 256);
+    size_t ml = align_up((size_t)B * n_heads * ms * 2 * 4, 256);
+    size_t cnt = align_up((size_t)B * n_heads * 4, 256);
+    return o + ml + cnt;
+}
+
+void decode_attn_bind_workspace(DecodeAttnArgs& a, void* ws, int max_pages_capacity) {
+    const int hd = a.geom.head_dim;
+    a.chunk_pages = decode_attn_chunk_pages(hd);
+    a.max_splits = (max_pages_capacity + a.chunk_pages - 1) / a.chunk_pages;
+    char* p = (char*)ws;
+    a.part_o = (float*)p;
+    p += align_up((size_t)a.B * a.n_heads * a.max_splits * hd * 4, 256);
+    a.part_ml = (float*)p;
+    p += align_up((size_t)a.B * a.n_heads * a.max_splits * 2 * 4, 256);
+    a.counters = (int*)p;
+}
+
+void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t s) {
+    const int max_pages = (max_ctx + kPage - 1) / kPage;
+    const int splits = (max_pages + a.chunk_pages - 1) / a.chunk_pages;
+    dim3 grid(splits, a.n_heads, a.B);
+    count_launch();
+    if (a.geom.head_dim == 64) {
+        const int smem = a.chunk_pages * 2 * kPage * 64 * 4;
+        ensure_smem(decode_attn_kernel<64>, smem);
+        decode_attn_kernel<64><<<grid, kAttnWarps * 32, smem, s>>>(a);
+    } else {
+        const int smem = a.chunk_pages * 2 * kPage * 128 * 4;
+        ensure_smem(decode_attn_kernel<128>, smem);
+        decode_attn_kernel<128><<<grid, kAttnWarps * 32, smem, s>>>(a);
+    }
+}
+
+void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
+    dim3 grid((a.T + kPrefillQ - 1) / kPrefillQ, a.n_heads);
+    count_launch();
+    if (a.geom.head_dim == 64) {
+        const int smem = (kStages * 2 * kPage * 64 + kPrefillQ * 64) * 4;
+        ensure_smem(prefill_attn_kernel<64>, smem);
+        prefill_attn_kernel<64><<<grid, kAttnWarps * 32, smem, s>>>(a);
+    } else {
+        const int smem = (kStages * 2 * kPage * 128 + kPrefillQ * 128) * 4;
+        ensure_smem(prefill_attn_kernel<128>, smem);
+        prefill_attn_kernel<128><<<grid, kAttnWarps * 32, smem, s>>>(a);
+    }
+}
+
+}  // namespace nitro

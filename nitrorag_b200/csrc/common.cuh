@@ -1,0 +1,108 @@
+// Device helpers shared by the engine's sm_100a kernels: bulk (TMA, non-tensor) copies
+// global -> shared completed on an mbarrier, bounded mbarrier waits, warp reductions and
+// the KV page addressing.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nitro {
+
+constexpr int kPage = 16;  // tokens per KV page (src/pagedMemory.hpp:9)
+
+// Error codes a kernel records in its error flag (first writer wins).
+constexpr int kErrWaitTimeout = 1;
+
+// Iteration limit of every mbarrier wait.  Each try_wait may itself suspend for a
+// hardware-chosen interval, so the limit bounds the wait to well under a second when a
+// copy never lands.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// Page layout of the device K and V pools: [page][layer][kv_head][16][head_dim] fp32, so
+// the 16 rows of one (page, layer, kv_head) form one contiguous tile of 16*head_dim floats.
+struct PoolGeom {
+    int n_layers;
+    int n_kv_heads;
+    int head_dim;
+    __host__ __device__ int64_t page_floats() const { return (int64_t)n_layers * n_kv_heads * kPage * head_dim; }
+    __host__ __device__ int64_t tile_offset(int64_t page, int layer, int kvh) const {
+        return page * page_floats() + ((int64_t)layer * n_kv_heads + kvh) * kPage * head_dim;
+    }
+};
+
+#if defined(__CUDACC__)
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Make mbarrier initialisation visible to the async proxy (the bulk-copy engine).
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// One bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from global
+// to this CTA's shared memory; completion is signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete, at most kSpinLimit polls.  On timeout
+// the error flag is set and false returned; the caller skips the work that needed the
+// data and returns.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < kSpinLimit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicCAS(err, 0, kErrWaitTimeout);
+    return false;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Greedy-sampling key: larger key = larger logit, ties broken towards the smaller index,
+// so an atomicMax over keys reproduces argmax's "first strictly greater" rule
+// (src/model_q8.cpp:559-569).  Only logits > 0 produce candidates; the initial key
+// encodes (0.0f, index 0), the reference's starting point.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
+}
+#endif  // __CUDACC__
+
+constexpr unsigned long long kArgmaxInitKey = (0x80000000ull << 32) | 0xffffffffull;
+
+}  // namespace nitro

@@ -1,0 +1,503 @@
+// Engine: model load, device pools and the forward passes of the Q8_0 decoder.
+//
+// forward_prefill follows forward_prefill_chunk (src/model_q8.cpp:424-557) and
+// forward_decode follows forward_decode_batch (:571-694), with the per-layer work fused
+// into five kernels:
+//   1. QKV projection  (RMSNorm prologue, RoPE + K/V page append epilogue)  :443-484 / :586-624
+//   2. paged attention                                                      :485-523 / :625-662
+//   3. output projection + residual                                         :524-528 / :663-666
+//   4. w1|w3 projection (RMSNorm prologue, SwiGLU epilogue)                  :529-545 / :668-681
+//   5. w2 projection + residual                                             :546-551 / :682-686
+// and the classifier (final RMSNorm prologue, fp32 embedding^T, greedy argmax keys).
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <string>
+
+#include "engine.h"
+
+namespace nitro {
+
+// ------------------------------------------------------------------ small kernels
+__global__ void embed_kernel(const float* emb, const int* tokens, int M, int dim, float* x,
+                             unsigned long long* keys) {
+    const int m = blockIdx.x;
+    const float4* src = reinterpret_cast<const float4*>(emb + (int64_t)tokens[m] * dim);
+    float4* dst = reinterpret_cast<float4*>(x + (int64_t)m * dim);
+    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) dst[i] = src[i];
+    if (threadIdx.x == 0) keys[m] = kArgmaxInitKey;
+}
+
+__global__ void argmax_finish_kernel(const unsigned long long* keys, int M, int* out) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m < M) out[m] = (int)(0xffffffffu - (uint32_t)(keys[m] & 0xffffffffull));
+}
+
+void launch_embed(const float* emb, const int* tokens, int M, int dim, float* x, unsigned long long* keys,
+                  cudaStream_t s) {
+    count_launch();
+    embed_kernel<<<M, 128, 0, s>>>(emb, tokens, M, dim, x, keys);
+}
+
+void launch_argmax_finish(const unsigned long long* keys, int M, int* out, cudaStream_t s) {
+    count_launch();
+    argmax_finish_kernel<<<(M + 127) / 128, 128, 0, s>>>(keys, M, out);
+}
+
+// ------------------------------------------------------------------ engine
+Engine::Engine(const nr_config& cfg, const ModelShape& shape) : cfg_(cfg), shape_(shape) {
+    mem_.reset(new KVBlockManager(cfg.total_blocks));
+    cache_.reset(new PrefixCacheManager(*mem_, cfg.total_blocks));
+    sched_.reset(new ContinuousScheduler(cfg.max_tokens_per_batch, cfg.max_new_tokens));
+}
+
+Engine::~Engine() {
+    if (!has_device()) return;
+    cudaSetDevice(cfg_.device);
+    if (stream_) cudaStreamSynchronize(stream_);
+    cudaFree(w_.base);
+    cudaFree(kpool_);
+    cudaFree(vpool_);
+    cudaFree(d_x_);
+    cudaFree(d_q_);
+    cudaFree(d_att_);
+    cudaFree(d_h_);
+    cudaFree(d_logits_);
+    cudaFree(d_keys_);
+    cudaFree(d_err_);
+    cudaFree(d_attn_ws_);
+    cudaFree(d_desc_);
+    cudaFreeHost(h_desc_);
+    cudaFreeHost(h_argmax_);
+    for (auto& ev : ev_pool_) cudaEventDestroy(ev);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+int Engine::check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return NR_OK;
+    return fail(NR_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define NR_CUDA(call)                                     \
+    do {                                                  \
+        int _rc = check_cuda((call), #call);              \
+        if (_rc != NR_OK) return _rc;                     \
+    } while (0)
+
+namespace {
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Repack `rows` rows of a Q8_0 tensor (array of 36-byte blocks, `K` weights per row) into
+// int8 [rows][K] + fp32 scales [rows][K/32], rows written at dst row indices rowmap(r).
+template <class RowMap>
+void repack_q8(const uint8_t* src, int rows, int K, int8_t* q, float* s, RowMap rowmap) {
+    const int nb = K / 32;
+    for (int r = 0; r < rows; r++) {
+        const int64_t dr = rowmap(r);
+        for (int b = 0; b < nb; b++) {
+            const uint8_t* blk = src + ((int64_t)r * nb + b) * 36;
+            memcpy(s + dr * nb + b, blk, 4);
+            memcpy(q + dr * K + (int64_t)b * 32, blk + 4, 32);
+        }
+    }
+}
+
+}  // namespace
+
+int Engine::upload_weights(const uint8_t* file, size_t size) {
+    const ModelShape& c = shape_;
+    const int D = c.dim, H = c.hidden, L = c.n_layers, KV = c.kv_dim(), hd = c.head_dim();
+    const int64_t q8 = 36;
+    // byte offsets of each tensor in the file (src/Server_Inference.cpp:53-68)
+    int64_t off = 28;
+    auto take = [&](int64_t bytes) { int64_t o = off; off += bytes; return o; };
+    const int64_t o_emb = take((int64_t)c.vocab * D * 4);
+    const int64_t o_rms_att = take((int64_t)L * D * 4);
+    const int64_t o_wq = take((int64_t)L * D * D / 32 * q8);
+    const int64_t o_wk = take((int64_t)L * D * KV / 32 * q8);
+    const int64_t o_wv = take((int64_t)L * D * KV / 32 * q8);
+    const int64_t o_wo = take((int64_t)L * D * D / 32 * q8);
+    const int64_t o_rms_ffn = take((int64_t)L * D * 4);
+    const int64_t o_w1 = take((int64_t)L * H * D / 32 * q8);
+    const int64_t o_w2 = take((int64_t)L * D * H / 32 * q8);
+    const int64_t o_w3 = take((int64_t)L * H * D / 32 * q8);
+    const int64_t o_rms_final = take((int64_t)D * 4);
+    const int64_t o_fre = take((int64_t)c.seq_len * hd / 2 * 4);
+    const int64_t o_fim = take((int64_t)c.seq_len * hd / 2 * 4);
+    if ((size_t)off > size)
+        return fail(NR_ERR_FORMAT, "model file is " + std::to_string(size) + " bytes, header implies " +
+                                       std::to_string(off));
+
+    // device layout: one allocation, 256-byte aligned pieces
+    const int NQKV = D + 2 * KV;
+    struct Piece { size_t bytes; void** dst; };
+    size_t total = 0;
+    std::vector<std::pair<size_t, void**>> pieces = {
+        {(size_t)c.vocab * D * 4, (void**)&w_.emb},
+        {(size_t)L * D * 4, (void**)&w_.rms_att},
+        {(size_t)L * D * 4, (void**)&w_.rms_ffn},
+        {(size_t)D * 4, (void**)&w_.rms_final},
+        {(size_t)c.seq_len * hd / 2 * 4, (void**)&w_.freq_re},
+        {(size_t)c.seq_len * hd / 2 * 4, (void**)&w_.freq_im},
+        {(size_t)L * NQKV * D, (void**)&w_.qkv_q},
+        {(size_t)L * NQKV * (D / 32) * 4, (void**)&w_.qkv_s},
+        {(size_t)L * D * D, (void**)&w_.wo_q},
+        {(size_t)L * D * (D / 32) * 4, (void**)&w_.wo_s},
+        {(size_t)L * 2 * H * D, (void**)&w_.w13_q},
+        {(size_t)L * 2 * H * (D / 32) * 4, (void**)&w_.w13_s},
+        {(size_t)L * D * H, (void**)&w_.w2_q},
+        {(size_t)L * D * (H / 32) * 4, (void**)&w_.w2_s},
+    };
+    for (auto& p : pieces) total += align256(p.first);
+    NR_CUDA(cudaMalloc(&w_.base, total));
+    w_.bytes = total;
+    {
+        char* p = (char*)w_.base;
+        for (auto& pc : pieces) {
+            *pc.second = p;
+            p += align256(pc.first);
+        }
+    }
+    // host image in the device layout, then one copy
+    std::vector<uint8_t> host(total);
+    auto hp = [&](void* dptr) { return host.data() + ((char*)dptr - (char*)w_.base); };
+    memcpy(hp(w_.emb), file + o_emb, (size_t)c.vocab * D * 4);
+    memcpy(hp(w_.rms_att), file + o_rms_att, (size_t)L * D * 4);
+    memcpy(hp(w_.rms_ffn), file + o_rms_ffn, (size_t)L * D * 4);
+    memcpy(hp(w_.rms_final), file + o_rms_final, (size_t)D * 4);
+    memcpy(hp(w_.freq_re), file + o_fre, (size_t)c.seq_len * hd / 2 * 4);
+    memcpy(hp(w_.freq_im), file + o_fim, (size_t)c.seq_len * hd / 2 * 4);
+    for (int l = 0; l < L; l++) {
+        int8_t* q = (int8_t*)hp(w_.qkv_q) + (int64_t)l * NQKV * D;
+        float* s = (float*)hp(w_.qkv_s) + (int64_t)l * NQKV * (D / 32);
+        repack_q8(file + o_wq + (int64_t)l * D * D / 32 * q8, D, D, q, s, [](int r) { return r; });
+        repack_q8(file + o_wk + (int64_t)l * KV * D / 32 * q8, KV, D, q, s, [&](int r) { return D + r; });
+        repack_q8(file + o_wv + (int64_t)l * KV * D / 32 * q8, KV, D, q, s, [&](int r) { return D + KV + r; });
+        repack_q8(file + o_wo + (int64_t)l * D * D / 32 * q8, D, D, (int8_t*)hp(w_.wo_q) + (int64_t)l * D * D,
+                  (float*)hp(w_.wo_s) + (int64_t)l * D * (D / 32), [](int r) { return r; });
+        int8_t* q13 = (int8_t*)hp(w_.w13_q) + (int64_t)l * 2 * H * D;
+        float* s13 = (float*)hp(w_.w13_s) + (int64_t)l * 2 * H * (D / 32);
+        repack_q8(file + o_w1 + (int64_t)l * H * D / 32 * q8, H, D, q13, s13, [](int r) { return 2 * r; });
+        repack_q8(file + o_w3 + (int64_t)l * H * D / 32 * q8, H, D, q13, s13, [](int r) { return 2 * r + 1; });
+        repack_q8(file + o_w2 + (int64_t)l * D * H / 32 * q8, D, H, (int8_t*)hp(w_.w2_q) + (int64_t)l * D * H,
+                  (float*)hp(w_.w2_s) + (int64_t)l * D * (H / 32), [](int r) { return r; });
+    }
+    NR_CUDA(cudaMemcpy(w_.base, host.data(), total, cudaMemcpyHostToDevice));
+    return NR_OK;
+}
+
+int Engine::init_device(const uint8_t* file, size_t size) {
+    if (!has_device()) return NR_OK;
+    const ModelShape& c = shape_;
+    if (c.head_dim() != 64 && c.head_dim() != 128)
+        return fail(NR_ERR_FORMAT, "head_dim must be 64 or 128, got " + std::to_string(c.head_dim()));
+    if (c.dim % 32 || c.hidden % 32 || c.kv_dim() % 32 || c.n_heads % c.n_kv_heads)
+        return fail(NR_ERR_FORMAT, "dim, hidden_dim and kv_dim must be multiples of 32");
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    NR_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    int rc = upload_weights(file, size);
+    if (rc != NR_OK) return rc;
+
+    geom_ = PoolGeom{c.n_layers, c.n_kv_heads, c.head_dim()};
+    const size_t pool_bytes = (size_t)cfg_.total_blocks * geom_.page_floats() * 4;
+    NR_CUDA(cudaMalloc(&kpool_, pool_bytes));
+    NR_CUDA(cudaMalloc(&vpool_, pool_bytes));
+    NR_CUDA(cudaMemsetAsync(kpool_, 0, pool_bytes, stream_));
+    NR_CUDA(cudaMemsetAsync(vpool_, 0, pool_bytes, stream_));
+
+    max_rows_ = std::max(cfg_.max_batch, cfg_.max_prefill_tokens);
+    const int R = max_rows_;
+    NR_CUDA(cudaMalloc(&d_x_, (size_t)R * c.dim * 4));
+    NR_CUDA(cudaMalloc(&d_q_, (size_t)R * c.dim * 4));
+    NR_CUDA(cudaMalloc(&d_att_, (size_t)R * c.dim * 4));
+    NR_CUDA(cudaMalloc(&d_h_, (size_t)R * c.hidden * 4));
+    NR_CUDA(cudaMalloc(&d_logits_, (size_t)cfg_.max_batch * c.vocab * 4));
+    NR_CUDA(cudaMalloc(&d_keys_, (size_t)R * 8));
+    NR_CUDA(cudaMalloc(&d_err_, (size_t)(R + 1) * 4));  // [0] error flag, [1..] argmax ids
+    d_argmax_ = d_err_ + 1;
+    NR_CUDA(cudaMemsetAsync(d_err_, 0, (size_t)(R + 1) * 4, stream_));
+    const size_t ws = decode_attn_workspace_bytes(cfg_.max_batch, c.n_heads, c.head_dim(), c.max_pages());
+    NR_CUDA(cudaMalloc(&d_attn_ws_, ws));
+    NR_CUDA(cudaMemsetAsync(d_attn_ws_, 0, ws, stream_));
+    desc_ints_ = (size_t)3 * R + cfg_.max_batch + (size_t)std::max(cfg_.max_batch, 1) * c.max_pages();
+    NR_CUDA(cudaMalloc(&d_desc_, desc_ints_ * 4));
+    NR_CUDA(cudaMallocHost(&h_desc_, desc_ints_ * 4));
+    NR_CUDA(cudaMallocHost(&h_argmax_, (size_t)(R + 1) * 4));
+    NR_CUDA(cudaStreamSynchronize(stream_));
+    return NR_OK;
+}
+
+void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos, int B_decode, int max_ctx,
+                        bool force_fixed) {
+    const ModelShape& c = shape_;
+    const int D = c.dim, H = c.hidden, KV = c.kv_dim(), NQKV = D + 2 * KV;
+    const bool faithful = cfg_.q8_mode == NR_Q8_FAITHFUL && !force_fixed;
+    for (int l = 0; l < c.n_layers; l++) {
+        // 1. q,k,v = Wqkv . rmsnorm(x); RoPE; k,v -> pages
+        GemmArgs g;
+        g.x = d_x_; g.ldx = D; g.norm_gain = w_.rms_att + (int64_t)l * D;
+        g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
+        g.M = M; g.N = NQKV; g.K = D; g.kbegin = faithful ? D - 32 : 0;
+        Epilogue e;
+        e.kind = kEpiQKV; e.q_out = d_q_; e.kpool = kpool_; e.vpool = vpool_; e.geom = geom_; e.layer = l;
+        e.tok_page = d_page_; e.tok_pos = d_pos_; e.freq_re = w_.freq_re; e.freq_im = w_.freq_im;
+        e.dim = D; e.kv_dim = KV; e.head_dim = c.head_dim();
+        { ProfScope ps(this, kKQKV); launch_gemm(g, e, stream_); }
+        // 2. attention
+        if (prefill) {
+            PrefillAttnArgs a;
+            a.q = d_q_; a.kpool = kpool_; a.vpool = vpool_; a.geom = geom_; a.layer = l;
+            a.block_table = d_bt_; a.T = M; a.start_pos = start_pos; a.n_heads = c.n_heads;
+            a.out = d_att_; a.err = d_err_;
+            ProfScope ps(this, kKAttn);
+            launch_prefill_attention(a, stream_);
+        } else {
+            DecodeAttnArgs a;
+            a.q = d_q_; a.kpool = kpool_; a.vpool = vpool_; a.geom = geom_; a.layer = l;
+            a.block_tables = d_bt_; a.max_pages = c.max_pages(); a.ctx_lens = d_ctx_;
+            a.B = B_decode; a.n_heads = c.n_heads; a.out = d_att_; a.err = d_err_;
+            // partial buffers are laid out for max_batch rows so B may vary per call
+            a.B = cfg_.max_batch;
+            decode_attn_bind_workspace(a, d_attn_ws_, c.max_pages());
+            a.B = B_decode;
+            ProfScope ps(this, kKAttn);
+            launch_decode_attention(a, max_ctx, stream_);
+        }
+        // 3. x += Wo . att
+        GemmArgs go;
+        go.x = d_att_; go.ldx = D; go.wq = w_.wo_q + (int64_t)l * D * D; go.ws = w_.wo_s + (int64_t)l * D * (D / 32);
+        go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
+        Epilogue eo;
+        eo.kind = kEpiResidual; eo.out = d_x_; eo.ldo = D;
+        { ProfScope ps(this, kKWo); launch_gemm(go, eo, stream_); }
+        // 4. h = silu(W1 . rmsnorm(x)) * (W3 . rmsnorm(x))
+        GemmArgs g13;
+        g13.x = d_x_; g13.ldx = D; g13.norm_gain = w_.rms_ffn + (int64_t)l * D;
+        g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
+        g13.M = M; g13.N = 2 * H; g13.K = D; g13.kbegin = faithful ? D - 32 : 0;
+        Epilogue e13;
+        e13.kind = kEpiSwiGLU; e13.out = d_h_; e13.ldo = H;
+        { ProfScope ps(this, kKW13); launch_gemm(g13, e13, stream_); }
+        // 5. x += W2 . h
+        GemmArgs g2;
+        g2.x = d_h_; g2.ldx = H; g2.wq = w_.w2_q + (int64_t)l * D * H; g2.ws = w_.w2_s + (int64_t)l * D * (H / 32);
+        g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
+        Epilogue e2;
+        e2.kind = kEpiResidual; e2.out = d_x_; e2.ldo = D;
+        { ProfScope ps(this, kKW2); launch_gemm(g2, e2, stream_); }
+    }
+    (void)seq;
+}
+
+int Engine::forward_prefill(const Sequence& seq, const int* tokens, int T, int start_pos, float* logits_out,
+                            int* argmax_out) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    const ModelShape& c = shape_;
+    if (T <= 0) return fail(NR_ERR_INVALID, "empty prefill chunk");
+    if (T > cfg_.max_prefill_tokens) return fail(NR_ERR_CAPACITY, "prefill chunk exceeds max_prefill_tokens");
+    if (start_pos < 0 || start_pos + T > c.seq_len) return fail(NR_ERR_INVALID, "positions exceed seq_len");
+    const int last_page = (start_pos + T - 1) / kBlockSize;
+    if (last_page >= (int)seq.block_table.size()) return fail(NR_ERR_INVALID, "block table does not cover the chunk");
+    for (int t = 0; t < T; t++)
+        if (tokens[t] < 0 || tokens[t] >= c.vocab) return fail(NR_ERR_INVALID, "token id out of range");
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    // descriptor: tok[T] pos[T] page[T] bt[n_pages]
+    const int np = (int)seq.block_table.size();
+    int* h = h_desc_;
+    h_tok_ = h; h_pos_ = h + T; h_page_ = h + 2 * T; h_bt_ = h + 3 * T;
+    for (int t = 0; t < T; t++) {
+        const int pos = start_pos + t;
+        h_tok_[t] = tokens[t];
+        h_pos_[t] = pos;
+        h_page_[t] = seq.block_table[pos / kBlockSize];
+    }
+    for (int p = 0; p < np; p++) h_bt_[p] = seq.block_table[p];
+    const size_t n_ints = (size_t)3 * T + np;
+    if (n_ints > desc_ints_) return fail(NR_ERR_CAPACITY, "descriptor overflow");
+    d_tok_ = d_desc_; d_pos_ = d_desc_ + T; d_page_ = d_desc_ + 2 * T; d_bt_ = d_desc_ + 3 * T;
+    NR_CUDA(cudaMemcpyAsync(d_desc_, h_desc_, n_ints * 4, cudaMemcpyHostToDevice, stream_));
+    last_valid_ = false;  // the descriptor no longer holds a decode step
+    { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, T, c.dim, d_x_, d_keys_, stream_); }
+    run_layers(T, true, &seq, start_pos, 0, start_pos + T, false);
+    // classifier over the last token (src/model_q8.cpp:553-556)
+    GemmArgs gl;
+    gl.x = d_x_ + (int64_t)(T - 1) * c.dim; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
+    gl.M = 1; gl.N = c.vocab; gl.K = c.dim;
+    Epilogue el;
+    el.kind = kEpiLogits; el.out = logits_out ? d_logits_ : nullptr; el.ldo = c.vocab; el.argmax_keys = d_keys_;
+    { ProfScope ps(this, kKLogits); launch_gemm(gl, el, stream_); }
+    { ProfScope ps(this, kKArgmax); launch_argmax_finish(d_keys_, 1, d_argmax_, stream_); }
+    NR_CUDA(cudaMemcpyAsync(h_argmax_, d_err_, 2 * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits_out)
+        NR_CUDA(cudaMemcpyAsync(logits_out, d_logits_, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+    NR_CUDA(cudaStreamSynchronize(stream_));
+    NR_CUDA(cudaGetLastError());
+    if (h_argmax_[0] != 0) return fail(NR_ERR_TIMEOUT, "device wait timed out");
+    if (argmax_out) *argmax_out = h_argmax_[1];
+    stats.prefill_tokens += T;
+    if (profiling_) return prof_flush();
+    return NR_OK;
+}
+
+int Engine::forward_decode(int B, const int* tokens, const int* positions, const Sequence* const* seqs,
+                           float* logits_out, int* argmax_out, bool force_fixed) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    const ModelShape& c = shape_;
+    if (B <= 0) return fail(NR_ERR_INVALID, "empty decode batch");
+    if (B > cfg_.max_batch) return fail(NR_ERR_CAPACITY, "decode batch exceeds max_batch");
+    const int MP = c.max_pages();
+    int max_ctx = 0;
+    for (int b = 0; b < B; b++) {
+        const int pos = positions[b];
+        if (pos < 0 || pos >= c.seq_len) return fail(NR_ERR_INVALID, "position outside [0, seq_len)");
+        if (tokens[b] < 0 || tokens[b] >= c.vocab) return fail(NR_ERR_INVALID, "token id out of range");
+        if (pos / kBlockSize >= (int)seqs[b]->block_table.size())
+            return fail(NR_ERR_INVALID, "block table does not cover the position");
+        max_ctx = std::max(max_ctx, pos + 1);
+    }
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    // descriptor: tok[B] pos[B] page[B] ctx[B] bt[B][MP]
+    int* h = h_desc_;
+    h_tok_ = h; h_pos_ = h + B; h_page_ = h + 2 * B; h_ctx_ = h + 3 * B; h_bt_ = h + 4 * B;
+    for (int b = 0; b < B; b++) {
+        const int pos = positions[b];
+        const std::vector<int>& bt = seqs[b]->block_table;
+        h_tok_[b] = tokens[b];
+        h_pos_[b] = pos;
+        h_page_[b] = bt[pos / kBlockSize];
+        h_ctx_[b] = pos + 1;
+        const int used = pos / kBlockSize + 1;
+        for (int p = 0; p < used; p++) h_bt_[(size_t)b * MP + p] = bt[p];
+    }
+    const size_t n_ints = (size_t)4 * B + (size_t)B * MP;
+    d_tok_ = d_desc_; d_pos_ = d_desc_ + B; d_page_ = d_desc_ + 2 * B; d_ctx_ = d_desc_ + 3 * B;
+    d_bt_ = d_desc_ + 4 * B;
+    NR_CUDA(cudaMemcpyAsync(d_desc_, h_desc_, n_ints * 4, cudaMemcpyHostToDevice, stream_));
+    enqueue_decode(B, max_ctx, force_fixed, logits_out != nullptr);
+    last_B_ = B; last_max_ctx_ = max_ctx; last_force_fixed_ = force_fixed; last_valid_ = true;
+    NR_CUDA(cudaMemcpyAsync(h_argmax_, d_err_, (size_t)(B + 1) * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits_out)
+        NR_CUDA(cudaMemcpyAsync(logits_out, d_logits_, (size_t)B * c.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+    NR_CUDA(cudaStreamSynchronize(stream_));
+    NR_CUDA(cudaGetLastError());
+    if (h_argmax_[0] != 0) return fail(NR_ERR_TIMEOUT, "device wait timed out");
+    if (argmax_out) memcpy(argmax_out, h_argmax_ + 1, (size_t)B * 4);
+    stats.decode_tokens += B;
+    if (profiling_) return prof_flush();
+    return NR_OK;
+}
+
+void Engine::enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logits) {
+    const ModelShape& c = shape_;
+    d_tok_ = d_desc_; d_pos_ = d_desc_ + B; d_page_ = d_desc_ + 2 * B; d_ctx_ = d_desc_ + 3 * B;
+    d_bt_ = d_desc_ + 4 * B;
+    { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, B, c.dim, d_x_, d_keys_, stream_); }
+    run_layers(B, false, nullptr, 0, B, max_ctx, force_fixed);
+    GemmArgs gl;
+    gl.x = d_x_; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
+    gl.M = B; gl.N = c.vocab; gl.K = c.dim;
+    Epilogue el;
+    el.kind = kEpiLogits; el.out = want_logits ? d_logits_ : nullptr; el.ldo = c.vocab; el.argmax_keys = d_keys_;
+    { ProfScope ps(this, kKLogits); launch_gemm(gl, el, stream_); }
+    { ProfScope ps(this, kKArgmax); launch_argmax_finish(d_keys_, B, d_argmax_, stream_); }
+}
+
+int Engine::replay_decode(int n) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    if (!last_valid_) return fail(NR_ERR_INVALID, "no decode step to replay");
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    for (int i = 0; i < n; i++) {
+        enqueue_decode(last_B_, last_max_ctx_, last_force_fixed_, false);
+        if (profiling_ && ev_used_ + 512 > ev_pool_.size()) {
+            int rc = prof_flush();
+            if (rc) return rc;
+        }
+    }
+    NR_CUDA(cudaGetLastError());
+    return NR_OK;
+}
+
+// ------------------------------------------------------------------ profiling
+int Engine::set_profiling(bool on) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    if (on && ev_pool_.empty()) {
+        ev_pool_.resize(8192);
+        for (auto& ev : ev_pool_) NR_CUDA(cudaEventCreate(&ev));
+    }
+    if (on) {
+        for (int i = 0; i < kKClasses; i++) { kt_ms_[i] = 0; kt_n_[i] = 0; }
+        ev_used_ = 0;
+        ev_pairs_.clear();
+    } else if (profiling_) {
+        int rc = prof_flush();
+        if (rc) return rc;
+    }
+    profiling_ = on;
+    return NR_OK;
+}
+
+void Engine::prof_mark(int cls, bool begin) {
+    if (!profiling_ || ev_used_ + 2 > ev_pool_.size()) return;
+    if (begin) {
+        open_cls_ = cls;
+        ev_pairs_.push_back({(int)ev_used_, cls});
+        cudaEventRecord(ev_pool_[ev_used_++], stream_);
+    } else {
+        cudaEventRecord(ev_pool_[ev_used_++], stream_);
+        open_cls_ = -1;
+    }
+}
+
+int Engine::prof_flush() {
+    if (ev_pairs_.empty()) return NR_OK;
+    NR_CUDA(cudaStreamSynchronize(stream_));
+    for (auto& pr : ev_pairs_) {
+        float ms = 0.0f;
+        NR_CUDA(cudaEventElapsedTime(&ms, ev_pool_[pr.first], ev_pool_[pr.first + 1]));
+        kt_ms_[pr.second] += ms;
+        kt_n_[pr.second] += 1;
+    }
+    ev_pairs_.clear();
+    ev_used_ = 0;
+    return NR_OK;
+}
+
+int Engine::kernel_times(double* ms, int64_t* launches) {
+    if (profiling_) {
+        int rc = prof_flush();
+        if (rc) return rc;
+    }
+    for (int i = 0; i < kKClasses; i++) {
+        if (ms) ms[i] = kt_ms_[i];
+        if (launches) launches[i] = kt_n_[i];
+    }
+    return NR_OK;
+}
+
+int Engine::read_page(int block, float* k_out, float* v_out) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    if (block < 0 || block >= cfg_.total_blocks) return fail(NR_ERR_INVALID, "block id out of range");
+    const ModelShape& c = shape_;
+    const int hd = c.head_dim(), KV = c.kv_dim();
+    const size_t pf = (size_t)geom_.page_floats();
+    std::vector<float> tmp(pf);
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    for (int which = 0; which < 2; which++) {
+        float* dst = which == 0 ? k_out : v_out;
+        if (!dst) continue;
+        const float* src = (which == 0 ? kpool_ : vpool_) + (size_t)block * pf;
+        NR_CUDA(cudaMemcpyAsync(tmp.data(), src, pf * 4, cudaMemcpyDeviceToHost, stream_));
+        NR_CUDA(cudaStreamSynchronize(stream_));
+        // [layer][kv_head][16][hd] -> [layer][16][kv_dim]
+        for (int l = 0; l < c.n_layers; l++)
+            for (int h = 0; h < c.n_kv_heads; h++)
+                for (int r = 0; r < kBlockSize; r++)
+                    memcpy(dst + ((size_t)l * kBlockSize + r) * KV + (size_t)h * hd,
+                           tmp.data() + (((size_t)l * c.n_kv_heads + h) * kBlockSize + r) * hd, (size_t)hd * 4);
+    }
+    return NR_OK;
+}
+
+}  // namespace nitro

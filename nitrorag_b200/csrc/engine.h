@@ -1,0 +1,150 @@
+// The engine object behind the C ABI: model shape, device weights, the device KV pools,
+// the host page metadata (paged_memory.h) and the forward passes.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/nitro_engine.h"
+#include "kernels.h"
+#include "paged_memory.h"
+
+namespace nitro {
+
+struct ModelShape {
+    int dim = 0, hidden = 0, n_layers = 0, n_heads = 0, n_kv_heads = 0, vocab = 0, seq_len = 0;
+    int head_dim() const { return dim / n_heads; }
+    int kv_dim() const { return n_kv_heads * head_dim(); }
+    int max_pages() const { return (seq_len + kBlockSize - 1) / kBlockSize; }
+};
+
+// Weights in device memory.  Q8_0 tensors are repacked at load time from the file's
+// array of 36-byte blocks (fp32 scale + 32 int8, src/model_q8.cpp:29-32) into two arrays
+// with the same values: int8 [rows][K] and fp32 scales [rows][K/32].  Per layer the q, k
+// and v projections are stacked into one [dim + 2*kv_dim][dim] matrix and w1/w3 are
+// interleaved row by row into one [2*hidden][dim] matrix so that one kernel computes each.
+struct DeviceWeights {
+    float* emb = nullptr;        // [vocab][dim], also the classifier (src/Server_Inference.cpp:69)
+    float* rms_att = nullptr;    // [L][dim]
+    float* rms_ffn = nullptr;    // [L][dim]
+    float* rms_final = nullptr;  // [dim]
+    float* freq_re = nullptr;    // [seq_len][head_dim/2]
+    float* freq_im = nullptr;
+    int8_t* qkv_q = nullptr; float* qkv_s = nullptr;  // [L][dim+2kv][dim]
+    int8_t* wo_q = nullptr;  float* wo_s = nullptr;   // [L][dim][dim]
+    int8_t* w13_q = nullptr; float* w13_s = nullptr;  // [L][2*hidden][dim]
+    int8_t* w2_q = nullptr;  float* w2_s = nullptr;   // [L][dim][hidden]
+    void* base = nullptr;
+    size_t bytes = 0;
+};
+
+// Kernel classes timed by the engine's optional per-launch CUDA-event profiling.
+enum KernelClass : int { kKEmbed = 0, kKQKV, kKAttn, kKWo, kKW13, kKW2, kKLogits, kKArgmax, kKClasses };
+
+class Engine {
+public:
+    Engine(const nr_config& cfg, const ModelShape& shape);
+    ~Engine();
+
+    // Device set-up; `file` is the whole model image (nullptr for host-only engines).
+    int init_device(const uint8_t* file, size_t size);
+
+    const nr_config& cfg() const { return cfg_; }
+    const ModelShape& shape() const { return shape_; }
+    bool has_device() const { return cfg_.device >= 0; }
+    cudaStream_t stream() const { return stream_; }
+
+    // page metadata
+    KVBlockManager& mem() { return *mem_; }
+    PrefixCacheManager& cache() { return *cache_; }
+    ContinuousScheduler& sched() { return *sched_; }
+
+    // requests and bare sequences share one table of Request objects
+    std::map<int, std::unique_ptr<Request>> requests;  // scheduler requests by req_id
+    std::map<int, std::unique_ptr<Request>> seqs;      // sequence handles
+    int next_seq_handle = 1;
+
+    // forward passes over already-allocated tokens (block tables complete)
+    int forward_prefill(const Sequence& seq, const int* tokens, int T, int start_pos, float* logits_out,
+                        int* argmax_out);
+    int forward_decode(int B, const int* tokens, const int* positions, const Sequence* const* seqs,
+                       float* logits_out, int* argmax_out, bool force_fixed = false);
+    int read_page(int block, float* k_out, float* v_out);
+    // Enqueue the kernels of the last decode step again, n times, on the engine stream
+    // (its descriptor is still resident); returns without synchronising.
+    int replay_decode(int n);
+
+    // profiling: CUDA events around every launch, accumulated per KernelClass
+    int set_profiling(bool on);
+    int kernel_times(double* ms, int64_t* launches);
+    void prof_mark(int cls, bool begin);
+
+    std::string last_error;
+    nr_stats stats{};
+
+    int fail(int code, const std::string& msg) {
+        last_error = msg;
+        return code;
+    }
+
+private:
+    int upload_weights(const uint8_t* file, size_t size);
+    void enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logits);
+    int prof_flush();
+    int check_cuda(cudaError_t e, const char* what);
+    void run_layers(int M, bool prefill, const Sequence* seq, int start_pos, int B_decode, int max_ctx,
+                    bool force_fixed);
+
+    nr_config cfg_;
+    ModelShape shape_;
+    std::unique_ptr<KVBlockManager> mem_;
+    std::unique_ptr<PrefixCacheManager> cache_;
+    std::unique_ptr<ContinuousScheduler> sched_;
+
+    // device state
+    cudaStream_t stream_ = nullptr;
+    DeviceWeights w_;
+    float* kpool_ = nullptr;
+    float* vpool_ = nullptr;
+    PoolGeom geom_{};
+    int max_rows_ = 0;
+    float* d_x_ = nullptr;     // [max_rows][dim] residual stream
+    float* d_q_ = nullptr;     // [max_rows][dim]
+    float* d_att_ = nullptr;   // [max_rows][dim]
+    float* d_h_ = nullptr;     // [max_rows][hidden]
+    float* d_logits_ = nullptr;  // [max_batch][vocab]
+    unsigned long long* d_keys_ = nullptr;  // [max_rows]
+    int* d_argmax_ = nullptr;  // [max_rows]
+    int* d_err_ = nullptr;
+    void* d_attn_ws_ = nullptr;
+    // step descriptor: tokens, positions, pages, ctx, block tables (device + pinned host)
+    int* d_desc_ = nullptr;
+    int* h_desc_ = nullptr;
+    size_t desc_ints_ = 0;
+    int* d_tok_ = nullptr; int* d_pos_ = nullptr; int* d_page_ = nullptr; int* d_ctx_ = nullptr; int* d_bt_ = nullptr;
+    int* h_tok_ = nullptr; int* h_pos_ = nullptr; int* h_page_ = nullptr; int* h_ctx_ = nullptr; int* h_bt_ = nullptr;
+    int* h_argmax_ = nullptr;
+    // last decode step (for replay)
+    int last_B_ = 0, last_max_ctx_ = 0;
+    bool last_force_fixed_ = false, last_valid_ = false;
+    // profiling state
+    bool profiling_ = false;
+    std::vector<cudaEvent_t> ev_pool_;
+    std::vector<std::pair<int, int>> ev_pairs_;  // (first event index, class)
+    size_t ev_used_ = 0;
+    int open_cls_ = -1;
+    double kt_ms_[kKClasses] = {};
+    int64_t kt_n_[kKClasses] = {};
+};
+
+struct ProfScope {
+    Engine* e;
+    int cls;
+    ProfScope(Engine* eng, int c) : e(eng), cls(c) { e->prof_mark(cls, true); }
+    ~ProfScope() { e->prof_mark(cls, false); }
+};
+
+}  // namespace nitro

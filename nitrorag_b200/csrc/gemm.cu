@@ -1,0 +1,338 @@
+// Q8_0 / fp32 projections on CUDA cores with fused prologue and epilogues.
+//
+// Two shapes:
+//   * gemv_kernel, M <= 8 token rows (decode at small batch, the last prefill token):
+//     HBM-bound matvec.  One warp owns an adjacent pair of output rows and streams their
+//     int8 weights with 16-byte loads (16 weights per lane per step, one fp32 scale per
+//     32-wide block), dequantises in registers (w = q * scale, as src/model_q8.cpp:107-111)
+//     and accumulates every token row against them.
+//   * gemm_tiled_kernel, M > 8: 64x64 output tiles staged through shared memory in
+//     32-wide K chunks (one Q8 block), register double-buffered, 8x4 micro-tile per thread.
+//
+// Both apply, when asked, the RMSNorm of the input rows (src/model_q8.cpp:128-140) while
+// loading them, and one of the epilogues of kernels.h.  Accumulation is fp32 throughout.
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nitro {
+
+namespace {
+
+std::atomic<int64_t> g_launches{0};
+
+__device__ __forceinline__ float silu_mul(float a, float b) {
+    // src/model_q8.cpp:541-542: val *= 1/(1+expf(-val)); val *= h3
+    float v = a * (1.0f / (1.0f + expf(-a)));
+    return v * b;
+}
+
+__device__ __forceinline__ void argmax_offer(unsigned long long* key_slot, unsigned long long key) {
+    // a plain read first: most offers lose to the current maximum and skip the atomic
+    if (key > *(volatile unsigned long long*)key_slot) atomicMax(key_slot, key);
+}
+
+// Epilogue for one token row m and the adjacent output rows (n, n+1), n even.
+__device__ __forceinline__ void epi_pair(const Epilogue& e, int m, int n, float v0, float v1) {
+    switch (e.kind) {
+    case kEpiStore:
+        e.out[(int64_t)m * e.ldo + n] = v0;
+        e.out[(int64_t)m * e.ldo + n + 1] = v1;
+        break;
+    case kEpiResidual:
+        e.out[(int64_t)m * e.ldo + n] += v0;
+        e.out[(int64_t)m * e.ldo + n + 1] += v1;
+        break;
+    case kEpiSwiGLU:
+        e.out[(int64_t)m * e.ldo + (n >> 1)] = silu_mul(v0, v1);
+        break;
+    case kEpiQKV: {
+        const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+        const int pos = e.tok_pos[m];
+        if (n < D + KV) {
+            // RoPE pair (j, j+1), angle index (j % head)/2 (src/model_q8.cpp:601-615)
+            int c = n < D ? n : n - D;
+            int fi = pos * (hd >> 1) + ((c % hd) >> 1);
+            float fcr = e.freq_re[fi], fci = e.freq_im[fi];
+            float r0 = v0 * fcr - v1 * fci;
+            float r1 = v0 * fci + v1 * fcr;
+            if (n < D) {
+                e.q_out[(int64_t)m * D + n] = r0;
+                e.q_out[(int64_t)m * D + n + 1] = r1;
+            } else {
+                float* dst = e.kpool + e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
+                             (int64_t)(pos & (kPage - 1)) * hd + (c % hd);
+                dst[0] = r0;
+                dst[1] = r1;
+            }
+        } else {
+            int c = n - D - KV;
+            float* dst = e.vpool + e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
+                         (int64_t)(pos & (kPage - 1)) * hd + (c % hd);
+            dst[0] = v0;
+            dst[1] = v1;
+        }
+        break;
+    }
+    default:
+        break;
+    }
+}
+
+__device__ __forceinline__ void load16_f32(const float* p, float* r) {
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float4 v = __ldg(p4 + i);
+        r[4 * i] = v.x; r[4 * i + 1] = v.y; r[4 * i + 2] = v.z; r[4 * i + 3] = v.w;
+    }
+}
+
+// 16 consecutive Q8 weights of row n starting at k (k % 16 == 0), dequantised.
+__device__ __forceinline__ void load16_q8(const int8_t* wq, const float* ws, int64_t n, int K, int k, float* r) {
+    int4 raw = __ldg(reinterpret_cast<const int4*>(wq + n * K + k));
+    float s = __ldg(ws + n * (K >> 5) + (k >> 5));
+    const int8_t* q = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 16; i++) r[i] = (float)q[i] * s;
+}
+
+// Per-row inverse RMS of x rows [m0, m0+count) into inv[] (one warp per row).
+__device__ __forceinline__ void rms_rows(const float* x, int ldx, int K, int m0, int count, int M, float* inv) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int r = warp; r < count; r += nw) {
+        int m = m0 + r;
+        float ss = 0.0f;
+        if (m < M) {
+            const float* row = x + (int64_t)m * ldx;
+            for (int k = lane * 4; k < K; k += 128) {
+                float4 v = *reinterpret_cast<const float4*>(row + k);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) inv[r] = 1.0f / sqrtf(ss / (float)K + 1e-5f);
+    }
+}
+
+// ------------------------------------------------------------------ matvec, M <= 8
+template <int MT, bool F32W>
+__global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
+    constexpr int WARPS = 4;
+    __shared__ float inv_rms[MT];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool norm = a.norm_gain != nullptr;
+    if (norm) {
+        rms_rows(a.x, a.ldx, a.K, 0, MT, a.M, inv_rms);
+        __syncthreads();
+    }
+    const int n = (blockIdx.x * WARPS + warp) * 2;
+    if (n >= a.N) return;
+    float acc0[MT], acc1[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) acc0[m] = acc1[m] = 0.0f;
+
+    for (int k = a.kbegin + lane * 16; k < a.K; k += 32 * 16) {
+        float w0[16], w1[16];
+        if (F32W) {
+            load16_f32(a.wf + (int64_t)n * a.K + k, w0);
+            load16_f32(a.wf + (int64_t)(n + 1) * a.K + k, w1);
+        } else {
+            load16_q8(a.wq, a.ws, n, a.K, k, w0);
+            load16_q8(a.wq, a.ws, n + 1, a.K, k, w1);
+        }
+        float g[16];
+        if (norm) load16_f32(a.norm_gain + k, g);
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            if (m < a.M) {
+                float xv[16];
+                load16_f32(a.x + (int64_t)m * a.ldx + k, xv);
+                if (norm) {
+                    float inv = inv_rms[m];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) xv[i] = g[i] * (inv * xv[i]);
+                }
+                float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    s0 = fmaf(w0[i], xv[i], s0);
+                    s1 = fmaf(w1[i], xv[i], s1);
+                }
+                acc0[m] += s0;
+                acc1[m] += s1;
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+        acc0[m] = warp_sum(acc0[m]);
+        acc1[m] = warp_sum(acc1[m]);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+        if (m < a.M && lane == m) {
+            if (e.kind == kEpiLogits) {
+                if (e.out) {
+                    e.out[(int64_t)m * e.ldo + n] = acc0[m];
+                    e.out[(int64_t)m * e.ldo + n + 1] = acc1[m];
+                }
+                // n before n+1: the smaller index wins a tie
+                float best = acc0[m];
+                int bi = n;
+                if (acc1[m] > best) { best = acc1[m]; bi = n + 1; }
+                if (best > 0.0f) argmax_offer(e.argmax_keys + m, argmax_key(best, bi));
+            } else {
+                epi_pair(e, m, n, acc0[m], acc1[m]);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ tiled, M > 8
+constexpr int TN = 64, TM = 64, KC = 32;
+
+template <bool F32W>
+__global__ void __launch_bounds__(128) gemm_tiled_kernel(GemmArgs a, Epilogue e) {
+    __shared__ __align__(16) float Ws[2][KC][TN];
+    __shared__ __align__(16) float Xs[2][KC][TM];
+    __shared__ float inv_rms[TM];
+    const int tid = threadIdx.x;
+    const int n_base = blockIdx.x * TN, m_base = blockIdx.y * TM;
+    const bool norm = a.norm_gain != nullptr;
+    if (norm) {
+        rms_rows(a.x, a.ldx, a.K, m_base, TM, a.M, inv_rms);
+        __syncthreads();
+    }
+    const int tn = tid & 15, tm = tid >> 4;      // compute: 4 n x 8 m per thread
+    const int lr = tid >> 1, lh = (tid & 1) * 16;  // loader: row/token lr, k half lh
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+
+    float wreg[16], xreg[16];
+    auto load_chunk = [&](int kc) {
+        const int n = n_base + lr;
+        if (n < a.N) {
+            if (F32W) load16_f32(a.wf + (int64_t)n * a.K + kc + lh, wreg);
+            else load16_q8(a.wq, a.ws, n, a.K, kc + lh, wreg);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; i++) wreg[i] = 0.0f;
+        }
+        const int m = m_base + lr;
+        if (m < a.M) {
+            load16_f32(a.x + (int64_t)m * a.ldx + kc + lh, xreg);
+            if (norm) {
+                float g[16];
+                load16_f32(a.norm_gain + kc + lh, g);
+                float inv = inv_rms[lr];
+#pragma unroll
+                for (int i = 0; i < 16; i++) xreg[i] = g[i] * (inv * xreg[i]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; i++) xreg[i] = 0.0f;
+        }
+    };
+    auto store_chunk = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            Ws[buf][lh + i][lr] = wreg[i];
+            Xs[buf][lh + i][lr] = xreg[i];
+        }
+    };
+
+    const int nk = (a.K - a.kbegin) / KC;
+    load_chunk(a.kbegin);
+    store_chunk(0);
+    __syncthreads();
+    for (int c = 0; c < nk; c++) {
+        const int buf = c & 1;
+        if (c + 1 < nk) load_chunk(a.kbegin + (c + 1) * KC);
+#pragma unroll
+        for (int k = 0; k < KC; k++) {
+            float4 w = *reinterpret_cast<const float4*>(&Ws[buf][k][tn * 4]);
+            float4 x0 = *reinterpret_cast<const float4*>(&Xs[buf][k][tm * 8]);
+            float4 x1 = *reinterpret_cast<const float4*>(&Xs[buf][k][tm * 8 + 4]);
+            float wv[4] = {w.x, w.y, w.z, w.w};
+            float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(wv[i], xv[j], acc[i][j]);
+        }
+        if (c + 1 < nk) store_chunk(buf ^ 1);
+        __syncthreads();
+    }
+
+    const int n0 = n_base + tn * 4;
+    if (e.kind == kEpiLogits) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int m = m_base + tm * 8 + j;
+            unsigned long long best = 0ull;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int n = n0 + i;
+                if (n < a.N && m < a.M) {
+                    if (e.out) e.out[(int64_t)m * e.ldo + n] = acc[i][j];
+                    if (acc[i][j] > 0.0f) {
+                        unsigned long long k = argmax_key(acc[i][j], n);
+                        best = k > best ? k : best;
+                    }
+                }
+            }
+            // the 16 lanes sharing tm hold the tile's 64 columns of row m
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+                best = other > best ? other : best;
+            }
+            if (tn == 0 && best != 0ull && m < a.M) argmax_offer(e.argmax_keys + m, best);
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int m = m_base + tm * 8 + j;
+        if (m >= a.M) continue;
+#pragma unroll
+        for (int i = 0; i < 4; i += 2) {
+            const int n = n0 + i;
+            if (n < a.N) epi_pair(e, m, n, acc[i][j], acc[i + 1][j]);
+        }
+    }
+}
+
+template <int MT>
+void gemv_dispatch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
+    dim3 grid((a.N / 2 + 3) / 4);
+    if (a.wf) gemv_kernel<MT, true><<<grid, 128, 0, s>>>(a, e);
+    else gemv_kernel<MT, false><<<grid, 128, 0, s>>>(a, e);
+}
+
+}  // namespace
+
+void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
+    g_launches++;
+    if (a.M <= 1) gemv_dispatch<1>(a, e, s);
+    else if (a.M <= 2) gemv_dispatch<2>(a, e, s);
+    else if (a.M <= 4) gemv_dispatch<4>(a, e, s);
+    else if (a.M <= 8) gemv_dispatch<8>(a, e, s);
+    else {
+        dim3 grid((a.N + TN - 1) / TN, (a.M + TM - 1) / TM);
+        if (a.wf) gemm_tiled_kernel<true><<<grid, 128, 0, s>>>(a, e);
+        else gemm_tiled_kernel<false><<<grid, 128, 0, s>>>(a, e);
+    }
+}
+
+int64_t kernel_launch_count() { return g_launches.load(); }
+void count_launch() { g_launches++; }
+
+}  // namespace nitro

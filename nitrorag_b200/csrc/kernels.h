@@ -1,0 +1,104 @@
+// Host-side launchers of the engine's sm_100a kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace nitro {
+
+// What a projection does with its result tile.
+enum EpiKind : int {
+    kEpiStore = 0,     // out[m][n] = acc
+    kEpiResidual = 1,  // out[m][n] += acc                          (src/model_q8.cpp:524-528, :546-551)
+    kEpiQKV = 2,       // RoPE on q,k; q -> q_out, k,v -> KV pages  (:451-484, :594-624)
+    kEpiSwiGLU = 3,    // rows interleaved (w1 i, w3 i): out[m][i] = silu(acc[2i]) * acc[2i+1]  (:535-545)
+    kEpiLogits = 4,    // optional store + greedy argmax keys      (:553-556, :688-693, :559-569)
+};
+
+struct Epilogue {
+    int kind = kEpiStore;
+    float* out = nullptr;   // STORE / RESIDUAL / SWIGLU / LOGITS (may be null for LOGITS)
+    int ldo = 0;
+    // QKV
+    float* q_out = nullptr;  // [M][dim]
+    float* kpool = nullptr;
+    float* vpool = nullptr;
+    PoolGeom geom{};
+    int layer = 0;
+    const int* tok_page = nullptr;  // [M] physical page of each row's token
+    const int* tok_pos = nullptr;   // [M] position of each row's token
+    const float* freq_re = nullptr; // [seq_len][head_dim/2]
+    const float* freq_im = nullptr;
+    int dim = 0, kv_dim = 0, head_dim = 0;
+    // LOGITS
+    unsigned long long* argmax_keys = nullptr;  // [M]
+};
+
+// out = x . W^T for M token rows: x [M][K] fp32 (row stride ldx), W either Q8_0 (int8
+// [N][K] + fp32 scales [N][K/32]) or fp32 [N][K].  If norm_gain is set, each x row is
+// RMS-normalised with that gain first (src/model_q8.cpp:128-140).  kbegin = K-32 limits
+// the contraction to the last 32-wide block (the reference's batched Q8 arithmetic).
+struct GemmArgs {
+    const float* x = nullptr;
+    int ldx = 0;
+    const float* norm_gain = nullptr;
+    const int8_t* wq = nullptr;
+    const float* ws = nullptr;
+    const float* wf = nullptr;
+    int M = 0, N = 0, K = 0;
+    int kbegin = 0;
+};
+
+void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s);
+
+// Decode attention over paged KV for one layer (see attention.cu).
+struct DecodeAttnArgs {
+    const float* q = nullptr;     // [B][n_heads*head_dim]
+    const float* kpool = nullptr;
+    const float* vpool = nullptr;
+    PoolGeom geom{};
+    int layer = 0;
+    const int* block_tables = nullptr;  // [B][max_pages]
+    int max_pages = 0;
+    const int* ctx_lens = nullptr;      // [B] tokens to attend (pos + 1)
+    int B = 0, n_heads = 0;
+    float* out = nullptr;               // [B][n_heads*head_dim]
+    float* part_o = nullptr;            // split partials [B][n_heads][max_splits][head_dim]
+    float* part_ml = nullptr;           // [B][n_heads][max_splits][2]
+    int* counters = nullptr;            // [B][n_heads], zero between calls
+    int max_splits = 0;
+    int chunk_pages = 0;
+    int* err = nullptr;
+};
+int decode_attn_chunk_pages(int head_dim);
+size_t decode_attn_workspace_bytes(int B, int n_heads, int head_dim, int max_pages);
+// Carve part_o/part_ml/counters out of a workspace of decode_attn_workspace_bytes().
+void decode_attn_bind_workspace(DecodeAttnArgs& a, void* ws, int max_pages_capacity);
+void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t s);
+
+// Causal prefill attention for T consecutive tokens of one sequence (see attention.cu).
+struct PrefillAttnArgs {
+    const float* q = nullptr;  // [T][n_heads*head_dim]
+    const float* kpool = nullptr;
+    const float* vpool = nullptr;
+    PoolGeom geom{};
+    int layer = 0;
+    const int* block_table = nullptr;  // pages of the sequence
+    int T = 0, start_pos = 0, n_heads = 0;
+    float* out = nullptr;  // [T][n_heads*head_dim]
+    int* err = nullptr;
+};
+void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
+
+// x[m] = emb[tokens[m]] and argmax keys reset (src/model_q8.cpp:431-435, :578-582).
+void launch_embed(const float* emb, const int* tokens, int M, int dim, float* x,
+                  unsigned long long* keys, cudaStream_t s);
+// Finalise argmax keys into token ids.
+void launch_argmax_finish(const unsigned long long* keys, int M, int* out, cudaStream_t s);
+
+// Kernel launches made so far by this process (host-side count of <<<>>> calls).
+int64_t kernel_launch_count();
+void count_launch();
+
+}  // namespace nitro

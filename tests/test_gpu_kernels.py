@@ -1,0 +1,121 @@
+"""Kernel-level parity on the GPU: Q8_0 matmul and paged decode attention, called through
+the C ABI (nr_q8_matmul, nr_paged_attention_decode) and compared with the CPU
+restatement of the reference (oracle/nitro_oracle.cpp)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import assert_close
+from nitrorag_b200 import synth
+from nitrorag_b200._lib import NR_Q8_FAITHFUL, NR_Q8_FIXED, lib
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for gpu tests")
+    return torch
+
+
+def _aos_to_soa(w_aos: bytes, rows: int, K: int):
+    blk = np.frombuffer(w_aos, np.uint8).reshape(rows, K // 32, 36)
+    scales = blk[:, :, :4].copy().view(np.float32).reshape(rows, K // 32)
+    q = blk[:, :, 4:].copy().view(np.int8).reshape(rows, K)
+    return q, scales
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 64, 130])
+@pytest.mark.parametrize("mode", [NR_Q8_FIXED, NR_Q8_FAITHFUL])
+@pytest.mark.parametrize("NK", [(768, 768), (256, 2048)])
+def test_q8_matmul(torch_cuda, restatement, M, mode, NK):
+    torch = torch_cuda
+    N, K = NK
+    rng = np.random.default_rng(M * 7 + N)
+    w = (rng.standard_normal(N * K) * 0.02).astype(np.float32)
+    w_aos = synth.quantize_q8(w)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    want = restatement.q8_matmul(x, w_aos, K, N, last_block_only=(mode == NR_Q8_FAITHFUL))
+    q, s = _aos_to_soa(w_aos, N, K)
+    dq, ds, dx = (torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), torch.from_numpy(x).cuda())
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    rc = lib().nr_q8_matmul(dx.data_ptr(), dq.data_ptr(), ds.data_ptr(), out.data_ptr(), M, N, K, mode,
+                            C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), want, rtol=1e-4, atol=1e-5, what=f"q8 M={M} mode={mode}")
+
+
+def _engine_pools(kref, vref, n_layers, n_kv, hd):
+    """[page][layer][16][kv_dim] (reference) -> [page][layer][kv_head][16][hd] (engine)."""
+    P = kref.shape[0]
+    k = kref.reshape(P, n_layers, 16, n_kv, hd).transpose(0, 1, 3, 2, 4).copy()
+    v = vref.reshape(P, n_layers, 16, n_kv, hd).transpose(0, 1, 3, 2, 4).copy()
+    return k, v
+
+
+def _run_decode_attention(torch, q, k_eng, v_eng, bt, ctx, n_heads, n_kv, hd, n_layers, layer, repeat=1):
+    B = len(ctx)
+    max_pages = bt.shape[1]
+    dq = torch.from_numpy(q).cuda()
+    dk = torch.from_numpy(k_eng).cuda()
+    dv = torch.from_numpy(v_eng).cuda()
+    dbt = torch.from_numpy(bt).cuda()
+    dctx = torch.from_numpy(ctx).cuda()
+    out = torch.zeros((B, n_heads * hd), dtype=torch.float32, device="cuda")
+    ws_bytes = lib().nr_paged_attention_workspace_size(B, n_heads, hd, max_pages)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(repeat):
+        rc = lib().nr_paged_attention_decode(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dbt.data_ptr(), max_pages,
+                                             dctx.data_ptr(), B, n_heads, n_kv, hd, n_layers, layer, out.data_ptr(),
+                                             ws.data_ptr(), err.data_ptr(), stream)
+        assert rc == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("hd,n_heads,n_kv", [(64, 12, 12), (128, 4, 4), (64, 8, 2)])
+def test_paged_attention_small(torch_cuda, restatement, hd, n_heads, n_kv):
+    """Ragged contexts incl. 1 token, exact page multiples, multi-chunk splits; 2 layers."""
+    torch = torch_cuda
+    rng = np.random.default_rng(hd + n_kv)
+    ctx = np.array([1, 15, 16, 17, 128, 129, 300, 513], np.int32)
+    B, n_layers, layer, P = len(ctx), 2, 1, 96
+    kv_dim = n_kv * hd
+    max_pages = 40
+    perm = rng.permutation(P).astype(np.int32)
+    bt = np.zeros((B, max_pages), np.int32)
+    at = 0
+    for b in range(B):
+        n = (ctx[b] + 15) // 16
+        bt[b, :n] = perm[at:at + n]
+        at += n
+    kref = rng.standard_normal((P, n_layers, 16, kv_dim)).astype(np.float32)
+    vref = rng.standard_normal((P, n_layers, 16, kv_dim)).astype(np.float32)
+    q = rng.standard_normal((B, n_heads * hd)).astype(np.float32)
+    want = restatement.paged_decode_attention(q, kref, vref, n_layers * 16 * kv_dim, layer * 16 * kv_dim, bt, ctx,
+                                              n_heads, n_kv, hd)
+    k_eng, v_eng = _engine_pools(kref, vref, n_layers, n_kv, hd)
+    got = _run_decode_attention(torch, q, k_eng, v_eng, bt, ctx, n_heads, n_kv, hd, n_layers, layer, repeat=2)
+    assert_close(got, want, rtol=1e-4, atol=1e-5, what="paged attention")
+
+
+def test_paged_attention_microbench_config(torch_cuda, restatement):
+    """The benchmark's configuration at full size: 64 sequences, ctx U[128,1024], 12x64,
+    8192-page single-layer pool, pages from a seeded permutation, N(0,1) values."""
+    torch = torch_cuda
+    ctx, bt, q = synth.paged_attention_case(seed=2)
+    P, hd, H = 8192, 64, 12
+    rng = np.random.default_rng(5)
+    kref = rng.standard_normal((P, 1, 16, H * hd), dtype=np.float32)
+    vref = rng.standard_normal((P, 1, 16, H * hd), dtype=np.float32)
+    want = restatement.paged_decode_attention(q, kref, vref, 16 * H * hd, 0, bt, ctx, H, H, hd)
+    k_eng, v_eng = _engine_pools(kref, vref, 1, H, hd)
+    got = _run_decode_attention(torch, q, k_eng, v_eng, bt, ctx, H, H, hd, 1, 0, repeat=3)
+    assert_close(got, want, rtol=1e-4, atol=1e-5, what="paged attention config 2")
