@@ -19,12 +19,14 @@
 // per-(sequence, head) arrival counter that the merging CTA resets to zero.
 #include <cuda_runtime.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace nitro {
-
-void count_launch();
 
 namespace {
 
@@ -291,16 +293,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
     }
 }
 
-// cudaFuncSetAttribute is per device: remember which devices have been configured.
+// cudaFuncSetAttribute is per (kernel, device): remember which pairs are configured.
 template <class K>
 void ensure_smem(K kernel, int bytes) {
-    static bool done[64] = {};
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !done[dev]) {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-        done[dev] = true;
-    }
+    std::lock_guard<std::mutex> lock(mu);
+    auto key = std::make_pair((const void*)kernel, dev);
+    if (done.count(key)) return;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done.insert(key);
 }
 
 }  // namespace

@@ -25,7 +25,10 @@ namespace {
 thread_local std::string g_create_error;
 
 int parse_shape(const void* bytes, size_t size, nitro::ModelShape* s) {
-    if (size < 28) return NR_ERR_FORMAT;
+    if (size < 28) {
+        g_create_error = "model file shorter than its 28-byte header";
+        return NR_ERR_FORMAT;
+    }
     int32_t h[7];
     memcpy(h, bytes, 28);
     s->dim = h[0]; s->hidden = h[1]; s->n_layers = h[2]; s->n_heads = h[3];
@@ -34,6 +37,19 @@ int parse_shape(const void* bytes, size_t size, nitro::ModelShape* s) {
         if (h[i] <= 0) return NR_ERR_FORMAT;
     if (s->dim % s->n_heads || s->n_heads % s->n_kv_heads || s->head_dim() % 2) return NR_ERR_FORMAT;
     return NR_OK;
+}
+
+// Bytes a model file of this shape must hold (header + tensors, src/Server_Inference.cpp:53-68).
+size_t expected_file_size(const nitro::ModelShape& s) {
+    const size_t D = s.dim, H = s.hidden, L = s.n_layers, V = s.vocab, KV = s.kv_dim(), hd = s.head_dim();
+    const size_t q8 = 36;
+    size_t n = 28;
+    n += V * D * 4 + L * D * 4;
+    n += (L * D * D + 2 * L * D * KV + L * D * D) / 32 * q8;
+    n += L * D * 4;
+    n += 3 * L * H * D / 32 * q8;
+    n += D * 4 + 2 * (size_t)s.seq_len * hd / 2 * 4;
+    return n;
 }
 
 int validate_cfg(const nr_config* c) {
@@ -104,6 +120,15 @@ int nr_engine_create_from_memory(const nr_config* cfg, const void* bytes, size_t
     nitro::ModelShape shape;
     rc = parse_shape(bytes, size, &shape);
     if (rc) return rc;
+    if (shape.dim % 32 || shape.hidden % 32 || shape.kv_dim() % 32) {
+        g_create_error = "dim, hidden_dim and kv_dim must be multiples of 32 (Q8_0 blocks)";
+        return NR_ERR_FORMAT;
+    }
+    if (size < expected_file_size(shape)) {
+        g_create_error = "model file is " + std::to_string(size) + " bytes, its header implies " +
+                         std::to_string(expected_file_size(shape));
+        return NR_ERR_FORMAT;
+    }
     return create_common(cfg, shape, (const uint8_t*)bytes, size, out);
 }
 
@@ -113,7 +138,10 @@ int nr_engine_create(const nr_config* cfg, const char* path, nr_engine** out) {
     int rc = validate_cfg(cfg);
     if (rc) return rc;
     int fd = open(path, O_RDONLY);
-    if (fd < 0) return NR_ERR_IO;
+    if (fd < 0) {
+        g_create_error = std::string("cannot open ") + path;
+        return NR_ERR_IO;
+    }
     struct stat st;
     if (fstat(fd, &st) != 0) { close(fd); return NR_ERR_IO; }
     void* data = mmap(nullptr, st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
@@ -580,13 +608,19 @@ int nr_paged_attention_decode(const float* q, const float* kpool, const float* v
 }
 
 int nr_q8_matmul(const float* x, const int8_t* q, const float* scales, float* out, int32_t M, int32_t N, int32_t K,
-                 int32_t q8_mode, void* stream) {
+                 int32_t q8_mode, void* workspace, size_t workspace_bytes, void* stream) {
     if (!x || !q || !scales || !out || M <= 0 || N <= 0 || K <= 0) return NR_ERR_INVALID;
     if (K % 32 || N % 2) return NR_ERR_INVALID;
     if (q8_mode != NR_Q8_FIXED && q8_mode != NR_Q8_FAITHFUL) return NR_ERR_INVALID;
     nitro::GemmArgs g;
     g.x = x; g.ldx = K; g.wq = q; g.ws = scales; g.M = M; g.N = N; g.K = K;
     g.kbegin = q8_mode == NR_Q8_FAITHFUL ? K - 32 : 0;
+    if (workspace && workspace_bytes >= 16384 + 4096) {
+        g.tc.counters_ptr = (int*)workspace;
+        g.tc.counters = 4096;
+        g.tc.ws = (float*)((char*)workspace + 16384);
+        g.tc.ws_floats = (workspace_bytes - 16384) / 4;
+    }
     nitro::Epilogue e;
     e.kind = nitro::kEpiStore; e.out = out; e.ldo = N;
     nitro::launch_gemm(g, e, (cudaStream_t)stream);

@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -319,7 +320,20 @@ void gemv_dispatch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
 
 }  // namespace
 
+static bool tc_disabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* env = getenv("NITRO_DISABLE_TC");
+        v = (env && env[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
 void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
+    if (a.M > 8 && !tc_disabled() && tc_gemm_supported(a)) {
+        launch_tc_gemm(a, e, a.tc, s);
+        return;
+    }
     g_launches++;
     if (a.M <= 1) gemv_dispatch<1>(a, e, s);
     else if (a.M <= 2) gemv_dispatch<2>(a, e, s);

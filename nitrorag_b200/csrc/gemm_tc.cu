@@ -1,0 +1,480 @@
+// Q8_0 (and fp32) projections on the 5th-generation tensor cores (tcgen05), for token
+// batches wide enough to make the product a real dense contraction (decode batches and
+// prefill chunks of more than 8 tokens).
+//
+// Orientation: D[n][m] = sum_k W[n][k] * X[m][k], weight rows n on the MMA's M side (128
+// rows per CTA), tokens m on its N side (NT = 64, 128 or 256 per CTA), fp32 accumulators
+// in tensor memory (TMEM), one column per token.
+//
+// Precision: the reference multiplies in fp32 (w = q * scale, then w * x, fp32 sums).
+// Each operand is split into two bf16 halves, v = hi + lo with hi = bf16(v) and
+// lo = bf16(v - hi) (17 significant bits together), and the product is accumulated as
+// hi*hi + hi*lo + lo*hi by three MMAs into the same fp32 accumulator; the dropped lo*lo
+// term and the split residues are ~2^-17 relative, far inside the 1e-3 / 1e-4 logits bar.
+//
+// Pipeline per CTA (128 threads): for each 64-wide K chunk, every thread dequantises one
+// weight row (16-byte int8 loads, w = q * scale) and part of the activation tile (the
+// RMSNorm of the row applied on the fly) into the UMMA canonical K-major layout in shared
+// memory; thread 0 issues 4 x 3 MMAs and commits them to the stage's mbarrier, and the
+// next chunk is converted while those run (2 stages).  When the weight tile is too narrow
+// to fill the GPU, the K range is split across CTAs; partial tiles go to a workspace and
+// the last CTA of a tile (arrival counter, reset by that CTA) sums them in split order and
+// runs the epilogue, so results do not depend on arrival order.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nitro {
+
+namespace {
+
+constexpr int TC_M = 128;     // weight rows per CTA = UMMA M
+constexpr int TC_KC = 64;     // K elements per pipeline stage
+constexpr int TC_STAGES = 2;
+constexpr int TC_THREADS = 128;
+
+// ------------------------------------------------------------------ tcgen05 wrappers
+// Shared-memory matrix descriptor, K-major without swizzle: core matrices of 8 rows x 16 B
+// stored contiguously (128 B); the next 8 K-elements are LBO = 128 B away, the next 8
+// rows SBO = 1024 B away (a 64-wide K chunk = 8 core matrices per row group).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((128u >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((1024u >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+    return d;                // base offset 0, layout type 0 (no swizzle)
+}
+
+// Instruction descriptor of kind::f16: D fp32, A and B bf16, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// ------------------------------------------------------------------ operand staging
+// Split 8 fp32 values into bf16 hi/lo and store them as one 16-byte row of a core matrix.
+__device__ __forceinline__ void split_store8(const float* v, uint8_t* hi_dst, uint8_t* lo_dst) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        float2 hf = __bfloat1622float2(hb);
+        __nv_bfloat162 lb = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+        h[i] = *reinterpret_cast<uint32_t*>(&hb);
+        l[i] = *reinterpret_cast<uint32_t*>(&lb);
+    }
+    *reinterpret_cast<uint4*>(hi_dst) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo_dst) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Byte offset of (row r, 8-element K group j) in the canonical layout above.
+__device__ __forceinline__ uint32_t core_off(int r, int j) { return (uint32_t)((r >> 3) * 1024 + j * 128 + (r & 7) * 16); }
+
+template <int NT>
+struct TcSmem {
+    static constexpr int A_BYTES = TC_M * TC_KC * 2;   // one bf16 half of the weight tile
+    static constexpr int B_BYTES = NT * TC_KC * 2;     // one bf16 half of the token tile
+    static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int TOTAL = TC_STAGES * STAGE;
+};
+
+struct SplitArgs {
+    int ksplit;          // K-range splits per tile
+    int chunks_per_split;
+    float* ws;           // [tiles][ksplit][NT][128] partial accumulators
+    int* counters;       // [tiles]
+};
+
+template <int NT, bool F32W>
+__global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
+    using S = TcSmem<NT>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ uint64_t mma_bar[TC_STAGES];
+    __shared__ uint32_t tmem_slot;
+    __shared__ float inv_rms[NT];
+    __shared__ unsigned long long red_key[4][NT];
+    __shared__ int is_last;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
+    const int n_base = n_tile * TC_M, m_base = m_tile * NT;
+    const int nchunk_total = a.K / TC_KC;
+    const int c_begin = split * sp.chunks_per_split;
+    const int c_end = min(nchunk_total, c_begin + sp.chunks_per_split);
+    // the reference's batched arithmetic keeps only the last 32-wide block (kbegin = K-32)
+    const int c_first = max(c_begin, a.kbegin / TC_KC);
+
+    if (warp == 0) {
+        tmem_alloc(&tmem_slot, NT);
+        tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int s = 0; s < TC_STAGES; s++) mbar_init(&mma_bar[s], 1);
+        fence_barrier_init();
+    }
+    if (a.norm_gain) {
+        const int nw = TC_THREADS / 32;
+        for (int r = warp; r < NT; r += nw) {
+            const int m = m_base + r;
+            float ss = 0.0f;
+            if (m < a.M) {
+                const float* row = a.x + (int64_t)m * a.ldx;
+                for (int k = lane * 4; k < a.K; k += 128) {
+                    float4 v = *reinterpret_cast<const float4*>(row + k);
+                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                }
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
+    const bool norm = a.norm_gain != nullptr;
+
+    int it = 0;
+    bool bail = false;
+    for (int c = c_first; c < c_end; c++, it++) {
+        const int s = it % TC_STAGES;
+        const int use = it / TC_STAGES;
+        if (use > 0) {
+            const bool got = mbar_wait(&mma_bar[s], (use - 1) & 1, a.err);
+            if (!__syncthreads_and(got)) { bail = true; break; }
+        }
+        uint8_t* a_hi = smem + s * S::STAGE;
+        uint8_t* a_lo = a_hi + S::A_BYTES;
+        uint8_t* b_hi = a_lo + S::A_BYTES;
+        uint8_t* b_lo = b_hi + S::B_BYTES;
+        const int k0 = c * TC_KC;
+        // ---- weights: thread = one row, 64 values
+        {
+            const int n = n_base + tid;
+            float w[TC_KC];
+            if (n < a.N) {
+                if (F32W) {
+                    const float4* src = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k0);
+#pragma unroll
+                    for (int i = 0; i < TC_KC / 4; i++) {
+                        float4 v = __ldg(src + i);
+                        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+                    }
+                } else {
+                    const int4* src = reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k0);
+                    const float s0 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5));
+                    const float s1 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5) + 1);
+#pragma unroll
+                    for (int i = 0; i < TC_KC / 16; i++) {
+                        int4 raw = __ldg(src + i);
+                        const int8_t* q = reinterpret_cast<const int8_t*>(&raw);
+                        const float sc = i < 2 ? s0 : s1;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) w[16 * i + j] = (float)q[j] * sc;
+                    }
+                }
+                if (k0 < a.kbegin) {  // faithful mode: only k >= kbegin contributes
+#pragma unroll
+                    for (int i = 0; i < TC_KC; i++)
+                        if (k0 + i < a.kbegin) w[i] = 0.0f;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < TC_KC; i++) w[i] = 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < TC_KC / 8; j++)
+                split_store8(w + 8 * j, a_hi + core_off(tid, j), a_lo + core_off(tid, j));
+        }
+        // ---- tokens: (token, half of the chunk) per iteration
+        for (int idx = tid; idx < NT * 2; idx += TC_THREADS) {
+            const int r = idx >> 1, half = idx & 1;
+            const int m = m_base + r;
+            float xv[32];
+            if (m < a.M) {
+                const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    float4 v = src[i];
+                    xv[4 * i] = v.x; xv[4 * i + 1] = v.y; xv[4 * i + 2] = v.z; xv[4 * i + 3] = v.w;
+                }
+                if (norm) {
+                    const float inv = inv_rms[r];
+                    const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k0 + half * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        float4 g = __ldg(g4 + i);
+                        xv[4 * i] = g.x * (inv * xv[4 * i]);
+                        xv[4 * i + 1] = g.y * (inv * xv[4 * i + 1]);
+                        xv[4 * i + 2] = g.z * (inv * xv[4 * i + 2]);
+                        xv[4 * i + 3] = g.w * (inv * xv[4 * i + 3]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) xv[i] = 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                split_store8(xv + 8 * j, b_hi + core_off(r, half * 4 + j), b_lo + core_off(r, half * 4 + j));
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t ah = smem_addr(a_hi), al = smem_addr(a_lo), bh = smem_addr(b_hi), bl = smem_addr(b_lo);
+#pragma unroll
+            for (int kk = 0; kk < TC_KC / 16; kk++) {
+                const uint32_t o = kk * 256;  // 16 K-elements = two core matrices along K
+                umma_bf16(tmem, umma_desc(ah + o), umma_desc(bh + o), idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                umma_bf16(tmem, umma_desc(ah + o), umma_desc(bl + o), idesc, 1u);
+                umma_bf16(tmem, umma_desc(al + o), umma_desc(bh + o), idesc, 1u);
+            }
+            umma_commit(&mma_bar[s]);
+        }
+    }
+    // all MMAs of this CTA are complete once the last commit's phase has completed
+    if (it > 0) {
+        const int s = (it - 1) % TC_STAGES;
+        if (!__syncthreads_and(mbar_wait(&mma_bar[s], ((it - 1) / TC_STAGES) & 1, a.err))) bail = true;
+    }
+    tc_fence_after();
+    if (bail) {  // a wait gave up (error flag set): release TMEM and leave
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) tmem_dealloc(tmem, NT);
+        return;
+    }
+
+    const int n = n_base + tid;
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    const int64_t tile = (int64_t)m_tile * gridDim.x + n_tile;
+    bool do_epi = true;
+    float* part = nullptr;
+    if (sp.ksplit > 1) {
+        // publish this split's partial tile: [NT][128], coalesced per column
+        part = sp.ws + (tile * sp.ksplit + split) * (int64_t)NT * TC_M;
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+            float v[16];
+            tmem_ld16(tl + c0, v);
+#pragma unroll
+            for (int j = 0; j < 16; j++) part[(int64_t)(c0 + j) * TC_M + tid] = (it > 0) ? v[j] : 0.0f;
+        }
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const int prev = atomicAdd(sp.counters + tile, 1);
+            is_last = prev == sp.ksplit - 1;
+        }
+        __syncthreads();
+        do_epi = is_last != 0;
+        if (do_epi) __threadfence();
+    }
+    if (do_epi) {
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+            float v[16];
+            if (sp.ksplit > 1) {
+                const float* base = sp.ws + tile * sp.ksplit * (int64_t)NT * TC_M;
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] = 0.0f;
+                for (int s2 = 0; s2 < sp.ksplit; s2++) {
+                    const float* ps = base + (int64_t)s2 * NT * TC_M;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] += __ldcg(ps + (int64_t)(c0 + j) * TC_M + tid);
+                }
+            } else if (it > 0) {
+                tmem_ld16(tl + c0, v);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] = 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int m = m_base + c0 + j;
+                const float mine = v[j];
+                const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
+                const bool ok = m < a.M && n < a.N;
+                if (e.kind == kEpiLogits) {
+                    if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
+                    unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = k2 > key ? k2 : key;
+                    }
+                    if (lane == 0) red_key[warp][c0 + j] = key;
+                    continue;
+                }
+                if (!ok) continue;
+                const bool even = (n & 1) == 0;
+                const float v0 = even ? mine : other;  // value of row n & ~1
+                const float v1 = even ? other : mine;  // value of row n | 1
+                switch (e.kind) {
+                case kEpiStore:
+                    e.out[(int64_t)m * e.ldo + n] = mine;
+                    break;
+                case kEpiResidual:
+                    e.out[(int64_t)m * e.ldo + n] += mine;
+                    break;
+                case kEpiSwiGLU:
+                    if (even) {
+                        float h = v0 * (1.0f / (1.0f + expf(-v0)));
+                        e.out[(int64_t)m * e.ldo + (n >> 1)] = h * v1;
+                    }
+                    break;
+                case kEpiQKV: {
+                    const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+                    const int pos = e.tok_pos[m];
+                    const int np = n & ~1;
+                    if (np < D + KV) {
+                        const int cc = np < D ? np : np - D;
+                        const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
+                        const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
+                        const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
+                        if (np < D) {
+                            e.q_out[(int64_t)m * D + n] = r;
+                        } else {
+                            const int c = n - D;
+                            e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
+                                    (int64_t)(pos & (kPage - 1)) * hd + (c % hd)] = r;
+                        }
+                    } else {
+                        const int c = n - D - KV;
+                        e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
+                                (int64_t)(pos & (kPage - 1)) * hd + (c % hd)] = mine;
+                    }
+                    break;
+                }
+                default:
+                    break;
+                }
+            }
+        }
+        if (e.kind == kEpiLogits) {
+            __syncthreads();
+            for (int c = tid; c < NT; c += TC_THREADS) {
+                unsigned long long best = red_key[0][c];
+#pragma unroll
+                for (int w = 1; w < 4; w++) best = red_key[w][c] > best ? red_key[w][c] : best;
+                const int m = m_base + c;
+                if (best != 0ull && m < a.M) {
+                    unsigned long long* slot = e.argmax_keys + m;
+                    if (best > *(volatile unsigned long long*)slot) atomicMax(slot, best);
+                }
+            }
+        }
+        if (sp.ksplit > 1 && tid == 0) sp.counters[tile] = 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, NT);
+}
+
+template <class K>
+void tc_ensure_smem(K kernel, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    auto key = std::make_pair((const void*)kernel, dev);
+    if (done.count(key)) return;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done.insert(key);
+}
+
+template <int NT>
+void tc_launch(const GemmArgs& a, const Epilogue& e, const TcWorkspace& ws, cudaStream_t s) {
+    const int n_tiles = (a.N + TC_M - 1) / TC_M;
+    const int m_tiles = (a.M + NT - 1) / NT;
+    const int chunks = a.K / TC_KC;
+    // fill the GPU: split K when the tiles alone are fewer than ~2 waves of 148 SMs;
+    // a split keeps at least 2 chunks unless K is tiny; never split the faithful path
+    int ksplit = 1;
+    if (ws.ws && a.kbegin == 0) {
+        const int tiles = n_tiles * m_tiles;
+        ksplit = tiles >= 148 ? 1 : std::min(std::max(1, (296 + tiles - 1) / tiles), std::max(1, chunks / 2));
+        while (ksplit > 1 && (size_t)tiles * ksplit * NT * TC_M > ws.ws_floats) ksplit--;
+        if (tiles > ws.counters) ksplit = 1;
+    }
+    SplitArgs sp;
+    sp.ksplit = ksplit;
+    sp.chunks_per_split = (chunks + ksplit - 1) / ksplit;
+    sp.ksplit = (chunks + sp.chunks_per_split - 1) / sp.chunks_per_split;  // no empty splits
+    sp.ws = ws.ws;
+    sp.counters = ws.counters_ptr;
+    dim3 grid(n_tiles, m_tiles, sp.ksplit);
+    const int smem = TcSmem<NT>::TOTAL;
+    if (a.wf) {
+        tc_ensure_smem(tc_gemm_kernel<NT, true>, smem);
+        tc_gemm_kernel<NT, true><<<grid, TC_THREADS, smem, s>>>(a, e, sp);
+    } else {
+        tc_ensure_smem(tc_gemm_kernel<NT, false>, smem);
+        tc_gemm_kernel<NT, false><<<grid, TC_THREADS, smem, s>>>(a, e, sp);
+    }
+}
+
+}  // namespace
+
+bool tc_gemm_supported(const GemmArgs& a) { return a.K % TC_KC == 0 && a.N % 2 == 0 && a.M > 8; }
+
+void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, const TcWorkspace& ws, cudaStream_t s) {
+    count_launch();
+    if (a.M <= 64) tc_launch<64>(a, e, ws, s);
+    else if (a.M <= 128) tc_launch<128>(a, e, ws, s);
+    else tc_launch<256>(a, e, ws, s);
+}
+
+size_t tc_workspace_floats(int max_tiles_times_split, int nt) { return (size_t)max_tiles_times_split * nt * TC_M; }
+
+}  // namespace nitro

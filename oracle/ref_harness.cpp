@@ -168,6 +168,7 @@ int ref_pool_only(int total_blocks, int n_layers, int kv_dim) {
     H->kv_dim = kv_dim;
     H->mem.reset(new KVBlock_Manager(total_blocks, n_layers, kv_dim));
     H->cache.reset(new PrefixCacheManager(*H->mem, total_blocks));
+    H->sched.reset(new Continuous_Scheduler());
     return 0;
 }
 
@@ -196,6 +197,7 @@ int ref_open(const char* path, int max_tokens, int total_blocks) {
     H->kv_dim = kv_dim;
     H->mem.reset(new KVBlock_Manager(total_blocks, H->c.n_layers, kv_dim));
     H->cache.reset(new PrefixCacheManager(*H->mem, total_blocks));
+    H->sched.reset(new Continuous_Scheduler());
     // The reference pool comes from aligned_alloc and is never zeroed; zero it so
     // unused rows read as 0 in comparisons.
     size_t floats = (size_t)total_blocks * H->c.n_layers * BLOCK_SIZE * kv_dim;
