@@ -53,7 +53,7 @@ typedef struct nr_config {
     int32_t block_size;            /* must be 16 (pagedMemory.hpp:9)                               */
     int32_t sched_mode;            /* NR_SCHED_*                                                  */
     int32_t q8_mode;               /* NR_Q8_*                                                     */
-    int32_t max_batch;             /* decode rows per forward call (scratch sizing), default 256 */
+    int32_t max_batch;             /* decode rows per forward call (scratch sizing), default 256, <= 1024 */
     int32_t max_prefill_tokens;    /* tokens per prefill call (scratch sizing), default 1024     */
     int32_t device;                /* CUDA device ordinal; -1 = host-only (metadata, no GPU)      */
     int32_t reserved[7];
@@ -213,7 +213,7 @@ int nr_engine_stats(nr_engine* e, nr_stats* out);
 /* ------------------------------------------------------------------ kernel-level entry points
  * Device pointers, enqueued on `stream` (a cudaStream_t; NULL = legacy default stream),
  * asynchronous: the call returns after the launch.  Page layout of the device pools is
- * [page][layer][kv_head][16][head_dim] fp32. */
+ * [page][layer][kv_head][16][head_dim] fp32.  B <= 1024. */
 
 /* Decode paged attention for one layer (the per-(b,h) loop of src/model_q8.cpp:625-662 with
  * softmax :142-159).  q, out: [B][n_heads*head_dim]; kpool/vpool as above with n_layers

@@ -31,6 +31,8 @@ namespace nitro {
 namespace {
 
 constexpr int kAttnWarps = 4;
+
+__device__ __forceinline__ void fence_async_smem_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Running softmax state of one query inside a warp.  Lane l owns output dims
@@ -106,115 +108,208 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
 }
 
 // ------------------------------------------------------------------ decode
+// Persistent kernel, one CTA per SM, every warp an independent worker: it takes work items
+// (sequence b, head h, chunk of up to chunk_pages pages) from a global counter and streams
+// their K/V page tiles through its own ring of kDecStages shared-memory slots, issuing the
+// next item's pages while the current item drains, so the copy engine always has pages
+// in flight.  No CTA-wide barrier is taken after set-up.
+constexpr int kDecStages = 3;
+
 template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32) decode_attn_kernel(DecodeAttnArgs a) {
-    constexpr int TILE = kPage * HD;  // floats per K (or V) tile
+struct DecCfg {
+    static constexpr int WARPS = HD == 64 ? 8 : 4;
+    static constexpr int TILE = kPage * HD;                              // floats per K or V tile
+    static constexpr int RING_FLOATS = WARPS * kDecStages * 2 * TILE;
+    static constexpr int SMEM = RING_FLOATS * 4 + WARPS * HD * 4;        // + one query per warp
+};
+
+struct DecItem {
+    int b, h, split, p0, np, ctx, nsplit;
+    bool valid;
+};
+
+__device__ __forceinline__ DecItem dec_item(int idx, int total, const int* prefix, int B, int n_heads,
+                                            int chunk_pages, const int* ctx_lens) {
+    DecItem it;
+    it.valid = idx < total;
+    if (!it.valid) { it.b = it.h = it.split = it.p0 = it.np = it.ctx = it.nsplit = 0; return it; }
+    int lo = 0, hi = B;  // largest b with prefix[b] <= idx
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (prefix[mid] <= idx) lo = mid; else hi = mid;
+    }
+    it.b = lo;
+    const int rem = idx - prefix[lo];
+    it.split = rem / n_heads;
+    it.h = rem % n_heads;
+    it.ctx = ctx_lens[lo];
+    const int pages = (it.ctx + kPage - 1) / kPage;
+    it.nsplit = (pages + chunk_pages - 1) / chunk_pages;
+    it.p0 = it.split * chunk_pages;
+    it.np = min(chunk_pages, pages - it.p0);
+    return it;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(DecodeAttnArgs a) {
+    using C = DecCfg<HD>;
     constexpr int DPL = HD / 32;
-    extern __shared__ __align__(128) float smem[];  // [chunk][2][TILE]
-    __shared__ uint64_t bars[16];
-    __shared__ __align__(16) float qs[HD];
-    __shared__ float red_m[kAttnWarps], red_l[kAttnWarps];
-    __shared__ __align__(16) float red_o[kAttnWarps][HD];
-    __shared__ int is_last;
+    extern __shared__ __align__(128) float smem[];
+    __shared__ uint64_t bars[C::WARPS][kDecStages];
+    __shared__ int prefix[1025];
+    __shared__ int warp_tot[32];
 
-    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int ctx = a.ctx_lens[b];
-    const int n_pages = (ctx + kPage - 1) / kPage;
-    const int nsplit = (n_pages + a.chunk_pages - 1) / a.chunk_pages;
-    if (split >= nsplit) return;
-    const int p0 = split * a.chunk_pages;
-    const int np = min(a.chunk_pages, n_pages - p0);
-    const int kvh = h / (a.n_heads / a.geom.n_kv_heads);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kvmul = a.n_heads / a.geom.n_kv_heads;
 
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < np; i++) mbar_init(&bars[i], 1);
+    // item table: prefix[b] = first item of sequence b (items of b: nsplit(b) * n_heads)
+    for (int base = 0; base < a.B; base += blockDim.x) {
+        const int b = base + threadIdx.x;
+        int cnt = 0;
+        if (b < a.B) {
+            const int pages = (a.ctx_lens[b] + kPage - 1) / kPage;
+            cnt = ((pages + a.chunk_pages - 1) / a.chunk_pages) * a.n_heads;
+        }
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) warp_tot[warp] = incl;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int run = base == 0 ? 0 : prefix[base];
+            for (int w = 0; w < C::WARPS; w++) {
+                const int t = warp_tot[w];
+                warp_tot[w] = run;
+                run += t;
+            }
+            prefix[min(base + (int)blockDim.x, a.B)] = run;
+        }
+        __syncthreads();
+        if (b < a.B) prefix[b] = warp_tot[warp] + incl - cnt;
+        __syncthreads();
+    }
+    const int total = prefix[a.B];
+
+    float* ring = smem + warp * kDecStages * 2 * C::TILE;
+    float* qs = smem + C::RING_FLOATS + warp * HD;
+    uint64_t* wb = bars[warp];
+    if (lane == 0) {
+        for (int s = 0; s < kDecStages; s++) mbar_init(&wb[s], 1);
         fence_barrier_init();
-        const int* bt = a.block_tables + (int64_t)b * a.max_pages;
-        for (int i = 0; i < np; i++) {
-            const int64_t off = a.geom.tile_offset(bt[p0 + i], a.layer, kvh);
-            mbar_arrive_expect_tx(&bars[i], 2u * TILE * 4u);
-            bulk_g2s(smem + (2 * i) * TILE, a.kpool + off, TILE * 4, &bars[i]);
-            bulk_g2s(smem + (2 * i + 1) * TILE, a.vpool + off, TILE * 4, &bars[i]);
+    }
+    __syncwarp();
+
+    auto fetch = [&]() -> int {
+        int v = 0;
+        if (lane == 0) v = atomicAdd(a.work, 1);
+        return __shfl_sync(0xffffffffu, v, 0);
+    };
+    DecItem cur = dec_item(fetch(), total, prefix, a.B, a.n_heads, a.chunk_pages, a.ctx_lens);
+    DecItem nxt = dec_item(cur.valid ? fetch() : total, total, prefix, a.B, a.n_heads, a.chunk_pages, a.ctx_lens);
+
+    // issue pointer: page `ip` of item `iq` (0 = cur, 1 = nxt); k-th issued page -> slot k % stages
+    int iq = 0, ip = 0;
+    uint32_t issued = 0, consumed = 0;
+    auto issue_some = [&]() {
+        while (issued - consumed < (uint32_t)kDecStages) {
+            const DecItem& src = iq == 0 ? cur : nxt;
+            if (iq > 1 || !src.valid) break;
+            if (ip >= src.np) { iq++; ip = 0; continue; }
+            if (lane == 0) {
+                const int slot = issued % kDecStages;
+                const int page = a.block_tables[(int64_t)src.b * a.max_pages + src.p0 + ip];
+                const int64_t off = a.geom.tile_offset(page, a.layer, src.h / kvmul);
+                fence_async_smem_cta();
+                mbar_arrive_expect_tx(&wb[slot], 2u * C::TILE * 4u);
+                bulk_g2s(ring + (2 * slot) * C::TILE, a.kpool + off, C::TILE * 4, &wb[slot]);
+                bulk_g2s(ring + (2 * slot + 1) * C::TILE, a.vpool + off, C::TILE * 4, &wb[slot]);
+            }
+            issued++;
+            ip++;
+        }
+    };
+
+    const float qscale = kLog2e / sqrtf((float)HD);
+    bool ok = true;
+    while (cur.valid) {
+        // this item's query
+        __syncwarp();
+        for (int d = lane; d < HD; d += 32) qs[d] = a.q[((int64_t)cur.b * a.n_heads + cur.h) * HD + d] * qscale;
+        __syncwarp();
+        QState<HD> st;
+        st.init();
+        for (int pg = 0; pg < cur.np; pg++) {
+            issue_some();
+            const int slot = consumed % kDecStages;
+            if (ok && !mbar_wait(&wb[slot], (consumed / kDecStages) & 1, a.err)) ok = false;
+            if (ok) {
+                const int first = (cur.p0 + pg) * kPage;
+                attend_page<HD>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
+                                min(kPage, cur.ctx - first), lane);
+            }
+            __syncwarp();  // every lane is done with the slot before it is refilled
+            consumed++;
+        }
+        // retire the item
+        const int64_t bh = (int64_t)cur.b * a.n_heads + cur.h;
+        float* out = a.out + bh * HD + lane * DPL;
+        if (cur.nsplit == 1) {
+            const float inv = 1.0f / st.l;
+#pragma unroll
+            for (int i = 0; i < DPL; i++) out[i] = st.o[i] * inv;
+        } else {
+            float* po = a.part_o + (bh * a.max_splits + cur.split) * HD + lane * DPL;
+#pragma unroll
+            for (int i = 0; i < DPL; i++) po[i] = st.o[i];
+            if (lane == 0) {
+                a.part_ml[(bh * a.max_splits + cur.split) * 2] = st.m;
+                a.part_ml[(bh * a.max_splits + cur.split) * 2 + 1] = st.l;
+            }
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = atomicAdd(a.counters + bh, 1) == cur.nsplit - 1;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                float GM = -INFINITY;
+                for (int sp = 0; sp < cur.nsplit; sp++) GM = fmaxf(GM, __ldcg(a.part_ml + (bh * a.max_splits + sp) * 2));
+                float GL = 0.0f, GO[DPL];
+#pragma unroll
+                for (int i = 0; i < DPL; i++) GO[i] = 0.0f;
+                for (int sp = 0; sp < cur.nsplit; sp++) {
+                    const float ms = __ldcg(a.part_ml + (bh * a.max_splits + sp) * 2);
+                    const float ls = __ldcg(a.part_ml + (bh * a.max_splits + sp) * 2 + 1);
+                    const float c = (ms == -INFINITY) ? 0.0f : exp2f(ms - GM);
+                    GL += ls * c;
+                    const float* ps = a.part_o + (bh * a.max_splits + sp) * HD + lane * DPL;
+#pragma unroll
+                    for (int i = 0; i < DPL; i++) GO[i] += __ldcg(ps + i) * c;
+                }
+                const float inv = 1.0f / GL;
+#pragma unroll
+                for (int i = 0; i < DPL; i++) out[i] = GO[i] * inv;
+                if (lane == 0) a.counters[bh] = 0;
+            }
+        }
+        // advance: the issue pointer moves with the item window
+        cur = nxt;
+        iq = iq > 0 ? iq - 1 : 0;
+        nxt = dec_item(cur.valid ? fetch() : total, total, prefix, a.B, a.n_heads, a.chunk_pages, a.ctx_lens);
+    }
+    // every copy this warp issued has been consumed (issued == consumed here); the last warp
+    // to finish resets the work counters for the next launch
+    if (lane == 0) {
+        __threadfence();
+        const int done = atomicAdd(a.work + 1, 1);
+        if (done == (int)(gridDim.x * C::WARPS) - 1) {
+            a.work[0] = 0;
+            a.work[1] = 0;
         }
     }
-    const float qscale = kLog2e / sqrtf((float)HD);
-    for (int d = threadIdx.x; d < HD; d += blockDim.x)
-        qs[d] = a.q[((int64_t)b * a.n_heads + h) * HD + d] * qscale;
-    __syncthreads();
-
-    QState<HD> st;
-    st.init();
-    bool ok = true;
-    for (int i = warp; i < np; i += kAttnWarps) {
-        if (!mbar_wait(&bars[i], 0, a.err)) { ok = false; break; }
-        const int first = (p0 + i) * kPage;
-        const int n_valid = min(kPage, ctx - first);
-        attend_page<HD>(st, qs, smem + (2 * i) * TILE, smem + (2 * i + 1) * TILE, n_valid, lane);
-    }
-    if (!ok) st.init();
-    // combine the warps of this CTA
-    if (lane == 0) { red_m[warp] = st.m; red_l[warp] = st.l; }
-#pragma unroll
-    for (int i = 0; i < DPL; i++) red_o[warp][lane * DPL + i] = st.o[i];
-    __syncthreads();
-    if (warp != 0) return;
-    float M = red_m[0];
-#pragma unroll
-    for (int w = 1; w < kAttnWarps; w++) M = fmaxf(M, red_m[w]);
-    float L = 0.0f, O[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; i++) O[i] = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; w++) {
-        const float c = (red_m[w] == -INFINITY) ? 0.0f : exp2f(red_m[w] - M);
-        L += red_l[w] * c;
-#pragma unroll
-        for (int i = 0; i < DPL; i++) O[i] += red_o[w][lane * DPL + i] * c;
-    }
-    float* out = a.out + ((int64_t)b * a.n_heads + h) * HD + lane * DPL;
-    if (nsplit == 1) {
-        const float inv = 1.0f / L;
-#pragma unroll
-        for (int i = 0; i < DPL; i++) out[i] = O[i] * inv;
-        return;
-    }
-    // publish this chunk's partial, then let the last-arriving CTA merge
-    const int64_t bh = (int64_t)b * a.n_heads + h;
-    float* po = a.part_o + (bh * a.max_splits + split) * HD + lane * DPL;
-#pragma unroll
-    for (int i = 0; i < DPL; i++) po[i] = O[i];
-    if (lane == 0) {
-        a.part_ml[(bh * a.max_splits + split) * 2] = M;
-        a.part_ml[(bh * a.max_splits + split) * 2 + 1] = L;
-    }
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) {
-        const int prev = atomicAdd(a.counters + bh, 1);
-        is_last = (prev == nsplit - 1);
-    }
-    __syncwarp();
-    if (!is_last) return;
-    __threadfence();
-    float GM = -INFINITY;
-    for (int s = 0; s < nsplit; s++) GM = fmaxf(GM, __ldcg(a.part_ml + (bh * a.max_splits + s) * 2));
-    float GL = 0.0f, GO[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; i++) GO[i] = 0.0f;
-    for (int s = 0; s < nsplit; s++) {
-        const float ms = __ldcg(a.part_ml + (bh * a.max_splits + s) * 2);
-        const float ls = __ldcg(a.part_ml + (bh * a.max_splits + s) * 2 + 1);
-        const float c = (ms == -INFINITY) ? 0.0f : exp2f(ms - GM);
-        GL += ls * c;
-        const float* ps = a.part_o + (bh * a.max_splits + s) * HD + lane * DPL;
-#pragma unroll
-        for (int i = 0; i < DPL; i++) GO[i] += __ldcg(ps + i) * c;
-    }
-    const float inv = 1.0f / GL;
-#pragma unroll
-    for (int i = 0; i < DPL; i++) out[i] = GO[i] * inv;
-    if (lane == 0) a.counters[bh] = 0;
 }
 
 // ------------------------------------------------------------------ prefill
@@ -318,7 +413,7 @@ size_t decode_attn_workspace_bytes(int B, int n_heads, int head_dim, int max_pag
     const int ms = (max_pages + cp - 1) / cp;
     size_t o = align_up((size_t)B * n_heads * ms * head_dim * 4, 256);
     size_t ml = align_up((size_t)B * n_heads * ms * 2 * 4, 256);
-    size_t cnt = align_up((size_t)B * n_heads * 4, 256);
+    size_t cnt = align_up((size_t)B * n_heads * 4 + 2 * 4, 256);
     return o + ml + cnt;
 }
 
@@ -332,21 +427,30 @@ void decode_attn_bind_workspace(DecodeAttnArgs& a, void* ws, int max_pages_capac
     a.part_ml = (float*)p;
     p += align_up((size_t)a.B * a.n_heads * a.max_splits * 2 * 4, 256);
     a.counters = (int*)p;
+    a.work = a.counters + (size_t)a.B * a.n_heads;
+}
+
+static int sm_count() {
+    static std::mutex mu;
+    static int counts[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!counts[dev]) cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev);
+    return counts[dev] > 0 ? counts[dev] : 148;
 }
 
 void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t s) {
-    const int max_pages = (max_ctx + kPage - 1) / kPage;
-    const int splits = (max_pages + a.chunk_pages - 1) / a.chunk_pages;
-    dim3 grid(splits, a.n_heads, a.B);
+    (void)max_ctx;
     count_launch();
+    const int grid = sm_count();
     if (a.geom.head_dim == 64) {
-        const int smem = a.chunk_pages * 2 * kPage * 64 * 4;
-        ensure_smem(decode_attn_kernel<64>, smem);
-        decode_attn_kernel<64><<<grid, kAttnWarps * 32, smem, s>>>(a);
+        ensure_smem(decode_attn_kernel<64>, DecCfg<64>::SMEM);
+        decode_attn_kernel<64><<<grid, DecCfg<64>::WARPS * 32, DecCfg<64>::SMEM, s>>>(a);
     } else {
-        const int smem = a.chunk_pages * 2 * kPage * 128 * 4;
-        ensure_smem(decode_attn_kernel<128>, smem);
-        decode_attn_kernel<128><<<grid, kAttnWarps * 32, smem, s>>>(a);
+        ensure_smem(decode_attn_kernel<128>, DecCfg<128>::SMEM);
+        decode_attn_kernel<128><<<grid, DecCfg<128>::WARPS * 32, DecCfg<128>::SMEM, s>>>(a);
     }
 }
 

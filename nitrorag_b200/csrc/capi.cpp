@@ -56,7 +56,7 @@ int validate_cfg(const nr_config* c) {
     if (!c) return NR_ERR_INVALID;
     if (c->block_size != nitro::kBlockSize) return NR_ERR_INVALID;
     if (c->total_blocks <= 0 || c->max_tokens_per_batch <= 0 || c->max_new_tokens <= 0) return NR_ERR_INVALID;
-    if (c->max_batch <= 0 || c->max_prefill_tokens <= 0) return NR_ERR_INVALID;
+    if (c->max_batch <= 0 || c->max_batch > 1024 || c->max_prefill_tokens <= 0) return NR_ERR_INVALID;
     if (c->q8_mode != NR_Q8_FIXED && c->q8_mode != NR_Q8_FAITHFUL) return NR_ERR_INVALID;
     if (c->sched_mode != NR_SCHED_REFERENCE) return NR_ERR_INVALID;
     return NR_OK;
@@ -594,7 +594,8 @@ int nr_paged_attention_decode(const float* q, const float* kpool, const float* v
                               int32_t n_kv_heads, int32_t head_dim, int32_t n_layers, int32_t layer, float* out,
                               void* workspace, int32_t* error_flag, void* stream) {
     if (!q || !kpool || !vpool || !block_tables || !ctx_lens || !out || !workspace) return NR_ERR_INVALID;
-    if (B <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || max_pages <= 0) return NR_ERR_INVALID;
+    if (B <= 0 || B > 1024 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || max_pages <= 0)
+        return NR_ERR_INVALID;
     if (head_dim != 64 && head_dim != 128) return NR_ERR_INVALID;
     if (n_layers <= 0 || layer < 0 || layer >= n_layers) return NR_ERR_INVALID;
     nitro::DecodeAttnArgs a;

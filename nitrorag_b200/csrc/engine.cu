@@ -20,12 +20,25 @@ namespace nitro {
 
 // ------------------------------------------------------------------ small kernels
 __global__ void embed_kernel(const float* emb, const int* tokens, int M, int dim, float* x,
-                             unsigned long long* keys) {
+                             unsigned long long* keys, float* ss, int ss_ld) {
     const int m = blockIdx.x;
     const float4* src = reinterpret_cast<const float4*>(emb + (int64_t)tokens[m] * dim);
     float4* dst = reinterpret_cast<float4*>(x + (int64_t)m * dim);
     for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) dst[i] = src[i];
     if (threadIdx.x == 0) keys[m] = kArgmaxInitKey;
+    if (!ss) return;
+    // sums of squares per 128-feature slice (blockDim 128: one element per thread)
+    __shared__ float part[4];
+    const float* row = emb + (int64_t)tokens[m] * dim;
+    for (int p = 0; p * 128 < dim; p++) {
+        const int i = p * 128 + threadIdx.x;
+        const float v = i < dim ? row[i] : 0.0f;
+        const float w = warp_sum(v * v);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = w;
+        __syncthreads();
+        if (threadIdx.x == 0) ss[(int64_t)p * ss_ld + m] = part[0] + part[1] + part[2] + part[3];
+        __syncthreads();
+    }
 }
 
 __global__ void argmax_finish_kernel(const unsigned long long* keys, int M, int* out) {
@@ -34,9 +47,9 @@ __global__ void argmax_finish_kernel(const unsigned long long* keys, int M, int*
 }
 
 void launch_embed(const float* emb, const int* tokens, int M, int dim, float* x, unsigned long long* keys,
-                  cudaStream_t s) {
+                  float* ss, int ss_ld, cudaStream_t s) {
     count_launch();
-    embed_kernel<<<M, 128, 0, s>>>(emb, tokens, M, dim, x, keys);
+    embed_kernel<<<M, 128, 0, s>>>(emb, tokens, M, dim, x, keys, ss, ss_ld);
 }
 
 void launch_argmax_finish(const unsigned long long* keys, int M, int* out, cudaStream_t s) {
@@ -64,6 +77,7 @@ Engine::~Engine() {
     cudaFree(d_h_);
     cudaFree(d_logits_);
     cudaFree(d_keys_);
+    cudaFree(d_ss_);
     cudaFree(d_err_);
     cudaFree(d_attn_ws_);
     cudaFree(tcws_.ws);
@@ -216,6 +230,7 @@ int Engine::init_device(const uint8_t* file, size_t size) {
     NR_CUDA(cudaMalloc(&d_h_, (size_t)R * c.hidden * 4));
     NR_CUDA(cudaMalloc(&d_logits_, (size_t)cfg_.max_batch * c.vocab * 4));
     NR_CUDA(cudaMalloc(&d_keys_, (size_t)R * 8));
+    NR_CUDA(cudaMalloc(&d_ss_, (size_t)((c.dim + 127) / 128) * R * 4));
     NR_CUDA(cudaMalloc(&d_err_, (size_t)(R + 1) * 4));  // [0] error flag, [1..] argmax ids
     d_argmax_ = d_err_ + 1;
     NR_CUDA(cudaMemsetAsync(d_err_, 0, (size_t)(R + 1) * 4, stream_));
@@ -235,11 +250,21 @@ int Engine::init_device(const uint8_t* file, size_t size) {
     return NR_OK;
 }
 
+// RMSNorm sums of squares travel from the residual epilogues to the next projection when
+// every projection of an M-row forward runs on the tensor-core path.
+bool Engine::use_ss(int M) const {
+    const ModelShape& c = shape_;
+    return gemm_uses_tc(M, c.dim, c.dim) && gemm_uses_tc(M, c.dim, c.hidden) &&
+           gemm_uses_tc(M, c.dim + 2 * c.kv_dim(), c.dim) && gemm_uses_tc(M, 2 * c.hidden, c.dim);
+}
+
 void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos, int B_decode, int max_ctx,
                         bool force_fixed) {
     const ModelShape& c = shape_;
     const int D = c.dim, H = c.hidden, KV = c.kv_dim(), NQKV = D + 2 * KV;
     const bool faithful = cfg_.q8_mode == NR_Q8_FAITHFUL && !force_fixed;
+    const bool ss = use_ss(M);
+    const int ss_parts = (D + 127) / 128;
     for (int l = 0; l < c.n_layers; l++) {
         // 1. q,k,v = Wqkv . rmsnorm(x); RoPE; k,v -> pages
         GemmArgs g;
@@ -248,6 +273,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g.x = d_x_; g.ldx = D; g.norm_gain = w_.rms_att + (int64_t)l * D;
         g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
         g.M = M; g.N = NQKV; g.K = D; g.kbegin = faithful ? D - 32 : 0;
+        if (ss) { g.ss_in = d_ss_; g.ss_parts = ss_parts; g.ss_ld = max_rows_; }
         Epilogue e;
         e.kind = kEpiQKV; e.q_out = d_q_; e.kpool = kpool_; e.vpool = vpool_; e.geom = geom_; e.layer = l;
         e.tok_page = d_page_; e.tok_pos = d_pos_; e.freq_re = w_.freq_re; e.freq_im = w_.freq_im;
@@ -281,6 +307,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
         Epilogue eo;
         eo.kind = kEpiResidual; eo.out = d_x_; eo.ldo = D;
+        if (ss) { eo.ss_out = d_ss_; eo.ss_ld = max_rows_; }
         { ProfScope ps(this, kKWo); launch_gemm(go, eo, stream_); }
         // 4. h = silu(W1 . rmsnorm(x)) * (W3 . rmsnorm(x))
         GemmArgs g13;
@@ -289,6 +316,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g13.x = d_x_; g13.ldx = D; g13.norm_gain = w_.rms_ffn + (int64_t)l * D;
         g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
         g13.M = M; g13.N = 2 * H; g13.K = D; g13.kbegin = faithful ? D - 32 : 0;
+        if (ss) { g13.ss_in = d_ss_; g13.ss_parts = ss_parts; g13.ss_ld = max_rows_; }
         Epilogue e13;
         e13.kind = kEpiSwiGLU; e13.out = d_h_; e13.ldo = H;
         { ProfScope ps(this, kKW13); launch_gemm(g13, e13, stream_); }
@@ -300,6 +328,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
         Epilogue e2;
         e2.kind = kEpiResidual; e2.out = d_x_; e2.ldo = D;
+        if (ss) { e2.ss_out = d_ss_; e2.ss_ld = max_rows_; }
         { ProfScope ps(this, kKW2); launch_gemm(g2, e2, stream_); }
     }
     (void)seq;
@@ -333,7 +362,7 @@ int Engine::forward_prefill(const Sequence& seq, const int* tokens, int T, int s
     d_tok_ = d_desc_; d_pos_ = d_desc_ + T; d_page_ = d_desc_ + 2 * T; d_bt_ = d_desc_ + 3 * T;
     NR_CUDA(cudaMemcpyAsync(d_desc_, h_desc_, n_ints * 4, cudaMemcpyHostToDevice, stream_));
     last_valid_ = false;  // the descriptor no longer holds a decode step
-    { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, T, c.dim, d_x_, d_keys_, stream_); }
+    { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, T, c.dim, d_x_, d_keys_, use_ss(T) ? d_ss_ : nullptr, max_rows_, stream_); }
     run_layers(T, true, &seq, start_pos, 0, start_pos + T, false);
     // classifier over the last token (src/model_q8.cpp:553-556)
     GemmArgs gl;
@@ -408,12 +437,13 @@ void Engine::enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logi
     const ModelShape& c = shape_;
     d_tok_ = d_desc_; d_pos_ = d_desc_ + B; d_page_ = d_desc_ + 2 * B; d_ctx_ = d_desc_ + 3 * B;
     d_bt_ = d_desc_ + 4 * B;
-    { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, B, c.dim, d_x_, d_keys_, stream_); }
+    { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, B, c.dim, d_x_, d_keys_, use_ss(B) ? d_ss_ : nullptr, max_rows_, stream_); }
     run_layers(B, false, nullptr, 0, B, max_ctx, force_fixed);
     GemmArgs gl;
     gl.tc = tcws_; gl.err = d_err_;
     gl.x = d_x_; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
     gl.M = B; gl.N = c.vocab; gl.K = c.dim;
+    if (use_ss(B)) { gl.ss_in = d_ss_; gl.ss_parts = (c.dim + 127) / 128; gl.ss_ld = max_rows_; }
     Epilogue el;
     el.kind = kEpiLogits; el.out = want_logits ? d_logits_ : nullptr; el.ldo = c.vocab; el.argmax_keys = d_keys_;
     { ProfScope ps(this, kKLogits); launch_gemm(gl, el, stream_); }

@@ -93,6 +93,7 @@ public:
 private:
     int upload_weights(const uint8_t* file, size_t size);
     void enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logits);
+    bool use_ss(int M) const;
     int prof_flush();
     int check_cuda(cudaError_t e, const char* what);
     void run_layers(int M, bool prefill, const Sequence* seq, int start_pos, int B_decode, int max_ctx,
@@ -117,6 +118,7 @@ private:
     float* d_h_ = nullptr;     // [max_rows][hidden]
     float* d_logits_ = nullptr;  // [max_batch][vocab]
     unsigned long long* d_keys_ = nullptr;  // [max_rows]
+    float* d_ss_ = nullptr;    // [ceil(dim/128)][max_rows] partial sums of squares of x
     int* d_argmax_ = nullptr;  // [max_rows]
     int* d_err_ = nullptr;
     void* d_attn_ws_ = nullptr;

@@ -329,6 +329,12 @@ static bool tc_disabled() {
     return v == 1;
 }
 
+bool gemm_uses_tc(int M, int N, int K) {
+    GemmArgs g;
+    g.M = M; g.N = N; g.K = K;
+    return M > 8 && !tc_disabled() && tc_gemm_supported(g);
+}
+
 void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     if (a.M > 8 && !tc_disabled() && tc_gemm_supported(a)) {
         launch_tc_gemm(a, e, a.tc, s);

@@ -134,6 +134,68 @@ struct SplitArgs {
     int* counters;       // [tiles]
 };
 
+// Raw global loads of one K chunk for this thread: its weight row (64 values) and, for
+// NT == 64, its (token, half-chunk) slice of the activations.  Issued one chunk ahead of
+// the conversion so their latency overlaps the previous chunk's work.
+template <int NT, bool F32W>
+struct ChunkRegs {
+    int4 wq[F32W ? 1 : 4];
+    float4 wf[F32W ? 16 : 1];
+    float s0, s1;
+    float4 x[NT == 64 ? 8 : 1];
+};
+
+template <int NT, bool F32W>
+__device__ __forceinline__ void load_chunk(ChunkRegs<NT, F32W>& r, const GemmArgs& a, int n, int m, int half, int k0) {
+    if (n < a.N) {
+        if (F32W) {
+            const float4* src = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k0);
+#pragma unroll
+            for (int i = 0; i < 16; i++) r.wf[i] = __ldg(src + i);
+        } else {
+            const int4* src = reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k0);
+#pragma unroll
+            for (int i = 0; i < 4; i++) r.wq[i] = __ldg(src + i);
+            r.s0 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5));
+            r.s1 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5) + 1);
+        }
+    }
+    if (NT == 64 && m < a.M) {
+        const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) r.x[i] = src[i];
+    }
+}
+
+// Activation slice (token m, 32 values at k) -> normalised fp32 -> bf16 hi/lo core rows.
+__device__ __forceinline__ void stage_tokens(const float4* xv4, const GemmArgs& a, float inv, int k, bool valid,
+                                             uint8_t* b_hi, uint8_t* b_lo, int r, int half) {
+    float xv[32];
+    if (valid) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            xv[4 * i] = xv4[i].x; xv[4 * i + 1] = xv4[i].y; xv[4 * i + 2] = xv4[i].z; xv[4 * i + 3] = xv4[i].w;
+        }
+        if (a.norm_gain) {
+            const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                float4 g = __ldg(g4 + i);
+                xv[4 * i] = g.x * (inv * xv[4 * i]);
+                xv[4 * i + 1] = g.y * (inv * xv[4 * i + 1]);
+                xv[4 * i + 2] = g.z * (inv * xv[4 * i + 2]);
+                xv[4 * i + 3] = g.w * (inv * xv[4 * i + 3]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) xv[i] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        split_store8(xv + 8 * j, b_hi + core_off(r, half * 4 + j), b_lo + core_off(r, half * 4 + j));
+}
+
 template <int NT, bool F32W>
 __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
     using S = TcSmem<NT>;
@@ -142,6 +204,7 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     __shared__ uint32_t tmem_slot;
     __shared__ float inv_rms[NT];
     __shared__ unsigned long long red_key[4][NT];
+    __shared__ float red_ss[4][NT];
     __shared__ int is_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -152,6 +215,12 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     const int c_end = min(nchunk_total, c_begin + sp.chunks_per_split);
     // the reference's batched arithmetic keeps only the last 32-wide block (kbegin = K-32)
     const int c_first = max(c_begin, a.kbegin / TC_KC);
+    const int n = n_base + tid;           // this thread's weight row
+    const int my_r = tid >> 1, my_half = tid & 1;  // NT == 64: this thread's token slice
+
+    // first chunk's loads go out before the set-up work
+    ChunkRegs<NT, F32W> cur;
+    if (c_first < c_end) load_chunk<NT, F32W>(cur, a, n, m_base + my_r, my_half, c_first * TC_KC);
 
     if (warp == 0) {
         tmem_alloc(&tmem_slot, NT);
@@ -162,19 +231,30 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         fence_barrier_init();
     }
     if (a.norm_gain) {
-        const int nw = TC_THREADS / 32;
-        for (int r = warp; r < NT; r += nw) {
-            const int m = m_base + r;
-            float ss = 0.0f;
-            if (m < a.M) {
-                const float* row = a.x + (int64_t)m * a.ldx;
-                for (int k = lane * 4; k < a.K; k += 128) {
-                    float4 v = *reinterpret_cast<const float4*>(row + k);
-                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-                }
+        if (a.ss_in) {
+            // sums of squares published by the producer of x, one per 128-feature slice
+            for (int r = tid; r < NT; r += TC_THREADS) {
+                const int m = m_base + r;
+                float ss = 0.0f;
+                if (m < a.M)
+                    for (int p = 0; p < a.ss_parts; p++) ss += __ldcg(a.ss_in + (int64_t)p * a.ss_ld + m);
+                inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
             }
-            ss = warp_sum(ss);
-            if (lane == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+        } else {
+            const int nw = TC_THREADS / 32;
+            for (int r = warp; r < NT; r += nw) {
+                const int m = m_base + r;
+                float ss = 0.0f;
+                if (m < a.M) {
+                    const float* row = a.x + (int64_t)m * a.ldx;
+                    for (int k = lane * 4; k < a.K; k += 128) {
+                        float4 v = *reinterpret_cast<const float4*>(row + k);
+                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    }
+                }
+                ss = warp_sum(ss);
+                if (lane == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+            }
         }
     }
     tc_fence_before();
@@ -182,13 +262,15 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
-    const bool norm = a.norm_gain != nullptr;
 
     int it = 0;
     bool bail = false;
     for (int c = c_first; c < c_end; c++, it++) {
         const int s = it % TC_STAGES;
         const int use = it / TC_STAGES;
+        const int k0 = c * TC_KC;
+        ChunkRegs<NT, F32W> nxt;
+        if (c + 1 < c_end) load_chunk<NT, F32W>(nxt, a, n, m_base + my_r, my_half, k0 + TC_KC);
         if (use > 0) {
             const bool got = mbar_wait(&mma_bar[s], (use - 1) & 1, a.err);
             if (!__syncthreads_and(got)) { bail = true; break; }
@@ -197,28 +279,21 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         uint8_t* a_lo = a_hi + S::A_BYTES;
         uint8_t* b_hi = a_lo + S::A_BYTES;
         uint8_t* b_lo = b_hi + S::B_BYTES;
-        const int k0 = c * TC_KC;
         // ---- weights: thread = one row, 64 values
         {
-            const int n = n_base + tid;
             float w[TC_KC];
             if (n < a.N) {
                 if (F32W) {
-                    const float4* src = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k0);
 #pragma unroll
-                    for (int i = 0; i < TC_KC / 4; i++) {
-                        float4 v = __ldg(src + i);
-                        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+                    for (int i = 0; i < 16; i++) {
+                        w[4 * i] = cur.wf[i].x; w[4 * i + 1] = cur.wf[i].y;
+                        w[4 * i + 2] = cur.wf[i].z; w[4 * i + 3] = cur.wf[i].w;
                     }
                 } else {
-                    const int4* src = reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k0);
-                    const float s0 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5));
-                    const float s1 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5) + 1);
 #pragma unroll
-                    for (int i = 0; i < TC_KC / 16; i++) {
-                        int4 raw = __ldg(src + i);
-                        const int8_t* q = reinterpret_cast<const int8_t*>(&raw);
-                        const float sc = i < 2 ? s0 : s1;
+                    for (int i = 0; i < 4; i++) {
+                        const int8_t* q = reinterpret_cast<const int8_t*>(&cur.wq[i]);
+                        const float sc = i < 2 ? cur.s0 : cur.s1;
 #pragma unroll
                         for (int j = 0; j < 16; j++) w[16 * i + j] = (float)q[j] * sc;
                     }
@@ -236,37 +311,22 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
             for (int j = 0; j < TC_KC / 8; j++)
                 split_store8(w + 8 * j, a_hi + core_off(tid, j), a_lo + core_off(tid, j));
         }
-        // ---- tokens: (token, half of the chunk) per iteration
-        for (int idx = tid; idx < NT * 2; idx += TC_THREADS) {
-            const int r = idx >> 1, half = idx & 1;
-            const int m = m_base + r;
-            float xv[32];
-            if (m < a.M) {
-                const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
+        // ---- tokens
+        if (NT == 64) {
+            const int m = m_base + my_r;
+            stage_tokens(cur.x, a, inv_rms[my_r], k0 + my_half * 32, m < a.M, b_hi, b_lo, my_r, my_half);
+        } else {
+            for (int idx = tid; idx < NT * 2; idx += TC_THREADS) {
+                const int r = idx >> 1, half = idx & 1;
+                const int m = m_base + r;
+                float4 xv4[8];
+                if (m < a.M) {
+                    const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    float4 v = src[i];
-                    xv[4 * i] = v.x; xv[4 * i + 1] = v.y; xv[4 * i + 2] = v.z; xv[4 * i + 3] = v.w;
+                    for (int i = 0; i < 8; i++) xv4[i] = src[i];
                 }
-                if (norm) {
-                    const float inv = inv_rms[r];
-                    const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k0 + half * 32);
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float4 g = __ldg(g4 + i);
-                        xv[4 * i] = g.x * (inv * xv[4 * i]);
-                        xv[4 * i + 1] = g.y * (inv * xv[4 * i + 1]);
-                        xv[4 * i + 2] = g.z * (inv * xv[4 * i + 2]);
-                        xv[4 * i + 3] = g.w * (inv * xv[4 * i + 3]);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; i++) xv[i] = 0.0f;
+                stage_tokens(xv4, a, inv_rms[r], k0 + half * 32, m < a.M, b_hi, b_lo, r, half);
             }
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                split_store8(xv + 8 * j, b_hi + core_off(r, half * 4 + j), b_lo + core_off(r, half * 4 + j));
         }
         fence_async_smem();
         __syncthreads();
@@ -282,9 +342,10 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
             }
             umma_commit(&mma_bar[s]);
         }
+        if (c + 1 < c_end) cur = nxt;
     }
     // all MMAs of this CTA are complete once the last commit's phase has completed
-    if (it > 0) {
+    if (it > 0 && !bail) {
         const int s = (it - 1) % TC_STAGES;
         if (!__syncthreads_and(mbar_wait(&mma_bar[s], ((it - 1) / TC_STAGES) & 1, a.err))) bail = true;
     }
@@ -296,17 +357,15 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         return;
     }
 
-    const int n = n_base + tid;
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
     const int64_t tile = (int64_t)m_tile * gridDim.x + n_tile;
     bool do_epi = true;
-    float* part = nullptr;
     if (sp.ksplit > 1) {
         // publish this split's partial tile: [NT][128], coalesced per column
-        part = sp.ws + (tile * sp.ksplit + split) * (int64_t)NT * TC_M;
+        float* part = sp.ws + (tile * sp.ksplit + split) * (int64_t)NT * TC_M;
         for (int c0 = 0; c0 < NT; c0 += 16) {
             float v[16];
-            tmem_ld16(tl + c0, v);
+            if (it > 0) tmem_ld16(tl + c0, v);
 #pragma unroll
             for (int j = 0; j < 16; j++) part[(int64_t)(c0 + j) * TC_M + tid] = (it > 0) ? v[j] : 0.0f;
         }
@@ -321,16 +380,25 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         if (do_epi) __threadfence();
     }
     if (do_epi) {
+        const float* pbase = sp.ws + tile * sp.ksplit * (int64_t)NT * TC_M;
         for (int c0 = 0; c0 < NT; c0 += 16) {
             float v[16];
             if (sp.ksplit > 1) {
-                const float* base = sp.ws + tile * sp.ksplit * (int64_t)NT * TC_M;
 #pragma unroll
                 for (int j = 0; j < 16; j++) v[j] = 0.0f;
-                for (int s2 = 0; s2 < sp.ksplit; s2++) {
-                    const float* ps = base + (int64_t)s2 * NT * TC_M;
+                // splits summed in index order (deterministic); 4 splits' loads in flight
+                for (int s2 = 0; s2 < sp.ksplit; s2 += 4) {
+                    float t[4][16];
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] += __ldcg(ps + (int64_t)(c0 + j) * TC_M + tid);
+                    for (int u = 0; u < 4; u++) {
+                        const float* ps = pbase + (int64_t)(s2 + u) * NT * TC_M + (int64_t)c0 * TC_M + tid;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) t[u][j] = (s2 + u < sp.ksplit) ? __ldcg(ps + (int64_t)j * TC_M) : 0.0f;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++)
+#pragma unroll
+                        for (int j = 0; j < 16; j++) v[j] += t[u][j];
                 }
             } else if (it > 0) {
                 tmem_ld16(tl + c0, v);
@@ -355,6 +423,19 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                     if (lane == 0) red_key[warp][c0 + j] = key;
                     continue;
                 }
+                if (e.kind == kEpiResidual) {
+                    float xn = 0.0f;
+                    if (ok) {
+                        float* dst = e.out + (int64_t)m * e.ldo + n;
+                        xn = *dst + mine;
+                        *dst = xn;
+                    }
+                    if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
+                        const float sq = warp_sum(xn * xn);
+                        if (lane == 0) red_ss[warp][c0 + j] = sq;
+                    }
+                    continue;
+                }
                 if (!ok) continue;
                 const bool even = (n & 1) == 0;
                 const float v0 = even ? mine : other;  // value of row n & ~1
@@ -362,9 +443,6 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                 switch (e.kind) {
                 case kEpiStore:
                     e.out[(int64_t)m * e.ldo + n] = mine;
-                    break;
-                case kEpiResidual:
-                    e.out[(int64_t)m * e.ldo + n] += mine;
                     break;
                 case kEpiSwiGLU:
                     if (even) {
@@ -384,14 +462,14 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                         if (np < D) {
                             e.q_out[(int64_t)m * D + n] = r;
                         } else {
-                            const int c = n - D;
-                            e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
-                                    (int64_t)(pos & (kPage - 1)) * hd + (c % hd)] = r;
+                            const int cidx = n - D;
+                            e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
+                                    (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = r;
                         }
                     } else {
-                        const int c = n - D - KV;
-                        e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
-                                (int64_t)(pos & (kPage - 1)) * hd + (c % hd)] = mine;
+                        const int cidx = n - D - KV;
+                        e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
+                                (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = mine;
                     }
                     break;
                 }
@@ -400,16 +478,22 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                 }
             }
         }
-        if (e.kind == kEpiLogits) {
+        if (e.kind == kEpiLogits || (e.kind == kEpiResidual && e.ss_out)) {
             __syncthreads();
-            for (int c = tid; c < NT; c += TC_THREADS) {
-                unsigned long long best = red_key[0][c];
+            for (int cix = tid; cix < NT; cix += TC_THREADS) {
+                const int m = m_base + cix;
+                if (m >= a.M) continue;
+                if (e.kind == kEpiLogits) {
+                    unsigned long long best = red_key[0][cix];
 #pragma unroll
-                for (int w = 1; w < 4; w++) best = red_key[w][c] > best ? red_key[w][c] : best;
-                const int m = m_base + c;
-                if (best != 0ull && m < a.M) {
-                    unsigned long long* slot = e.argmax_keys + m;
-                    if (best > *(volatile unsigned long long*)slot) atomicMax(slot, best);
+                    for (int w = 1; w < 4; w++) best = red_key[w][cix] > best ? red_key[w][cix] : best;
+                    if (best != 0ull) {
+                        unsigned long long* slot = e.argmax_keys + m;
+                        if (best > *(volatile unsigned long long*)slot) atomicMax(slot, best);
+                    }
+                } else {
+                    e.ss_out[(int64_t)n_tile * e.ss_ld + m] =
+                        red_ss[0][cix] + red_ss[1][cix] + red_ss[2][cix] + red_ss[3][cix];
                 }
             }
         }

@@ -33,6 +33,10 @@ struct Epilogue {
     int dim = 0, kv_dim = 0, head_dim = 0;
     // LOGITS
     unsigned long long* argmax_keys = nullptr;  // [M]
+    // RESIDUAL (tensor-core path): per 128-feature tile, sum of squares of the updated rows,
+    // ss_out[tile * ss_ld + m], consumed by the next RMSNorm (GemmArgs::ss_in)
+    float* ss_out = nullptr;
+    int ss_ld = 0;
 };
 
 // Split-K workspace of the tensor-core GEMM: partial tiles + per-tile arrival counters
@@ -58,6 +62,10 @@ struct GemmArgs {
     int M = 0, N = 0, K = 0;
     int kbegin = 0;
     TcWorkspace tc{};     // split-K workspace for the tensor-core path (optional)
+    // RMSNorm from precomputed partial sums of squares of x: ss_in[p * ss_ld + m] for
+    // p < ss_parts (tensor-core path only; otherwise the rows are re-read)
+    const float* ss_in = nullptr;
+    int ss_parts = 0, ss_ld = 0;
     int* err = nullptr;   // device error flag for bounded waits
 };
 
@@ -65,6 +73,8 @@ struct GemmArgs {
 // the CUDA-core tiled kernel.
 void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s);
 bool tc_gemm_supported(const GemmArgs& a);
+// Whether launch_gemm takes the tensor-core path for this shape.
+bool gemm_uses_tc(int M, int N, int K);
 void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, const TcWorkspace& ws, cudaStream_t s);
 
 // Decode attention over paged KV for one layer (see attention.cu).
@@ -82,6 +92,7 @@ struct DecodeAttnArgs {
     float* part_o = nullptr;            // split partials [B][n_heads][max_splits][head_dim]
     float* part_ml = nullptr;           // [B][n_heads][max_splits][2]
     int* counters = nullptr;            // [B][n_heads], zero between calls
+    int* work = nullptr;                // [2] work-item and finished-warp counters, zero between calls
     int max_splits = 0;
     int chunk_pages = 0;
     int* err = nullptr;
@@ -106,9 +117,10 @@ struct PrefillAttnArgs {
 };
 void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
 
-// x[m] = emb[tokens[m]] and argmax keys reset (src/model_q8.cpp:431-435, :578-582).
+// x[m] = emb[tokens[m]] and argmax keys reset (src/model_q8.cpp:431-435, :578-582); with
+// ss != null also the per-128-feature sums of squares of each row (ss[p * ss_ld + m]).
 void launch_embed(const float* emb, const int* tokens, int M, int dim, float* x,
-                  unsigned long long* keys, cudaStream_t s);
+                  unsigned long long* keys, float* ss, int ss_ld, cudaStream_t s);
 // Finalise argmax keys into token ids.
 void launch_argmax_finish(const unsigned long long* keys, int M, int* out, cudaStream_t s);
 

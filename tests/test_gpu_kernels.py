@@ -51,7 +51,14 @@ def test_q8_matmul(torch_cuda, restatement, M, mode, NK, split):
                                 C.c_void_p(torch.cuda.current_stream().cuda_stream))
         assert rc == 0
         torch.cuda.synchronize()
-        assert_close(out.cpu().numpy(), want, rtol=1e-4, atol=1e-5, what=f"q8 M={M} mode={mode}")
+        got = out.cpu().numpy()
+        if M <= 8:  # fp32 CUDA-core path
+            assert_close(got, want, rtol=1e-4, atol=1e-5, what=f"q8 M={M} mode={mode}")
+        else:
+            # bf16 hi/lo split on the tensor cores: ~2^-16 of each product's magnitude, so the
+            # absolute bound scales with the output's RMS (cancelling outputs can be tiny)
+            scale = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+            assert_close(got, want, rtol=1e-3, atol=1e-4 * scale, what=f"q8 M={M} mode={mode}")
     if split:
         assert int(ws[:16384].view(torch.int32).abs().sum().item()) == 0  # counters reset
 

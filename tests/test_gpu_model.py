@@ -135,12 +135,12 @@ def test_scheduler_with_prefix_sharing(request, tiny_model, mode):
 def test_scheduler_pool_pressure_eviction(ref_fixed, tiny_model):
     """A pool small enough that finished requests' cached pages are evicted (5% / 20% rule)."""
     ref = ref_fixed
-    ref.open(tiny_model, 256, 40)
-    eng = _engine(tiny_model, NR_Q8_FIXED, total_blocks=40, max_new=6)
+    ref.open(tiny_model, 256, 32)
+    eng = _engine(tiny_model, NR_Q8_FIXED, total_blocks=32, max_new=6)
     rng = np.random.default_rng(23)
     V = ref.vocab
     shared = rng.integers(0, V, 32)
-    prompts = [np.concatenate([shared, rng.integers(0, V, 40)]).astype(np.int32) for _ in range(12)]
+    prompts = [np.concatenate([shared, rng.integers(0, V, 40)]).astype(np.int32) for _ in range(24)]
     _run_scheduler_pair(ref, eng, prompts, max_new=6)
     assert eng.stats()["evictions"] > 0
     eng.close()
