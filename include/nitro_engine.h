@@ -230,11 +230,10 @@ int nr_paged_attention_decode(const float* q, const float* kpool, const float* v
 /* Q8_0 matrix product out[m][n] = sum_k x[m][k] * q[n][k] * scale[n][k/32] (src/model_q8.cpp
  * :92-125 / :382-420).  q: device int8 [N][K]; scales: device fp32 [N][K/32]; x: [M][K];
  * out: [M][N].  q8_mode as NR_Q8_*.  M <= 8 runs on CUDA cores; wider M on the tensor
- * cores, splitting K across CTAs when `workspace` (device, workspace_bytes >= 16 KiB,
- * zero-filled before its first use and left zero-filled by every call) is given. */
+ * cores (K a multiple of 64), splitting K over the CTAs of a thread-block cluster when
+ * the weight tiles alone cannot fill the GPU.  N must be even. */
 int nr_q8_matmul(const float* x, const int8_t* q, const float* scales, float* out,
-                 int32_t M, int32_t N, int32_t K, int32_t q8_mode, void* workspace,
-                 size_t workspace_bytes, void* stream);
+                 int32_t M, int32_t N, int32_t K, int32_t q8_mode, void* stream);
 
 #ifdef __cplusplus
 }

@@ -609,19 +609,13 @@ int nr_paged_attention_decode(const float* q, const float* kpool, const float* v
 }
 
 int nr_q8_matmul(const float* x, const int8_t* q, const float* scales, float* out, int32_t M, int32_t N, int32_t K,
-                 int32_t q8_mode, void* workspace, size_t workspace_bytes, void* stream) {
+                 int32_t q8_mode, void* stream) {
     if (!x || !q || !scales || !out || M <= 0 || N <= 0 || K <= 0) return NR_ERR_INVALID;
     if (K % 32 || N % 2) return NR_ERR_INVALID;
     if (q8_mode != NR_Q8_FIXED && q8_mode != NR_Q8_FAITHFUL) return NR_ERR_INVALID;
     nitro::GemmArgs g;
     g.x = x; g.ldx = K; g.wq = q; g.ws = scales; g.M = M; g.N = N; g.K = K;
     g.kbegin = q8_mode == NR_Q8_FAITHFUL ? K - 32 : 0;
-    if (workspace && workspace_bytes >= 16384 + 4096) {
-        g.tc.counters_ptr = (int*)workspace;
-        g.tc.counters = 4096;
-        g.tc.ws = (float*)((char*)workspace + 16384);
-        g.tc.ws_floats = (workspace_bytes - 16384) / 4;
-    }
     nitro::Epilogue e;
     e.kind = nitro::kEpiStore; e.out = out; e.ldo = N;
     nitro::launch_gemm(g, e, (cudaStream_t)stream);

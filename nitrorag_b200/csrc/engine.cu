@@ -80,8 +80,6 @@ Engine::~Engine() {
     cudaFree(d_ss_);
     cudaFree(d_err_);
     cudaFree(d_attn_ws_);
-    cudaFree(tcws_.ws);
-    cudaFree(tcws_.counters_ptr);
     cudaFree(d_desc_);
     cudaFreeHost(h_desc_);
     cudaFreeHost(h_argmax_);
@@ -237,11 +235,6 @@ int Engine::init_device(const uint8_t* file, size_t size) {
     const size_t ws = decode_attn_workspace_bytes(cfg_.max_batch, c.n_heads, c.head_dim(), c.max_pages());
     NR_CUDA(cudaMalloc(&d_attn_ws_, ws));
     NR_CUDA(cudaMemsetAsync(d_attn_ws_, 0, ws, stream_));
-    tcws_.ws_floats = (size_t)8 << 20;  // 32 MB of split-K partial tiles
-    tcws_.counters = 4096;
-    NR_CUDA(cudaMalloc(&tcws_.ws, tcws_.ws_floats * 4));
-    NR_CUDA(cudaMalloc(&tcws_.counters_ptr, (size_t)tcws_.counters * 4));
-    NR_CUDA(cudaMemsetAsync(tcws_.counters_ptr, 0, (size_t)tcws_.counters * 4, stream_));
     desc_ints_ = (size_t)3 * R + cfg_.max_batch + (size_t)std::max(cfg_.max_batch, 1) * c.max_pages();
     NR_CUDA(cudaMalloc(&d_desc_, desc_ints_ * 4));
     NR_CUDA(cudaMallocHost(&h_desc_, desc_ints_ * 4));
@@ -268,8 +261,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
     for (int l = 0; l < c.n_layers; l++) {
         // 1. q,k,v = Wqkv . rmsnorm(x); RoPE; k,v -> pages
         GemmArgs g;
-    g.tc = tcws_; g.err = d_err_;
-        g.tc = tcws_; g.err = d_err_;
+        g.err = d_err_;
         g.x = d_x_; g.ldx = D; g.norm_gain = w_.rms_att + (int64_t)l * D;
         g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
         g.M = M; g.N = NQKV; g.K = D; g.kbegin = faithful ? D - 32 : 0;
@@ -301,8 +293,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         }
         // 3. x += Wo . att
         GemmArgs go;
-    go.tc = tcws_; go.err = d_err_;
-        go.tc = tcws_; go.err = d_err_;
+        go.err = d_err_;
         go.x = d_att_; go.ldx = D; go.wq = w_.wo_q + (int64_t)l * D * D; go.ws = w_.wo_s + (int64_t)l * D * (D / 32);
         go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
         Epilogue eo;
@@ -311,8 +302,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         { ProfScope ps(this, kKWo); launch_gemm(go, eo, stream_); }
         // 4. h = silu(W1 . rmsnorm(x)) * (W3 . rmsnorm(x))
         GemmArgs g13;
-    g13.tc = tcws_; g13.err = d_err_;
-        g13.tc = tcws_; g13.err = d_err_;
+        g13.err = d_err_;
         g13.x = d_x_; g13.ldx = D; g13.norm_gain = w_.rms_ffn + (int64_t)l * D;
         g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
         g13.M = M; g13.N = 2 * H; g13.K = D; g13.kbegin = faithful ? D - 32 : 0;
@@ -322,8 +312,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         { ProfScope ps(this, kKW13); launch_gemm(g13, e13, stream_); }
         // 5. x += W2 . h
         GemmArgs g2;
-    g2.tc = tcws_; g2.err = d_err_;
-        g2.tc = tcws_; g2.err = d_err_;
+        g2.err = d_err_;
         g2.x = d_h_; g2.ldx = H; g2.wq = w_.w2_q + (int64_t)l * D * H; g2.ws = w_.w2_s + (int64_t)l * D * (H / 32);
         g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
         Epilogue e2;
@@ -366,7 +355,7 @@ int Engine::forward_prefill(const Sequence& seq, const int* tokens, int T, int s
     run_layers(T, true, &seq, start_pos, 0, start_pos + T, false);
     // classifier over the last token (src/model_q8.cpp:553-556)
     GemmArgs gl;
-    gl.tc = tcws_; gl.err = d_err_;
+    gl.err = d_err_;
     gl.x = d_x_ + (int64_t)(T - 1) * c.dim; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
     gl.M = 1; gl.N = c.vocab; gl.K = c.dim;
     Epilogue el;
@@ -440,7 +429,7 @@ void Engine::enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logi
     { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, B, c.dim, d_x_, d_keys_, use_ss(B) ? d_ss_ : nullptr, max_rows_, stream_); }
     run_layers(B, false, nullptr, 0, B, max_ctx, force_fixed);
     GemmArgs gl;
-    gl.tc = tcws_; gl.err = d_err_;
+    gl.err = d_err_;
     gl.x = d_x_; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
     gl.M = B; gl.N = c.vocab; gl.K = c.dim;
     if (use_ss(B)) { gl.ss_in = d_ss_; gl.ss_parts = (c.dim + 127) / 128; gl.ss_ld = max_rows_; }

@@ -122,7 +122,6 @@ private:
     int* d_argmax_ = nullptr;  // [max_rows]
     int* d_err_ = nullptr;
     void* d_attn_ws_ = nullptr;
-    TcWorkspace tcws_{};  // split-K workspace of the tensor-core projections
     // step descriptor: tokens, positions, pages, ctx, block tables (device + pinned host)
     int* d_desc_ = nullptr;
     int* h_desc_ = nullptr;

@@ -337,7 +337,7 @@ bool gemm_uses_tc(int M, int N, int K) {
 
 void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     if (a.M > 8 && !tc_disabled() && tc_gemm_supported(a)) {
-        launch_tc_gemm(a, e, a.tc, s);
+        launch_tc_gemm(a, e, s);
         return;
     }
     g_launches++;

@@ -16,10 +16,11 @@
 // weight row (16-byte int8 loads, w = q * scale) and part of the activation tile (the
 // RMSNorm of the row applied on the fly) into the UMMA canonical K-major layout in shared
 // memory; thread 0 issues 4 x 3 MMAs and commits them to the stage's mbarrier, and the
-// next chunk is converted while those run (2 stages).  When the weight tile is too narrow
-// to fill the GPU, the K range is split across CTAs; partial tiles go to a workspace and
-// the last CTA of a tile (arrival counter, reset by that CTA) sums them in split order and
-// runs the epilogue, so results do not depend on arrival order.
+// next chunk is converted while those run (2 stages); each chunk's global loads are issued
+// one chunk ahead.  When the weight tiles are too few to fill the GPU, the K range of a
+// tile is split over the CTAs of a thread-block cluster; each parks its fp32 partial tile
+// in its own shared memory and CTA r sums token slice r over the cluster through
+// distributed shared memory in rank order (deterministic), then runs the epilogue.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -28,8 +29,12 @@
 #include <set>
 #include <utility>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace nitro {
 
@@ -128,10 +133,7 @@ struct TcSmem {
 };
 
 struct SplitArgs {
-    int ksplit;          // K-range splits per tile
-    int chunks_per_split;
-    float* ws;           // [tiles][ksplit][NT][128] partial accumulators
-    int* counters;       // [tiles]
+    int ksplit;  // K-range splits per tile = CTAs per thread-block cluster (grid.x)
 };
 
 // Raw global loads of one K chunk for this thread: its weight row (64 values) and, for
@@ -205,14 +207,14 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     __shared__ float inv_rms[NT];
     __shared__ unsigned long long red_key[4][NT];
     __shared__ float red_ss[4][NT];
-    __shared__ int is_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
+    // grid (ksplit, n_tiles, m_tiles); the ksplit CTAs of one tile form one cluster
+    const int split = blockIdx.x, n_tile = blockIdx.y, m_tile = blockIdx.z;
     const int n_base = n_tile * TC_M, m_base = m_tile * NT;
     const int nchunk_total = a.K / TC_KC;
-    const int c_begin = split * sp.chunks_per_split;
-    const int c_end = min(nchunk_total, c_begin + sp.chunks_per_split);
+    const int c_begin = (int)((int64_t)split * nchunk_total / sp.ksplit);
+    const int c_end = (int)((int64_t)(split + 1) * nchunk_total / sp.ksplit);
     // the reference's batched arithmetic keeps only the last 32-wide block (kbegin = K-32)
     const int c_first = max(c_begin, a.kbegin / TC_KC);
     const int n = n_base + tid;           // this thread's weight row
@@ -358,147 +360,144 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     }
 
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    const int64_t tile = (int64_t)m_tile * gridDim.x + n_tile;
-    bool do_epi = true;
-    if (sp.ksplit > 1) {
-        // publish this split's partial tile: [NT][128], coalesced per column
-        float* part = sp.ws + (tile * sp.ksplit + split) * (int64_t)NT * TC_M;
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-            float v[16];
-            if (it > 0) tmem_ld16(tl + c0, v);
+
+    // Epilogue over 8 token columns [c, c+8) of this thread's row n.
+    auto process8 = [&](const float* v, int c) {
 #pragma unroll
-            for (int j = 0; j < 16; j++) part[(int64_t)(c0 + j) * TC_M + tid] = (it > 0) ? v[j] : 0.0f;
-        }
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) {
-            const int prev = atomicAdd(sp.counters + tile, 1);
-            is_last = prev == sp.ksplit - 1;
-        }
-        __syncthreads();
-        do_epi = is_last != 0;
-        if (do_epi) __threadfence();
-    }
-    if (do_epi) {
-        const float* pbase = sp.ws + tile * sp.ksplit * (int64_t)NT * TC_M;
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-            float v[16];
-            if (sp.ksplit > 1) {
+        for (int j = 0; j < 8; j++) {
+            const int m = m_base + c + j;
+            const float mine = v[j];
+            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
+            const bool ok = m < a.M && n < a.N;
+            if (e.kind == kEpiLogits) {
+                if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
+                unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
 #pragma unroll
-                for (int j = 0; j < 16; j++) v[j] = 0.0f;
-                // splits summed in index order (deterministic); 4 splits' loads in flight
-                for (int s2 = 0; s2 < sp.ksplit; s2 += 4) {
-                    float t[4][16];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const float* ps = pbase + (int64_t)(s2 + u) * NT * TC_M + (int64_t)c0 * TC_M + tid;
-#pragma unroll
-                        for (int j = 0; j < 16; j++) t[u][j] = (s2 + u < sp.ksplit) ? __ldcg(ps + (int64_t)j * TC_M) : 0.0f;
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++)
-#pragma unroll
-                        for (int j = 0; j < 16; j++) v[j] += t[u][j];
+                for (int o = 16; o > 0; o >>= 1) {
+                    unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = k2 > key ? k2 : key;
                 }
-            } else if (it > 0) {
+                if (lane == 0) red_key[warp][c + j] = key;
+                continue;
+            }
+            if (e.kind == kEpiResidual) {
+                float xn = 0.0f;
+                if (ok) {
+                    float* dst = e.out + (int64_t)m * e.ldo + n;
+                    xn = *dst + mine;
+                    *dst = xn;
+                }
+                if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
+                    const float sq = warp_sum(xn * xn);
+                    if (lane == 0) red_ss[warp][c + j] = sq;
+                }
+                continue;
+            }
+            if (!ok) continue;
+            const bool even = (n & 1) == 0;
+            const float v0 = even ? mine : other;  // value of row n & ~1
+            const float v1 = even ? other : mine;  // value of row n | 1
+            switch (e.kind) {
+            case kEpiStore:
+                e.out[(int64_t)m * e.ldo + n] = mine;
+                break;
+            case kEpiSwiGLU:
+                if (even) {
+                    float hgate = v0 * (1.0f / (1.0f + expf(-v0)));
+                    e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * v1;
+                }
+                break;
+            case kEpiQKV: {
+                const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+                const int pos = e.tok_pos[m];
+                const int np = n & ~1;
+                if (np < D + KV) {
+                    const int cc = np < D ? np : np - D;
+                    const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
+                    const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
+                    const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
+                    if (np < D) {
+                        e.q_out[(int64_t)m * D + n] = r;
+                    } else {
+                        const int cidx = n - D;
+                        e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
+                                (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = r;
+                    }
+                } else {
+                    const int cidx = n - D - KV;
+                    e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
+                            (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = mine;
+                }
+                break;
+            }
+            default:
+                break;
+            }
+        }
+    };
+
+    // columns this CTA finalises: all of them, or its slice of the cluster's tile
+    int col_begin = 0, col_end = NT;
+    if (sp.ksplit == 1) {
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+            float v[16];
+            if (it > 0) {
                 tmem_ld16(tl + c0, v);
             } else {
 #pragma unroll
                 for (int j = 0; j < 16; j++) v[j] = 0.0f;
             }
-#pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int m = m_base + c0 + j;
-                const float mine = v[j];
-                const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
-                const bool ok = m < a.M && n < a.N;
-                if (e.kind == kEpiLogits) {
-                    if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
-                    unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-                        key = k2 > key ? k2 : key;
-                    }
-                    if (lane == 0) red_key[warp][c0 + j] = key;
-                    continue;
-                }
-                if (e.kind == kEpiResidual) {
-                    float xn = 0.0f;
-                    if (ok) {
-                        float* dst = e.out + (int64_t)m * e.ldo + n;
-                        xn = *dst + mine;
-                        *dst = xn;
-                    }
-                    if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
-                        const float sq = warp_sum(xn * xn);
-                        if (lane == 0) red_ss[warp][c0 + j] = sq;
-                    }
-                    continue;
-                }
-                if (!ok) continue;
-                const bool even = (n & 1) == 0;
-                const float v0 = even ? mine : other;  // value of row n & ~1
-                const float v1 = even ? other : mine;  // value of row n | 1
-                switch (e.kind) {
-                case kEpiStore:
-                    e.out[(int64_t)m * e.ldo + n] = mine;
-                    break;
-                case kEpiSwiGLU:
-                    if (even) {
-                        float h = v0 * (1.0f / (1.0f + expf(-v0)));
-                        e.out[(int64_t)m * e.ldo + (n >> 1)] = h * v1;
-                    }
-                    break;
-                case kEpiQKV: {
-                    const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
-                    const int pos = e.tok_pos[m];
-                    const int np = n & ~1;
-                    if (np < D + KV) {
-                        const int cc = np < D ? np : np - D;
-                        const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
-                        const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
-                        const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
-                        if (np < D) {
-                            e.q_out[(int64_t)m * D + n] = r;
-                        } else {
-                            const int cidx = n - D;
-                            e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
-                                    (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = r;
-                        }
-                    } else {
-                        const int cidx = n - D - KV;
-                        e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
-                                (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = mine;
-                    }
-                    break;
-                }
-                default:
-                    break;
-                }
-            }
+            process8(v, c0);
+            process8(v + 8, c0 + 8);
         }
-        if (e.kind == kEpiLogits || (e.kind == kEpiResidual && e.ss_out)) {
-            __syncthreads();
-            for (int cix = tid; cix < NT; cix += TC_THREADS) {
-                const int m = m_base + cix;
-                if (m >= a.M) continue;
-                if (e.kind == kEpiLogits) {
-                    unsigned long long best = red_key[0][cix];
+    } else {
+        // Split-K reduction through distributed shared memory: every CTA of the cluster
+        // parks its partial tile [NT][128] in its own shared memory (the operand stages are
+        // free now), then CTA r sums column slice r over all CTAs in rank order.
+        cg::cluster_group cluster = cg::this_cluster();
+        float* part = reinterpret_cast<float*>(smem);
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+            float v[16];
+            if (it > 0) tmem_ld16(tl + c0, v);
 #pragma unroll
-                    for (int w = 1; w < 4; w++) best = red_key[w][cix] > best ? red_key[w][cix] : best;
-                    if (best != 0ull) {
-                        unsigned long long* slot = e.argmax_keys + m;
-                        if (best > *(volatile unsigned long long*)slot) atomicMax(slot, best);
-                    }
-                } else {
-                    e.ss_out[(int64_t)n_tile * e.ss_ld + m] =
-                        red_ss[0][cix] + red_ss[1][cix] + red_ss[2][cix] + red_ss[3][cix];
-                }
-            }
+            for (int j = 0; j < 16; j++) part[(c0 + j) * TC_M + tid] = (it > 0) ? v[j] : 0.0f;
         }
-        if (sp.ksplit > 1 && tid == 0) sp.counters[tile] = 0;
+        cluster.sync();
+        const int slice = NT / sp.ksplit;
+        col_begin = (int)cluster.block_rank() * slice;
+        col_end = col_begin + slice;
+        for (int c = col_begin; c < col_end; c += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = 0.0f;
+            for (int q = 0; q < sp.ksplit; q++) {
+                const float* peer = cluster.map_shared_rank(part, q);
+#pragma unroll
+                for (int j = 0; j < 8; j++) v[j] += peer[(c + j) * TC_M + tid];
+            }
+            process8(v, c);
+        }
     }
+    if (e.kind == kEpiLogits || (e.kind == kEpiResidual && e.ss_out)) {
+        __syncthreads();
+        for (int cix = col_begin + tid; cix < col_end; cix += TC_THREADS) {
+            const int m = m_base + cix;
+            if (m >= a.M) continue;
+            if (e.kind == kEpiLogits) {
+                unsigned long long best = red_key[0][cix];
+#pragma unroll
+                for (int w = 1; w < 4; w++) best = red_key[w][cix] > best ? red_key[w][cix] : best;
+                if (best != 0ull) {
+                    unsigned long long* slot = e.argmax_keys + m;
+                    if (best > *(volatile unsigned long long*)slot) atomicMax(slot, best);
+                }
+            } else {
+                e.ss_out[(int64_t)n_tile * e.ss_ld + m] =
+                    red_ss[0][cix] + red_ss[1][cix] + red_ss[2][cix] + red_ss[3][cix];
+            }
+        }
+    }
+    if (sp.ksplit > 1) cg::this_cluster().sync();  // peers may still be reading this CTA's partial
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, NT);
@@ -518,33 +517,38 @@ void tc_ensure_smem(K kernel, int bytes) {
 }
 
 template <int NT>
-void tc_launch(const GemmArgs& a, const Epilogue& e, const TcWorkspace& ws, cudaStream_t s) {
+void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     const int n_tiles = (a.N + TC_M - 1) / TC_M;
     const int m_tiles = (a.M + NT - 1) / NT;
     const int chunks = a.K / TC_KC;
-    // fill the GPU: split K when the tiles alone are fewer than ~2 waves of 148 SMs;
-    // a split keeps at least 2 chunks unless K is tiny; never split the faithful path
+    // Fill the GPU: when the tiles alone are fewer than the SMs, split K across the CTAs
+    // of a cluster (power of two up to 8, at most one split per chunk, NT/ksplit >= 8).
+    // The faithful path reads one chunk per row and never splits.
     int ksplit = 1;
-    if (ws.ws && a.kbegin == 0) {
-        const int tiles = n_tiles * m_tiles;
-        ksplit = tiles >= 148 ? 1 : std::min(std::max(1, (296 + tiles - 1) / tiles), std::max(1, chunks / 2));
-        while (ksplit > 1 && (size_t)tiles * ksplit * NT * TC_M > ws.ws_floats) ksplit--;
-        if (tiles > ws.counters) ksplit = 1;
-    }
+    const int tiles = n_tiles * m_tiles;
+    if (a.kbegin == 0)
+        while (ksplit < 8 && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
     SplitArgs sp;
     sp.ksplit = ksplit;
-    sp.chunks_per_split = (chunks + ksplit - 1) / ksplit;
-    sp.ksplit = (chunks + sp.chunks_per_split - 1) / sp.chunks_per_split;  // no empty splits
-    sp.ws = ws.ws;
-    sp.counters = ws.counters_ptr;
-    dim3 grid(n_tiles, m_tiles, sp.ksplit);
     const int smem = TcSmem<NT>::TOTAL;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ksplit, n_tiles, m_tiles);
+    cfg.blockDim = dim3(TC_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ksplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (a.wf) {
         tc_ensure_smem(tc_gemm_kernel<NT, true>, smem);
-        tc_gemm_kernel<NT, true><<<grid, TC_THREADS, smem, s>>>(a, e, sp);
+        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<NT, true>, a, e, sp);
     } else {
         tc_ensure_smem(tc_gemm_kernel<NT, false>, smem);
-        tc_gemm_kernel<NT, false><<<grid, TC_THREADS, smem, s>>>(a, e, sp);
+        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<NT, false>, a, e, sp);
     }
 }
 
@@ -552,13 +556,12 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, const TcWorkspace& ws, cuda
 
 bool tc_gemm_supported(const GemmArgs& a) { return a.K % TC_KC == 0 && a.N % 2 == 0 && a.M > 8; }
 
-void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, const TcWorkspace& ws, cudaStream_t s) {
+void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     count_launch();
-    if (a.M <= 64) tc_launch<64>(a, e, ws, s);
-    else if (a.M <= 128) tc_launch<128>(a, e, ws, s);
-    else tc_launch<256>(a, e, ws, s);
+    if (a.M <= 64) tc_launch<64>(a, e, s);
+    else if (a.M <= 128) tc_launch<128>(a, e, s);
+    else tc_launch<256>(a, e, s);
 }
 
-size_t tc_workspace_floats(int max_tiles_times_split, int nt) { return (size_t)max_tiles_times_split * nt * TC_M; }
 
 }  // namespace nitro

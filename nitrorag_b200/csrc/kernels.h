@@ -39,15 +39,6 @@ struct Epilogue {
     int ss_ld = 0;
 };
 
-// Split-K workspace of the tensor-core GEMM: partial tiles + per-tile arrival counters
-// (counters zero between launches; each launch leaves them zero).
-struct TcWorkspace {
-    float* ws = nullptr;
-    size_t ws_floats = 0;
-    int* counters_ptr = nullptr;
-    int counters = 0;
-};
-
 // out = x . W^T for M token rows: x [M][K] fp32 (row stride ldx), W either Q8_0 (int8
 // [N][K] + fp32 scales [N][K/32]) or fp32 [N][K].  If norm_gain is set, each x row is
 // RMS-normalised with that gain first (src/model_q8.cpp:128-140).  kbegin = K-32 limits
@@ -61,7 +52,6 @@ struct GemmArgs {
     const float* wf = nullptr;
     int M = 0, N = 0, K = 0;
     int kbegin = 0;
-    TcWorkspace tc{};     // split-K workspace for the tensor-core path (optional)
     // RMSNorm from precomputed partial sums of squares of x: ss_in[p * ss_ld + m] for
     // p < ss_parts (tensor-core path only; otherwise the rows are re-read)
     const float* ss_in = nullptr;
@@ -75,7 +65,7 @@ void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s);
 bool tc_gemm_supported(const GemmArgs& a);
 // Whether launch_gemm takes the tensor-core path for this shape.
 bool gemm_uses_tc(int M, int N, int K);
-void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, const TcWorkspace& ws, cudaStream_t s);
+void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s);
 
 // Decode attention over paged KV for one layer (see attention.cu).
 struct DecodeAttnArgs {
