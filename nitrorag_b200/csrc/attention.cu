@@ -32,7 +32,6 @@ namespace {
 
 constexpr int kAttnWarps = 4;
 
-__device__ __forceinline__ void fence_async_smem_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Running softmax state of one query inside a warp.  Lane l owns output dims
@@ -126,27 +125,40 @@ struct DecCfg {
 struct DecItem {
     int b, h, split, p0, np, ctx, nsplit;
     bool valid;
+    int pid;       // lane i < np: physical page of the item's i-th page
+    float q[4];    // lane l: query dims l + 32 j (pre-scaled), j < head_dim / 32
 };
 
-__device__ __forceinline__ DecItem dec_item(int idx, int total, const int* prefix, int B, int n_heads,
-                                            int chunk_pages, const int* ctx_lens) {
+// Decode work item `idx` into its sequence / head / chunk, and prefetch everything its
+// processing needs (page ids, query) so no dependent global load sits in front of the
+// bulk copies later.
+template <int HD>
+__device__ __forceinline__ DecItem dec_item(int idx, int total, const int* prefix, const int* ctx_s,
+                                            const DecodeAttnArgs& a, int lane, float qscale) {
     DecItem it;
     it.valid = idx < total;
+    it.pid = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) it.q[j] = 0.0f;
     if (!it.valid) { it.b = it.h = it.split = it.p0 = it.np = it.ctx = it.nsplit = 0; return it; }
-    int lo = 0, hi = B;  // largest b with prefix[b] <= idx
+    int lo = 0, hi = a.B;  // largest b with prefix[b] <= idx
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
         if (prefix[mid] <= idx) lo = mid; else hi = mid;
     }
     it.b = lo;
     const int rem = idx - prefix[lo];
-    it.split = rem / n_heads;
-    it.h = rem % n_heads;
-    it.ctx = ctx_lens[lo];
+    it.split = rem / a.n_heads;
+    it.h = rem % a.n_heads;
+    it.ctx = ctx_s[lo];
     const int pages = (it.ctx + kPage - 1) / kPage;
-    it.nsplit = (pages + chunk_pages - 1) / chunk_pages;
-    it.p0 = it.split * chunk_pages;
-    it.np = min(chunk_pages, pages - it.p0);
+    it.nsplit = (pages + a.chunk_pages - 1) / a.chunk_pages;
+    it.p0 = it.split * a.chunk_pages;
+    it.np = min(a.chunk_pages, pages - it.p0);
+    if (lane < it.np) it.pid = a.block_tables[(int64_t)it.b * a.max_pages + it.p0 + lane];
+    const float* qrow = a.q + ((int64_t)it.b * a.n_heads + it.h) * HD;
+#pragma unroll
+    for (int j = 0; j < HD / 32; j++) it.q[j] = qrow[lane + 32 * j] * qscale;
     return it;
 }
 
@@ -157,17 +169,21 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
     extern __shared__ __align__(128) float smem[];
     __shared__ uint64_t bars[C::WARPS][kDecStages];
     __shared__ int prefix[1025];
+    __shared__ int ctx_s[1024];
     __shared__ int warp_tot[32];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kvmul = a.n_heads / a.geom.n_kv_heads;
 
-    // item table: prefix[b] = first item of sequence b (items of b: nsplit(b) * n_heads)
+    // item table from the step descriptor (written before this step's first kernel, so it
+    // is read before waiting on the previous kernel): prefix[b] = first item of sequence b
     for (int base = 0; base < a.B; base += blockDim.x) {
         const int b = base + threadIdx.x;
         int cnt = 0;
         if (b < a.B) {
-            const int pages = (a.ctx_lens[b] + kPage - 1) / kPage;
+            const int ctx = a.ctx_lens[b];
+            ctx_s[b] = ctx;
+            const int pages = (ctx + kPage - 1) / kPage;
             cnt = ((pages + a.chunk_pages - 1) / a.chunk_pages) * a.n_heads;
         }
         int incl = cnt;
@@ -201,14 +217,16 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
         fence_barrier_init();
     }
     __syncwarp();
+    grid_dependency_wait();  // q, the K/V pages and the work counters come from earlier kernels
 
     auto fetch = [&]() -> int {
         int v = 0;
         if (lane == 0) v = atomicAdd(a.work, 1);
         return __shfl_sync(0xffffffffu, v, 0);
     };
-    DecItem cur = dec_item(fetch(), total, prefix, a.B, a.n_heads, a.chunk_pages, a.ctx_lens);
-    DecItem nxt = dec_item(cur.valid ? fetch() : total, total, prefix, a.B, a.n_heads, a.chunk_pages, a.ctx_lens);
+    const float qscale = kLog2e / sqrtf((float)HD);
+    DecItem cur = dec_item<HD>(fetch(), total, prefix, ctx_s, a, lane, qscale);
+    DecItem nxt = dec_item<HD>(cur.valid ? fetch() : total, total, prefix, ctx_s, a, lane, qscale);
 
     // issue pointer: page `ip` of item `iq` (0 = cur, 1 = nxt); k-th issued page -> slot k % stages
     int iq = 0, ip = 0;
@@ -218,11 +236,12 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
             const DecItem& src = iq == 0 ? cur : nxt;
             if (iq > 1 || !src.valid) break;
             if (ip >= src.np) { iq++; ip = 0; continue; }
+            const int page = __shfl_sync(0xffffffffu, src.pid, ip);
             if (lane == 0) {
+                // the slot's previous page was consumed by every lane before the __syncwarp
+                // that ended its processing, so the copy cannot overwrite live data
                 const int slot = issued % kDecStages;
-                const int page = a.block_tables[(int64_t)src.b * a.max_pages + src.p0 + ip];
                 const int64_t off = a.geom.tile_offset(page, a.layer, src.h / kvmul);
-                fence_async_smem_cta();
                 mbar_arrive_expect_tx(&wb[slot], 2u * C::TILE * 4u);
                 bulk_g2s(ring + (2 * slot) * C::TILE, a.kpool + off, C::TILE * 4, &wb[slot]);
                 bulk_g2s(ring + (2 * slot + 1) * C::TILE, a.vpool + off, C::TILE * 4, &wb[slot]);
@@ -232,12 +251,12 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
         }
     };
 
-    const float qscale = kLog2e / sqrtf((float)HD);
     bool ok = true;
     while (cur.valid) {
-        // this item's query
+        issue_some();
         __syncwarp();
-        for (int d = lane; d < HD; d += 32) qs[d] = a.q[((int64_t)cur.b * a.n_heads + cur.h) * HD + d] * qscale;
+#pragma unroll
+        for (int j = 0; j < HD / 32; j++) qs[lane + 32 * j] = cur.q[j];
         __syncwarp();
         QState<HD> st;
         st.init();
@@ -275,19 +294,30 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
                 __threadfence();
+                // lanes fetch the splits' (max, sum) 32 at a time; weights broadcast by shuffle
                 float GM = -INFINITY;
-                for (int sp = 0; sp < cur.nsplit; sp++) GM = fmaxf(GM, __ldcg(a.part_ml + (bh * a.max_splits + sp) * 2));
+                for (int base = 0; base < cur.nsplit; base += 32)
+                    if (base + lane < cur.nsplit)
+                        GM = fmaxf(GM, __ldcg(a.part_ml + (bh * a.max_splits + base + lane) * 2));
+                GM = warp_max(GM);
                 float GL = 0.0f, GO[DPL];
 #pragma unroll
                 for (int i = 0; i < DPL; i++) GO[i] = 0.0f;
-                for (int sp = 0; sp < cur.nsplit; sp++) {
-                    const float ms = __ldcg(a.part_ml + (bh * a.max_splits + sp) * 2);
-                    const float ls = __ldcg(a.part_ml + (bh * a.max_splits + sp) * 2 + 1);
-                    const float c = (ms == -INFINITY) ? 0.0f : exp2f(ms - GM);
-                    GL += ls * c;
-                    const float* ps = a.part_o + (bh * a.max_splits + sp) * HD + lane * DPL;
+                for (int base = 0; base < cur.nsplit; base += 32) {
+                    float ms = -INFINITY, ls = 0.0f;
+                    if (base + lane < cur.nsplit) {
+                        ms = __ldcg(a.part_ml + (bh * a.max_splits + base + lane) * 2);
+                        ls = __ldcg(a.part_ml + (bh * a.max_splits + base + lane) * 2 + 1);
+                    }
+                    const float cl = (ms == -INFINITY) ? 0.0f : exp2f(ms - GM);
+                    GL += warp_sum(ls * cl);
+                    const int cnt = min(32, cur.nsplit - base);
+                    for (int sp = 0; sp < cnt; sp++) {
+                        const float c = __shfl_sync(0xffffffffu, cl, sp);
+                        const float* ps = a.part_o + (bh * a.max_splits + base + sp) * HD + lane * DPL;
 #pragma unroll
-                    for (int i = 0; i < DPL; i++) GO[i] += __ldcg(ps + i) * c;
+                        for (int i = 0; i < DPL; i++) GO[i] += __ldcg(ps + i) * c;
+                    }
                 }
                 const float inv = 1.0f / GL;
 #pragma unroll
@@ -298,8 +328,9 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
         // advance: the issue pointer moves with the item window
         cur = nxt;
         iq = iq > 0 ? iq - 1 : 0;
-        nxt = dec_item(cur.valid ? fetch() : total, total, prefix, a.B, a.n_heads, a.chunk_pages, a.ctx_lens);
+        nxt = dec_item<HD>(cur.valid ? fetch() : total, total, prefix, ctx_s, a, lane, qscale);
     }
+    grid_dependents_launch();
     // every copy this warp issued has been consumed (issued == consumed here); the last warp
     // to finish resets the work counters for the next launch
     if (lane == 0) {
@@ -345,8 +376,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
         fence_barrier_init();
-        for (int i = 0; i < kStages && i < n_pages; i++) issue(i);
     }
+    grid_dependency_wait();  // q and this chunk's K/V rows come from the projection kernel
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kStages && i < n_pages; i++) issue(i);
     const float qscale = kLog2e / sqrtf((float)HD);
     for (int i = threadIdx.x; i < kPrefillQ * HD; i += blockDim.x) {
         const int qi = i / HD, d = i % HD;
@@ -376,6 +409,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
         if (!__syncthreads_and(ok)) { ok = false; break; }
         if (threadIdx.x == 0 && p + kStages < n_pages) issue(p + kStages);
     }
+    grid_dependents_launch();
     if (!ok) return;
 #pragma unroll
     for (int j = 0; j < QPW; j++) {
@@ -447,10 +481,10 @@ void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t 
     const int grid = sm_count();
     if (a.geom.head_dim == 64) {
         ensure_smem(decode_attn_kernel<64>, DecCfg<64>::SMEM);
-        decode_attn_kernel<64><<<grid, DecCfg<64>::WARPS * 32, DecCfg<64>::SMEM, s>>>(a);
+        launch_ex(decode_attn_kernel<64>, dim3(grid), dim3(DecCfg<64>::WARPS * 32), DecCfg<64>::SMEM, s, 1, a);
     } else {
         ensure_smem(decode_attn_kernel<128>, DecCfg<128>::SMEM);
-        decode_attn_kernel<128><<<grid, DecCfg<128>::WARPS * 32, DecCfg<128>::SMEM, s>>>(a);
+        launch_ex(decode_attn_kernel<128>, dim3(grid), dim3(DecCfg<128>::WARPS * 32), DecCfg<128>::SMEM, s, 1, a);
     }
 }
 
@@ -460,11 +494,11 @@ void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
     if (a.geom.head_dim == 64) {
         const int smem = (kStages * 2 * kPage * 64 + kPrefillQ * 64) * 4;
         ensure_smem(prefill_attn_kernel<64>, smem);
-        prefill_attn_kernel<64><<<grid, kAttnWarps * 32, smem, s>>>(a);
+        launch_ex(prefill_attn_kernel<64>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
     } else {
         const int smem = (kStages * 2 * kPage * 128 + kPrefillQ * 128) * 4;
         ensure_smem(prefill_attn_kernel<128>, smem);
-        prefill_attn_kernel<128><<<grid, kAttnWarps * 32, smem, s>>>(a);
+        launch_ex(prefill_attn_kernel<128>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
     }
 }
 

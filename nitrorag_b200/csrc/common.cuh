@@ -3,6 +3,8 @@
 // the KV page addressing.
 #pragma once
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 #include <cuda_runtime.h>
 
 namespace nitro {
@@ -80,6 +82,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Programmatic dependent launch: wait until the previous kernel in the stream has
+// completed and its writes are visible (a no-op when launched without the attribute), and
+// allow the next kernel to start its independent prologue early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -104,5 +112,44 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 #endif  // __CUDACC__
 
 constexpr unsigned long long kArgmaxInitKey = (0x80000000ull << 32) | 0xffffffffull;
+
+// Programmatic dependent launch for every engine kernel (NITRO_PDL=0 turns it off): each
+// kernel waits (griddepcontrol.wait) before touching what earlier kernels produce, so the
+// launch of kernel N+1 and its independent prologue overlap kernel N's tail.
+inline bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* env = getenv("NITRO_PDL");
+        v = (env && env[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+template <typename Kern, typename... Args>
+inline cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, unsigned cluster_x,
+                             Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    if (pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        n++;
+    }
+    if (cluster_x > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster_x;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        n++;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace nitro

@@ -11,6 +11,7 @@
 // and the classifier (final RMSNorm prologue, fp32 embedding^T, greedy argmax keys).
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -22,6 +23,8 @@ namespace nitro {
 __global__ void embed_kernel(const float* emb, const int* tokens, int M, int dim, float* x,
                              unsigned long long* keys, float* ss, int ss_ld) {
     const int m = blockIdx.x;
+    grid_dependency_wait();  // x, keys and sums of squares may still be read by the previous step
+    grid_dependents_launch();
     const float4* src = reinterpret_cast<const float4*>(emb + (int64_t)tokens[m] * dim);
     float4* dst = reinterpret_cast<float4*>(x + (int64_t)m * dim);
     for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) dst[i] = src[i];
@@ -43,18 +46,20 @@ __global__ void embed_kernel(const float* emb, const int* tokens, int M, int dim
 
 __global__ void argmax_finish_kernel(const unsigned long long* keys, int M, int* out) {
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    grid_dependency_wait();
+    grid_dependents_launch();
     if (m < M) out[m] = (int)(0xffffffffu - (uint32_t)(keys[m] & 0xffffffffull));
 }
 
 void launch_embed(const float* emb, const int* tokens, int M, int dim, float* x, unsigned long long* keys,
                   float* ss, int ss_ld, cudaStream_t s) {
     count_launch();
-    embed_kernel<<<M, 128, 0, s>>>(emb, tokens, M, dim, x, keys, ss, ss_ld);
+    launch_ex(embed_kernel, dim3(M), dim3(128), 0, s, 1, emb, tokens, M, dim, x, keys, ss, ss_ld);
 }
 
 void launch_argmax_finish(const unsigned long long* keys, int M, int* out, cudaStream_t s) {
     count_launch();
-    argmax_finish_kernel<<<(M + 127) / 128, 128, 0, s>>>(keys, M, out);
+    launch_ex(argmax_finish_kernel, dim3((M + 127) / 128), dim3(128), 0, s, 1, keys, M, out);
 }
 
 // ------------------------------------------------------------------ engine
@@ -84,6 +89,8 @@ Engine::~Engine() {
     cudaFreeHost(h_desc_);
     cudaFreeHost(h_argmax_);
     for (auto& ev : ev_pool_) cudaEventDestroy(ev);
+    for (auto& kv : graphs_)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -408,8 +415,12 @@ int Engine::forward_decode(int B, const int* tokens, const int* positions, const
     d_tok_ = d_desc_; d_pos_ = d_desc_ + B; d_page_ = d_desc_ + 2 * B; d_ctx_ = d_desc_ + 3 * B;
     d_bt_ = d_desc_ + 4 * B;
     NR_CUDA(cudaMemcpyAsync(d_desc_, h_desc_, n_ints * 4, cudaMemcpyHostToDevice, stream_));
-    enqueue_decode(B, max_ctx, force_fixed, logits_out != nullptr);
+    {
+        int rc = launch_decode_step(B, max_ctx, force_fixed, logits_out != nullptr);
+        if (rc) return rc;
+    }
     last_B_ = B; last_max_ctx_ = max_ctx; last_force_fixed_ = force_fixed; last_valid_ = true;
+    last_logits_ = logits_out != nullptr;
     NR_CUDA(cudaMemcpyAsync(h_argmax_, d_err_, (size_t)(B + 1) * 4, cudaMemcpyDeviceToHost, stream_));
     if (logits_out)
         NR_CUDA(cudaMemcpyAsync(logits_out, d_logits_, (size_t)B * c.vocab * 4, cudaMemcpyDeviceToHost, stream_));
@@ -439,12 +450,60 @@ void Engine::enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logi
     { ProfScope ps(this, kKArgmax); launch_argmax_finish(d_keys_, B, d_argmax_, stream_); }
 }
 
+static bool graphs_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* env = getenv("NITRO_GRAPHS");
+        v = (env && env[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+// Run one decode step's kernels: eagerly, or as a CUDA graph once the step shape has been
+// seen before (graph replay removes the per-kernel launch work; the kernels' programmatic
+// dependencies are kept as graph edges).
+int Engine::launch_decode_step(int B, int max_ctx, bool force_fixed, bool want_logits) {
+    if (profiling_ || !graphs_enabled()) {
+        enqueue_decode(B, max_ctx, force_fixed, want_logits);
+        return NR_OK;
+    }
+    GraphEntry& g = graphs_[std::make_tuple(B, force_fixed, want_logits)];
+    if (!g.exec && g.seen++ == 0) {
+        enqueue_decode(B, max_ctx, force_fixed, want_logits);
+        return NR_OK;
+    }
+    if (!g.exec) {
+        cudaGraph_t graph = nullptr;
+        NR_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        const int64_t before = kernel_launch_count();
+        enqueue_decode(B, max_ctx, force_fixed, want_logits);
+        const cudaError_t cap = cudaStreamEndCapture(stream_, &graph);
+        if (cap != cudaSuccess) {
+            cudaGetLastError();
+            return fail(NR_ERR_CUDA, std::string("decode graph capture: ") + cudaGetErrorString(cap));
+        }
+        g.kernels = kernel_launch_count() - before;
+        const cudaError_t inst = cudaGraphInstantiate(&g.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (inst != cudaSuccess) {
+            g.exec = nullptr;
+            return fail(NR_ERR_CUDA, std::string("decode graph instantiate: ") + cudaGetErrorString(inst));
+        }
+    }
+    NR_CUDA(cudaGraphLaunch(g.exec, stream_));
+    for (int64_t i = 0; i < g.kernels; i++) count_launch();
+    return NR_OK;
+}
+
 int Engine::replay_decode(int n) {
     if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
     if (!last_valid_) return fail(NR_ERR_INVALID, "no decode step to replay");
     NR_CUDA(cudaSetDevice(cfg_.device));
     for (int i = 0; i < n; i++) {
-        enqueue_decode(last_B_, last_max_ctx_, last_force_fixed_, false);
+        {
+            int rc = launch_decode_step(last_B_, last_max_ctx_, last_force_fixed_, false);
+            if (rc) return rc;
+        }
         if (profiling_ && ev_used_ + 512 > ev_pool_.size()) {
             int rc = prof_flush();
             if (rc) return rc;

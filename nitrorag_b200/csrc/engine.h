@@ -5,6 +5,7 @@
 
 #include <map>
 #include <memory>
+#include <tuple>
 #include <string>
 #include <vector>
 
@@ -131,7 +132,16 @@ private:
     int* h_argmax_ = nullptr;
     // last decode step (for replay)
     int last_B_ = 0, last_max_ctx_ = 0;
-    bool last_force_fixed_ = false, last_valid_ = false;
+    bool last_force_fixed_ = false, last_valid_ = false, last_logits_ = false;
+    // decode steps captured as CUDA graphs, keyed by (rows, force_fixed, logits); a key is
+    // captured the second time it is seen (the first, eager run configures the kernels)
+    struct GraphEntry {
+        cudaGraphExec_t exec = nullptr;
+        int64_t kernels = 0;
+        int seen = 0;
+    };
+    std::map<std::tuple<int, bool, bool>, GraphEntry> graphs_;
+    int launch_decode_step(int B, int max_ctx, bool force_fixed, bool want_logits);
     // profiling state
     bool profiling_ = false;
     std::vector<cudaEvent_t> ev_pool_;

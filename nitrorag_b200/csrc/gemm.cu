@@ -126,6 +126,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
     __shared__ float inv_rms[MT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool norm = a.norm_gain != nullptr;
+    grid_dependency_wait();
     if (norm) {
         rms_rows(a.x, a.ldx, a.K, 0, MT, a.M, inv_rms);
         __syncthreads();
@@ -168,6 +169,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
             }
         }
     }
+    grid_dependents_launch();
 #pragma unroll
     for (int m = 0; m < MT; m++) {
         acc0[m] = warp_sum(acc0[m]);
@@ -204,6 +206,7 @@ __global__ void __launch_bounds__(128) gemm_tiled_kernel(GemmArgs a, Epilogue e)
     const int tid = threadIdx.x;
     const int n_base = blockIdx.x * TN, m_base = blockIdx.y * TM;
     const bool norm = a.norm_gain != nullptr;
+    grid_dependency_wait();
     if (norm) {
         rms_rows(a.x, a.ldx, a.K, m_base, TM, a.M, inv_rms);
         __syncthreads();
@@ -272,6 +275,7 @@ __global__ void __launch_bounds__(128) gemm_tiled_kernel(GemmArgs a, Epilogue e)
         __syncthreads();
     }
 
+    grid_dependents_launch();
     const int n0 = n_base + tn * 4;
     if (e.kind == kEpiLogits) {
 #pragma unroll
@@ -314,8 +318,8 @@ __global__ void __launch_bounds__(128) gemm_tiled_kernel(GemmArgs a, Epilogue e)
 template <int MT>
 void gemv_dispatch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     dim3 grid((a.N / 2 + 3) / 4);
-    if (a.wf) gemv_kernel<MT, true><<<grid, 128, 0, s>>>(a, e);
-    else gemv_kernel<MT, false><<<grid, 128, 0, s>>>(a, e);
+    if (a.wf) launch_ex(gemv_kernel<MT, true>, grid, dim3(128), 0, s, 1, a, e);
+    else launch_ex(gemv_kernel<MT, false>, grid, dim3(128), 0, s, 1, a, e);
 }
 
 }  // namespace
@@ -347,8 +351,8 @@ void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     else if (a.M <= 8) gemv_dispatch<8>(a, e, s);
     else {
         dim3 grid((a.N + TN - 1) / TN, (a.M + TM - 1) / TM);
-        if (a.wf) gemm_tiled_kernel<true><<<grid, 128, 0, s>>>(a, e);
-        else gemm_tiled_kernel<false><<<grid, 128, 0, s>>>(a, e);
+        if (a.wf) launch_ex(gemm_tiled_kernel<true>, grid, dim3(128), 0, s, 1, a, e);
+        else launch_ex(gemm_tiled_kernel<false>, grid, dim3(128), 0, s, 1, a, e);
     }
 }
 

@@ -148,6 +148,32 @@ struct ChunkRegs {
 };
 
 template <int NT, bool F32W>
+__device__ __forceinline__ void load_chunk_w(ChunkRegs<NT, F32W>& r, const GemmArgs& a, int n, int k0) {
+    if (n < a.N) {
+        if (F32W) {
+            const float4* src = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k0);
+#pragma unroll
+            for (int i = 0; i < 16; i++) r.wf[i] = __ldg(src + i);
+        } else {
+            const int4* src = reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k0);
+#pragma unroll
+            for (int i = 0; i < 4; i++) r.wq[i] = __ldg(src + i);
+            r.s0 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5));
+            r.s1 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5) + 1);
+        }
+    }
+}
+
+template <int NT, bool F32W>
+__device__ __forceinline__ void load_chunk_x(ChunkRegs<NT, F32W>& r, const GemmArgs& a, int m, int half, int k0) {
+    if (NT == 64 && m < a.M) {
+        const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) r.x[i] = src[i];
+    }
+}
+
+template <int NT, bool F32W>
 __device__ __forceinline__ void load_chunk(ChunkRegs<NT, F32W>& r, const GemmArgs& a, int n, int m, int half, int k0) {
     if (n < a.N) {
         if (F32W) {
@@ -220,9 +246,10 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     const int n = n_base + tid;           // this thread's weight row
     const int my_r = tid >> 1, my_half = tid & 1;  // NT == 64: this thread's token slice
 
-    // first chunk's loads go out before the set-up work
+    // the first chunk's weight loads go out before the set-up work and before waiting for
+    // the previous kernel (weights are read-only; activations are not)
     ChunkRegs<NT, F32W> cur;
-    if (c_first < c_end) load_chunk<NT, F32W>(cur, a, n, m_base + my_r, my_half, c_first * TC_KC);
+    if (c_first < c_end) load_chunk_w<NT, F32W>(cur, a, n, c_first * TC_KC);
 
     if (warp == 0) {
         tmem_alloc(&tmem_slot, NT);
@@ -232,6 +259,8 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         for (int s = 0; s < TC_STAGES; s++) mbar_init(&mma_bar[s], 1);
         fence_barrier_init();
     }
+    grid_dependency_wait();
+    if (c_first < c_end) load_chunk_x<NT, F32W>(cur, a, m_base + my_r, my_half, c_first * TC_KC);
     if (a.norm_gain) {
         if (a.ss_in) {
             // sums of squares published by the producer of x, one per 128-feature slice
@@ -352,6 +381,7 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         if (!__syncthreads_and(mbar_wait(&mma_bar[s], ((it - 1) / TC_STAGES) & 1, a.err))) bail = true;
     }
     tc_fence_after();
+    grid_dependents_launch();
     if (bail) {  // a wait gave up (error flag set): release TMEM and leave
         tc_fence_before();
         __syncthreads();
@@ -531,24 +561,13 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     SplitArgs sp;
     sp.ksplit = ksplit;
     const int smem = TcSmem<NT>::TOTAL;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ksplit, n_tiles, m_tiles);
-    cfg.blockDim = dim3(TC_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = ksplit;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    const dim3 grid(ksplit, n_tiles, m_tiles);
     if (a.wf) {
         tc_ensure_smem(tc_gemm_kernel<NT, true>, smem);
-        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<NT, true>, a, e, sp);
+        launch_ex(tc_gemm_kernel<NT, true>, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
     } else {
         tc_ensure_smem(tc_gemm_kernel<NT, false>, smem);
-        cudaLaunchKernelEx(&cfg, tc_gemm_kernel<NT, false>, a, e, sp);
+        launch_ex(tc_gemm_kernel<NT, false>, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
     }
 }
 
