@@ -112,11 +112,20 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
 // their K/V page tiles through its own ring of kDecStages shared-memory slots, issuing the
 // next item's pages while the current item drains, so the copy engine always has pages
 // in flight.  No CTA-wide barrier is taken after set-up.
-constexpr int kDecStages = 3;
+#ifndef NITRO_DEC_STAGES
+#define NITRO_DEC_STAGES 3
+#endif
+#ifndef NITRO_DEC_WARPS64
+#define NITRO_DEC_WARPS64 8
+#endif
+#ifndef NITRO_DEC_CHUNK64
+#define NITRO_DEC_CHUNK64 8
+#endif
+constexpr int kDecStages = NITRO_DEC_STAGES;
 
 template <int HD>
 struct DecCfg {
-    static constexpr int WARPS = HD == 64 ? 8 : 4;
+    static constexpr int WARPS = HD == 64 ? NITRO_DEC_WARPS64 : NITRO_DEC_WARPS64 / 2;
     static constexpr int TILE = kPage * HD;                              // floats per K or V tile
     static constexpr int RING_FLOATS = WARPS * kDecStages * 2 * TILE;
     static constexpr int SMEM = RING_FLOATS * 4 + WARPS * HD * 4;        // + one query per warp
@@ -325,9 +334,12 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
                 if (lane == 0) a.counters[bh] = 0;
             }
         }
-        // advance: the issue pointer moves with the item window
+        // advance: the issue pointer moves with the item window.  It is at or past the end
+        // of the retired item; if it had not crossed into the next one yet, it starts that
+        // item from its first page.
+        if (iq == 0) { iq = 1; ip = 0; }
         cur = nxt;
-        iq = iq > 0 ? iq - 1 : 0;
+        iq -= 1;
         nxt = dec_item<HD>(cur.valid ? fetch() : total, total, prefix, ctx_s, a, lane, qscale);
     }
     grid_dependents_launch();
@@ -438,7 +450,7 @@ void ensure_smem(K kernel, int bytes) {
 
 }  // namespace
 
-int decode_attn_chunk_pages(int head_dim) { return head_dim <= 64 ? 8 : 4; }
+int decode_attn_chunk_pages(int head_dim) { return head_dim <= 64 ? NITRO_DEC_CHUNK64 : NITRO_DEC_CHUNK64 / 2; }
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

@@ -14,10 +14,9 @@ constexpr int kPage = 16;  // tokens per KV page (src/pagedMemory.hpp:9)
 // Error codes a kernel records in its error flag (first writer wins).
 constexpr int kErrWaitTimeout = 1;
 
-// Iteration limit of every mbarrier wait.  Each try_wait may itself suspend for a
-// hardware-chosen interval, so the limit bounds the wait to well under a second when a
-// copy never lands.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Time limit of every mbarrier wait (nanoseconds of %globaltimer).  A wait that gives up
+// sets the kernel's error flag; the kernel then skips the work that needed the data.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 // Page layout of the device K and V pools: [page][layer][kv_head][16][head_dim] fp32, so
 // the 16 rows of one (page, layer, kv_head) form one contiguous tile of 16*head_dim floats.
@@ -64,20 +63,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(1000u)  // suspend at most ~1 us per poll
         : "memory");
     return ok != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete, at most kSpinLimit polls.  On timeout
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for phase `parity` of `bar` to complete, for at most kWaitLimitNs.  On timeout
 // the error flag is set and false returned; the caller skips the work that needed the
 // data and returns.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-    for (uint32_t i = 0; i < kSpinLimit; i++)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    }
     if (err) atomicCAS(err, 0, kErrWaitTimeout);
     return false;
 }
