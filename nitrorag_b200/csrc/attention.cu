@@ -13,10 +13,11 @@
 // (src/model_q8.cpp:625-662, :142-159), and prefill with a single-pass online softmax
 // (:485-523); both equal softmax(q.k/sqrt(head)) . V up to fp32 rounding.
 //
-// Decode work is split ("flash-decoding"): each CTA takes one (sequence, head, chunk of
-// up to chunk_pages pages); a sequence whose context spans several chunks has its partial
-// (max, sum, unnormalised output) merged by whichever CTA finishes last, found with a
-// per-(sequence, head) arrival counter that the merging CTA resets to zero.
+// Decode work is split ("flash-decoding"): a persistent kernel streams (sequence, head,
+// chunk of up to chunk_pages pages) items through per-warp bulk-copy rings; an item that
+// covers a whole context writes its output, the others write their partial (max, sum,
+// unnormalised output) and a small merge kernel, chained behind it with programmatic
+// dependent launch, combines them.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -60,7 +61,7 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
     const int t = lane >> 1, half = lane & 1;
     const float4* krow = reinterpret_cast<const float4*>(Kt + t * HD + half * (HD / 2));
     const float4* qrow = reinterpret_cast<const float4*>(qs + half * (HD / 2));
-    float s = 0.0f;
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;  // four short FMA chains
 #pragma unroll
     for (int j = 0; j < HALF4; j++) {
         // rotate the float4 index with the lane so the 8 lanes of each shared-memory
@@ -68,11 +69,12 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
         const int jj = (j + lane) & (HALF4 - 1);
         float4 kv = krow[jj];
         float4 qv = qrow[jj];
-        s = fmaf(qv.x, kv.x, s);
-        s = fmaf(qv.y, kv.y, s);
-        s = fmaf(qv.z, kv.z, s);
-        s = fmaf(qv.w, kv.w, s);
+        s0 = fmaf(qv.x, kv.x, s0);
+        s1 = fmaf(qv.y, kv.y, s1);
+        s2 = fmaf(qv.z, kv.z, s2);
+        s3 = fmaf(qv.w, kv.w, s3);
     }
+    float s = (s0 + s1) + (s2 + s3);
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     if (t >= n_valid) s = -INFINITY;
     float mp = s;
@@ -119,7 +121,7 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
 #define NITRO_DEC_WARPS64 8
 #endif
 #ifndef NITRO_DEC_CHUNK64
-#define NITRO_DEC_CHUNK64 8
+#define NITRO_DEC_CHUNK64 16
 #endif
 constexpr int kDecStages = NITRO_DEC_STAGES;
 
@@ -289,49 +291,14 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
 #pragma unroll
             for (int i = 0; i < DPL; i++) out[i] = st.o[i] * inv;
         } else {
+            // a split of a longer context: publish (max, sum, unnormalised output); the merge
+            // kernel that follows in the stream combines the splits
             float* po = a.part_o + (bh * a.max_splits + cur.split) * HD + lane * DPL;
 #pragma unroll
             for (int i = 0; i < DPL; i++) po[i] = st.o[i];
             if (lane == 0) {
                 a.part_ml[(bh * a.max_splits + cur.split) * 2] = st.m;
                 a.part_ml[(bh * a.max_splits + cur.split) * 2 + 1] = st.l;
-            }
-            __threadfence();
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) last = atomicAdd(a.counters + bh, 1) == cur.nsplit - 1;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                __threadfence();
-                // lanes fetch the splits' (max, sum) 32 at a time; weights broadcast by shuffle
-                float GM = -INFINITY;
-                for (int base = 0; base < cur.nsplit; base += 32)
-                    if (base + lane < cur.nsplit)
-                        GM = fmaxf(GM, __ldcg(a.part_ml + (bh * a.max_splits + base + lane) * 2));
-                GM = warp_max(GM);
-                float GL = 0.0f, GO[DPL];
-#pragma unroll
-                for (int i = 0; i < DPL; i++) GO[i] = 0.0f;
-                for (int base = 0; base < cur.nsplit; base += 32) {
-                    float ms = -INFINITY, ls = 0.0f;
-                    if (base + lane < cur.nsplit) {
-                        ms = __ldcg(a.part_ml + (bh * a.max_splits + base + lane) * 2);
-                        ls = __ldcg(a.part_ml + (bh * a.max_splits + base + lane) * 2 + 1);
-                    }
-                    const float cl = (ms == -INFINITY) ? 0.0f : exp2f(ms - GM);
-                    GL += warp_sum(ls * cl);
-                    const int cnt = min(32, cur.nsplit - base);
-                    for (int sp = 0; sp < cnt; sp++) {
-                        const float c = __shfl_sync(0xffffffffu, cl, sp);
-                        const float* ps = a.part_o + (bh * a.max_splits + base + sp) * HD + lane * DPL;
-#pragma unroll
-                        for (int i = 0; i < DPL; i++) GO[i] += __ldcg(ps + i) * c;
-                    }
-                }
-                const float inv = 1.0f / GL;
-#pragma unroll
-                for (int i = 0; i < DPL; i++) out[i] = GO[i] * inv;
-                if (lane == 0) a.counters[bh] = 0;
             }
         }
         // advance: the issue pointer moves with the item window.  It is at or past the end
@@ -353,6 +320,49 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
             a.work[1] = 0;
         }
     }
+}
+
+// Combine the splits of every (sequence, head) whose context spans more than one chunk:
+// one warp per (sequence, head), weights exp2(m_s - max) broadcast by shuffle.
+template <int HD>
+__global__ void __launch_bounds__(256) decode_merge_kernel(DecodeAttnArgs a) {
+    constexpr int DPL = HD / 32;
+    const int lane = threadIdx.x & 31;
+    const int64_t bh = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    grid_dependency_wait();
+    grid_dependents_launch();
+    if (bh >= (int64_t)a.B * a.n_heads) return;
+    const int b = (int)(bh / a.n_heads);
+    const int pages = (a.ctx_lens[b] + kPage - 1) / kPage;
+    const int nsplit = (pages + a.chunk_pages - 1) / a.chunk_pages;
+    if (nsplit <= 1) return;
+    float GM = -INFINITY;
+    for (int base = 0; base < nsplit; base += 32)
+        if (base + lane < nsplit) GM = fmaxf(GM, a.part_ml[(bh * a.max_splits + base + lane) * 2]);
+    GM = warp_max(GM);
+    float GL = 0.0f, GO[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) GO[i] = 0.0f;
+    for (int base = 0; base < nsplit; base += 32) {
+        float ms = -INFINITY, ls = 0.0f;
+        if (base + lane < nsplit) {
+            ms = a.part_ml[(bh * a.max_splits + base + lane) * 2];
+            ls = a.part_ml[(bh * a.max_splits + base + lane) * 2 + 1];
+        }
+        const float cl = (ms == -INFINITY) ? 0.0f : exp2f(ms - GM);
+        GL += warp_sum(ls * cl);
+        const int cnt = min(32, nsplit - base);
+        for (int sp = 0; sp < cnt; sp++) {
+            const float c = __shfl_sync(0xffffffffu, cl, sp);
+            const float* ps = a.part_o + (bh * a.max_splits + base + sp) * HD + lane * DPL;
+#pragma unroll
+            for (int i = 0; i < DPL; i++) GO[i] += ps[i] * c;
+        }
+    }
+    const float inv = 1.0f / GL;
+    float* out = a.out + bh * HD + lane * DPL;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) out[i] = GO[i] * inv;
 }
 
 // ------------------------------------------------------------------ prefill
@@ -491,12 +501,16 @@ void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t 
     (void)max_ctx;
     count_launch();
     const int grid = sm_count();
+    const dim3 mgrid((unsigned)(((int64_t)a.B * a.n_heads + 7) / 8));
+    count_launch();
     if (a.geom.head_dim == 64) {
         ensure_smem(decode_attn_kernel<64>, DecCfg<64>::SMEM);
         launch_ex(decode_attn_kernel<64>, dim3(grid), dim3(DecCfg<64>::WARPS * 32), DecCfg<64>::SMEM, s, 1, a);
+        launch_ex(decode_merge_kernel<64>, mgrid, dim3(256), 0, s, 1, a);
     } else {
         ensure_smem(decode_attn_kernel<128>, DecCfg<128>::SMEM);
         launch_ex(decode_attn_kernel<128>, dim3(grid), dim3(DecCfg<128>::WARPS * 32), DecCfg<128>::SMEM, s, 1, a);
+        launch_ex(decode_merge_kernel<128>, mgrid, dim3(256), 0, s, 1, a);
     }
 }
 
