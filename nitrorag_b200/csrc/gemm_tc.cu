@@ -42,7 +42,8 @@ namespace {
 
 constexpr int TC_M = 128;     // weight rows per CTA = UMMA M
 constexpr int TC_KC = 64;     // K elements per pipeline stage
-constexpr int TC_STAGES = 2;
+constexpr int TC_STAGES = 2;      // pipeline stages of the 128/256-token tiles
+constexpr int TC_MAX_STAGES = 4;  // 64-token tiles stage up to 4 chunks
 constexpr int TC_THREADS = 128;
 
 // ------------------------------------------------------------------ tcgen05 wrappers
@@ -129,11 +130,12 @@ struct TcSmem {
     static constexpr int A_BYTES = TC_M * TC_KC * 2;   // one bf16 half of the weight tile
     static constexpr int B_BYTES = NT * TC_KC * 2;     // one bf16 half of the token tile
     static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr int TOTAL = TC_STAGES * STAGE;
+    static constexpr int MAX_STAGES = NT == 64 ? TC_MAX_STAGES : TC_STAGES;
 };
 
 struct SplitArgs {
     int ksplit;  // K-range splits per tile = CTAs per thread-block cluster (grid.x)
+    int stages;  // shared-memory stages (one per chunk when a CTA's chunks all fit)
 };
 
 // Raw global loads of one K chunk for this thread: its weight row (64 values) and, for
@@ -224,11 +226,74 @@ __device__ __forceinline__ void stage_tokens(const float4* xv4, const GemmArgs& 
         split_store8(xv + 8 * j, b_hi + core_off(r, half * 4 + j), b_lo + core_off(r, half * 4 + j));
 }
 
+// Dequantise this thread's weight row of one chunk (registers -> bf16 hi/lo core rows).
+template <int NT, bool F32W>
+__device__ __forceinline__ void stage_weights(const ChunkRegs<NT, F32W>& r, const GemmArgs& a, int n, int k0,
+                                              uint8_t* a_hi, uint8_t* a_lo, int tid) {
+    float w[TC_KC];
+    if (n < a.N) {
+        if (F32W) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                w[4 * i] = r.wf[i].x; w[4 * i + 1] = r.wf[i].y; w[4 * i + 2] = r.wf[i].z; w[4 * i + 3] = r.wf[i].w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int8_t* q = reinterpret_cast<const int8_t*>(&r.wq[i]);
+                const float sc = i < 2 ? r.s0 : r.s1;
+#pragma unroll
+                for (int j = 0; j < 16; j++) w[16 * i + j] = (float)q[j] * sc;
+            }
+        }
+        if (k0 < a.kbegin) {  // faithful mode: only k >= kbegin contributes
+#pragma unroll
+            for (int i = 0; i < TC_KC; i++)
+                if (k0 + i < a.kbegin) w[i] = 0.0f;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < TC_KC; i++) w[i] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < TC_KC / 8; j++) split_store8(w + 8 * j, a_hi + core_off(tid, j), a_lo + core_off(tid, j));
+}
+
+// The activation tile of one chunk (all NT token rows) -> bf16 hi/lo core rows.
+template <int NT, bool F32W>
+__device__ __forceinline__ void stage_chunk_tokens(const GemmArgs& a, const float* inv_rms, int m_base, int k0,
+                                                   uint8_t* b_hi, uint8_t* b_lo, int tid) {
+    for (int idx = tid; idx < NT * 2; idx += TC_THREADS) {
+        const int r = idx >> 1, half = idx & 1;
+        const int m = m_base + r;
+        float4 xv4[8];
+        if (m < a.M) {
+            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++) xv4[i] = src[i];
+        }
+        stage_tokens(xv4, a, inv_rms[r], k0 + half * 32, m < a.M, b_hi, b_lo, r, half);
+    }
+}
+
+__device__ __forceinline__ void issue_chunk_mmas(uint32_t tmem, uint32_t idesc, const uint8_t* a_hi, const uint8_t* a_lo,
+                                                 const uint8_t* b_hi, const uint8_t* b_lo, bool first) {
+    const uint32_t ah = smem_addr(a_hi), al = smem_addr(a_lo), bh = smem_addr(b_hi), bl = smem_addr(b_lo);
+#pragma unroll
+    for (int kk = 0; kk < TC_KC / 16; kk++) {
+        const uint32_t o = kk * 256;  // 16 K-elements = two core matrices along K
+        umma_bf16(tmem, umma_desc(ah + o), umma_desc(bh + o), idesc, (!first || kk > 0) ? 1u : 0u);
+        umma_bf16(tmem, umma_desc(ah + o), umma_desc(bl + o), idesc, 1u);
+        umma_bf16(tmem, umma_desc(al + o), umma_desc(bh + o), idesc, 1u);
+    }
+}
+
 template <int NT, bool F32W>
 __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
     using S = TcSmem<NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ uint64_t mma_bar[TC_STAGES];
+    __shared__ uint64_t mma_bar[TC_MAX_STAGES];
+    __shared__ uint64_t done_bar;
     __shared__ uint32_t tmem_slot;
     __shared__ float inv_rms[NT];
     __shared__ unsigned long long red_key[4][NT];
@@ -243,24 +308,47 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     const int c_end = (int)((int64_t)(split + 1) * nchunk_total / sp.ksplit);
     // the reference's batched arithmetic keeps only the last 32-wide block (kbegin = K-32)
     const int c_first = max(c_begin, a.kbegin / TC_KC);
-    const int n = n_base + tid;           // this thread's weight row
-    const int my_r = tid >> 1, my_half = tid & 1;  // NT == 64: this thread's token slice
-
-    // the first chunk's weight loads go out before the set-up work and before waiting for
+    const int nch = max(0, c_end - c_first);
+    const int stages = sp.stages;
+    // every chunk of this CTA has its own stage: all weights are staged before waiting for
     // the previous kernel (weights are read-only; activations are not)
-    ChunkRegs<NT, F32W> cur;
-    if (c_first < c_end) load_chunk_w<NT, F32W>(cur, a, n, c_first * TC_KC);
+    const bool staged = nch <= stages;
+    const int n = n_base + tid;  // this thread's weight row
+    auto stage_ptr = [&](int st, int part) { return smem + st * S::STAGE + (part < 2 ? part * S::A_BYTES : 2 * S::A_BYTES + (part - 2) * S::B_BYTES); };
 
     if (warp == 0) {
         tmem_alloc(&tmem_slot, NT);
         tmem_relinquish();
     }
     if (tid == 0) {
-        for (int s = 0; s < TC_STAGES; s++) mbar_init(&mma_bar[s], 1);
+        for (int st = 0; st < TC_MAX_STAGES; st++) mbar_init(&mma_bar[st], 1);
+        mbar_init(&done_bar, 1);
         fence_barrier_init();
     }
+    ChunkRegs<NT, F32W> cur;
+    if (staged) {
+        if (!F32W && nch >= 2) {
+            // two chunks' loads in flight before converting either
+            ChunkRegs<NT, F32W> r1;
+            load_chunk_w<NT, F32W>(cur, a, n, c_first * TC_KC);
+            load_chunk_w<NT, F32W>(r1, a, n, (c_first + 1) * TC_KC);
+            stage_weights<NT, F32W>(cur, a, n, c_first * TC_KC, stage_ptr(0, 0), stage_ptr(0, 1), tid);
+            stage_weights<NT, F32W>(r1, a, n, (c_first + 1) * TC_KC, stage_ptr(1, 0), stage_ptr(1, 1), tid);
+            for (int i = 2; i < nch; i++) {
+                load_chunk_w<NT, F32W>(cur, a, n, (c_first + i) * TC_KC);
+                stage_weights<NT, F32W>(cur, a, n, (c_first + i) * TC_KC, stage_ptr(i, 0), stage_ptr(i, 1), tid);
+            }
+        } else {
+            for (int i = 0; i < nch; i++) {
+                load_chunk_w<NT, F32W>(cur, a, n, (c_first + i) * TC_KC);
+                stage_weights<NT, F32W>(cur, a, n, (c_first + i) * TC_KC, stage_ptr(i, 0), stage_ptr(i, 1), tid);
+            }
+        }
+    } else if (nch > 0) {
+        load_chunk_w<NT, F32W>(cur, a, n, c_first * TC_KC);
+    }
+
     grid_dependency_wait();
-    if (c_first < c_end) load_chunk_x<NT, F32W>(cur, a, m_base + my_r, my_half, c_first * TC_KC);
     if (a.norm_gain) {
         if (a.ss_in) {
             // sums of squares published by the producer of x, one per 128-feature slice
@@ -294,218 +382,149 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     const uint32_t tmem = tmem_slot;
     const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
 
-    int it = 0;
     bool bail = false;
-    for (int c = c_first; c < c_end; c++, it++) {
-        const int s = it % TC_STAGES;
-        const int use = it / TC_STAGES;
-        const int k0 = c * TC_KC;
-        ChunkRegs<NT, F32W> nxt;
-        if (c + 1 < c_end) load_chunk<NT, F32W>(nxt, a, n, m_base + my_r, my_half, k0 + TC_KC);
-        if (use > 0) {
-            const bool got = mbar_wait(&mma_bar[s], (use - 1) & 1, a.err);
-            if (!__syncthreads_and(got)) { bail = true; break; }
-        }
-        uint8_t* a_hi = smem + s * S::STAGE;
-        uint8_t* a_lo = a_hi + S::A_BYTES;
-        uint8_t* b_hi = a_lo + S::A_BYTES;
-        uint8_t* b_lo = b_hi + S::B_BYTES;
-        // ---- weights: thread = one row, 64 values
-        {
-            float w[TC_KC];
-            if (n < a.N) {
-                if (F32W) {
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        w[4 * i] = cur.wf[i].x; w[4 * i + 1] = cur.wf[i].y;
-                        w[4 * i + 2] = cur.wf[i].z; w[4 * i + 3] = cur.wf[i].w;
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int8_t* q = reinterpret_cast<const int8_t*>(&cur.wq[i]);
-                        const float sc = i < 2 ? cur.s0 : cur.s1;
-#pragma unroll
-                        for (int j = 0; j < 16; j++) w[16 * i + j] = (float)q[j] * sc;
-                    }
-                }
-                if (k0 < a.kbegin) {  // faithful mode: only k >= kbegin contributes
-#pragma unroll
-                    for (int i = 0; i < TC_KC; i++)
-                        if (k0 + i < a.kbegin) w[i] = 0.0f;
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < TC_KC; i++) w[i] = 0.0f;
-            }
-#pragma unroll
-            for (int j = 0; j < TC_KC / 8; j++)
-                split_store8(w + 8 * j, a_hi + core_off(tid, j), a_lo + core_off(tid, j));
-        }
-        // ---- tokens
-        if (NT == 64) {
-            const int m = m_base + my_r;
-            stage_tokens(cur.x, a, inv_rms[my_r], k0 + my_half * 32, m < a.M, b_hi, b_lo, my_r, my_half);
-        } else {
-            for (int idx = tid; idx < NT * 2; idx += TC_THREADS) {
-                const int r = idx >> 1, half = idx & 1;
-                const int m = m_base + r;
-                float4 xv4[8];
-                if (m < a.M) {
-                    const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
-#pragma unroll
-                    for (int i = 0; i < 8; i++) xv4[i] = src[i];
-                }
-                stage_tokens(xv4, a, inv_rms[r], k0 + half * 32, m < a.M, b_hi, b_lo, r, half);
-            }
-        }
+    if (staged) {
+        for (int i = 0; i < nch; i++)
+            stage_chunk_tokens<NT, F32W>(a, inv_rms, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
         fence_async_smem();
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t ah = smem_addr(a_hi), al = smem_addr(a_lo), bh = smem_addr(b_hi), bl = smem_addr(b_lo);
-#pragma unroll
-            for (int kk = 0; kk < TC_KC / 16; kk++) {
-                const uint32_t o = kk * 256;  // 16 K-elements = two core matrices along K
-                umma_bf16(tmem, umma_desc(ah + o), umma_desc(bh + o), idesc, (it > 0 || kk > 0) ? 1u : 0u);
-                umma_bf16(tmem, umma_desc(ah + o), umma_desc(bl + o), idesc, 1u);
-                umma_bf16(tmem, umma_desc(al + o), umma_desc(bh + o), idesc, 1u);
-            }
-            umma_commit(&mma_bar[s]);
+            for (int i = 0; i < nch; i++)
+                issue_chunk_mmas(tmem, idesc, stage_ptr(i, 0), stage_ptr(i, 1), stage_ptr(i, 2), stage_ptr(i, 3), i == 0);
+            umma_commit(&done_bar);
         }
-        if (c + 1 < c_end) cur = nxt;
+    } else {
+        // more chunks than stages: a ring, the next chunk's weight loads one chunk ahead
+        for (int it = 0; it < nch; it++) {
+            const int st = it % stages;
+            const int use = it / stages;
+            const int k0 = (c_first + it) * TC_KC;
+            ChunkRegs<NT, F32W> nxt;
+            if (it + 1 < nch) load_chunk_w<NT, F32W>(nxt, a, n, k0 + TC_KC);
+            if (use > 0) {
+                const bool got = mbar_wait(&mma_bar[st], (use - 1) & 1, a.err);
+                if (!__syncthreads_and(got)) { bail = true; break; }
+            }
+            stage_weights<NT, F32W>(cur, a, n, k0, stage_ptr(st, 0), stage_ptr(st, 1), tid);
+            stage_chunk_tokens<NT, F32W>(a, inv_rms, m_base, k0, stage_ptr(st, 2), stage_ptr(st, 3), tid);
+            fence_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
+                umma_commit(&mma_bar[st]);
+            }
+            if (it + 1 < nch) cur = nxt;
+        }
+        if (tid == 0 && !bail && nch > 0) umma_commit(&done_bar);  // completes after every MMA above
     }
-    // all MMAs of this CTA are complete once the last commit's phase has completed
-    if (it > 0 && !bail) {
-        const int s = (it - 1) % TC_STAGES;
-        if (!__syncthreads_and(mbar_wait(&mma_bar[s], ((it - 1) / TC_STAGES) & 1, a.err))) bail = true;
+    if (nch > 0 && !bail) {
+        if (!__syncthreads_and(mbar_wait(&done_bar, 0, a.err))) bail = true;
     }
     tc_fence_after();
     grid_dependents_launch();
-    if (bail) {  // a wait gave up (error flag set): release TMEM and leave
+    if (bail) {  // a wait gave up (error flag set): release TMEM and leave, taking the same
+                 // two cluster barriers as the normal path so the peers are not left waiting
+        if (sp.ksplit > 1) {
+            cg::this_cluster().sync();
+            cg::this_cluster().sync();
+        }
         tc_fence_before();
         __syncthreads();
         if (warp == 0) tmem_dealloc(tmem, NT);
         return;
     }
 
+    // Park the accumulator tile [NT][128] in this CTA's shared memory (the stages are free
+    // now).  With K split over a cluster, CTA r then sums token slice r over every CTA of
+    // the cluster through distributed shared memory, in rank order (deterministic).
+    float* part = reinterpret_cast<float*>(smem);
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-
-    // Epilogue over 8 token columns [c, c+8) of this thread's row n.
-    auto process8 = [&](const float* v, int c) {
+    for (int c0 = 0; c0 < NT; c0 += 16) {
+        float v[16];
+        if (nch > 0) tmem_ld16(tl + c0, v);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int m = m_base + c + j;
-            const float mine = v[j];
-            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
-            const bool ok = m < a.M && n < a.N;
-            if (e.kind == kEpiLogits) {
-                if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
-                unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-                    key = k2 > key ? k2 : key;
-                }
-                if (lane == 0) red_key[warp][c + j] = key;
-                continue;
-            }
-            if (e.kind == kEpiResidual) {
-                float xn = 0.0f;
-                if (ok) {
-                    float* dst = e.out + (int64_t)m * e.ldo + n;
-                    xn = *dst + mine;
-                    *dst = xn;
-                }
-                if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
-                    const float sq = warp_sum(xn * xn);
-                    if (lane == 0) red_ss[warp][c + j] = sq;
-                }
-                continue;
-            }
-            if (!ok) continue;
-            const bool even = (n & 1) == 0;
-            const float v0 = even ? mine : other;  // value of row n & ~1
-            const float v1 = even ? other : mine;  // value of row n | 1
-            switch (e.kind) {
-            case kEpiStore:
-                e.out[(int64_t)m * e.ldo + n] = mine;
-                break;
-            case kEpiSwiGLU:
-                if (even) {
-                    float hgate = v0 * (1.0f / (1.0f + expf(-v0)));
-                    e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * v1;
-                }
-                break;
-            case kEpiQKV: {
-                const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
-                const int pos = e.tok_pos[m];
-                const int np = n & ~1;
-                if (np < D + KV) {
-                    const int cc = np < D ? np : np - D;
-                    const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
-                    const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
-                    const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
-                    if (np < D) {
-                        e.q_out[(int64_t)m * D + n] = r;
-                    } else {
-                        const int cidx = n - D;
-                        e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
-                                (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = r;
-                    }
-                } else {
-                    const int cidx = n - D - KV;
-                    e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
-                            (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = mine;
-                }
-                break;
-            }
-            default:
-                break;
-            }
-        }
-    };
-
-    // columns this CTA finalises: all of them, or its slice of the cluster's tile
+        for (int j = 0; j < 16; j++) part[(c0 + j) * TC_M + tid] = nch > 0 ? v[j] : 0.0f;
+    }
     int col_begin = 0, col_end = NT;
-    if (sp.ksplit == 1) {
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-            float v[16];
-            if (it > 0) {
-                tmem_ld16(tl + c0, v);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; j++) v[j] = 0.0f;
-            }
-            process8(v, c0);
-            process8(v + 8, c0 + 8);
-        }
-    } else {
-        // Split-K reduction through distributed shared memory: every CTA of the cluster
-        // parks its partial tile [NT][128] in its own shared memory (the operand stages are
-        // free now), then CTA r sums column slice r over all CTAs in rank order.
+    if (sp.ksplit > 1) {
         cg::cluster_group cluster = cg::this_cluster();
-        float* part = reinterpret_cast<float*>(smem);
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-            float v[16];
-            if (it > 0) tmem_ld16(tl + c0, v);
-#pragma unroll
-            for (int j = 0; j < 16; j++) part[(c0 + j) * TC_M + tid] = (it > 0) ? v[j] : 0.0f;
-        }
         cluster.sync();
-        const int slice = NT / sp.ksplit;
-        col_begin = (int)cluster.block_rank() * slice;
-        col_end = col_begin + slice;
-        for (int c = col_begin; c < col_end; c += 8) {
-            float v[8];
+        const int rank = (int)cluster.block_rank();
+        col_begin = rank * NT / sp.ksplit;
+        col_end = (rank + 1) * NT / sp.ksplit;
+    } else {
+        __syncthreads();
+    }
+    const bool even = (n & 1) == 0;
+#pragma unroll 1
+    for (int c = col_begin; c < col_end; c++) {
+        float mine = 0.0f;
+        if (sp.ksplit > 1) {
+            cg::cluster_group cluster = cg::this_cluster();
+            for (int q = 0; q < sp.ksplit; q++) mine += cluster.map_shared_rank(part, q)[c * TC_M + tid];
+        } else {
+            mine = part[c * TC_M + tid];
+        }
+        const int m = m_base + c;
+        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
+        const bool ok = m < a.M && n < a.N;
+        if (e.kind == kEpiLogits) {
+            if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
+            unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
 #pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = 0.0f;
-            for (int q = 0; q < sp.ksplit; q++) {
-                const float* peer = cluster.map_shared_rank(part, q);
-#pragma unroll
-                for (int j = 0; j < 8; j++) v[j] += peer[(c + j) * TC_M + tid];
+            for (int o = 16; o > 0; o >>= 1) {
+                unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                key = k2 > key ? k2 : key;
             }
-            process8(v, c);
+            if (lane == 0) red_key[warp][c] = key;
+            continue;
+        }
+        if (e.kind == kEpiResidual) {
+            float xn = 0.0f;
+            if (ok) {
+                float* dst = e.out + (int64_t)m * e.ldo + n;
+                xn = *dst + mine;
+                *dst = xn;
+            }
+            if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
+                const float sq = warp_sum(xn * xn);
+                if (lane == 0) red_ss[warp][c] = sq;
+            }
+            continue;
+        }
+        if (!ok) continue;
+        const float v0 = even ? mine : other;  // value of row n & ~1
+        const float v1 = even ? other : mine;  // value of row n | 1
+        if (e.kind == kEpiStore) {
+            e.out[(int64_t)m * e.ldo + n] = mine;
+        } else if (e.kind == kEpiSwiGLU) {
+            if (even) {
+                const float hgate = v0 * (1.0f / (1.0f + expf(-v0)));
+                e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * v1;
+            }
+        } else if (e.kind == kEpiQKV) {
+            const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+            const int pos = e.tok_pos[m];
+            const int np = n & ~1;
+            if (np < D + KV) {
+                const int cc = np < D ? np : np - D;
+                const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
+                const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
+                const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
+                if (np < D) {
+                    e.q_out[(int64_t)m * D + n] = r;
+                } else {
+                    const int cidx = n - D;
+                    e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) + (int64_t)(pos & (kPage - 1)) * hd +
+                            (cidx % hd)] = r;
+                }
+            } else {
+                const int cidx = n - D - KV;
+                e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) + (int64_t)(pos & (kPage - 1)) * hd +
+                        (cidx % hd)] = mine;
+            }
         }
     }
     if (e.kind == kEpiLogits || (e.kind == kEpiResidual && e.ss_out)) {
@@ -522,8 +541,7 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                     if (best > *(volatile unsigned long long*)slot) atomicMax(slot, best);
                 }
             } else {
-                e.ss_out[(int64_t)n_tile * e.ss_ld + m] =
-                    red_ss[0][cix] + red_ss[1][cix] + red_ss[2][cix] + red_ss[3][cix];
+                e.ss_out[(int64_t)n_tile * e.ss_ld + m] = red_ss[0][cix] + red_ss[1][cix] + red_ss[2][cix] + red_ss[3][cix];
             }
         }
     }
@@ -560,13 +578,15 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
         while (ksplit < 8 && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
     SplitArgs sp;
     sp.ksplit = ksplit;
-    const int smem = TcSmem<NT>::TOTAL;
+    const int max_chunks_per_cta = (chunks + ksplit - 1) / ksplit;
+    sp.stages = std::max(TC_STAGES, std::min(TcSmem<NT>::MAX_STAGES, max_chunks_per_cta));
+    const int smem = sp.stages * TcSmem<NT>::STAGE;
     const dim3 grid(ksplit, n_tiles, m_tiles);
     if (a.wf) {
-        tc_ensure_smem(tc_gemm_kernel<NT, true>, smem);
+        tc_ensure_smem(tc_gemm_kernel<NT, true>, TcSmem<NT>::MAX_STAGES * TcSmem<NT>::STAGE);
         launch_ex(tc_gemm_kernel<NT, true>, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
     } else {
-        tc_ensure_smem(tc_gemm_kernel<NT, false>, smem);
+        tc_ensure_smem(tc_gemm_kernel<NT, false>, TcSmem<NT>::MAX_STAGES * TcSmem<NT>::STAGE);
         launch_ex(tc_gemm_kernel<NT, false>, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
     }
 }
