@@ -288,7 +288,7 @@ __device__ __forceinline__ void issue_chunk_mmas(uint32_t tmem, uint32_t idesc, 
     }
 }
 
-template <int NT, bool F32W>
+template <int NT, bool F32W, int EPI>
 __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
     using S = TcSmem<NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -355,8 +355,10 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
             for (int r = tid; r < NT; r += TC_THREADS) {
                 const int m = m_base + r;
                 float ss = 0.0f;
-                if (m < a.M)
+                if (m < a.M) {
+#pragma unroll 8
                     for (int p = 0; p < a.ss_parts; p++) ss += __ldcg(a.ss_in + (int64_t)p * a.ss_ld + m);
+                }
                 inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
             }
         } else {
@@ -458,81 +460,101 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         __syncthreads();
     }
     const bool even = (n & 1) == 0;
-#pragma unroll 1
-    for (int c = col_begin; c < col_end; c++) {
-        float mine = 0.0f;
+    for (int c0 = col_begin; c0 < col_end; c0 += 8) {
+        // the 8 columns' sums: over the cluster in rank order (all loads in flight at once)
+        float v[8];
         if (sp.ksplit > 1) {
             cg::cluster_group cluster = cg::this_cluster();
-            for (int q = 0; q < sp.ksplit; q++) mine += cluster.map_shared_rank(part, q)[c * TC_M + tid];
-        } else {
-            mine = part[c * TC_M + tid];
-        }
-        const int m = m_base + c;
-        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
-        const bool ok = m < a.M && n < a.N;
-        if (e.kind == kEpiLogits) {
-            if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
-            unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
+            float t[8][8];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-                key = k2 > key ? k2 : key;
-            }
-            if (lane == 0) red_key[warp][c] = key;
-            continue;
-        }
-        if (e.kind == kEpiResidual) {
-            float xn = 0.0f;
-            if (ok) {
-                float* dst = e.out + (int64_t)m * e.ldo + n;
-                xn = *dst + mine;
-                *dst = xn;
-            }
-            if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
-                const float sq = warp_sum(xn * xn);
-                if (lane == 0) red_ss[warp][c] = sq;
-            }
-            continue;
-        }
-        if (!ok) continue;
-        const float v0 = even ? mine : other;  // value of row n & ~1
-        const float v1 = even ? other : mine;  // value of row n | 1
-        if (e.kind == kEpiStore) {
-            e.out[(int64_t)m * e.ldo + n] = mine;
-        } else if (e.kind == kEpiSwiGLU) {
-            if (even) {
-                const float hgate = v0 * (1.0f / (1.0f + expf(-v0)));
-                e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * v1;
-            }
-        } else if (e.kind == kEpiQKV) {
-            const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
-            const int pos = e.tok_pos[m];
-            const int np = n & ~1;
-            if (np < D + KV) {
-                const int cc = np < D ? np : np - D;
-                const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
-                const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
-                const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
-                if (np < D) {
-                    e.q_out[(int64_t)m * D + n] = r;
-                } else {
-                    const int cidx = n - D;
-                    e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) + (int64_t)(pos & (kPage - 1)) * hd +
-                            (cidx % hd)] = r;
+            for (int q = 0; q < 8; q++) {
+                if (q < sp.ksplit) {
+                    const float* peer = cluster.map_shared_rank(part, q);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) t[q][j] = peer[(c0 + j) * TC_M + tid];
                 }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = t[0][j];
+#pragma unroll
+            for (int q = 1; q < 8; q++)
+                if (q < sp.ksplit)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) v[j] += t[q][j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = part[(c0 + j) * TC_M + tid];
+        }
+        // epilogue of the group; each kernel instantiation carries only its own kind
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int c = c0 + j;
+            const int m = m_base + c;
+            const float mine = v[j];
+            const bool ok = m < a.M && n < a.N;
+            if (EPI == kEpiLogits) {
+                if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
+                unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = k2 > key ? k2 : key;
+                }
+                if (lane == 0) red_key[warp][c] = key;
+            } else if (EPI == kEpiResidual) {
+                float xn = 0.0f;
+                if (ok) {
+                    float* dst = e.out + (int64_t)m * e.ldo + n;
+                    xn = *dst + mine;
+                    *dst = xn;
+                }
+                if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
+                    const float sq = warp_sum(xn * xn);
+                    if (lane == 0) red_ss[warp][c] = sq;
+                }
+            } else if (EPI == kEpiStore) {
+                if (ok) e.out[(int64_t)m * e.ldo + n] = mine;
             } else {
-                const int cidx = n - D - KV;
-                e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) + (int64_t)(pos & (kPage - 1)) * hd +
-                        (cidx % hd)] = mine;
+                const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
+                if (!ok) continue;
+                const float v0 = even ? mine : other;  // value of row n & ~1
+                const float v1 = even ? other : mine;  // value of row n | 1
+                if (EPI == kEpiSwiGLU) {
+                    if (even) {
+                        const float hgate = v0 * (1.0f / (1.0f + expf(-v0)));
+                        e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * v1;
+                    }
+                } else if (EPI == kEpiQKV) {
+                    const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+                    const int pos = e.tok_pos[m];
+                    const int np = n & ~1;
+                    if (np < D + KV) {
+                        const int cc = np < D ? np : np - D;
+                        const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
+                        const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
+                        const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
+                        if (np < D) {
+                            e.q_out[(int64_t)m * D + n] = r;
+                        } else {
+                            const int cidx = n - D;
+                            e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
+                                    (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = r;
+                        }
+                    } else {
+                        const int cidx = n - D - KV;
+                        e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
+                                (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = mine;
+                    }
+                }
             }
         }
     }
-    if (e.kind == kEpiLogits || (e.kind == kEpiResidual && e.ss_out)) {
+    if (EPI == kEpiLogits || (EPI == kEpiResidual && e.ss_out)) {
         __syncthreads();
         for (int cix = col_begin + tid; cix < col_end; cix += TC_THREADS) {
             const int m = m_base + cix;
             if (m >= a.M) continue;
-            if (e.kind == kEpiLogits) {
+            if (EPI == kEpiLogits) {
                 unsigned long long best = red_key[0][cix];
 #pragma unroll
                 for (int w = 1; w < 4; w++) best = red_key[w][cix] > best ? red_key[w][cix] : best;
@@ -582,12 +604,20 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     sp.stages = std::max(TC_STAGES, std::min(TcSmem<NT>::MAX_STAGES, max_chunks_per_cta));
     const int smem = sp.stages * TcSmem<NT>::STAGE;
     const dim3 grid(ksplit, n_tiles, m_tiles);
+    const int smem_max = TcSmem<NT>::MAX_STAGES * TcSmem<NT>::STAGE;
+    auto go = [&](auto kernel) {
+        tc_ensure_smem(kernel, smem_max);
+        launch_ex(kernel, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
+    };
     if (a.wf) {
-        tc_ensure_smem(tc_gemm_kernel<NT, true>, TcSmem<NT>::MAX_STAGES * TcSmem<NT>::STAGE);
-        launch_ex(tc_gemm_kernel<NT, true>, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
+        go(tc_gemm_kernel<NT, true, kEpiLogits>);
     } else {
-        tc_ensure_smem(tc_gemm_kernel<NT, false>, TcSmem<NT>::MAX_STAGES * TcSmem<NT>::STAGE);
-        launch_ex(tc_gemm_kernel<NT, false>, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
+        switch (e.kind) {
+        case kEpiResidual: go(tc_gemm_kernel<NT, false, kEpiResidual>); break;
+        case kEpiQKV: go(tc_gemm_kernel<NT, false, kEpiQKV>); break;
+        case kEpiSwiGLU: go(tc_gemm_kernel<NT, false, kEpiSwiGLU>); break;
+        default: go(tc_gemm_kernel<NT, false, kEpiStore>); break;
+        }
     }
 }
 
