@@ -349,6 +349,14 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     }
 
     grid_dependency_wait();
+    // 64-token tiles: the activation slices of the first two staged chunks are requested
+    // before the RMS partial sums so the two round trips overlap
+    ChunkRegs<NT, F32W> xr0, xr1;
+    const int my_r = tid >> 1, my_half = tid & 1;
+    if (NT == 64 && staged) {
+        if (nch > 0) load_chunk_x<NT, F32W>(xr0, a, m_base + my_r, my_half, c_first * TC_KC);
+        if (nch > 1) load_chunk_x<NT, F32W>(xr1, a, m_base + my_r, my_half, (c_first + 1) * TC_KC);
+    }
     if (a.norm_gain) {
         if (a.ss_in) {
             // sums of squares published by the producer of x, one per 128-feature slice
@@ -386,8 +394,16 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
 
     bool bail = false;
     if (staged) {
-        for (int i = 0; i < nch; i++)
-            stage_chunk_tokens<NT, F32W>(a, inv_rms, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
+        for (int i = 0; i < nch; i++) {
+            if (NT == 64 && i < 2) {
+                const int m = m_base + my_r;
+                stage_tokens(i == 0 ? xr0.x : xr1.x, a, inv_rms[my_r], (c_first + i) * TC_KC + my_half * 32, m < a.M,
+                             stage_ptr(i, 2), stage_ptr(i, 3), my_r, my_half);
+            } else {
+                stage_chunk_tokens<NT, F32W>(a, inv_rms, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3),
+                                             tid);
+            }
+        }
         fence_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -427,60 +443,62 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     tc_fence_after();
     grid_dependents_launch();
     if (bail) {  // a wait gave up (error flag set): release TMEM and leave, taking the same
-                 // two cluster barriers as the normal path so the peers are not left waiting
-        if (sp.ksplit > 1) {
-            cg::this_cluster().sync();
-            cg::this_cluster().sync();
-        }
+                 // cluster barrier as the normal path so the peers are not left waiting
+        if (sp.ksplit > 1) cg::this_cluster().sync();
         tc_fence_before();
         __syncthreads();
         if (warp == 0) tmem_dealloc(tmem, NT);
         return;
     }
 
-    // Park the accumulator tile [NT][128] in this CTA's shared memory (the stages are free
-    // now).  With K split over a cluster, CTA r then sums token slice r over every CTA of
-    // the cluster through distributed shared memory, in rank order (deterministic).
-    float* part = reinterpret_cast<float*>(smem);
+    // Accumulators -> shared memory.  Without a split they are parked in this CTA's free
+    // stage memory.  With K split over a cluster, token slice r of the tile belongs to the
+    // cluster's CTA r: every CTA pushes its partial of slice r straight into CTA r's receive
+    // buffer (distributed shared memory stores), one cluster barrier publishes them, and
+    // CTA r sums its slice locally in rank order (deterministic).  Nothing is read remotely,
+    // so no second barrier is needed before exit.
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    for (int c0 = 0; c0 < NT; c0 += 16) {
-        float v[16];
-        if (nch > 0) tmem_ld16(tl + c0, v);
-#pragma unroll
-        for (int j = 0; j < 16; j++) part[(c0 + j) * TC_M + tid] = nch > 0 ? v[j] : 0.0f;
-    }
+    const int ks = sp.ksplit;
     int col_begin = 0, col_end = NT;
-    if (sp.ksplit > 1) {
+    float* part = reinterpret_cast<float*>(smem);                          // ks == 1
+    float* recv = reinterpret_cast<float*>(smem + stages * S::STAGE);       // ks > 1: [ks][slice][128]
+    if (ks > 1) {
         cg::cluster_group cluster = cg::this_cluster();
-        cluster.sync();
         const int rank = (int)cluster.block_rank();
-        col_begin = rank * NT / sp.ksplit;
-        col_end = (rank + 1) * NT / sp.ksplit;
+        const int slice = NT / ks;
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+            float v[16];
+            if (nch > 0) tmem_ld16(tl + c0, v);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int c = c0 + j;
+                float* dst = cluster.map_shared_rank(recv, c / slice);
+                dst[(rank * slice + (c % slice)) * TC_M + tid] = nch > 0 ? v[j] : 0.0f;
+            }
+        }
+        cluster.sync();
+        col_begin = rank * slice;
+        col_end = col_begin + slice;
     } else {
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+            float v[16];
+            if (nch > 0) tmem_ld16(tl + c0, v);
+#pragma unroll
+            for (int j = 0; j < 16; j++) part[(c0 + j) * TC_M + tid] = nch > 0 ? v[j] : 0.0f;
+        }
         __syncthreads();
     }
     const bool even = (n & 1) == 0;
     for (int c0 = col_begin; c0 < col_end; c0 += 8) {
-        // the 8 columns' sums: over the cluster in rank order (all loads in flight at once)
         float v[8];
-        if (sp.ksplit > 1) {
-            cg::cluster_group cluster = cg::this_cluster();
-            float t[8][8];
+        if (ks > 1) {
+            const int slice = NT / ks;
+            const int l0 = c0 - col_begin;
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                if (q < sp.ksplit) {
-                    const float* peer = cluster.map_shared_rank(part, q);
+            for (int j = 0; j < 8; j++) v[j] = recv[(l0 + j) * TC_M + tid];
+            for (int q = 1; q < ks; q++)
 #pragma unroll
-                    for (int j = 0; j < 8; j++) t[q][j] = peer[(c0 + j) * TC_M + tid];
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = t[0][j];
-#pragma unroll
-            for (int q = 1; q < 8; q++)
-                if (q < sp.ksplit)
-#pragma unroll
-                    for (int j = 0; j < 8; j++) v[j] += t[q][j];
+                for (int j = 0; j < 8; j++) v[j] += recv[(q * slice + l0 + j) * TC_M + tid];
         } else {
 #pragma unroll
             for (int j = 0; j < 8; j++) v[j] = part[(c0 + j) * TC_M + tid];
@@ -567,14 +585,15 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
             }
         }
     }
-    if (sp.ksplit > 1) cg::this_cluster().sync();  // peers may still be reading this CTA's partial
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, NT);
 }
 
+// Allow the kernel the largest dynamic shared memory the device offers next to its static
+// shared memory (per kernel and device, once).
 template <class K>
-void tc_ensure_smem(K kernel, int bytes) {
+void tc_ensure_smem(K kernel) {
     static std::mutex mu;
     static std::set<std::pair<const void*, int>> done;
     int dev = 0;
@@ -582,7 +601,11 @@ void tc_ensure_smem(K kernel, int bytes) {
     std::lock_guard<std::mutex> lock(mu);
     auto key = std::make_pair((const void*)kernel, dev);
     if (done.count(key)) return;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncAttributes fa;
+    int optin = 0;
+    cudaFuncGetAttributes(&fa, kernel);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
     done.insert(key);
 }
 
@@ -596,17 +619,21 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     // The faithful path reads one chunk per row and never splits.
     int ksplit = 1;
     const int tiles = n_tiles * m_tiles;
-    if (a.kbegin == 0)
+    if (a.kbegin == 0 && NT <= 128)
         while (ksplit < 8 && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
     SplitArgs sp;
     sp.ksplit = ksplit;
     const int max_chunks_per_cta = (chunks + ksplit - 1) / ksplit;
-    sp.stages = std::max(TC_STAGES, std::min(TcSmem<NT>::MAX_STAGES, max_chunks_per_cta));
-    const int smem = sp.stages * TcSmem<NT>::STAGE;
+    // receive buffer for the split-K partials: NT x 128 fp32 next to the stages; 64-token
+    // tiles keep at most 3 stages then, to stay within 227 KB
+    const int recv_bytes = ksplit > 1 ? NT * TC_M * 4 : 0;
+    int max_st = TcSmem<NT>::MAX_STAGES;
+    while (max_st > TC_STAGES && max_st * TcSmem<NT>::STAGE + recv_bytes > 200 * 1024) max_st--;
+    sp.stages = std::max(TC_STAGES, std::min(max_st, max_chunks_per_cta));
+    const int smem = sp.stages * TcSmem<NT>::STAGE + recv_bytes;
     const dim3 grid(ksplit, n_tiles, m_tiles);
-    const int smem_max = TcSmem<NT>::MAX_STAGES * TcSmem<NT>::STAGE;
     auto go = [&](auto kernel) {
-        tc_ensure_smem(kernel, smem_max);
+        tc_ensure_smem(kernel);
         launch_ex(kernel, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
     };
     if (a.wf) {
@@ -627,8 +654,10 @@ bool tc_gemm_supported(const GemmArgs& a) { return a.K % TC_KC == 0 && a.N % 2 =
 
 void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     count_launch();
+    // 256-token tiles only when they alone fill the GPU (they never split K)
+    const int n_tiles = (a.N + TC_M - 1) / TC_M;
     if (a.M <= 64) tc_launch<64>(a, e, s);
-    else if (a.M <= 128) tc_launch<128>(a, e, s);
+    else if (a.M <= 128 || n_tiles * ((a.M + 255) / 256) < 148) tc_launch<128>(a, e, s);
     else tc_launch<256>(a, e, s);
 }
 
