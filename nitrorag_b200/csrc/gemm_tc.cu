@@ -106,6 +106,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 8 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // ------------------------------------------------------------------ operand staging
 // Split 8 fp32 values into bf16 hi/lo and store them as one 16-byte row of a core matrix.
 __device__ __forceinline__ void split_store8(const float* v, uint8_t* hi_dst, uint8_t* lo_dst) {
@@ -451,117 +462,159 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         return;
     }
 
-    // Accumulators -> shared memory.  Without a split they are parked in this CTA's free
-    // stage memory.  With K split over a cluster, token slice r of the tile belongs to the
-    // cluster's CTA r: every CTA pushes its partial of slice r straight into CTA r's receive
-    // buffer (distributed shared memory stores), one cluster barrier publishes them, and
-    // CTA r sums its slice locally in rank order (deterministic).  Nothing is read remotely,
-    // so no second barrier is needed before exit.
+    // Accumulators -> shared memory, row-major per thread ([row][column]).  Without a split
+    // they are parked in this CTA's free stage memory.  With K split over a cluster, token
+    // slice r of the tile belongs to the cluster's CTA r: every CTA pushes its partial of
+    // slice r straight into CTA r's receive buffer with 16-byte distributed-shared-memory
+    // stores, one cluster barrier publishes them, and CTA r sums its slice locally in rank
+    // order (deterministic).  Nothing is read remotely, so no second barrier is needed.
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
     const int ks = sp.ksplit;
-    int col_begin = 0, col_end = NT;
-    float* part = reinterpret_cast<float*>(smem);                          // ks == 1
-    float* recv = reinterpret_cast<float*>(smem + stages * S::STAGE);       // ks > 1: [ks][slice][128]
+    const int slice = NT / ks;  // multiple of 8
+    // row strides padded by 4 floats: the 8 threads of a 16-byte shared-memory phase then
+    // touch 8 different bank groups
+    const int pst = NT + 4, rst = slice + 4;
+    int col_begin = 0;
+    float* part = reinterpret_cast<float*>(smem);                     // ks == 1: [128][NT + 4]
+    float* recv = reinterpret_cast<float*>(smem + stages * S::STAGE);  // ks > 1: [ks][128][slice + 4]
     if (ks > 1) {
         cg::cluster_group cluster = cg::this_cluster();
         const int rank = (int)cluster.block_rank();
-        const int slice = NT / ks;
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-            float v[16];
-            if (nch > 0) tmem_ld16(tl + c0, v);
+        for (int c0 = 0; c0 < NT; c0 += 8) {
+            float v[8];
+            if (nch > 0) {
+                tmem_ld8(tl + c0, v);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int c = c0 + j;
-                float* dst = cluster.map_shared_rank(recv, c / slice);
-                dst[(rank * slice + (c % slice)) * TC_M + tid] = nch > 0 ? v[j] : 0.0f;
+                for (int j = 0; j < 8; j++) v[j] = 0.0f;
             }
+            const int q = c0 / slice;
+            float4* dst = reinterpret_cast<float4*>(cluster.map_shared_rank(recv, q) +
+                                                    ((size_t)rank * TC_M + tid) * rst + (c0 - q * slice));
+            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
         }
         cluster.sync();
         col_begin = rank * slice;
-        col_end = col_begin + slice;
     } else {
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-            float v[16];
-            if (nch > 0) tmem_ld16(tl + c0, v);
+        for (int c0 = 0; c0 < NT; c0 += 8) {
+            float v[8];
+            if (nch > 0) {
+                tmem_ld8(tl + c0, v);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 16; j++) part[(c0 + j) * TC_M + tid] = nch > 0 ? v[j] : 0.0f;
+                for (int j = 0; j < 8; j++) v[j] = 0.0f;
+            }
+            float4* dst = reinterpret_cast<float4*>(part + (size_t)tid * pst + c0);
+            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
         }
-        __syncthreads();
     }
+    const int col_end = col_begin + slice;
     const bool even = (n & 1) == 0;
     for (int c0 = col_begin; c0 < col_end; c0 += 8) {
         float v[8];
-        if (ks > 1) {
-            const int slice = NT / ks;
-            const int l0 = c0 - col_begin;
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = recv[(l0 + j) * TC_M + tid];
-            for (int q = 1; q < ks; q++)
-#pragma unroll
-                for (int j = 0; j < 8; j++) v[j] += recv[(q * slice + l0 + j) * TC_M + tid];
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = part[(c0 + j) * TC_M + tid];
+        {
+            const float* src = ks > 1 ? recv + (size_t)tid * rst + (c0 - col_begin) : part + (size_t)tid * pst + c0;
+            const float4 a4 = reinterpret_cast<const float4*>(src)[0], b4 = reinterpret_cast<const float4*>(src)[1];
+            v[0] = a4.x; v[1] = a4.y; v[2] = a4.z; v[3] = a4.w; v[4] = b4.x; v[5] = b4.y; v[6] = b4.z; v[7] = b4.w;
+            for (int q = 1; q < ks; q++) {
+                const float4* r4 = reinterpret_cast<const float4*>(src + (size_t)q * TC_M * rst);
+                const float4 c4 = r4[0], d4 = r4[1];
+                v[0] += c4.x; v[1] += c4.y; v[2] += c4.z; v[3] += c4.w;
+                v[4] += d4.x; v[5] += d4.y; v[6] += d4.z; v[7] += d4.w;
+            }
         }
-        // epilogue of the group; each kernel instantiation carries only its own kind
+        // Epilogue of the group.  Every global load of the 8 columns is issued before any
+        // store (the outputs may alias as far as the compiler knows).
+        if (EPI == kEpiLogits) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int c = c0 + j;
-            const int m = m_base + c;
-            const float mine = v[j];
-            const bool ok = m < a.M && n < a.N;
-            if (EPI == kEpiLogits) {
-                if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = mine;
-                unsigned long long key = (ok && mine > 0.0f) ? argmax_key(mine, n) : 0ull;
+            for (int j = 0; j < 8; j++) {
+                const int c = c0 + j, m = m_base + c;
+                const bool ok = m < a.M && n < a.N;
+                if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = v[j];
+                unsigned long long key = (ok && v[j] > 0.0f) ? argmax_key(v[j], n) : 0ull;
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
                     unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
                     key = k2 > key ? k2 : key;
                 }
                 if (lane == 0) red_key[warp][c] = key;
-            } else if (EPI == kEpiResidual) {
-                float xn = 0.0f;
-                if (ok) {
-                    float* dst = e.out + (int64_t)m * e.ldo + n;
-                    xn = *dst + mine;
-                    *dst = xn;
-                }
+            }
+        } else if (EPI == kEpiResidual) {
+            float xo[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int m = m_base + c0 + j;
+                xo[j] = (m < a.M && n < a.N) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int c = c0 + j, m = m_base + c;
+                const bool ok = m < a.M && n < a.N;
+                const float xn = ok ? xo[j] + v[j] : 0.0f;
+                if (ok) e.out[(int64_t)m * e.ldo + n] = xn;
                 if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
                     const float sq = warp_sum(xn * xn);
                     if (lane == 0) red_ss[warp][c] = sq;
                 }
-            } else if (EPI == kEpiStore) {
-                if (ok) e.out[(int64_t)m * e.ldo + n] = mine;
-            } else {
-                const float other = __shfl_xor_sync(0xffffffffu, mine, 1);  // the pair partner's row
-                if (!ok) continue;
-                const float v0 = even ? mine : other;  // value of row n & ~1
-                const float v1 = even ? other : mine;  // value of row n | 1
-                if (EPI == kEpiSwiGLU) {
-                    if (even) {
-                        const float hgate = v0 * (1.0f / (1.0f + expf(-v0)));
-                        e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * v1;
+            }
+        } else if (EPI == kEpiStore) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int m = m_base + c0 + j;
+                if (m < a.M && n < a.N) e.out[(int64_t)m * e.ldo + n] = v[j];
+            }
+        } else {
+            float other[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) other[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);  // pair partner's row
+            if (EPI == kEpiSwiGLU) {
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int m = m_base + c0 + j;
+                    if (even && m < a.M && n < a.N) {
+                        const float g = v[j];
+                        const float hgate = g * (1.0f / (1.0f + expf(-g)));
+                        e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * other[j];
                     }
-                } else if (EPI == kEpiQKV) {
-                    const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
-                    const int pos = e.tok_pos[m];
-                    const int np = n & ~1;
-                    if (np < D + KV) {
-                        const int cc = np < D ? np : np - D;
-                        const int fi = pos * (hd >> 1) + ((cc % hd) >> 1);
-                        const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
-                        const float r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
-                        if (np < D) {
-                            e.q_out[(int64_t)m * D + n] = r;
-                        } else {
-                            const int cidx = n - D;
-                            e.kpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
-                                    (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = r;
-                        }
+                }
+            } else if (EPI == kEpiQKV) {
+                const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+                const int np = n & ~1;
+                const bool rope = np < D + KV;
+                const int cc = np < D ? np : (np < D + KV ? np - D : np - D - KV);
+                int pos[8], page[8];
+                float fcr[8], fci[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int m = min(m_base + c0 + j, a.M - 1);
+                    pos[j] = e.tok_pos[m];
+                    page[j] = e.tok_page[m];
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    fcr[j] = 1.0f; fci[j] = 0.0f;
+                    if (rope) {
+                        const int fi = pos[j] * (hd >> 1) + ((cc % hd) >> 1);
+                        fcr[j] = e.freq_re[fi];
+                        fci[j] = e.freq_im[fi];
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int m = m_base + c0 + j;
+                    if (m >= a.M || n >= a.N) continue;
+                    const float v0 = even ? v[j] : other[j];  // value of row n & ~1
+                    const float v1 = even ? other[j] : v[j];  // value of row n | 1
+                    const float r = rope ? (even ? (v0 * fcr[j] - v1 * fci[j]) : (v0 * fci[j] + v1 * fcr[j])) : v[j];
+                    if (np < D) {
+                        e.q_out[(int64_t)m * D + n] = r;
                     } else {
-                        const int cidx = n - D - KV;
-                        e.vpool[e.geom.tile_offset(e.tok_page[m], e.layer, cidx / hd) +
-                                (int64_t)(pos & (kPage - 1)) * hd + (cidx % hd)] = mine;
+                        const int cidx = np < D + KV ? n - D : n - D - KV;
+                        float* pool = np < D + KV ? e.kpool : e.vpool;
+                        pool[e.geom.tile_offset(page[j], e.layer, cidx / hd) + (int64_t)(pos[j] & (kPage - 1)) * hd +
+                             (cidx % hd)] = r;
                     }
                 }
             }
@@ -626,7 +679,7 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     const int max_chunks_per_cta = (chunks + ksplit - 1) / ksplit;
     // receive buffer for the split-K partials: NT x 128 fp32 next to the stages; 64-token
     // tiles keep at most 3 stages then, to stay within 227 KB
-    const int recv_bytes = ksplit > 1 ? NT * TC_M * 4 : 0;
+    const int recv_bytes = ksplit > 1 ? (NT + 4 * ksplit) * TC_M * 4 : 0;
     int max_st = TcSmem<NT>::MAX_STAGES;
     while (max_st > TC_STAGES && max_st * TcSmem<NT>::STAGE + recv_bytes > 200 * 1024) max_st--;
     sp.stages = std::max(TC_STAGES, std::min(max_st, max_chunks_per_cta));
