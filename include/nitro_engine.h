@@ -227,6 +227,22 @@ int nr_paged_attention_decode(const float* q, const float* kpool, const float* v
                               int32_t n_layers, int32_t layer, float* out, void* workspace,
                               int32_t* error_flag, void* stream);
 
+/* nr_paged_attention_decode without a workspace argument, for callers that may not
+ * allocate device memory while stepping (their pool already holds all of HBM, or
+ * cudaMalloc's device-wide synchronisation would stall their other streams).  No
+ * counterpart in the reference.  The scratch is one fixed array of
+ * NR_ATTN_STATIC_SCRATCH_BYTES in the library's device image, shared by every call on a
+ * device: calls needing nr_paged_attention_workspace_size() above that return
+ * NR_ERR_CAPACITY; the call clears the counters it needs, and two calls that overlap on
+ * the device race on the array.  The first call on each device resolves the array's
+ * address and sets kernel attributes: make it before any stream capture. */
+#define NR_ATTN_STATIC_SCRATCH_BYTES ((size_t)8 << 20)
+int nr_paged_attention_decode_static(const float* q, const float* kpool, const float* vpool,
+                                     const int32_t* block_tables, int32_t max_pages, const int32_t* ctx_lens,
+                                     int32_t B, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                     int32_t n_layers, int32_t layer, float* out, int32_t* error_flag,
+                                     void* stream);
+
 /* Q8_0 matrix product out[m][n] = sum_k x[m][k] * q[n][k] * scale[n][k/32] (src/model_q8.cpp
  * :92-125 / :382-420).  q: device int8 [N][K]; scales: device fp32 [N][K/32]; x: [M][K];
  * out: [M][N].  q8_mode as NR_Q8_*.  M <= 8 runs on CUDA cores; wider M on the tensor

@@ -108,6 +108,7 @@ SIGNATURES = {
     "nr_replay_decode": (C.c_int, [P, I32]),
     "nr_paged_attention_workspace_size": (C.c_size_t, [I32, I32, I32, I32]),
     "nr_paged_attention_decode": (C.c_int, [P, P, P, P, I32, P, I32, I32, I32, I32, I32, I32, P, P, P, P]),
+    "nr_paged_attention_decode_static": (C.c_int, [P, P, P, P, I32, P, I32, I32, I32, I32, I32, I32, P, P, P]),
     "nr_q8_matmul": (C.c_int, [P, P, P, P, I32, I32, I32, I32, P]),
 }
 

@@ -529,3 +529,73 @@ void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
 }
 
 }  // namespace nitro
+
+// ---------------------------------------------------------------------------------------
+// Decode attention with library-owned scratch (nr_paged_attention_decode_static).
+//
+// Some callers may not allocate device memory at all while they step: a server that handed
+// all of HBM to its own KV page pool at start-up has nothing left for a cudaMalloc, and
+// cudaMalloc/cudaFree synchronise the device, which a step loop that keeps several
+// streams busy cannot afford.  This entry point runs the same two kernels as
+// nr_paged_attention_decode with their split partials and work counters in one fixed
+// array that is part of the library's device image, so the call itself allocates nothing.
+//
+// The array is shared by every call on a device and keeps whatever the last call left in
+// it: the work counters are cleared on the stream before each launch, the partials are
+// always written before they are read.  Two calls whose kernels overlap (different
+// streams, or different host threads on one stream without ordering) race on it.
+// The first call on each device resolves the array's address (cudaGetSymbolAddress, which
+// may load the module) and sets the kernels' shared-memory limits; make that first call
+// outside any stream capture.
+namespace nitro {
+
+static constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+
+static int static_scratch(void** out) {
+    static std::mutex mu;
+    static void* ptrs[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p) return -1;
+        ptrs[dev] = p;
+    }
+    *out = ptrs[dev];
+    return 0;
+}
+
+}  // namespace nitro
+
+#include "../../include/nitro_engine.h"
+
+static_assert(nitro::kStaticScratchBytes == NR_ATTN_STATIC_SCRATCH_BYTES, "scratch size and header disagree");
+
+extern "C" int nr_paged_attention_decode_static(const float* q, const float* kpool, const float* vpool,
+                                                const int32_t* block_tables, int32_t max_pages,
+                                                const int32_t* ctx_lens, int32_t B, int32_t n_heads,
+                                                int32_t n_kv_heads, int32_t head_dim, int32_t n_layers,
+                                                int32_t layer, float* out, int32_t* error_flag, void* stream) {
+    if (!q || !kpool || !vpool || !block_tables || !ctx_lens || !out) return NR_ERR_INVALID;
+    if (B <= 0 || B > 1024 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || max_pages <= 0)
+        return NR_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128) return NR_ERR_INVALID;
+    if (n_layers <= 0 || layer < 0 || layer >= n_layers) return NR_ERR_INVALID;
+    if (nitro::decode_attn_workspace_bytes(B, n_heads, head_dim, max_pages) > nitro::kStaticScratchBytes)
+        return NR_ERR_CAPACITY;
+    void* ws = nullptr;
+    if (nitro::static_scratch(&ws) != 0) return NR_ERR_CUDA;
+    nitro::DecodeAttnArgs a;
+    a.q = q; a.kpool = kpool; a.vpool = vpool;
+    a.geom = nitro::PoolGeom{n_layers, n_kv_heads, head_dim};
+    a.layer = layer; a.block_tables = block_tables; a.max_pages = max_pages; a.ctx_lens = ctx_lens;
+    a.B = B; a.n_heads = n_heads; a.out = out; a.err = error_flag;
+    nitro::decode_attn_bind_workspace(a, ws, max_pages);
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t counter_bytes = ((size_t)B * n_heads + 2) * sizeof(int);
+    if (cudaMemsetAsync(a.counters, 0, counter_bytes, s) != cudaSuccess) return NR_ERR_CUDA;
+    nitro::launch_decode_attention(a, max_pages * nitro::kPage, s);
+    return cudaGetLastError() == cudaSuccess ? NR_OK : NR_ERR_CUDA;
+}
