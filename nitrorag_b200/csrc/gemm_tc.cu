@@ -25,8 +25,10 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <set>
+#include <tuple>
 #include <utility>
 
 #include <cooperative_groups.h>
@@ -116,6 +118,11 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
 }
+
+// Split cluster barrier: arrive (publishing this thread's earlier memory operations) and,
+// later, wait for every thread of the cluster to have arrived.
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------------ operand staging
 // Split 8 fp32 values into bf16 hi/lo and store them as one 16-byte row of a core matrix.
@@ -453,9 +460,17 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     }
     tc_fence_after();
     grid_dependents_launch();
+    // With K split over a cluster the partials are pushed into the peers' stage memory, which
+    // is free only once the peer's own MMAs have read it: every CTA announces that here
+    // (arrive) and waits for all peers just before pushing, so the wait mostly overlaps
+    // the accumulator loads.
+    if (sp.ksplit > 1) cluster_arrive_release();
     if (bail) {  // a wait gave up (error flag set): release TMEM and leave, taking the same
-                 // cluster barrier as the normal path so the peers are not left waiting
-        if (sp.ksplit > 1) cg::this_cluster().sync();
+                 // cluster barriers as the normal path so the peers are not left waiting
+        if (sp.ksplit > 1) {
+            cluster_wait_acquire();
+            cg::this_cluster().sync();
+        }
         tc_fence_before();
         __syncthreads();
         if (warp == 0) tmem_dealloc(tmem, NT);
@@ -475,8 +490,8 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     // touch 8 different bank groups
     const int pst = NT + 4, rst = slice + 4;
     int col_begin = 0;
-    float* part = reinterpret_cast<float*>(smem);                     // ks == 1: [128][NT + 4]
-    float* recv = reinterpret_cast<float*>(smem + stages * S::STAGE);  // ks > 1: [ks][128][slice + 4]
+    float* part = reinterpret_cast<float*>(smem);  // ks == 1: [128][NT + 4]
+    float* recv = reinterpret_cast<float*>(smem);  // ks > 1: [ks][128][slice + 4]
     if (ks > 1) {
         cg::cluster_group cluster = cg::this_cluster();
         const int rank = (int)cluster.block_rank();
@@ -488,6 +503,7 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
 #pragma unroll
                 for (int j = 0; j < 8; j++) v[j] = 0.0f;
             }
+            if (c0 == 0) cluster_wait_acquire();  // every peer's MMAs are done with its stages
             const int q = c0 / slice;
             float4* dst = reinterpret_cast<float4*>(cluster.map_shared_rank(recv, q) +
                                                     ((size_t)rank * TC_M + tid) * rst + (c0 - q * slice));
@@ -662,43 +678,82 @@ void tc_ensure_smem(K kernel) {
     done.insert(key);
 }
 
+using TcKernel = void (*)(GemmArgs, Epilogue, SplitArgs);
+
+// Clusters of `ks` CTAs with `smem` bytes each that fit on the device at once (cached per
+// device; a failed query reports "no limit").
+int tc_max_clusters(TcKernel kernel, int ks, int smem, int n_tiles, int m_tiles) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto key = std::make_tuple((const void*)kernel, ks, smem, dev);
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ks, n_tiles, m_tiles);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = ks;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = 1 << 30;
+    }
+    cache[key] = n;
+    return n;
+}
+
 template <int NT>
 void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     const int n_tiles = (a.N + TC_M - 1) / TC_M;
     const int m_tiles = (a.M + NT - 1) / NT;
     const int chunks = a.K / TC_KC;
+    TcKernel kernel;
+    if (a.wf) {
+        kernel = tc_gemm_kernel<NT, true, kEpiLogits>;
+    } else {
+        switch (e.kind) {
+        case kEpiResidual: kernel = tc_gemm_kernel<NT, false, kEpiResidual>; break;
+        case kEpiQKV: kernel = tc_gemm_kernel<NT, false, kEpiQKV>; break;
+        case kEpiSwiGLU: kernel = tc_gemm_kernel<NT, false, kEpiSwiGLU>; break;
+        default: kernel = tc_gemm_kernel<NT, false, kEpiStore>; break;
+        }
+    }
+    tc_ensure_smem(kernel);
+    // Stages and shared memory for a split: a stage per chunk up to the limit; the
+    // accumulators are later parked (ks == 1) or received (ks > 1) in the stage memory.
+    auto plan = [&](int ks, SplitArgs* sp) {
+        const int per_cta = (chunks + ks - 1) / ks;
+        int max_st = TcSmem<NT>::MAX_STAGES;
+        while (max_st > TC_STAGES && max_st * TcSmem<NT>::STAGE > 200 * 1024) max_st--;
+        sp->ksplit = ks;
+        sp->stages = std::max(TC_STAGES, std::min(max_st, per_cta));
+        const int park = (NT + 4 * ks) * TC_M * 4;
+        return std::max(sp->stages * TcSmem<NT>::STAGE, park);
+    };
     // Fill the GPU: when the tiles alone are fewer than the SMs, split K across the CTAs
-    // of a cluster (power of two up to 8, at most one split per chunk, NT/ksplit >= 8).
-    // The faithful path reads one chunk per row and never splits.
+    // of a cluster (power of two up to 8, at most one split per chunk, NT/ksplit >= 8), but
+    // only as far as every cluster of the launch can be resident at once.  The faithful
+    // path reads one chunk per row and never splits.
     int ksplit = 1;
     const int tiles = n_tiles * m_tiles;
     if (a.kbegin == 0 && NT <= 128)
         while (ksplit < 8 && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
     SplitArgs sp;
-    sp.ksplit = ksplit;
-    const int max_chunks_per_cta = (chunks + ksplit - 1) / ksplit;
-    // receive buffer for the split-K partials: NT x 128 fp32 next to the stages; 64-token
-    // tiles keep at most 3 stages then, to stay within 227 KB
-    const int recv_bytes = ksplit > 1 ? (NT + 4 * ksplit) * TC_M * 4 : 0;
-    int max_st = TcSmem<NT>::MAX_STAGES;
-    while (max_st > TC_STAGES && max_st * TcSmem<NT>::STAGE + recv_bytes > 200 * 1024) max_st--;
-    sp.stages = std::max(TC_STAGES, std::min(max_st, max_chunks_per_cta));
-    const int smem = sp.stages * TcSmem<NT>::STAGE + recv_bytes;
-    const dim3 grid(ksplit, n_tiles, m_tiles);
-    auto go = [&](auto kernel) {
-        tc_ensure_smem(kernel);
-        launch_ex(kernel, grid, dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
-    };
-    if (a.wf) {
-        go(tc_gemm_kernel<NT, true, kEpiLogits>);
-    } else {
-        switch (e.kind) {
-        case kEpiResidual: go(tc_gemm_kernel<NT, false, kEpiResidual>); break;
-        case kEpiQKV: go(tc_gemm_kernel<NT, false, kEpiQKV>); break;
-        case kEpiSwiGLU: go(tc_gemm_kernel<NT, false, kEpiSwiGLU>); break;
-        default: go(tc_gemm_kernel<NT, false, kEpiStore>); break;
-        }
+    int smem = plan(ksplit, &sp);
+    while (ksplit > 1 && tc_max_clusters(kernel, ksplit, smem, n_tiles, m_tiles) < tiles) {
+        ksplit /= 2;
+        smem = plan(ksplit, &sp);
     }
+    launch_ex(kernel, dim3(ksplit, n_tiles, m_tiles), dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
 }
 
 }  // namespace
