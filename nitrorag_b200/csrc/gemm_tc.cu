@@ -12,15 +12,17 @@
 // hi*hi + hi*lo + lo*hi by three MMAs into the same fp32 accumulator; the dropped lo*lo
 // term and the split residues are ~2^-17 relative, far inside the 1e-3 / 1e-4 logits bar.
 //
-// Pipeline per CTA (128 threads): for each 64-wide K chunk, every thread dequantises one
-// weight row (16-byte int8 loads, w = q * scale) and part of the activation tile (the
-// RMSNorm of the row applied on the fly) into the UMMA canonical K-major layout in shared
-// memory; thread 0 issues 4 x 3 MMAs and commits them to the stage's mbarrier, and the
-// next chunk is converted while those run (2 stages); each chunk's global loads are issued
-// one chunk ahead.  When the weight tiles are too few to fill the GPU, the K range of a
-// tile is split over the CTAs of a thread-block cluster; each parks its fp32 partial tile
-// in its own shared memory and CTA r sums token slice r over the cluster through
-// distributed shared memory in rank order (deterministic), then runs the epilogue.
+// Pipeline per CTA (256 threads, two warpgroups): every thread dequantises half a weight
+// row of each 64-wide K chunk (one Q8_0 block, w = q * scale) and a quarter-chunk slice of
+// one token's activations (the RMSNorm of the row applied on the fly) into the UMMA
+// canonical K-major layout in shared memory; thread 0 issues 4 x 3 MMAs per chunk.  When a
+// CTA's chunks all fit in shared memory (the decode shapes), its weights are staged before
+// the grid-dependency wait, i.e. while the previous kernel still runs, and only the
+// activations wait; otherwise chunks go through a 2-stage ring with the next chunk's loads
+// issued one ahead.  When the weight tiles are too few to fill the GPU, the K range of a
+// tile is split over the CTAs of a thread-block cluster; token slice r of the tile is
+// summed by CTA r from partials its peers push into its shared memory (deterministic rank
+// order), then the epilogue runs.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -46,7 +48,7 @@ constexpr int TC_M = 128;     // weight rows per CTA = UMMA M
 constexpr int TC_KC = 64;     // K elements per pipeline stage
 constexpr int TC_STAGES = 2;      // pipeline stages of the 128/256-token tiles
 constexpr int TC_MAX_STAGES = 4;  // 64-token tiles stage up to 4 chunks
-constexpr int TC_THREADS = 128;
+constexpr int TC_THREADS = 256;  // two warpgroups
 
 // ------------------------------------------------------------------ tcgen05 wrappers
 // Shared-memory matrix descriptor, K-major without swizzle: core matrices of 8 rows x 16 B
@@ -95,17 +97,15 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 16 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
+// 4 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 4; i++) v[i] = __uint_as_float(r[i]);
 }
 
 // 8 consecutive fp32 columns of this thread's TMEM lane.
@@ -154,143 +154,108 @@ struct TcSmem {
 struct SplitArgs {
     int ksplit;  // K-range splits per tile = CTAs per thread-block cluster (grid.x)
     int stages;  // shared-memory stages (one per chunk when a CTA's chunks all fit)
+    int gain_off;  // byte offset of the staged RMSNorm gain slice in dynamic shared memory
 };
 
-// Raw global loads of one K chunk for this thread: its weight row (64 values) and, for
-// NT == 64, its (token, half-chunk) slice of the activations.  Issued one chunk ahead of
-// the conversion so their latency overlaps the previous chunk's work.
-template <int NT, bool F32W>
-struct ChunkRegs {
-    int4 wq[F32W ? 1 : 4];
-    float4 wf[F32W ? 16 : 1];
-    float s0, s1;
-    float4 x[NT == 64 ? 8 : 1];
+// Thread roles.  Thread t owns weight row (t & 127) of the tile, which is also its TMEM
+// lane, and K half (t >> 7) of every chunk (32 values = one Q8_0 block).  Activation units
+// are (token, 16-wide K quarter) pairs.  In the epilogue warpgroup g (= t >> 7) takes the
+// g-th half of the columns this CTA finishes.
+
+// Raw global loads of this thread's share of one chunk's weights (issued ahead of the
+// conversion so their latency overlaps other work).
+template <bool F32W>
+struct WRegs {
+    int4 q[F32W ? 1 : 2];
+    float4 f[F32W ? 8 : 1];
+    float s;
 };
 
-template <int NT, bool F32W>
-__device__ __forceinline__ void load_chunk_w(ChunkRegs<NT, F32W>& r, const GemmArgs& a, int n, int k0) {
+template <bool F32W>
+__device__ __forceinline__ void load_w(WRegs<F32W>& r, const GemmArgs& a, int n, int k) {
     if (n < a.N) {
         if (F32W) {
-            const float4* src = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k0);
+            const float4* src = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k);
 #pragma unroll
-            for (int i = 0; i < 16; i++) r.wf[i] = __ldg(src + i);
+            for (int i = 0; i < 8; i++) r.f[i] = __ldg(src + i);
         } else {
-            const int4* src = reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k0);
-#pragma unroll
-            for (int i = 0; i < 4; i++) r.wq[i] = __ldg(src + i);
-            r.s0 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5));
-            r.s1 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5) + 1);
+            const int4* src = reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k);
+            r.q[0] = __ldg(src);
+            r.q[1] = __ldg(src + 1);
+            r.s = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k >> 5));
         }
     }
 }
 
-template <int NT, bool F32W>
-__device__ __forceinline__ void load_chunk_x(ChunkRegs<NT, F32W>& r, const GemmArgs& a, int m, int half, int k0) {
-    if (NT == 64 && m < a.M) {
-        const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
-#pragma unroll
-        for (int i = 0; i < 8; i++) r.x[i] = src[i];
-    }
-}
-
-template <int NT, bool F32W>
-__device__ __forceinline__ void load_chunk(ChunkRegs<NT, F32W>& r, const GemmArgs& a, int n, int m, int half, int k0) {
+// This thread's 32 weights of one chunk (registers -> bf16 hi/lo core rows).
+template <bool F32W>
+__device__ __forceinline__ void stage_w(const WRegs<F32W>& r, const GemmArgs& a, int n, int k, uint8_t* a_hi,
+                                        uint8_t* a_lo, int row, int half) {
+    float w[32];
     if (n < a.N) {
         if (F32W) {
-            const float4* src = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k0);
-#pragma unroll
-            for (int i = 0; i < 16; i++) r.wf[i] = __ldg(src + i);
-        } else {
-            const int4* src = reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k0);
-#pragma unroll
-            for (int i = 0; i < 4; i++) r.wq[i] = __ldg(src + i);
-            r.s0 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5));
-            r.s1 = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k0 >> 5) + 1);
-        }
-    }
-    if (NT == 64 && m < a.M) {
-        const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
-#pragma unroll
-        for (int i = 0; i < 8; i++) r.x[i] = src[i];
-    }
-}
-
-// Activation slice (token m, 32 values at k) -> normalised fp32 -> bf16 hi/lo core rows.
-__device__ __forceinline__ void stage_tokens(const float4* xv4, const GemmArgs& a, float inv, int k, bool valid,
-                                             uint8_t* b_hi, uint8_t* b_lo, int r, int half) {
-    float xv[32];
-    if (valid) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            xv[4 * i] = xv4[i].x; xv[4 * i + 1] = xv4[i].y; xv[4 * i + 2] = xv4[i].z; xv[4 * i + 3] = xv4[i].w;
-        }
-        if (a.norm_gain) {
-            const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k);
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                float4 g = __ldg(g4 + i);
-                xv[4 * i] = g.x * (inv * xv[4 * i]);
-                xv[4 * i + 1] = g.y * (inv * xv[4 * i + 1]);
-                xv[4 * i + 2] = g.z * (inv * xv[4 * i + 2]);
-                xv[4 * i + 3] = g.w * (inv * xv[4 * i + 3]);
-            }
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; i++) xv[i] = 0.0f;
-    }
-#pragma unroll
-    for (int j = 0; j < 4; j++)
-        split_store8(xv + 8 * j, b_hi + core_off(r, half * 4 + j), b_lo + core_off(r, half * 4 + j));
-}
-
-// Dequantise this thread's weight row of one chunk (registers -> bf16 hi/lo core rows).
-template <int NT, bool F32W>
-__device__ __forceinline__ void stage_weights(const ChunkRegs<NT, F32W>& r, const GemmArgs& a, int n, int k0,
-                                              uint8_t* a_hi, uint8_t* a_lo, int tid) {
-    float w[TC_KC];
-    if (n < a.N) {
-        if (F32W) {
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                w[4 * i] = r.wf[i].x; w[4 * i + 1] = r.wf[i].y; w[4 * i + 2] = r.wf[i].z; w[4 * i + 3] = r.wf[i].w;
+                w[4 * i] = r.f[i].x; w[4 * i + 1] = r.f[i].y; w[4 * i + 2] = r.f[i].z; w[4 * i + 3] = r.f[i].w;
             }
         } else {
+            const int8_t* q = reinterpret_cast<const int8_t*>(r.q);
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int8_t* q = reinterpret_cast<const int8_t*>(&r.wq[i]);
-                const float sc = i < 2 ? r.s0 : r.s1;
-#pragma unroll
-                for (int j = 0; j < 16; j++) w[16 * i + j] = (float)q[j] * sc;
-            }
+            for (int j = 0; j < 32; j++) w[j] = (float)q[j] * r.s;
         }
-        if (k0 < a.kbegin) {  // faithful mode: only k >= kbegin contributes
+        if (k < a.kbegin) {  // faithful mode: only k >= kbegin contributes
 #pragma unroll
-            for (int i = 0; i < TC_KC; i++)
-                if (k0 + i < a.kbegin) w[i] = 0.0f;
+            for (int j = 0; j < 32; j++)
+                if (k + j < a.kbegin) w[j] = 0.0f;
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < TC_KC; i++) w[i] = 0.0f;
+        for (int j = 0; j < 32; j++) w[j] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < TC_KC / 8; j++) split_store8(w + 8 * j, a_hi + core_off(tid, j), a_lo + core_off(tid, j));
+    for (int j = 0; j < 4; j++) split_store8(w + 8 * j, a_hi + core_off(row, half * 4 + j), a_lo + core_off(row, half * 4 + j));
 }
 
-// The activation tile of one chunk (all NT token rows) -> bf16 hi/lo core rows.
-template <int NT, bool F32W>
-__device__ __forceinline__ void stage_chunk_tokens(const GemmArgs& a, const float* inv_rms, int m_base, int k0,
-                                                   uint8_t* b_hi, uint8_t* b_lo, int tid) {
-    for (int idx = tid; idx < NT * 2; idx += TC_THREADS) {
-        const int r = idx >> 1, half = idx & 1;
-        const int m = m_base + r;
-        float4 xv4[8];
-        if (m < a.M) {
-            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + half * 32);
+// 16 activations of token row r (K quarter kq of a chunk) -> normalised -> bf16 hi/lo.
+__device__ __forceinline__ void stage_x16(const float4* x4, const float* g, float inv, bool valid, uint8_t* b_hi,
+                                          uint8_t* b_lo, int r, int kq) {
+    float xv[16];
+    if (valid) {
 #pragma unroll
-            for (int i = 0; i < 8; i++) xv4[i] = src[i];
+        for (int i = 0; i < 4; i++) {
+            xv[4 * i] = x4[i].x; xv[4 * i + 1] = x4[i].y; xv[4 * i + 2] = x4[i].z; xv[4 * i + 3] = x4[i].w;
         }
-        stage_tokens(xv4, a, inv_rms[r], k0 + half * 32, m < a.M, b_hi, b_lo, r, half);
+        if (g) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float4 g4 = reinterpret_cast<const float4*>(g)[i];
+                xv[4 * i] = g4.x * (inv * xv[4 * i]);
+                xv[4 * i + 1] = g4.y * (inv * xv[4 * i + 1]);
+                xv[4 * i + 2] = g4.z * (inv * xv[4 * i + 2]);
+                xv[4 * i + 3] = g4.w * (inv * xv[4 * i + 3]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) xv[i] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++) split_store8(xv + 8 * j, b_hi + core_off(r, kq * 2 + j), b_lo + core_off(r, kq * 2 + j));
+}
+
+// The activation tile of one chunk (all NT token rows), loaded and staged by unit.
+template <int NT>
+__device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* inv_rms, const float* g, int m_base,
+                                              int k0, uint8_t* b_hi, uint8_t* b_lo, int tid) {
+    for (int u = tid; u < NT * 4; u += TC_THREADS) {
+        const int r = u >> 2, kq = u & 3, m = m_base + r;
+        float4 x4[4];
+        if (m < a.M) {
+            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k0 + kq * 16);
+#pragma unroll
+            for (int i = 0; i < 4; i++) x4[i] = src[i];
+        }
+        stage_x16(x4, g ? g + kq * 16 : nullptr, inv_rms[r], m < a.M, b_hi, b_lo, r, kq);
     }
 }
 
@@ -307,7 +272,7 @@ __device__ __forceinline__ void issue_chunk_mmas(uint32_t tmem, uint32_t idesc, 
 }
 
 template <int NT, bool F32W, int EPI>
-__global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
     using S = TcSmem<NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t mma_bar[TC_MAX_STAGES];
@@ -318,6 +283,7 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     __shared__ float red_ss[4][NT];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row = tid & (TC_M - 1), wg = tid >> 7;  // weight row / TMEM lane, warpgroup = K half
     // grid (ksplit, n_tiles, m_tiles); the ksplit CTAs of one tile form one cluster
     const int split = blockIdx.x, n_tile = blockIdx.y, m_tile = blockIdx.z;
     const int n_base = n_tile * TC_M, m_base = m_tile * NT;
@@ -328,11 +294,24 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     const int c_first = max(c_begin, a.kbegin / TC_KC);
     const int nch = max(0, c_end - c_first);
     const int stages = sp.stages;
+    const int ks = sp.ksplit;
     // every chunk of this CTA has its own stage: all weights are staged before waiting for
     // the previous kernel (weights are read-only; activations are not)
     const bool staged = nch <= stages;
-    const int n = n_base + tid;  // this thread's weight row
+    const int n = n_base + row;  // this thread's weight row
     auto stage_ptr = [&](int st, int part) { return smem + st * S::STAGE + (part < 2 ? part * S::A_BYTES : 2 * S::A_BYTES + (part - 2) * S::B_BYTES); };
+    float* gain_s = reinterpret_cast<float*>(smem + sp.gain_off);  // [nch][64] when staged
+
+    // Columns (tokens) this CTA finishes: its slice of the tile when K is split, else all;
+    // warpgroup wg takes half of them.
+    const int slice = NT / ks;  // multiple of 8
+    int rank = 0;
+    if (ks > 1) rank = (int)cg::this_cluster().block_rank();
+    const int fin_begin = ks > 1 ? rank * slice : 0;
+    const int fin_cols = ks > 1 ? slice : NT;
+    const int my_cols = fin_cols / 2;  // multiple of 4
+    const int my_begin = fin_begin + wg * my_cols;
+    constexpr int PRE = 8;  // epilogue columns whose inputs are fetched early
 
     if (warp == 0) {
         tmem_alloc(&tmem_slot, NT);
@@ -343,49 +322,94 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         mbar_init(&done_bar, 1);
         fence_barrier_init();
     }
-    ChunkRegs<NT, F32W> cur;
+    // ---- before the grid dependency: everything that does not depend on the previous kernel
+    WRegs<F32W> cur;
     if (staged) {
-        if (!F32W && nch >= 2) {
-            // two chunks' loads in flight before converting either
-            ChunkRegs<NT, F32W> r1;
-            load_chunk_w<NT, F32W>(cur, a, n, c_first * TC_KC);
-            load_chunk_w<NT, F32W>(r1, a, n, (c_first + 1) * TC_KC);
-            stage_weights<NT, F32W>(cur, a, n, c_first * TC_KC, stage_ptr(0, 0), stage_ptr(0, 1), tid);
-            stage_weights<NT, F32W>(r1, a, n, (c_first + 1) * TC_KC, stage_ptr(1, 0), stage_ptr(1, 1), tid);
+        if (a.norm_gain)
+            for (int t = tid; t < nch * (TC_KC / 4); t += TC_THREADS)
+                reinterpret_cast<float4*>(gain_s)[t] =
+                    __ldg(reinterpret_cast<const float4*>(a.norm_gain + c_first * TC_KC) + t);
+        if (nch >= 2) {
+            WRegs<F32W> r1;
+            load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
+            load_w<F32W>(r1, a, n, (c_first + 1) * TC_KC + wg * 32);
+            stage_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32, stage_ptr(0, 0), stage_ptr(0, 1), row, wg);
+            stage_w<F32W>(r1, a, n, (c_first + 1) * TC_KC + wg * 32, stage_ptr(1, 0), stage_ptr(1, 1), row, wg);
             for (int i = 2; i < nch; i++) {
-                load_chunk_w<NT, F32W>(cur, a, n, (c_first + i) * TC_KC);
-                stage_weights<NT, F32W>(cur, a, n, (c_first + i) * TC_KC, stage_ptr(i, 0), stage_ptr(i, 1), tid);
+                load_w<F32W>(cur, a, n, (c_first + i) * TC_KC + wg * 32);
+                stage_w<F32W>(cur, a, n, (c_first + i) * TC_KC + wg * 32, stage_ptr(i, 0), stage_ptr(i, 1), row, wg);
             }
-        } else {
-            for (int i = 0; i < nch; i++) {
-                load_chunk_w<NT, F32W>(cur, a, n, (c_first + i) * TC_KC);
-                stage_weights<NT, F32W>(cur, a, n, (c_first + i) * TC_KC, stage_ptr(i, 0), stage_ptr(i, 1), tid);
-            }
+        } else if (nch == 1) {
+            load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
+            stage_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32, stage_ptr(0, 0), stage_ptr(0, 1), row, wg);
         }
     } else if (nch > 0) {
-        load_chunk_w<NT, F32W>(cur, a, n, c_first * TC_KC);
+        load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
+    }
+    // QKV: token positions, pages and rotary factors of the first PRE epilogue columns
+    // (the decode descriptors are written before the step's first kernel)
+    int pos_pre[EPI == kEpiQKV ? PRE : 1], page_pre[EPI == kEpiQKV ? PRE : 1];
+    float fcr_pre[EPI == kEpiQKV ? PRE : 1], fci_pre[EPI == kEpiQKV ? PRE : 1];
+    const int np = n & ~1;
+    if (EPI == kEpiQKV) {
+        const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+        const int cc = np < D ? np : (np < D + KV ? np - D : np - D - KV);
+        const bool rope = np < D + KV;
+#pragma unroll
+        for (int j = 0; j < PRE; j++) {
+            const int m = min(m_base + my_begin + j, a.M - 1);
+            pos_pre[j] = e.tok_pos[m];
+            page_pre[j] = e.tok_page[m];
+        }
+#pragma unroll
+        for (int j = 0; j < PRE; j++) {
+            fcr_pre[j] = 1.0f;
+            fci_pre[j] = 0.0f;
+            if (rope && j < my_cols) {
+                const int fi = pos_pre[j] * (hd >> 1) + ((cc % hd) >> 1);
+                fcr_pre[j] = e.freq_re[fi];
+                fci_pre[j] = e.freq_im[fi];
+            }
+        }
     }
 
     grid_dependency_wait();
-    // 64-token tiles: the activation slices of the first two staged chunks are requested
-    // before the RMS partial sums so the two round trips overlap
-    ChunkRegs<NT, F32W> xr0, xr1;
-    const int my_r = tid >> 1, my_half = tid & 1;
+    // ---- after it: activations, RMS sums, residual inputs
+    // 64-token tiles with every chunk staged: the activation units of all chunks are
+    // requested before the RMS partial sums so the round trips overlap
+    float4 xr[S::MAX_STAGES][NT == 64 ? 4 : 1];
+    const int ur = tid >> 2, ukq = tid & 3;  // NT == 64: this thread's activation unit
     if (NT == 64 && staged) {
-        if (nch > 0) load_chunk_x<NT, F32W>(xr0, a, m_base + my_r, my_half, c_first * TC_KC);
-        if (nch > 1) load_chunk_x<NT, F32W>(xr1, a, m_base + my_r, my_half, (c_first + 1) * TC_KC);
+#pragma unroll
+        for (int i = 0; i < S::MAX_STAGES; i++) {
+            if (i < nch && m_base + ur < a.M) {
+                const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)(m_base + ur) * a.ldx +
+                                                                    (c_first + i) * TC_KC + ukq * 16);
+#pragma unroll
+                for (int j = 0; j < 4; j++) xr[i][j] = src[j];
+            }
+        }
+    }
+    float xo_pre[EPI == kEpiResidual ? PRE : 1];
+    if (EPI == kEpiResidual) {
+#pragma unroll
+        for (int j = 0; j < PRE; j++) {
+            const int m = m_base + my_begin + j;
+            xo_pre[j] = (j < my_cols && m < a.M && n < a.N) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
+        }
     }
     if (a.norm_gain) {
         if (a.ss_in) {
-            // sums of squares published by the producer of x, one per 128-feature slice
-            for (int r = tid; r < NT; r += TC_THREADS) {
-                const int m = m_base + r;
+            // sums of squares published by the producer of x, one per 128-feature slice;
+            // four threads per token, joined by two shuffles
+            for (int u = tid; u < NT * 4; u += TC_THREADS) {
+                const int r = u >> 2, p0 = u & 3, m = m_base + r;
                 float ss = 0.0f;
-                if (m < a.M) {
-#pragma unroll 8
-                    for (int p = 0; p < a.ss_parts; p++) ss += __ldcg(a.ss_in + (int64_t)p * a.ss_ld + m);
-                }
-                inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+                if (m < a.M)
+                    for (int p = p0; p < a.ss_parts; p += 4) ss += __ldcg(a.ss_in + (int64_t)p * a.ss_ld + m);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                if (p0 == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
             }
         } else {
             const int nw = TC_THREADS / 32;
@@ -393,9 +417,9 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                 const int m = m_base + r;
                 float ss = 0.0f;
                 if (m < a.M) {
-                    const float* row = a.x + (int64_t)m * a.ldx;
+                    const float* xrow = a.x + (int64_t)m * a.ldx;
                     for (int k = lane * 4; k < a.K; k += 128) {
-                        float4 v = *reinterpret_cast<const float4*>(row + k);
+                        float4 v = *reinterpret_cast<const float4*>(xrow + k);
                         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                     }
                 }
@@ -413,13 +437,21 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     bool bail = false;
     if (staged) {
         for (int i = 0; i < nch; i++) {
-            if (NT == 64 && i < 2) {
-                const int m = m_base + my_r;
-                stage_tokens(i == 0 ? xr0.x : xr1.x, a, inv_rms[my_r], (c_first + i) * TC_KC + my_half * 32, m < a.M,
-                             stage_ptr(i, 2), stage_ptr(i, 3), my_r, my_half);
+            const float* g = a.norm_gain ? gain_s + i * TC_KC : nullptr;
+            if (NT == 64) {
+                const int m = m_base + ur;
+                float4 x4[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) x4[j] = xr[0][j];
+#pragma unroll
+                for (int s2 = 1; s2 < S::MAX_STAGES; s2++)
+                    if (i == s2)
+#pragma unroll
+                        for (int j = 0; j < 4; j++) x4[j] = xr[s2][j];
+                stage_x16(x4, g ? g + ukq * 16 : nullptr, a.norm_gain ? inv_rms[ur] : 1.0f, m < a.M, stage_ptr(i, 2),
+                          stage_ptr(i, 3), ur, ukq);
             } else {
-                stage_chunk_tokens<NT, F32W>(a, inv_rms, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3),
-                                             tid);
+                stage_chunk_x<NT>(a, inv_rms, g, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
             }
         }
         fence_async_smem();
@@ -436,14 +468,15 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
             const int st = it % stages;
             const int use = it / stages;
             const int k0 = (c_first + it) * TC_KC;
-            ChunkRegs<NT, F32W> nxt;
-            if (it + 1 < nch) load_chunk_w<NT, F32W>(nxt, a, n, k0 + TC_KC);
+            WRegs<F32W> nxt;
+            if (it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
             if (use > 0) {
                 const bool got = mbar_wait(&mma_bar[st], (use - 1) & 1, a.err);
                 if (!__syncthreads_and(got)) { bail = true; break; }
             }
-            stage_weights<NT, F32W>(cur, a, n, k0, stage_ptr(st, 0), stage_ptr(st, 1), tid);
-            stage_chunk_tokens<NT, F32W>(a, inv_rms, m_base, k0, stage_ptr(st, 2), stage_ptr(st, 3), tid);
+            stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
+            stage_chunk_x<NT>(a, inv_rms, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2),
+                              stage_ptr(st, 3), tid);
             fence_async_smem();
             __syncthreads();
             if (tid == 0) {
@@ -464,10 +497,10 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     // is free only once the peer's own MMAs have read it: every CTA announces that here
     // (arrive) and waits for all peers just before pushing, so the wait mostly overlaps
     // the accumulator loads.
-    if (sp.ksplit > 1) cluster_arrive_release();
+    if (ks > 1) cluster_arrive_release();
     if (bail) {  // a wait gave up (error flag set): release TMEM and leave, taking the same
                  // cluster barriers as the normal path so the peers are not left waiting
-        if (sp.ksplit > 1) {
+        if (ks > 1) {
             cluster_wait_acquire();
             cg::this_cluster().sync();
         }
@@ -477,25 +510,19 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
         return;
     }
 
-    // Accumulators -> shared memory, row-major per thread ([row][column]).  Without a split
-    // they are parked in this CTA's free stage memory.  With K split over a cluster, token
-    // slice r of the tile belongs to the cluster's CTA r: every CTA pushes its partial of
-    // slice r straight into CTA r's receive buffer with 16-byte distributed-shared-memory
-    // stores, one cluster barrier publishes them, and CTA r sums its slice locally in rank
-    // order (deterministic).  Nothing is read remotely, so no second barrier is needed.
-    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    const int ks = sp.ksplit;
-    const int slice = NT / ks;  // multiple of 8
-    // row strides padded by 4 floats: the 8 threads of a 16-byte shared-memory phase then
-    // touch 8 different bank groups
-    const int pst = NT + 4, rst = slice + 4;
-    int col_begin = 0;
-    float* part = reinterpret_cast<float*>(smem);  // ks == 1: [128][NT + 4]
-    float* recv = reinterpret_cast<float*>(smem);  // ks > 1: [ks][128][slice + 4]
+    // Accumulators.  With K split over a cluster, token slice r of the tile belongs to the
+    // cluster's CTA r: every CTA pushes its partial of slice r straight into CTA r's receive
+    // buffer ([ks][128][slice + 4] fp32, row-major per thread, in CTA r's stage memory) with
+    // 16-byte distributed-shared-memory stores, one cluster barrier publishes them, and CTA
+    // r sums its slice locally in rank order (deterministic).  Without a split the epilogue
+    // reads TMEM directly.
+    const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const int rst = slice + 4;  // padded row stride: the 8 rows of a 16-byte phase hit 8 bank groups
+    float* recv = reinterpret_cast<float*>(smem);
     if (ks > 1) {
         cg::cluster_group cluster = cg::this_cluster();
-        const int rank = (int)cluster.block_rank();
-        for (int c0 = 0; c0 < NT; c0 += 8) {
+        const int half = NT / 2;
+        for (int c0 = wg * half; c0 < (wg + 1) * half; c0 += 8) {
             float v[8];
             if (nch > 0) {
                 tmem_ld8(tl + c0, v);
@@ -503,49 +530,37 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
 #pragma unroll
                 for (int j = 0; j < 8; j++) v[j] = 0.0f;
             }
-            if (c0 == 0) cluster_wait_acquire();  // every peer's MMAs are done with its stages
+            if (c0 == wg * half) cluster_wait_acquire();  // every peer's MMAs are done with its stages
             const int q = c0 / slice;
             float4* dst = reinterpret_cast<float4*>(cluster.map_shared_rank(recv, q) +
-                                                    ((size_t)rank * TC_M + tid) * rst + (c0 - q * slice));
+                                                    ((size_t)rank * TC_M + row) * rst + (c0 - q * slice));
             dst[0] = make_float4(v[0], v[1], v[2], v[3]);
             dst[1] = make_float4(v[4], v[5], v[6], v[7]);
         }
         cluster.sync();
-        col_begin = rank * slice;
-    } else {
-        for (int c0 = 0; c0 < NT; c0 += 8) {
-            float v[8];
-            if (nch > 0) {
-                tmem_ld8(tl + c0, v);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; j++) v[j] = 0.0f;
-            }
-            float4* dst = reinterpret_cast<float4*>(part + (size_t)tid * pst + c0);
-            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-        }
     }
-    const int col_end = col_begin + slice;
     const bool even = (n & 1) == 0;
-    for (int c0 = col_begin; c0 < col_end; c0 += 8) {
-        float v[8];
-        {
-            const float* src = ks > 1 ? recv + (size_t)tid * rst + (c0 - col_begin) : part + (size_t)tid * pst + c0;
-            const float4 a4 = reinterpret_cast<const float4*>(src)[0], b4 = reinterpret_cast<const float4*>(src)[1];
-            v[0] = a4.x; v[1] = a4.y; v[2] = a4.z; v[3] = a4.w; v[4] = b4.x; v[5] = b4.y; v[6] = b4.z; v[7] = b4.w;
+    for (int c0 = my_begin; c0 < my_begin + my_cols; c0 += 4) {
+        const int jb = c0 - my_begin;  // index of the group's first column among this thread's
+        float v[4];
+        if (ks > 1) {
+            const float* src = recv + (size_t)row * rst + (c0 - fin_begin);
+            float4 s4 = reinterpret_cast<const float4*>(src)[0];
             for (int q = 1; q < ks; q++) {
-                const float4* r4 = reinterpret_cast<const float4*>(src + (size_t)q * TC_M * rst);
-                const float4 c4 = r4[0], d4 = r4[1];
-                v[0] += c4.x; v[1] += c4.y; v[2] += c4.z; v[3] += c4.w;
-                v[4] += d4.x; v[5] += d4.y; v[6] += d4.z; v[7] += d4.w;
+                const float4 t4 = reinterpret_cast<const float4*>(src + (size_t)q * TC_M * rst)[0];
+                s4.x += t4.x; s4.y += t4.y; s4.z += t4.z; s4.w += t4.w;
             }
+            v[0] = s4.x; v[1] = s4.y; v[2] = s4.z; v[3] = s4.w;
+        } else if (nch > 0) {
+            tmem_ld4(tl + c0, v);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] = 0.0f;
         }
-        // Epilogue of the group.  Every global load of the 8 columns is issued before any
-        // store (the outputs may alias as far as the compiler knows).
+        // Epilogue of the group; every global load of the group comes before its stores.
         if (EPI == kEpiLogits) {
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < 4; j++) {
                 const int c = c0 + j, m = m_base + c;
                 const bool ok = m < a.M && n < a.N;
                 if (ok && e.out) e.out[(int64_t)m * e.ldo + n] = v[j];
@@ -555,39 +570,44 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                     unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
                     key = k2 > key ? k2 : key;
                 }
-                if (lane == 0) red_key[warp][c] = key;
+                if (lane == 0) red_key[warp & 3][c] = key;
             }
         } else if (EPI == kEpiResidual) {
-            float xo[8];
+            float xo[4];
+            if (jb == 0 || jb == 4) {  // fetched right after the grid dependency wait
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int m = m_base + c0 + j;
-                xo[j] = (m < a.M && n < a.N) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
+                for (int j = 0; j < 4; j++) xo[j] = jb == 0 ? xo_pre[j] : xo_pre[4 + j];
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int m = m_base + c0 + j;
+                    xo[j] = (m < a.M && n < a.N) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
+                }
             }
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < 4; j++) {
                 const int c = c0 + j, m = m_base + c;
                 const bool ok = m < a.M && n < a.N;
                 const float xn = ok ? xo[j] + v[j] : 0.0f;
                 if (ok) e.out[(int64_t)m * e.ldo + n] = xn;
                 if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
                     const float sq = warp_sum(xn * xn);
-                    if (lane == 0) red_ss[warp][c] = sq;
+                    if (lane == 0) red_ss[warp & 3][c] = sq;
                 }
             }
         } else if (EPI == kEpiStore) {
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < 4; j++) {
                 const int m = m_base + c0 + j;
                 if (m < a.M && n < a.N) e.out[(int64_t)m * e.ldo + n] = v[j];
             }
         } else {
-            float other[8];
+            float other[4];
 #pragma unroll
-            for (int j = 0; j < 8; j++) other[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);  // pair partner's row
+            for (int j = 0; j < 4; j++) other[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);  // pair partner's row
             if (EPI == kEpiSwiGLU) {
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
+                for (int j = 0; j < 4; j++) {
                     const int m = m_base + c0 + j;
                     if (even && m < a.M && n < a.N) {
                         const float g = v[j];
@@ -597,28 +617,37 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
                 }
             } else if (EPI == kEpiQKV) {
                 const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
-                const int np = n & ~1;
                 const bool rope = np < D + KV;
                 const int cc = np < D ? np : (np < D + KV ? np - D : np - D - KV);
-                int pos[8], page[8];
-                float fcr[8], fci[8];
+                int pos[4], page[4];
+                float fcr[4], fci[4];
+                if (jb == 0 || jb == 4) {  // fetched before the grid dependency wait
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const int m = min(m_base + c0 + j, a.M - 1);
-                    pos[j] = e.tok_pos[m];
-                    page[j] = e.tok_page[m];
-                }
+                    for (int j = 0; j < 4; j++) {
+                        pos[j] = jb == 0 ? pos_pre[j] : pos_pre[4 + j];
+                        page[j] = jb == 0 ? page_pre[j] : page_pre[4 + j];
+                        fcr[j] = jb == 0 ? fcr_pre[j] : fcr_pre[4 + j];
+                        fci[j] = jb == 0 ? fci_pre[j] : fci_pre[4 + j];
+                    }
+                } else {
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    fcr[j] = 1.0f; fci[j] = 0.0f;
-                    if (rope) {
-                        const int fi = pos[j] * (hd >> 1) + ((cc % hd) >> 1);
-                        fcr[j] = e.freq_re[fi];
-                        fci[j] = e.freq_im[fi];
+                    for (int j = 0; j < 4; j++) {
+                        const int m = min(m_base + c0 + j, a.M - 1);
+                        pos[j] = e.tok_pos[m];
+                        page[j] = e.tok_page[m];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        fcr[j] = 1.0f; fci[j] = 0.0f;
+                        if (rope) {
+                            const int fi = pos[j] * (hd >> 1) + ((cc % hd) >> 1);
+                            fcr[j] = e.freq_re[fi];
+                            fci[j] = e.freq_im[fi];
+                        }
                     }
                 }
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
+                for (int j = 0; j < 4; j++) {
                     const int m = m_base + c0 + j;
                     if (m >= a.M || n >= a.N) continue;
                     const float v0 = even ? v[j] : other[j];  // value of row n & ~1
@@ -638,7 +667,7 @@ __global__ void __launch_bounds__(TC_THREADS) tc_gemm_kernel(GemmArgs a, Epilogu
     }
     if (EPI == kEpiLogits || (EPI == kEpiResidual && e.ss_out)) {
         __syncthreads();
-        for (int cix = col_begin + tid; cix < col_end; cix += TC_THREADS) {
+        for (int cix = fin_begin + tid; cix < fin_begin + fin_cols; cix += TC_THREADS) {
             const int m = m_base + cix;
             if (m >= a.M) continue;
             if (EPI == kEpiLogits) {
@@ -729,15 +758,17 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     }
     tc_ensure_smem(kernel);
     // Stages and shared memory for a split: a stage per chunk up to the limit; the
-    // accumulators are later parked (ks == 1) or received (ks > 1) in the stage memory.
+    // partial accumulators of a split are later received in the stage memory; the
+    // RMSNorm gain slice of the CTA's chunks sits behind both.
     auto plan = [&](int ks, SplitArgs* sp) {
         const int per_cta = (chunks + ks - 1) / ks;
         int max_st = TcSmem<NT>::MAX_STAGES;
         while (max_st > TC_STAGES && max_st * TcSmem<NT>::STAGE > 200 * 1024) max_st--;
         sp->ksplit = ks;
         sp->stages = std::max(TC_STAGES, std::min(max_st, per_cta));
-        const int park = (NT + 4 * ks) * TC_M * 4;
-        return std::max(sp->stages * TcSmem<NT>::STAGE, park);
+        const int park = ks > 1 ? (NT + 4 * ks) * TC_M * 4 : 0;
+        sp->gain_off = std::max(sp->stages * TcSmem<NT>::STAGE, park);
+        return sp->gain_off + (a.norm_gain ? sp->stages * TC_KC * 4 : 0);
     };
     // Fill the GPU: when the tiles alone are fewer than the SMs, split K across the CTAs
     // of a cluster (power of two up to 8, at most one split per chunk, NT/ksplit >= 8), but
