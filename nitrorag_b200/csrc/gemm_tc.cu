@@ -346,15 +346,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     } else if (nch > 0) {
         load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
     }
-    // QKV: token positions, pages and rotary factors of the first PRE epilogue columns
-    // (the decode descriptors are written before the step's first kernel)
+    // QKV: where this thread's row goes (q row, or a K/V pool column) and the token
+    // positions, pages and rotary factors of its first PRE epilogue columns (the decode
+    // descriptors are written before the step's first kernel)
     int pos_pre[EPI == kEpiQKV ? PRE : 1], page_pre[EPI == kEpiQKV ? PRE : 1];
     float fcr_pre[EPI == kEpiQKV ? PRE : 1], fci_pre[EPI == kEpiQKV ? PRE : 1];
     const int np = n & ~1;
+    int qkv_kind = 3, fbase = 0;  // 0 q, 1 k, 2 v, 3 none; rotary pair index of the row
+    int64_t row_off = 0;          // q: column in q_out; k/v: offset inside page 0's tile row
+    float* pool = nullptr;
     if (EPI == kEpiQKV) {
         const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
-        const int cc = np < D ? np : (np < D + KV ? np - D : np - D - KV);
-        const bool rope = np < D + KV;
+        if (n < a.N) {
+            if (np < D) {
+                qkv_kind = 0;
+                row_off = n;
+                fbase = (np % hd) >> 1;
+            } else {
+                const int cidx = np < D + KV ? n - D : n - D - KV;
+                qkv_kind = np < D + KV ? 1 : 2;
+                pool = qkv_kind == 1 ? e.kpool : e.vpool;
+                row_off = e.geom.tile_offset(0, e.layer, cidx / hd) + cidx % hd;
+                fbase = ((cidx & ~1) % hd) >> 1;
+            }
+        }
+        const bool rope = qkv_kind < 2;
 #pragma unroll
         for (int j = 0; j < PRE; j++) {
             const int m = min(m_base + my_begin + j, a.M - 1);
@@ -366,7 +382,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             fcr_pre[j] = 1.0f;
             fci_pre[j] = 0.0f;
             if (rope && j < my_cols) {
-                const int fi = pos_pre[j] * (hd >> 1) + ((cc % hd) >> 1);
+                const int fi = pos_pre[j] * (hd >> 1) + fbase;
                 fcr_pre[j] = e.freq_re[fi];
                 fci_pre[j] = e.freq_im[fi];
             }
@@ -453,15 +469,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             } else {
                 stage_chunk_x<NT>(a, inv_rms, g, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
             }
-        }
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            for (int i = 0; i < nch; i++)
+            // chunk i is complete: its MMAs run while the next chunk is converted
+            fence_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
                 issue_chunk_mmas(tmem, idesc, stage_ptr(i, 0), stage_ptr(i, 1), stage_ptr(i, 2), stage_ptr(i, 3), i == 0);
-            umma_commit(&done_bar);
+            }
         }
+        if (tid == 0 && nch > 0) umma_commit(&done_bar);
     } else {
         // more chunks than stages: a ring, the next chunk's weight loads one chunk ahead
         for (int it = 0; it < nch; it++) {
@@ -616,9 +632,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
                     }
                 }
             } else if (EPI == kEpiQKV) {
-                const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
-                const bool rope = np < D + KV;
-                const int cc = np < D ? np : (np < D + KV ? np - D : np - D - KV);
+                const int D = e.dim, hd = e.head_dim;
+                const bool rope = qkv_kind < 2;
                 int pos[4], page[4];
                 float fcr[4], fci[4];
                 if (jb == 0 || jb == 4) {  // fetched before the grid dependency wait
@@ -640,27 +655,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
                     for (int j = 0; j < 4; j++) {
                         fcr[j] = 1.0f; fci[j] = 0.0f;
                         if (rope) {
-                            const int fi = pos[j] * (hd >> 1) + ((cc % hd) >> 1);
+                            const int fi = pos[j] * (hd >> 1) + fbase;
                             fcr[j] = e.freq_re[fi];
                             fci[j] = e.freq_im[fi];
                         }
                     }
                 }
+                const int64_t pf = e.geom.page_floats();
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int m = m_base + c0 + j;
-                    if (m >= a.M || n >= a.N) continue;
+                    if (m >= a.M || qkv_kind == 3) continue;
                     const float v0 = even ? v[j] : other[j];  // value of row n & ~1
                     const float v1 = even ? other[j] : v[j];  // value of row n | 1
                     const float r = rope ? (even ? (v0 * fcr[j] - v1 * fci[j]) : (v0 * fci[j] + v1 * fcr[j])) : v[j];
-                    if (np < D) {
-                        e.q_out[(int64_t)m * D + n] = r;
-                    } else {
-                        const int cidx = np < D + KV ? n - D : n - D - KV;
-                        float* pool = np < D + KV ? e.kpool : e.vpool;
-                        pool[e.geom.tile_offset(page[j], e.layer, cidx / hd) + (int64_t)(pos[j] & (kPage - 1)) * hd +
-                             (cidx % hd)] = r;
-                    }
+                    if (qkv_kind == 0)
+                        e.q_out[(int64_t)m * D + row_off] = r;
+                    else
+                        pool[(int64_t)page[j] * pf + (int64_t)(pos[j] & (kPage - 1)) * hd + row_off] = r;
                 }
             }
         }
@@ -765,7 +777,9 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
         int max_st = TcSmem<NT>::MAX_STAGES;
         while (max_st > TC_STAGES && max_st * TcSmem<NT>::STAGE > 200 * 1024) max_st--;
         sp->ksplit = ks;
-        sp->stages = std::max(TC_STAGES, std::min(max_st, per_cta));
+        // a ring (more chunks than stages) keeps 2 stages: its loads run one chunk ahead in
+        // registers, and the smaller footprint lets two CTAs share an SM
+        sp->stages = per_cta > max_st ? TC_STAGES : std::max(TC_STAGES, per_cta);
         const int park = ks > 1 ? (NT + 4 * ks) * TC_M * 4 : 0;
         sp->gain_off = std::max(sp->stages * TcSmem<NT>::STAGE, park);
         return sp->gain_off + (a.norm_gain ? sp->stages * TC_KC * 4 : 0);
