@@ -115,10 +115,10 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
 // next item's pages while the current item drains, so the copy engine always has pages
 // in flight.  No CTA-wide barrier is taken after set-up.
 #ifndef NITRO_DEC_STAGES
-#define NITRO_DEC_STAGES 3
+#define NITRO_DEC_STAGES 4
 #endif
 #ifndef NITRO_DEC_WARPS64
-#define NITRO_DEC_WARPS64 8
+#define NITRO_DEC_WARPS64 6
 #endif
 #ifndef NITRO_DEC_CHUNK64
 #define NITRO_DEC_CHUNK64 16
@@ -140,29 +140,52 @@ struct DecItem {
     float q[4];    // lane l: query dims l + 32 j (pre-scaled), j < head_dim / 32
 };
 
+// Work items are numbered longest first: every full chunk (chunk_pages pages) of every
+// (sequence, head) in sequence order, then the shorter last chunks, longest remainder
+// first, so that the items still running when the counter runs dry are the short ones.
+struct DecTable {
+    int full_prefix[1025];  // full_prefix[b]: first full-chunk item of sequence b
+    int tail_seq[1024];     // sequences with a shorter last chunk, longest remainder first
+    int ctx[1024];
+    int group_off[32][32];  // [32-sequence group][remainder]: count, then offset in bucket
+    int bucket[33];         // [remainder]: first slot of the bucket; [0]: number of tails
+    int warp_tot[32];
+};
+
 // Decode work item `idx` into its sequence / head / chunk, and prefetch everything its
 // processing needs (page ids, query) so no dependent global load sits in front of the
 // bulk copies later.
 template <int HD>
-__device__ __forceinline__ DecItem dec_item(int idx, int total, const int* prefix, const int* ctx_s,
-                                            const DecodeAttnArgs& a, int lane, float qscale) {
+__device__ __forceinline__ DecItem dec_item(int idx, int total, const DecTable& t, const DecodeAttnArgs& a, int lane,
+                                            float qscale) {
     DecItem it;
     it.valid = idx < total;
     it.pid = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) it.q[j] = 0.0f;
     if (!it.valid) { it.b = it.h = it.split = it.p0 = it.np = it.ctx = it.nsplit = 0; return it; }
-    int lo = 0, hi = a.B;  // largest b with prefix[b] <= idx
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (prefix[mid] <= idx) lo = mid; else hi = mid;
+    const int total_full = t.full_prefix[a.B];
+    int pages;
+    if (idx < total_full) {
+        int lo = 0, hi = a.B;  // largest b with full_prefix[b] <= idx
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (t.full_prefix[mid] <= idx) lo = mid; else hi = mid;
+        }
+        it.b = lo;
+        const int rem = idx - t.full_prefix[lo];
+        it.split = rem / a.n_heads;
+        it.h = rem % a.n_heads;
+        it.ctx = t.ctx[lo];
+        pages = (it.ctx + kPage - 1) / kPage;
+    } else {
+        const int j = idx - total_full;
+        it.b = t.tail_seq[j / a.n_heads];
+        it.h = j % a.n_heads;
+        it.ctx = t.ctx[it.b];
+        pages = (it.ctx + kPage - 1) / kPage;
+        it.split = pages / a.chunk_pages;
     }
-    it.b = lo;
-    const int rem = idx - prefix[lo];
-    it.split = rem / a.n_heads;
-    it.h = rem % a.n_heads;
-    it.ctx = ctx_s[lo];
-    const int pages = (it.ctx + kPage - 1) / kPage;
     it.nsplit = (pages + a.chunk_pages - 1) / a.chunk_pages;
     it.p0 = it.split * a.chunk_pages;
     it.np = min(a.chunk_pages, pages - it.p0);
@@ -179,23 +202,24 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
     constexpr int DPL = HD / 32;
     extern __shared__ __align__(128) float smem[];
     __shared__ uint64_t bars[C::WARPS][kDecStages];
-    __shared__ int prefix[1025];
-    __shared__ int ctx_s[1024];
-    __shared__ int warp_tot[32];
+    __shared__ DecTable tab;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kvmul = a.n_heads / a.geom.n_kv_heads;
+    const int cp = a.chunk_pages;
 
     // item table from the step descriptor (written before this step's first kernel, so it
-    // is read before waiting on the previous kernel): prefix[b] = first item of sequence b
+    // is read before waiting on the previous kernel).  Every CTA builds the same table, so
+    // it must not depend on timing: the tail order is a stable counting sort.
+    for (int i = threadIdx.x; i < 32 * 32; i += blockDim.x) (&tab.group_off[0][0])[i] = 0;
     for (int base = 0; base < a.B; base += blockDim.x) {
         const int b = base + threadIdx.x;
         int cnt = 0;
         if (b < a.B) {
             const int ctx = a.ctx_lens[b];
-            ctx_s[b] = ctx;
+            tab.ctx[b] = ctx;
             const int pages = (ctx + kPage - 1) / kPage;
-            cnt = ((pages + a.chunk_pages - 1) / a.chunk_pages) * a.n_heads;
+            cnt = (pages / cp) * a.n_heads;
         }
         int incl = cnt;
 #pragma unroll
@@ -203,22 +227,63 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
             const int v = __shfl_up_sync(0xffffffffu, incl, o);
             if (lane >= o) incl += v;
         }
-        if (lane == 31) warp_tot[warp] = incl;
+        if (lane == 31) tab.warp_tot[warp] = incl;
         __syncthreads();
         if (threadIdx.x == 0) {
-            int run = base == 0 ? 0 : prefix[base];
+            int run = base == 0 ? 0 : tab.full_prefix[base];
             for (int w = 0; w < C::WARPS; w++) {
-                const int t = warp_tot[w];
-                warp_tot[w] = run;
+                const int t = tab.warp_tot[w];
+                tab.warp_tot[w] = run;
                 run += t;
             }
-            prefix[min(base + (int)blockDim.x, a.B)] = run;
+            tab.full_prefix[min(base + (int)blockDim.x, a.B)] = run;
         }
         __syncthreads();
-        if (b < a.B) prefix[b] = warp_tot[warp] + incl - cnt;
+        if (b < a.B) tab.full_prefix[b] = tab.warp_tot[warp] + incl - cnt;
         __syncthreads();
     }
-    const int total = prefix[a.B];
+    // last chunks shorter than chunk_pages, bucketed by remainder (longest first), in
+    // sequence order inside a bucket: per 32-sequence group, lanes with equal remainders
+    // rank themselves by lane; group counts are then turned into offsets per bucket
+    const int n_groups = (a.B + 31) / 32;
+    auto tail_rem = [&](int b) {
+        return b < a.B ? ((tab.ctx[b] + kPage - 1) / kPage) % cp : 0;
+    };
+    for (int g = warp; g < n_groups; g += C::WARPS) {
+        const int r = tail_rem(g * 32 + lane);
+        const unsigned same = __match_any_sync(0xffffffffu, r);
+        if (r > 0 && lane == __ffs(same) - 1) tab.group_off[g][r] = __popc(same);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int r = threadIdx.x;
+        int run = 0;
+        for (int g = 0; g < n_groups; g++) {
+            const int c = tab.group_off[g][r];
+            tab.group_off[g][r] = run;
+            run += c;
+        }
+        tab.bucket[r] = run;  // sequences with remainder r
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int r = cp - 1; r >= 1; r--) {
+            const int c = tab.bucket[r];
+            tab.bucket[r] = run;
+            run += c;
+        }
+        tab.bucket[0] = run;
+    }
+    __syncthreads();
+    for (int g = warp; g < n_groups; g += C::WARPS) {
+        const int b = g * 32 + lane;
+        const int r = tail_rem(b);
+        const unsigned same = __match_any_sync(0xffffffffu, r);
+        if (r > 0) tab.tail_seq[tab.bucket[r] + tab.group_off[g][r] + __popc(same & ((1u << lane) - 1u))] = b;
+    }
+    __syncthreads();
+    const int total = tab.full_prefix[a.B] + tab.bucket[0] * a.n_heads;
 
     float* ring = smem + warp * kDecStages * 2 * C::TILE;
     float* qs = smem + C::RING_FLOATS + warp * HD;
@@ -236,8 +301,8 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
         return __shfl_sync(0xffffffffu, v, 0);
     };
     const float qscale = kLog2e / sqrtf((float)HD);
-    DecItem cur = dec_item<HD>(fetch(), total, prefix, ctx_s, a, lane, qscale);
-    DecItem nxt = dec_item<HD>(cur.valid ? fetch() : total, total, prefix, ctx_s, a, lane, qscale);
+    DecItem cur = dec_item<HD>(fetch(), total, tab, a, lane, qscale);
+    DecItem nxt = dec_item<HD>(cur.valid ? fetch() : total, total, tab, a, lane, qscale);
 
     // issue pointer: page `ip` of item `iq` (0 = cur, 1 = nxt); k-th issued page -> slot k % stages
     int iq = 0, ip = 0;
@@ -307,7 +372,7 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
         if (iq == 0) { iq = 1; ip = 0; }
         cur = nxt;
         iq -= 1;
-        nxt = dec_item<HD>(cur.valid ? fetch() : total, total, prefix, ctx_s, a, lane, qscale);
+        nxt = dec_item<HD>(cur.valid ? fetch() : total, total, tab, a, lane, qscale);
     }
     grid_dependents_launch();
     // every copy this warp issued has been consumed (issued == consumed here); the last warp

@@ -124,6 +124,47 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
 __device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// Distributed shared memory: this CTA's shared address `saddr` mapped into CTA `rank` of
+// the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// 16-byte asynchronous store into a cluster peer's shared memory that completes as 16
+// transaction bytes on the peer's mbarrier `bar` (both addresses from map_rank).
+__device__ __forceinline__ void st_async4(uint32_t addr, float a, float b, float c, float d, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+                 "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
+                 : "memory");
+}
+
+// Bounded wait on a local mbarrier whose transaction bytes come from other CTAs of the
+// cluster (acquire at cluster scope makes their data visible to this thread).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(1000u)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    }
+    if (err) atomicCAS(err, 0, kErrWaitTimeout);
+    return false;
+}
+
 // ------------------------------------------------------------------ operand staging
 // Split 8 fp32 values into bf16 hi/lo and store them as one 16-byte row of a core matrix.
 __device__ __forceinline__ void split_store8(const float* v, uint8_t* hi_dst, uint8_t* lo_dst) {
@@ -154,6 +195,8 @@ struct TcSmem {
 struct SplitArgs {
     int ksplit;  // K-range splits per tile = CTAs per thread-block cluster (grid.x)
     int stages;  // shared-memory stages (one per chunk when a CTA's chunks all fit)
+    int recv_off;  // byte offset of the split-K receive buffer in dynamic shared memory
+    int recv_pad;  // floats of padding per receive-buffer row (4, or 0 when short of space)
     int gain_off;  // byte offset of the staged RMSNorm gain slice in dynamic shared memory
 };
 
@@ -216,9 +259,10 @@ __device__ __forceinline__ void stage_w(const WRegs<F32W>& r, const GemmArgs& a,
     for (int j = 0; j < 4; j++) split_store8(w + 8 * j, a_hi + core_off(row, half * 4 + j), a_lo + core_off(row, half * 4 + j));
 }
 
-// 16 activations of token row r (K quarter kq of a chunk) -> normalised -> bf16 hi/lo.
-__device__ __forceinline__ void stage_x16(const float4* x4, const float* g, float inv, bool valid, uint8_t* b_hi,
-                                          uint8_t* b_lo, int r, int kq) {
+// 16 activations of token row r (K quarter kq of a chunk), times the RMSNorm gain when
+// there is one -> bf16 hi/lo.  The row's 1/rms is applied to the accumulators instead.
+__device__ __forceinline__ void stage_x16(const float4* x4, const float* g, bool valid, uint8_t* b_hi, uint8_t* b_lo,
+                                          int r, int kq) {
     float xv[16];
     if (valid) {
 #pragma unroll
@@ -229,10 +273,10 @@ __device__ __forceinline__ void stage_x16(const float4* x4, const float* g, floa
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const float4 g4 = reinterpret_cast<const float4*>(g)[i];
-                xv[4 * i] = g4.x * (inv * xv[4 * i]);
-                xv[4 * i + 1] = g4.y * (inv * xv[4 * i + 1]);
-                xv[4 * i + 2] = g4.z * (inv * xv[4 * i + 2]);
-                xv[4 * i + 3] = g4.w * (inv * xv[4 * i + 3]);
+                xv[4 * i] *= g4.x;
+                xv[4 * i + 1] *= g4.y;
+                xv[4 * i + 2] *= g4.z;
+                xv[4 * i + 3] *= g4.w;
             }
         }
     } else {
@@ -245,8 +289,8 @@ __device__ __forceinline__ void stage_x16(const float4* x4, const float* g, floa
 
 // The activation tile of one chunk (all NT token rows), loaded and staged by unit.
 template <int NT>
-__device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* inv_rms, const float* g, int m_base,
-                                              int k0, uint8_t* b_hi, uint8_t* b_lo, int tid) {
+__device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* g, int m_base, int k0, uint8_t* b_hi,
+                                              uint8_t* b_lo, int tid) {
     for (int u = tid; u < NT * 4; u += TC_THREADS) {
         const int r = u >> 2, kq = u & 3, m = m_base + r;
         float4 x4[4];
@@ -255,7 +299,7 @@ __device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* in
 #pragma unroll
             for (int i = 0; i < 4; i++) x4[i] = src[i];
         }
-        stage_x16(x4, g ? g + kq * 16 : nullptr, inv_rms[r], m < a.M, b_hi, b_lo, r, kq);
+        stage_x16(x4, g ? g + kq * 16 : nullptr, m < a.M, b_hi, b_lo, r, kq);
     }
 }
 
@@ -277,10 +321,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t mma_bar[TC_MAX_STAGES];
     __shared__ uint64_t done_bar;
+    __shared__ uint64_t recv_bar;  // split K: the partials of this CTA's slice have all arrived
     __shared__ uint32_t tmem_slot;
     __shared__ float inv_rms[NT];
-    __shared__ unsigned long long red_key[4][NT];
-    __shared__ float red_ss[4][NT];
+    __shared__ unsigned long long red_key[4][EPI == kEpiLogits ? NT : 1];
+    __shared__ float red_ss[4][EPI == kEpiResidual ? NT : 1];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row = tid & (TC_M - 1), wg = tid >> 7;  // weight row / TMEM lane, warpgroup = K half
@@ -320,8 +365,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     if (tid == 0) {
         for (int st = 0; st < TC_MAX_STAGES; st++) mbar_init(&mma_bar[st], 1);
         mbar_init(&done_bar, 1);
+        mbar_init(&recv_bar, 1);
+        if (ks > 1) mbar_arrive_expect_tx(&recv_bar, (uint32_t)(TC_M * NT * 4));  // ks partials of slice x 128 rows
         fence_barrier_init();
     }
+    // the peers may push into this CTA's receive buffer once its barrier exists: arrive
+    // here, wait right before the first push
+    if (ks > 1) cluster_arrive_release();
     // ---- before the grid dependency: everything that does not depend on the previous kernel
     WRegs<F32W> cur;
     if (staged) {
@@ -414,8 +464,89 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             xo_pre[j] = (j < my_cols && m < a.M && n < a.N) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
         }
     }
+    // RMSNorm: a token's 1/rms scales its accumulators in the epilogue (the sum over k is
+    // linear), so the sums of squares are needed only after the MMAs.  64-token tiles
+    // request them here, four threads per token, and add them up later.
+    constexpr int SSP = 8;
+    float ssv[SSP];
+    const bool ss_pre = NT == 64 && a.norm_gain && a.ss_in && a.ss_parts <= 4 * SSP;
+    if (ss_pre) {
+        const int m = m_base + ur;
+#pragma unroll
+        for (int i = 0; i < SSP; i++) {
+            const int p = ukq + 4 * i;
+            ssv[i] = (m < a.M && p < a.ss_parts) ? __ldcg(a.ss_in + (int64_t)p * a.ss_ld + m) : 0.0f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
+
+    bool bail = false;
+    if (staged) {
+        for (int i = 0; i < nch; i++) {
+            const float* g = a.norm_gain ? gain_s + i * TC_KC : nullptr;
+            if (NT == 64) {
+                const int m = m_base + ur;
+                float4 x4[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) x4[j] = xr[0][j];
+#pragma unroll
+                for (int s2 = 1; s2 < S::MAX_STAGES; s2++)
+                    if (i == s2)
+#pragma unroll
+                        for (int j = 0; j < 4; j++) x4[j] = xr[s2][j];
+                stage_x16(x4, g ? g + ukq * 16 : nullptr, m < a.M, stage_ptr(i, 2), stage_ptr(i, 3), ur, ukq);
+            } else {
+                stage_chunk_x<NT>(a, g, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
+            }
+            // chunk i is complete: its MMAs run while the next chunk is converted
+            fence_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                issue_chunk_mmas(tmem, idesc, stage_ptr(i, 0), stage_ptr(i, 1), stage_ptr(i, 2), stage_ptr(i, 3), i == 0);
+            }
+        }
+        if (tid == 0 && nch > 0) umma_commit(&done_bar);
+    } else {
+        // more chunks than stages: a ring, the next chunk's weight loads one chunk ahead
+        for (int it = 0; it < nch; it++) {
+            const int st = it % stages;
+            const int use = it / stages;
+            const int k0 = (c_first + it) * TC_KC;
+            WRegs<F32W> nxt;
+            if (it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
+            if (use > 0) {
+                const bool got = mbar_wait(&mma_bar[st], (use - 1) & 1, a.err);
+                if (!__syncthreads_and(got)) { bail = true; break; }
+            }
+            stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
+            stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2), stage_ptr(st, 3),
+                              tid);
+            fence_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
+                umma_commit(&mma_bar[st]);
+            }
+            if (it + 1 < nch) cur = nxt;
+        }
+        if (tid == 0 && !bail && nch > 0) umma_commit(&done_bar);  // completes after every MMA above
+    }
+    // 1/rms per token while the MMAs run
     if (a.norm_gain) {
-        if (a.ss_in) {
+        if (ss_pre) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int i = 0; i < SSP; i++) ss += ssv[i];
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+            if (ukq == 0) inv_rms[ur] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+        } else if (a.ss_in) {
             // sums of squares published by the producer of x, one per 128-feature slice;
             // four threads per token, joined by two shuffles
             for (int u = tid; u < NT * 4; u += TC_THREADS) {
@@ -444,116 +575,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             }
         }
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = tmem_slot;
-    const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
-
-    bool bail = false;
-    if (staged) {
-        for (int i = 0; i < nch; i++) {
-            const float* g = a.norm_gain ? gain_s + i * TC_KC : nullptr;
-            if (NT == 64) {
-                const int m = m_base + ur;
-                float4 x4[4];
-#pragma unroll
-                for (int j = 0; j < 4; j++) x4[j] = xr[0][j];
-#pragma unroll
-                for (int s2 = 1; s2 < S::MAX_STAGES; s2++)
-                    if (i == s2)
-#pragma unroll
-                        for (int j = 0; j < 4; j++) x4[j] = xr[s2][j];
-                stage_x16(x4, g ? g + ukq * 16 : nullptr, a.norm_gain ? inv_rms[ur] : 1.0f, m < a.M, stage_ptr(i, 2),
-                          stage_ptr(i, 3), ur, ukq);
-            } else {
-                stage_chunk_x<NT>(a, inv_rms, g, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
-            }
-            // chunk i is complete: its MMAs run while the next chunk is converted
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
-                tc_fence_after();
-                issue_chunk_mmas(tmem, idesc, stage_ptr(i, 0), stage_ptr(i, 1), stage_ptr(i, 2), stage_ptr(i, 3), i == 0);
-            }
-        }
-        if (tid == 0 && nch > 0) umma_commit(&done_bar);
-    } else {
-        // more chunks than stages: a ring, the next chunk's weight loads one chunk ahead
-        for (int it = 0; it < nch; it++) {
-            const int st = it % stages;
-            const int use = it / stages;
-            const int k0 = (c_first + it) * TC_KC;
-            WRegs<F32W> nxt;
-            if (it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
-            if (use > 0) {
-                const bool got = mbar_wait(&mma_bar[st], (use - 1) & 1, a.err);
-                if (!__syncthreads_and(got)) { bail = true; break; }
-            }
-            stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
-            stage_chunk_x<NT>(a, inv_rms, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2),
-                              stage_ptr(st, 3), tid);
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
-                tc_fence_after();
-                issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
-                umma_commit(&mma_bar[st]);
-            }
-            if (it + 1 < nch) cur = nxt;
-        }
-        if (tid == 0 && !bail && nch > 0) umma_commit(&done_bar);  // completes after every MMA above
-    }
-    if (nch > 0 && !bail) {
-        if (!__syncthreads_and(mbar_wait(&done_bar, 0, a.err))) bail = true;
+    {   // every MMA done (and inv_rms published)
+        const bool got = (nch > 0 && !bail) ? mbar_wait(&done_bar, 0, a.err) : true;
+        if (!__syncthreads_and(got)) bail = true;
     }
     tc_fence_after();
     grid_dependents_launch();
-    // With K split over a cluster the partials are pushed into the peers' stage memory, which
-    // is free only once the peer's own MMAs have read it: every CTA announces that here
-    // (arrive) and waits for all peers just before pushing, so the wait mostly overlaps
-    // the accumulator loads.
-    if (ks > 1) cluster_arrive_release();
-    if (bail) {  // a wait gave up (error flag set): release TMEM and leave, taking the same
-                 // cluster barriers as the normal path so the peers are not left waiting
-        if (ks > 1) {
-            cluster_wait_acquire();
-            cg::this_cluster().sync();
-        }
-        tc_fence_before();
-        __syncthreads();
-        if (warp == 0) tmem_dealloc(tmem, NT);
-        return;
-    }
 
     // Accumulators.  With K split over a cluster, token slice r of the tile belongs to the
-    // cluster's CTA r: every CTA pushes its partial of slice r straight into CTA r's receive
-    // buffer ([ks][128][slice + 4] fp32, row-major per thread, in CTA r's stage memory) with
-    // 16-byte distributed-shared-memory stores, one cluster barrier publishes them, and CTA
-    // r sums its slice locally in rank order (deterministic).  Without a split the epilogue
-    // reads TMEM directly.
+    // cluster's CTA r: every CTA sends its partial of slice r straight into CTA r's receive
+    // buffer ([ks][128][slice + 4] fp32, row-major per thread) with asynchronous 16-byte
+    // distributed-shared-memory stores that count down CTA r's receive barrier, and CTA r
+    // sums its slice locally in rank order (deterministic) once all ks x 128 x slice values
+    // are in.  A CTA whose wait gave up sends zeros so its peers still complete.  Without a
+    // split the epilogue reads TMEM directly.
     const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const int rst = slice + 4;  // padded row stride: the 8 rows of a 16-byte phase hit 8 bank groups
-    float* recv = reinterpret_cast<float*>(smem);
+    const int rst = slice + sp.recv_pad;  // padded: the 8 rows of a 16-byte phase hit 8 bank groups
+    float* recv = reinterpret_cast<float*>(smem + sp.recv_off);
     if (ks > 1) {
-        cg::cluster_group cluster = cg::this_cluster();
         const int half = NT / 2;
+        const uint32_t my_recv = smem_addr(recv + ((size_t)rank * TC_M + row) * rst);
+        const uint32_t my_bar = smem_addr(&recv_bar);
         for (int c0 = wg * half; c0 < (wg + 1) * half; c0 += 8) {
             float v[8];
-            if (nch > 0) {
+            if (nch > 0 && !bail) {
                 tmem_ld8(tl + c0, v);
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; j++) v[j] = 0.0f;
             }
-            if (c0 == wg * half) cluster_wait_acquire();  // every peer's MMAs are done with its stages
+            if (c0 == wg * half) cluster_wait_acquire();  // every peer's receive barrier is initialised
             const int q = c0 / slice;
-            float4* dst = reinterpret_cast<float4*>(cluster.map_shared_rank(recv, q) +
-                                                    ((size_t)rank * TC_M + row) * rst + (c0 - q * slice));
-            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+            const uint32_t dst = map_rank(my_recv + (uint32_t)(c0 - q * slice) * 4u, (uint32_t)q);
+            const uint32_t bar = map_rank(my_bar, (uint32_t)q);
+            st_async4(dst, v[0], v[1], v[2], v[3], bar);
+            st_async4(dst + 16u, v[4], v[5], v[6], v[7], bar);
         }
-        cluster.sync();
+        if (!__syncthreads_and(mbar_wait_cluster(&recv_bar, 0, a.err))) bail = true;
+    }
+    if (bail) {  // a wait gave up (error flag set): release TMEM and leave
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) tmem_dealloc(tmem, NT);
+        return;
     }
     const bool even = (n & 1) == 0;
     for (int c0 = my_begin; c0 < my_begin + my_cols; c0 += 4) {
@@ -572,6 +636,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
         } else {
 #pragma unroll
             for (int j = 0; j < 4; j++) v[j] = 0.0f;
+        }
+        if (a.norm_gain) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] *= inv_rms[c0 + j];
         }
         // Epilogue of the group; every global load of the group comes before its stores.
         if (EPI == kEpiLogits) {
@@ -703,20 +771,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
 // Allow the kernel the largest dynamic shared memory the device offers next to its static
 // shared memory (per kernel and device, once).
 template <class K>
-void tc_ensure_smem(K kernel) {
+int tc_ensure_smem(K kernel) {
     static std::mutex mu;
-    static std::set<std::pair<const void*, int>> done;
+    static std::map<std::pair<const void*, int>, int> done;
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     auto key = std::make_pair((const void*)kernel, dev);
-    if (done.count(key)) return;
+    auto it = done.find(key);
+    if (it != done.end()) return it->second;
     cudaFuncAttributes fa;
     int optin = 0;
     cudaFuncGetAttributes(&fa, kernel);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
-    done.insert(key);
+    const int budget = optin - (int)fa.sharedSizeBytes;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, budget);
+    done[key] = budget;
+    return budget;
 }
 
 using TcKernel = void (*)(GemmArgs, Epilogue, SplitArgs);
@@ -768,21 +839,29 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
         default: kernel = tc_gemm_kernel<NT, false, kEpiStore>; break;
         }
     }
-    tc_ensure_smem(kernel);
-    // Stages and shared memory for a split: a stage per chunk up to the limit; the
-    // partial accumulators of a split are later received in the stage memory; the
-    // RMSNorm gain slice of the CTA's chunks sits behind both.
+    const int budget = tc_ensure_smem(kernel);
+    // Stages and shared memory for a split: a stage per chunk when all of a CTA's chunks
+    // fit (the receive buffer of a split, padded if there is room, and the RMSNorm gain
+    // slice next to them), else a 2-stage ring: its loads run one chunk ahead in registers,
+    // and the small footprint lets two CTAs share an SM.
     auto plan = [&](int ks, SplitArgs* sp) {
         const int per_cta = (chunks + ks - 1) / ks;
-        int max_st = TcSmem<NT>::MAX_STAGES;
-        while (max_st > TC_STAGES && max_st * TcSmem<NT>::STAGE > 200 * 1024) max_st--;
         sp->ksplit = ks;
-        // a ring (more chunks than stages) keeps 2 stages: its loads run one chunk ahead in
-        // registers, and the smaller footprint lets two CTAs share an SM
-        sp->stages = per_cta > max_st ? TC_STAGES : std::max(TC_STAGES, per_cta);
-        const int park = ks > 1 ? (NT + 4 * ks) * TC_M * 4 : 0;
-        sp->gain_off = std::max(sp->stages * TcSmem<NT>::STAGE, park);
-        return sp->gain_off + (a.norm_gain ? sp->stages * TC_KC * 4 : 0);
+        auto layout = [&](int stages, int pad) {
+            sp->stages = stages;
+            sp->recv_pad = pad;
+            sp->recv_off = stages * TcSmem<NT>::STAGE;
+            sp->gain_off = sp->recv_off + (ks > 1 ? (NT + pad * ks) * TC_M * 4 : 0);
+            return sp->gain_off + (a.norm_gain ? stages * TC_KC * 4 : 0);
+        };
+        if (per_cta <= TcSmem<NT>::MAX_STAGES) {
+            const int st = std::max(TC_STAGES, per_cta);
+            for (int pad = 4; pad >= 0; pad -= 4) {
+                const int bytes = layout(st, pad);
+                if (bytes <= budget) return bytes;
+            }
+        }
+        return layout(TC_STAGES, 4);
     };
     // Fill the GPU: when the tiles alone are fewer than the SMs, split K across the CTAs
     // of a cluster (power of two up to 8, at most one split per chunk, NT/ksplit >= 8), but
