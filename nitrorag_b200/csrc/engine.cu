@@ -74,6 +74,7 @@ Engine::~Engine() {
     cudaSetDevice(cfg_.device);
     if (stream_) cudaStreamSynchronize(stream_);
     cudaFree(w_.base);
+    cudaFree(w_.tbase);
     cudaFree(kpool_);
     cudaFree(vpool_);
     cudaFree(d_x_);
@@ -205,6 +206,37 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
                   (float*)hp(w_.w2_s) + (int64_t)l * D * (H / 32), [](int r) { return r; });
     }
     NR_CUDA(cudaMemcpy(w_.base, host.data(), total, cudaMemcpyHostToDevice));
+
+    // tiled hi/lo copies for the tensor-core path (made on the device from the above)
+    const char* tiled_env = getenv("NITRO_TILED_WEIGHTS");
+    if (!(tiled_env && tiled_env[0] == '0') && D % 64 == 0 && H % 64 == 0) {
+        w_.qkv_t_layer = align256(tc_tiled_weight_bytes(NQKV, D));
+        w_.wo_t_layer = align256(tc_tiled_weight_bytes(D, D));
+        w_.w13_t_layer = align256(tc_tiled_weight_bytes(2 * H, D));
+        w_.w2_t_layer = align256(tc_tiled_weight_bytes(D, H));
+        const size_t cls = align256(tc_tiled_weight_bytes(c.vocab, D));
+        w_.tbytes = (size_t)L * (w_.qkv_t_layer + w_.wo_t_layer + w_.w13_t_layer + w_.w2_t_layer) + cls;
+        NR_CUDA(cudaMalloc(&w_.tbase, w_.tbytes));
+        uint8_t* p = (uint8_t*)w_.tbase;
+        w_.qkv_t = p; p += (size_t)L * w_.qkv_t_layer;
+        w_.wo_t = p; p += (size_t)L * w_.wo_t_layer;
+        w_.w13_t = p; p += (size_t)L * w_.w13_t_layer;
+        w_.w2_t = p; p += (size_t)L * w_.w2_t_layer;
+        w_.cls_t = p;
+        for (int l = 0; l < L; l++) {
+            tc_tile_weights(w_.qkv_q + (int64_t)l * NQKV * D, w_.qkv_s + (int64_t)l * NQKV * (D / 32), nullptr, NQKV, D,
+                            w_.qkv_t + l * w_.qkv_t_layer, stream_);
+            tc_tile_weights(w_.wo_q + (int64_t)l * D * D, w_.wo_s + (int64_t)l * D * (D / 32), nullptr, D, D,
+                            w_.wo_t + l * w_.wo_t_layer, stream_);
+            tc_tile_weights(w_.w13_q + (int64_t)l * 2 * H * D, w_.w13_s + (int64_t)l * 2 * H * (D / 32), nullptr, 2 * H,
+                            D, w_.w13_t + l * w_.w13_t_layer, stream_);
+            tc_tile_weights(w_.w2_q + (int64_t)l * D * H, w_.w2_s + (int64_t)l * D * (H / 32), nullptr, D, H,
+                            w_.w2_t + l * w_.w2_t_layer, stream_);
+        }
+        tc_tile_weights(nullptr, nullptr, w_.emb, c.vocab, D, w_.cls_t, stream_);
+        NR_CUDA(cudaStreamSynchronize(stream_));
+        NR_CUDA(cudaGetLastError());
+    }
     return NR_OK;
 }
 
@@ -272,6 +304,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g.x = d_x_; g.ldx = D; g.norm_gain = w_.rms_att + (int64_t)l * D;
         g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
         g.M = M; g.N = NQKV; g.K = D; g.kbegin = faithful ? D - 32 : 0;
+        if (w_.qkv_t && !faithful) g.wt = w_.qkv_t + l * w_.qkv_t_layer;
         if (ss) { g.ss_in = d_ss_; g.ss_parts = ss_parts; g.ss_ld = max_rows_; }
         Epilogue e;
         e.kind = kEpiQKV; e.q_out = d_q_; e.kpool = kpool_; e.vpool = vpool_; e.geom = geom_; e.layer = l;
@@ -303,6 +336,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         go.err = d_err_;
         go.x = d_att_; go.ldx = D; go.wq = w_.wo_q + (int64_t)l * D * D; go.ws = w_.wo_s + (int64_t)l * D * (D / 32);
         go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
+        if (w_.wo_t && !faithful) go.wt = w_.wo_t + l * w_.wo_t_layer;
         Epilogue eo;
         eo.kind = kEpiResidual; eo.out = d_x_; eo.ldo = D;
         if (ss) { eo.ss_out = d_ss_; eo.ss_ld = max_rows_; }
@@ -313,6 +347,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g13.x = d_x_; g13.ldx = D; g13.norm_gain = w_.rms_ffn + (int64_t)l * D;
         g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
         g13.M = M; g13.N = 2 * H; g13.K = D; g13.kbegin = faithful ? D - 32 : 0;
+        if (w_.w13_t && !faithful) g13.wt = w_.w13_t + l * w_.w13_t_layer;
         if (ss) { g13.ss_in = d_ss_; g13.ss_parts = ss_parts; g13.ss_ld = max_rows_; }
         Epilogue e13;
         e13.kind = kEpiSwiGLU; e13.out = d_h_; e13.ldo = H;
@@ -322,6 +357,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g2.err = d_err_;
         g2.x = d_h_; g2.ldx = H; g2.wq = w_.w2_q + (int64_t)l * D * H; g2.ws = w_.w2_s + (int64_t)l * D * (H / 32);
         g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
+        if (w_.w2_t && !faithful) g2.wt = w_.w2_t + l * w_.w2_t_layer;
         Epilogue e2;
         e2.kind = kEpiResidual; e2.out = d_x_; e2.ldo = D;
         if (ss) { e2.ss_out = d_ss_; e2.ss_ld = max_rows_; }
@@ -364,6 +400,7 @@ int Engine::forward_prefill(const Sequence& seq, const int* tokens, int T, int s
     GemmArgs gl;
     gl.err = d_err_;
     gl.x = d_x_ + (int64_t)(T - 1) * c.dim; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
+    gl.wt = w_.cls_t;
     gl.M = 1; gl.N = c.vocab; gl.K = c.dim;
     Epilogue el;
     el.kind = kEpiLogits; el.out = logits_out ? d_logits_ : nullptr; el.ldo = c.vocab; el.argmax_keys = d_keys_;
@@ -442,6 +479,7 @@ void Engine::enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logi
     GemmArgs gl;
     gl.err = d_err_;
     gl.x = d_x_; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
+    gl.wt = w_.cls_t;
     gl.M = B; gl.N = c.vocab; gl.K = c.dim;
     if (use_ss(B)) { gl.ss_in = d_ss_; gl.ss_parts = (c.dim + 127) / 128; gl.ss_ld = max_rows_; }
     Epilogue el;

@@ -40,6 +40,14 @@ struct DeviceWeights {
     int8_t* w2_q = nullptr;  float* w2_s = nullptr;   // [L][dim][hidden]
     void* base = nullptr;
     size_t bytes = 0;
+    // The projection weights once more, pre-split into bf16 hi/lo tiles for the tensor-core
+    // kernel (tc_tile_weights; 4 bytes per weight): per layer, then the classifier.  Null
+    // when disabled (NITRO_TILED_WEIGHTS=0); the kernel then converts q * scale itself.
+    uint8_t* qkv_t = nullptr; uint8_t* wo_t = nullptr; uint8_t* w13_t = nullptr; uint8_t* w2_t = nullptr;
+    uint8_t* cls_t = nullptr;
+    size_t qkv_t_layer = 0, wo_t_layer = 0, w13_t_layer = 0, w2_t_layer = 0;
+    void* tbase = nullptr;
+    size_t tbytes = 0;
 };
 
 // Kernel classes timed by the engine's optional per-launch CUDA-event profiling.

@@ -49,6 +49,7 @@ constexpr int TC_KC = 64;     // K elements per pipeline stage
 constexpr int TC_STAGES = 2;      // pipeline stages of the 128/256-token tiles
 constexpr int TC_MAX_STAGES = 4;  // 64-token tiles stage up to 4 chunks
 constexpr int TC_THREADS = 256;  // two warpgroups
+constexpr uint32_t TC_TILE_BYTES = 2u * TC_M * TC_KC * 2u;  // hi + lo halves of one 128 x 64 weight tile
 
 // ------------------------------------------------------------------ tcgen05 wrappers
 // Shared-memory matrix descriptor, K-major without swizzle: core matrices of 8 rows x 16 B
@@ -320,6 +321,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     using S = TcSmem<NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t mma_bar[TC_MAX_STAGES];
+    __shared__ uint64_t w_bar[TC_MAX_STAGES];  // tiled weights: the stage's bulk copy has landed
     __shared__ uint64_t done_bar;
     __shared__ uint64_t recv_bar;  // split K: the partials of this CTA's slice have all arrived
     __shared__ uint32_t tmem_slot;
@@ -363,7 +365,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
         tmem_relinquish();
     }
     if (tid == 0) {
-        for (int st = 0; st < TC_MAX_STAGES; st++) mbar_init(&mma_bar[st], 1);
+        for (int st = 0; st < TC_MAX_STAGES; st++) {
+            mbar_init(&mma_bar[st], 1);
+            mbar_init(&w_bar[st], 1);
+        }
         mbar_init(&done_bar, 1);
         mbar_init(&recv_bar, 1);
         if (ks > 1) mbar_arrive_expect_tx(&recv_bar, (uint32_t)(TC_M * NT * 4));  // ks partials of slice x 128 rows
@@ -374,7 +379,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     if (ks > 1) cluster_arrive_release();
     // ---- before the grid dependency: everything that does not depend on the previous kernel
     WRegs<F32W> cur;
-    if (staged) {
+    // tiled weights: one bulk copy per chunk (all of them when staged, the first for a ring)
+    auto fetch_tile = [&](int i, int st) {
+        mbar_arrive_expect_tx(&w_bar[st], TC_TILE_BYTES);
+        bulk_g2s(stage_ptr(st, 0), a.wt + ((size_t)n_tile * nchunk_total + c_first + i) * TC_TILE_BYTES, TC_TILE_BYTES,
+                 &w_bar[st]);
+    };
+    if (a.wt) {
+        if (tid == 0)
+            for (int i = 0; i < (staged ? nch : min(nch, 1)); i++) fetch_tile(i, i);
+        if (staged && a.norm_gain)
+            for (int t = tid; t < nch * (TC_KC / 4); t += TC_THREADS)
+                reinterpret_cast<float4*>(gain_s)[t] =
+                    __ldg(reinterpret_cast<const float4*>(a.norm_gain + c_first * TC_KC) + t);
+    } else if (staged) {
         if (a.norm_gain)
             for (int t = tid; t < nch * (TC_KC / 4); t += TC_THREADS)
                 reinterpret_cast<float4*>(gain_s)[t] =
@@ -485,6 +503,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
 
     bool bail = false;
+    bool wfail = false;  // thread 0: a tiled-weight copy did not land in time
     if (staged) {
         for (int i = 0; i < nch; i++) {
             const float* g = a.norm_gain ? gain_s + i * TC_KC : nullptr;
@@ -506,11 +525,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             fence_async_smem();
             __syncthreads();
             if (tid == 0) {
+                if (a.wt && !wfail && !mbar_wait(&w_bar[i], 0, a.err)) wfail = true;
                 tc_fence_after();
-                issue_chunk_mmas(tmem, idesc, stage_ptr(i, 0), stage_ptr(i, 1), stage_ptr(i, 2), stage_ptr(i, 3), i == 0);
+                if (!wfail)
+                    issue_chunk_mmas(tmem, idesc, stage_ptr(i, 0), stage_ptr(i, 1), stage_ptr(i, 2), stage_ptr(i, 3), i == 0);
             }
         }
         if (tid == 0 && nch > 0) umma_commit(&done_bar);
+    } else if (a.wt) {
+        // more chunks than stages, tiled weights: a ring in which the tile of chunk it + 1
+        // is requested as soon as the MMAs that last read its stage are done
+        for (int it = 0; it < nch; it++) {
+            const int st = it % stages;
+            const int use = it / stages;
+            const int k0 = (c_first + it) * TC_KC;
+            if (it + 1 < nch) {
+                const int st1 = (it + 1) % stages, use1 = (it + 1) / stages;
+                const bool free1 = use1 == 0 || mbar_wait(&mma_bar[st1], (use1 - 1) & 1, a.err);
+                if (!__syncthreads_and(free1)) { bail = true; break; }
+                if (tid == 0) fetch_tile(it + 1, st1);
+            }
+            // stage st was last read by chunk it - stages, waited for one iteration ago
+            stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2), stage_ptr(st, 3),
+                              tid);
+            fence_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                if (!wfail && !mbar_wait(&w_bar[st], use & 1, a.err)) wfail = true;
+                tc_fence_after();
+                if (!wfail)
+                    issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
+                umma_commit(&mma_bar[st]);  // always, so the stage's phases stay in step
+            }
+        }
+        if (tid == 0 && !bail && nch > 0) umma_commit(&done_bar);
     } else {
         // more chunks than stages: a ring, the next chunk's weight loads one chunk ahead
         for (int it = 0; it < nch; it++) {
@@ -577,7 +625,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     }
     {   // every MMA done (and inv_rms published)
         const bool got = (nch > 0 && !bail) ? mbar_wait(&done_bar, 0, a.err) : true;
-        if (!__syncthreads_and(got)) bail = true;
+        if (!__syncthreads_and(got && !wfail)) bail = true;
     }
     tc_fence_after();
     grid_dependents_launch();
@@ -880,7 +928,44 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     launch_ex(kernel, dim3(ksplit, n_tiles, m_tiles), dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
 }
 
+// Pre-split weights: one thread per (row, 8-wide K group) writes the bf16 hi/lo halves of
+// w = q * scale (or w) at the place the kernel's staging would put them; tile (t, c) of
+// the output is [hi 16 KB][lo 16 KB] for rows 128t.. and K chunk c.
+__global__ void tile_weights_kernel(const int8_t* q, const float* scales, const float* wf, int N, int K, uint8_t* out) {
+    const int groups = K / 8;
+    const int64_t rows = (int64_t)((N + TC_M - 1) / TC_M) * TC_M;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= rows * groups) return;
+    const int n = (int)(t / groups), g = (int)(t % groups);
+    float w[8];
+    if (n < N) {
+        if (wf) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) w[j] = wf[(int64_t)n * K + g * 8 + j];
+        } else {
+            const float sc = scales[(int64_t)n * (K / 32) + g / 4];
+#pragma unroll
+            for (int j = 0; j < 8; j++) w[j] = (float)q[(int64_t)n * K + g * 8 + j] * sc;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) w[j] = 0.0f;
+    }
+    uint8_t* tile = out + ((int64_t)(n / TC_M) * (K / TC_KC) + g / 8) * TC_TILE_BYTES;
+    const uint32_t o = core_off(n % TC_M, g % 8);
+    split_store8(w, tile + o, tile + TC_TILE_BYTES / 2 + o);
+}
+
 }  // namespace
+
+size_t tc_tiled_weight_bytes(int N, int K) {
+    return (size_t)((N + TC_M - 1) / TC_M) * (size_t)(K / TC_KC) * TC_TILE_BYTES;
+}
+
+void tc_tile_weights(const int8_t* q, const float* scales, const float* wf, int N, int K, uint8_t* out, cudaStream_t s) {
+    const int64_t n = (int64_t)((N + TC_M - 1) / TC_M) * TC_M * (K / 8);
+    tile_weights_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, scales, wf, N, K, out);
+}
 
 bool tc_gemm_supported(const GemmArgs& a) { return a.K % TC_KC == 0 && a.N % 2 == 0 && a.M > 8; }
 

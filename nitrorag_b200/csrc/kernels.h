@@ -57,6 +57,10 @@ struct GemmArgs {
     const float* ss_in = nullptr;
     int ss_parts = 0, ss_ld = 0;
     int* err = nullptr;   // device error flag for bounded waits
+    // Optional: the same weights pre-split into bf16 hi/lo halves in the tensor-core
+    // kernel's shared-memory tile layout (tc_tile_weights); the kernel then fetches each
+    // 128-row x 64-column tile with one bulk copy instead of converting q * scale itself.
+    const uint8_t* wt = nullptr;
 };
 
 // M <= 8: CUDA-core matvec; M > 8 with K % 64 == 0: tcgen05 GEMM (gemm_tc.cu); otherwise
@@ -66,6 +70,11 @@ bool tc_gemm_supported(const GemmArgs& a);
 // Whether launch_gemm takes the tensor-core path for this shape.
 bool gemm_uses_tc(int M, int N, int K);
 void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s);
+// Bytes of the tiled hi/lo copy of an [N][K] weight matrix (K % 64 == 0; rows padded to
+// a multiple of 128 with zeros), and the kernel that writes it from Q8_0 (q, scales) or
+// fp32 (wf) weights.
+size_t tc_tiled_weight_bytes(int N, int K);
+void tc_tile_weights(const int8_t* q, const float* scales, const float* wf, int N, int K, uint8_t* out, cudaStream_t s);
 
 // Decode attention over paged KV for one layer (see attention.cu).
 struct DecodeAttnArgs {
