@@ -303,10 +303,14 @@ def engine_arm(args, rank, world, local_rank):
     time.sleep(0.3)
     launches0 = eng.stats()["kernel_launches"]
     v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.profile_range:  # lets `ncu --profile-from-start off` capture exactly these launches
+        torch.cuda.profiler.start()
     v0.record(stream)
     eng.replay_decode(K)
     v1.record(stream)
     torch.cuda.synchronize()
+    if args.profile_range:
+        torch.cuda.profiler.stop()
     launches = eng.stats()["kernel_launches"] - launches0
     clocks = sampler.stop()
     value_ms = max_over_ranks(v0.elapsed_time(v1))
@@ -374,6 +378,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="mark the timed device-resident replays as the CUDA profiler range")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -48,7 +48,9 @@ constexpr int TC_M = 128;     // weight rows per CTA = UMMA M
 constexpr int TC_KC = 64;     // K elements per pipeline stage
 constexpr int TC_STAGES = 2;      // pipeline stages of the 128/256-token tiles
 constexpr int TC_MAX_STAGES = 4;  // 64-token tiles stage up to 4 chunks
-constexpr int TC_THREADS = 256;  // two warpgroups
+constexpr int TC_WORKERS = 256;              // staging and epilogue threads: two warpgroups
+constexpr int TC_THREADS = TC_WORKERS + 32;  // + one warp that issues the MMAs
+constexpr int kIssuerWarp = TC_WORKERS / 32;
 constexpr uint32_t TC_TILE_BYTES = 2u * TC_M * TC_KC * 2u;  // hi + lo halves of one 128 x 64 weight tile
 
 // ------------------------------------------------------------------ tcgen05 wrappers
@@ -118,6 +120,14 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Named CTA barriers between the staging warps (arrive) and the MMA-issuing warp (sync).
+__device__ __forceinline__ void named_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // Split cluster barrier: arrive (publishing this thread's earlier memory operations) and,
@@ -292,7 +302,7 @@ __device__ __forceinline__ void stage_x16(const float4* x4, const float* g, bool
 template <int NT>
 __device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* g, int m_base, int k0, uint8_t* b_hi,
                                               uint8_t* b_lo, int tid) {
-    for (int u = tid; u < NT * 4; u += TC_THREADS) {
+    for (int u = tid; u < NT * 4; u += TC_WORKERS) {
         const int r = u >> 2, kq = u & 3, m = m_base + r;
         float4 x4[4];
         if (m < a.M) {
@@ -317,7 +327,7 @@ __device__ __forceinline__ void issue_chunk_mmas(uint32_t tmem, uint32_t idesc, 
 }
 
 template <int NT, bool F32W, int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
+__global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
     using S = TcSmem<NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t mma_bar[TC_MAX_STAGES];
@@ -330,7 +340,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     __shared__ float red_ss[4][EPI == kEpiResidual ? NT : 1];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row = tid & (TC_M - 1), wg = tid >> 7;  // weight row / TMEM lane, warpgroup = K half
+    const bool worker = warp < kIssuerWarp;  // else: the warp whose lane 0 issues the MMAs
+    const int row = tid & (TC_M - 1), wg = (tid >> 7) & 1;  // weight row / TMEM lane, warpgroup = K half
     // grid (ksplit, n_tiles, m_tiles); the ksplit CTAs of one tile form one cluster
     const int split = blockIdx.x, n_tile = blockIdx.y, m_tile = blockIdx.z;
     const int n_base = n_tile * TC_M, m_base = m_tile * NT;
@@ -387,12 +398,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     };
     if (a.wt) {
         if (tid == 0)
-            for (int i = 0; i < (staged ? nch : min(nch, 1)); i++) fetch_tile(i, i);
+            for (int i = 0; i < min(nch, stages); i++) fetch_tile(i, i);
         if (staged && a.norm_gain)
             for (int t = tid; t < nch * (TC_KC / 4); t += TC_THREADS)
                 reinterpret_cast<float4*>(gain_s)[t] =
                     __ldg(reinterpret_cast<const float4*>(a.norm_gain + c_first * TC_KC) + t);
-    } else if (staged) {
+    } else if (staged && worker) {
         if (a.norm_gain)
             for (int t = tid; t < nch * (TC_KC / 4); t += TC_THREADS)
                 reinterpret_cast<float4*>(gain_s)[t] =
@@ -411,7 +422,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
             stage_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32, stage_ptr(0, 0), stage_ptr(0, 1), row, wg);
         }
-    } else if (nch > 0) {
+    } else if (nch > 0 && worker) {
         load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
     }
     // QKV: where this thread's row goes (q row, or a K/V pool column) and the token
@@ -463,7 +474,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     // requested before the RMS partial sums so the round trips overlap
     float4 xr[S::MAX_STAGES][NT == 64 ? 4 : 1];
     const int ur = tid >> 2, ukq = tid & 3;  // NT == 64: this thread's activation unit
-    if (NT == 64 && staged) {
+    if (NT == 64 && staged && worker) {
 #pragma unroll
         for (int i = 0; i < S::MAX_STAGES; i++) {
             if (i < nch && m_base + ur < a.M) {
@@ -488,7 +499,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     constexpr int SSP = 8;
     float ssv[SSP];
     const bool ss_pre = NT == 64 && a.norm_gain && a.ss_in && a.ss_parts <= 4 * SSP;
-    if (ss_pre) {
+    if (ss_pre && worker) {
         const int m = m_base + ur;
 #pragma unroll
         for (int i = 0; i < SSP; i++) {
@@ -502,91 +513,76 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     const uint32_t tmem = tmem_slot;
     const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
 
-    bool bail = false;
-    bool wfail = false;  // thread 0: a tiled-weight copy did not land in time
-    if (staged) {
-        for (int i = 0; i < nch; i++) {
-            const float* g = a.norm_gain ? gain_s + i * TC_KC : nullptr;
-            if (NT == 64) {
-                const int m = m_base + ur;
-                float4 x4[4];
+    // Workers convert each chunk's activations (and, without tiled weights in a ring, its
+    // weights) into the chunk's stage and arrive on named barrier 1 + stage; the issuer
+    // warp syncs on it and its lane 0 issues the chunk's MMAs, so MMAs run while the next
+    // chunk is converted.  Every wait is bounded; a thread whose wait gave up still takes
+    // every barrier (skipping its work), so no party is left waiting.
+    bool ok = true;
+    if (worker) {
+        if (staged) {
+            for (int i = 0; i < nch; i++) {
+                const float* g = a.norm_gain ? gain_s + i * TC_KC : nullptr;
+                if (NT == 64) {
+                    const int m = m_base + ur;
+                    float4 x4[4];
 #pragma unroll
-                for (int j = 0; j < 4; j++) x4[j] = xr[0][j];
+                    for (int j = 0; j < 4; j++) x4[j] = xr[0][j];
 #pragma unroll
-                for (int s2 = 1; s2 < S::MAX_STAGES; s2++)
-                    if (i == s2)
+                    for (int s2 = 1; s2 < S::MAX_STAGES; s2++)
+                        if (i == s2)
 #pragma unroll
-                        for (int j = 0; j < 4; j++) x4[j] = xr[s2][j];
-                stage_x16(x4, g ? g + ukq * 16 : nullptr, m < a.M, stage_ptr(i, 2), stage_ptr(i, 3), ur, ukq);
-            } else {
-                stage_chunk_x<NT>(a, g, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
+                            for (int j = 0; j < 4; j++) x4[j] = xr[s2][j];
+                    stage_x16(x4, g ? g + ukq * 16 : nullptr, m < a.M, stage_ptr(i, 2), stage_ptr(i, 3), ur, ukq);
+                } else {
+                    stage_chunk_x<NT>(a, g, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
+                }
+                fence_async_smem();
+                named_arrive(1 + i, TC_THREADS);
             }
-            // chunk i is complete: its MMAs run while the next chunk is converted
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
-                if (a.wt && !wfail && !mbar_wait(&w_bar[i], 0, a.err)) wfail = true;
-                tc_fence_after();
-                if (!wfail)
-                    issue_chunk_mmas(tmem, idesc, stage_ptr(i, 0), stage_ptr(i, 1), stage_ptr(i, 2), stage_ptr(i, 3), i == 0);
+        } else {
+            for (int it = 0; it < nch; it++) {
+                const int st = it % stages, use = it / stages;
+                const int k0 = (c_first + it) * TC_KC;
+                WRegs<F32W> nxt;
+                if (!a.wt && it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
+                // the stage was last read by the MMAs of chunk it - stages
+                if (ok && use > 0 && !mbar_wait(&mma_bar[st], (use - 1) & 1, a.err)) ok = false;
+                if (ok) {
+                    if (!a.wt) stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
+                    stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2),
+                                      stage_ptr(st, 3), tid);
+                }
+                fence_async_smem();
+                named_arrive(1 + st, TC_THREADS);
+                if (!a.wt && it + 1 < nch) cur = nxt;
             }
         }
-        if (tid == 0 && nch > 0) umma_commit(&done_bar);
-    } else if (a.wt) {
-        // more chunks than stages, tiled weights: a ring in which the tile of chunk it + 1
-        // is requested as soon as the MMAs that last read its stage are done
-        for (int it = 0; it < nch; it++) {
-            const int st = it % stages;
-            const int use = it / stages;
-            const int k0 = (c_first + it) * TC_KC;
-            if (it + 1 < nch) {
-                const int st1 = (it + 1) % stages, use1 = (it + 1) / stages;
-                const bool free1 = use1 == 0 || mbar_wait(&mma_bar[st1], (use1 - 1) & 1, a.err);
-                if (!__syncthreads_and(free1)) { bail = true; break; }
-                if (tid == 0) fetch_tile(it + 1, st1);
-            }
-            // stage st was last read by chunk it - stages, waited for one iteration ago
-            stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2), stage_ptr(st, 3),
-                              tid);
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
-                if (!wfail && !mbar_wait(&w_bar[st], use & 1, a.err)) wfail = true;
-                tc_fence_after();
-                if (!wfail)
-                    issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
-                umma_commit(&mma_bar[st]);  // always, so the stage's phases stay in step
-            }
-        }
-        if (tid == 0 && !bail && nch > 0) umma_commit(&done_bar);
     } else {
-        // more chunks than stages: a ring, the next chunk's weight loads one chunk ahead
+        // issuer warp; with tiled weights in a ring, lane 0 also refills each stage with the
+        // tile of chunk it - 1 + stages once the MMAs of chunk it - 1 are done with it
         for (int it = 0; it < nch; it++) {
-            const int st = it % stages;
-            const int use = it / stages;
-            const int k0 = (c_first + it) * TC_KC;
-            WRegs<F32W> nxt;
-            if (it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
-            if (use > 0) {
-                const bool got = mbar_wait(&mma_bar[st], (use - 1) & 1, a.err);
-                if (!__syncthreads_and(got)) { bail = true; break; }
+            const int st = staged ? it : it % stages, use = staged ? 0 : it / stages;
+            if (!staged && a.wt && lane == 0 && ok && it >= 1 && it - 1 + stages < nch) {
+                const int sp_ = (it - 1) % stages;
+                if (mbar_wait(&mma_bar[sp_], ((it - 1) / stages) & 1, a.err)) fetch_tile(it - 1 + stages, sp_);
+                else ok = false;
             }
-            stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
-            stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2), stage_ptr(st, 3),
-                              tid);
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
+            __syncwarp();
+            named_sync(1 + st, TC_THREADS);
+            if (lane == 0) {
+                if (a.wt && ok && !mbar_wait(&w_bar[st], use & 1, a.err)) ok = false;
                 tc_fence_after();
-                issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
-                umma_commit(&mma_bar[st]);
+                if (ok)
+                    issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
+                if (!staged) umma_commit(&mma_bar[st]);  // always, so the stage's phases stay in step
             }
-            if (it + 1 < nch) cur = nxt;
+            __syncwarp();
         }
-        if (tid == 0 && !bail && nch > 0) umma_commit(&done_bar);  // completes after every MMA above
+        if (lane == 0 && nch > 0) umma_commit(&done_bar);  // completes after every MMA above
     }
     // 1/rms per token while the MMAs run
-    if (a.norm_gain) {
+    if (a.norm_gain && worker) {
         if (ss_pre) {
             float ss = 0.0f;
 #pragma unroll
@@ -597,7 +593,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
         } else if (a.ss_in) {
             // sums of squares published by the producer of x, one per 128-feature slice;
             // four threads per token, joined by two shuffles
-            for (int u = tid; u < NT * 4; u += TC_THREADS) {
+            for (int u = tid; u < NT * 4; u += TC_WORKERS) {
                 const int r = u >> 2, p0 = u & 3, m = m_base + r;
                 float ss = 0.0f;
                 if (m < a.M)
@@ -607,7 +603,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
                 if (p0 == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
             }
         } else {
-            const int nw = TC_THREADS / 32;
+            const int nw = TC_WORKERS / 32;
             for (int r = warp; r < NT; r += nw) {
                 const int m = m_base + r;
                 float ss = 0.0f;
@@ -623,9 +619,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             }
         }
     }
+    bool bail = false;
     {   // every MMA done (and inv_rms published)
-        const bool got = (nch > 0 && !bail) ? mbar_wait(&done_bar, 0, a.err) : true;
-        if (!__syncthreads_and(got && !wfail)) bail = true;
+        const bool got = nch > 0 ? mbar_wait(&done_bar, 0, a.err) : true;
+        if (!__syncthreads_and(got && ok)) bail = true;
     }
     tc_fence_after();
     grid_dependents_launch();
@@ -640,7 +637,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
     const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const int rst = slice + sp.recv_pad;  // padded: the 8 rows of a 16-byte phase hit 8 bank groups
     float* recv = reinterpret_cast<float*>(smem + sp.recv_off);
-    if (ks > 1) {
+    if (ks > 1 && !worker) cluster_wait_acquire();
+    if (ks > 1 && worker) {
         const int half = NT / 2;
         const uint32_t my_recv = smem_addr(recv + ((size_t)rank * TC_M + row) * rst);
         const uint32_t my_bar = smem_addr(&recv_bar);
@@ -659,8 +657,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
             st_async4(dst, v[0], v[1], v[2], v[3], bar);
             st_async4(dst + 16u, v[4], v[5], v[6], v[7], bar);
         }
-        if (!__syncthreads_and(mbar_wait_cluster(&recv_bar, 0, a.err))) bail = true;
     }
+    if (ks > 1 && !__syncthreads_and(mbar_wait_cluster(&recv_bar, 0, a.err))) bail = true;
     if (bail) {  // a wait gave up (error flag set): release TMEM and leave
         tc_fence_before();
         __syncthreads();
@@ -668,7 +666,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(GemmArgs a, Epil
         return;
     }
     const bool even = (n & 1) == 0;
-    for (int c0 = my_begin; c0 < my_begin + my_cols; c0 += 4) {
+    for (int c0 = my_begin; worker && c0 < my_begin + my_cols; c0 += 4) {
         const int jb = c0 - my_begin;  // index of the group's first column among this thread's
         float v[4];
         if (ks > 1) {
