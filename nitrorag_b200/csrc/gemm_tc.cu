@@ -100,6 +100,22 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// 32 consecutive fp32 columns of this thread's TMEM lane (one load, one wait).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // 4 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
     uint32_t r[4];
@@ -642,20 +658,24 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
         const int half = NT / 2;
         const uint32_t my_recv = smem_addr(recv + ((size_t)rank * TC_M + row) * rst);
         const uint32_t my_bar = smem_addr(&recv_bar);
-        for (int c0 = wg * half; c0 < (wg + 1) * half; c0 += 8) {
-            float v[8];
+        for (int c32 = wg * half; c32 < (wg + 1) * half; c32 += 32) {
+            float v[32];
             if (nch > 0 && !bail) {
-                tmem_ld8(tl + c0, v);
+                tmem_ld32(tl + c32, v);
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; j++) v[j] = 0.0f;
+                for (int j = 0; j < 32; j++) v[j] = 0.0f;
             }
-            if (c0 == wg * half) cluster_wait_acquire();  // every peer's receive barrier is initialised
-            const int q = c0 / slice;
-            const uint32_t dst = map_rank(my_recv + (uint32_t)(c0 - q * slice) * 4u, (uint32_t)q);
-            const uint32_t bar = map_rank(my_bar, (uint32_t)q);
-            st_async4(dst, v[0], v[1], v[2], v[3], bar);
-            st_async4(dst + 16u, v[4], v[5], v[6], v[7], bar);
+            if (c32 == wg * half) cluster_wait_acquire();  // every peer's receive barrier is initialised
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int c0 = c32 + 8 * u;
+                const int q = c0 / slice;
+                const uint32_t dst = map_rank(my_recv + (uint32_t)(c0 - q * slice) * 4u, (uint32_t)q);
+                const uint32_t bar = map_rank(my_bar, (uint32_t)q);
+                st_async4(dst, v[8 * u], v[8 * u + 1], v[8 * u + 2], v[8 * u + 3], bar);
+                st_async4(dst + 16u, v[8 * u + 4], v[8 * u + 5], v[8 * u + 6], v[8 * u + 7], bar);
+            }
         }
     }
     if (ks > 1 && !__syncthreads_and(mbar_wait_cluster(&recv_bar, 0, a.err))) bail = true;
