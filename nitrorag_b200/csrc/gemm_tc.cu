@@ -352,8 +352,11 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     __shared__ uint64_t recv_bar;  // split K: the partials of this CTA's slice have all arrived
     __shared__ uint32_t tmem_slot;
     __shared__ float inv_rms[NT];
-    __shared__ unsigned long long red_key[4][EPI == kEpiLogits ? NT : 1];
-    __shared__ float red_ss[4][EPI == kEpiResidual ? NT : 1];
+    // per-warp-quarter column reductions of the epilogue (argmax keys, sums of squares) in
+    // stage memory, which is free once every MMA has completed
+    unsigned long long* red_key = reinterpret_cast<unsigned long long*>(smem);  // [4][NT]
+    float* red_ss = reinterpret_cast<float*>(smem + 4 * NT * 8);                 // [4][NT]
+    const int epi = EPI >= 0 ? EPI : e.kind;  // EPI < 0: the epilogue kind is read at run time
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool worker = warp < kIssuerWarp;  // else: the warp whose lane 0 issues the MMAs
@@ -444,13 +447,13 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     // QKV: where this thread's row goes (q row, or a K/V pool column) and the token
     // positions, pages and rotary factors of its first PRE epilogue columns (the decode
     // descriptors are written before the step's first kernel)
-    int pos_pre[EPI == kEpiQKV ? PRE : 1], page_pre[EPI == kEpiQKV ? PRE : 1];
-    float fcr_pre[EPI == kEpiQKV ? PRE : 1], fci_pre[EPI == kEpiQKV ? PRE : 1];
+    int pos_pre[EPI == kEpiQKV || EPI < 0 ? PRE : 1], page_pre[EPI == kEpiQKV || EPI < 0 ? PRE : 1];
+    float fcr_pre[EPI == kEpiQKV || EPI < 0 ? PRE : 1], fci_pre[EPI == kEpiQKV || EPI < 0 ? PRE : 1];
     const int np = n & ~1;
     int qkv_kind = 3, fbase = 0;  // 0 q, 1 k, 2 v, 3 none; rotary pair index of the row
     int64_t row_off = 0;          // q: column in q_out; k/v: offset inside page 0's tile row
     float* pool = nullptr;
-    if (EPI == kEpiQKV) {
+    if (epi == kEpiQKV) {
         const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
         if (n < a.N) {
             if (np < D) {
@@ -501,8 +504,8 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             }
         }
     }
-    float xo_pre[EPI == kEpiResidual ? PRE : 1];
-    if (EPI == kEpiResidual) {
+    float xo_pre[EPI == kEpiResidual || EPI < 0 ? PRE : 1];
+    if (epi == kEpiResidual) {
 #pragma unroll
         for (int j = 0; j < PRE; j++) {
             const int m = m_base + my_begin + j;
@@ -708,7 +711,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             for (int j = 0; j < 4; j++) v[j] *= inv_rms[c0 + j];
         }
         // Epilogue of the group; every global load of the group comes before its stores.
-        if (EPI == kEpiLogits) {
+        if (epi == kEpiLogits) {
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const int c = c0 + j, m = m_base + c;
@@ -720,9 +723,9 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                     unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
                     key = k2 > key ? k2 : key;
                 }
-                if (lane == 0) red_key[warp & 3][c] = key;
+                if (lane == 0) red_key[(warp & 3) * NT + c] = key;
             }
-        } else if (EPI == kEpiResidual) {
+        } else if (epi == kEpiResidual) {
             float xo[4];
             if (jb == 0 || jb == 4) {  // fetched right after the grid dependency wait
 #pragma unroll
@@ -742,10 +745,10 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 if (ok) e.out[(int64_t)m * e.ldo + n] = xn;
                 if (e.ss_out) {  // this tile's share of the next RMSNorm's sum of squares
                     const float sq = warp_sum(xn * xn);
-                    if (lane == 0) red_ss[warp & 3][c] = sq;
+                    if (lane == 0) red_ss[(warp & 3) * NT + c] = sq;
                 }
             }
-        } else if (EPI == kEpiStore) {
+        } else if (epi == kEpiStore) {
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const int m = m_base + c0 + j;
@@ -755,7 +758,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             float other[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) other[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);  // pair partner's row
-            if (EPI == kEpiSwiGLU) {
+            if (epi == kEpiSwiGLU) {
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int m = m_base + c0 + j;
@@ -765,7 +768,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                         e.out[(int64_t)m * e.ldo + (n >> 1)] = hgate * other[j];
                     }
                 }
-            } else if (EPI == kEpiQKV) {
+            } else if (epi == kEpiQKV) {
                 const int D = e.dim, hd = e.head_dim;
                 const bool rope = qkv_kind < 2;
                 int pos[4], page[4];
@@ -811,21 +814,21 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             }
         }
     }
-    if (EPI == kEpiLogits || (EPI == kEpiResidual && e.ss_out)) {
+    if (epi == kEpiLogits || (epi == kEpiResidual && e.ss_out)) {
         __syncthreads();
         for (int cix = fin_begin + tid; cix < fin_begin + fin_cols; cix += TC_THREADS) {
             const int m = m_base + cix;
             if (m >= a.M) continue;
-            if (EPI == kEpiLogits) {
-                unsigned long long best = red_key[0][cix];
+            if (epi == kEpiLogits) {
+                unsigned long long best = red_key[cix];
 #pragma unroll
-                for (int w = 1; w < 4; w++) best = red_key[w][cix] > best ? red_key[w][cix] : best;
+                for (int w = 1; w < 4; w++) best = red_key[w * NT + cix] > best ? red_key[w * NT + cix] : best;
                 if (best != 0ull) {
                     unsigned long long* slot = e.argmax_keys + m;
                     if (best > *(volatile unsigned long long*)slot) atomicMax(slot, best);
                 }
             } else {
-                e.ss_out[(int64_t)n_tile * e.ss_ld + m] = red_ss[0][cix] + red_ss[1][cix] + red_ss[2][cix] + red_ss[3][cix];
+                e.ss_out[(int64_t)n_tile * e.ss_ld + m] = red_ss[cix] + red_ss[NT + cix] + red_ss[2 * NT + cix] + red_ss[3 * NT + cix];
             }
         }
     }
@@ -898,12 +901,10 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     if (a.wf) {
         kernel = tc_gemm_kernel<NT, true, kEpiLogits>;
     } else {
-        switch (e.kind) {
-        case kEpiResidual: kernel = tc_gemm_kernel<NT, false, kEpiResidual>; break;
-        case kEpiQKV: kernel = tc_gemm_kernel<NT, false, kEpiQKV>; break;
-        case kEpiSwiGLU: kernel = tc_gemm_kernel<NT, false, kEpiSwiGLU>; break;
-        default: kernel = tc_gemm_kernel<NT, false, kEpiStore>; break;
-        }
+        // one kernel for every Q8 projection kind: the four projections of a layer then
+        // share their instruction-cache footprint (measured ~1.5 % faster per step than a
+        // kernel per kind)
+        kernel = tc_gemm_kernel<NT, false, -1>;
     }
     const int budget = tc_ensure_smem(kernel);
     // Stages and shared memory for a split: a stage per chunk when all of a CTA's chunks
