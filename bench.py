@@ -232,6 +232,232 @@ def workload_config(ctx):
             "parallelism": "replicas (one engine per GPU, no collectives)"}
 
 
+# ------------------------------------------------------------------ other configs
+# The survey's other workloads, one JSON line each (`--workload config1|config3|config4|
+# config5`); the default `decode64` line above is the headline.  All run on one GPU.
+W110_BYTES = 193_932_288          # Q8 projections + fp32 classifier + RMS gains, 110M
+KV110_PER_TOKEN = 12 * 2 * 768 * 4  # K and V of every layer, 110M
+
+
+def _dev_events(torch, stream):
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _profile_classes(eng, n):
+    eng.set_profiling(True)
+    eng.replay_decode(n)
+    kt = eng.kernel_times()
+    eng.set_profiling(False)
+    return {k: (v[0] / n, v[1] // max(n, 1)) for k, v in kt.items()}
+
+
+def run_config1(args):
+    """Config 1: one request, 256-token prompt, 128 greedy tokens (B = 1 decode: the Q8_0
+    matvec path).  value = device-resident decode step at the end of the run;
+    e2e = the 127 decode steps through nr_step."""
+    import torch
+    peak, peak_src = load_peaks()
+    model = synth.cached_model(synth.SHAPE_110M, seed=MODEL_SEED)
+    eng = NitroEngine(model, EngineConfig(total_blocks=64, max_new_tokens=128, max_batch=1, max_prefill_tokens=256,
+                                          device=0))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    prompt = np.random.default_rng(11).integers(0, 32000, 256).astype(np.int32)
+    eng.add_request(0, prompt)
+    t0 = time.perf_counter()
+    eng.step()  # prefill of the whole prompt (budget 256) and the first token
+    prefill_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    n_dec = 0
+    while eng.has_active_requests():
+        r = eng.step()
+        n_dec += r.n_decode
+    e2e_s = time.perf_counter() - t0
+    pos = 256 + 127 - 1  # position of the last decode step (replayed below)
+    eng.replay_decode(args.warmup)
+    torch.cuda.synchronize()
+    e0, e1 = _dev_events(torch, stream)
+    e0.record(stream)
+    eng.replay_decode(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    step_ms = e0.elapsed_time(e1) / args.steps
+    step_bytes = W110_BYTES + (pos + 1) * KV110_PER_TOKEN + KV110_PER_TOKEN
+    prof = _profile_classes(eng, args.steps)
+    per_class_bytes = {"qkv": 12 * 2304 * 768 * 1.125, "wo": 12 * 768 * 768 * 1.125, "w13": 12 * 4096 * 768 * 1.125,
+                       "w2": 12 * 768 * 2048 * 1.125, "logits": 32000 * 768 * 4,
+                       "attention": (pos + 1) * KV110_PER_TOKEN}
+    kernels = {}
+    for k, nb in per_class_bytes.items():
+        ms = prof[k][0]
+        kernels[k] = {"ms_per_step": round(ms, 4), "GB/s": round(nb / (ms * 1e-3) / 1e9, 1),
+                      "frac": round(nb / (ms * 1e-3) / 1e9 / peak, 3)}
+    matvec_bytes = sum(per_class_bytes[k] for k in ("qkv", "wo", "w13", "w2", "logits"))
+    matvec_ms = sum(prof[k][0] for k in ("qkv", "wo", "w13", "w2", "logits"))
+    eng.close()
+    return {"workload": "config1", "metric": "decode tok/s, 1 request (110M Q8_0, 256-token prompt, 128 greedy tokens)",
+            "value": round(1000.0 / step_ms, 1), "unit": "tok/s", "ms_per_step": round(step_ms, 4),
+            "e2e": {"value": round(n_dec / e2e_s, 1), "unit": "tok/s", "decode_steps": n_dec},
+            "prefill_ms": round(1000 * prefill_s, 3),
+            "roofline": {"bound": "hbm", "bytes_per_step": step_bytes,
+                         "achieved": round(step_bytes / (step_ms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / peak, 4), "peak_source": peak_src},
+            "matvec": {"bytes_per_step": int(matvec_bytes), "ms_per_step": round(matvec_ms, 4),
+                       "achieved": round(matvec_bytes / (matvec_ms * 1e-3) / 1e9, 1),
+                       "frac": round(matvec_bytes / (matvec_ms * 1e-3) / 1e9 / peak, 4),
+                       "note": "per-launch CUDA events around every matvec launch (second pass)"},
+            "kernels": kernels, "steps": args.steps}
+
+
+def run_config3(args):
+    """Config 3: 50 requests arriving by a seeded Poisson process (mean 20 req/s), prompts
+    U[64, 512], 60 % of them sharing a 384-token prefix, 256 greedy tokens each, through
+    nr_step (reference scheduler, prefix cache on).  Arrivals are mapped to steps by a
+    virtual clock (step k admits every arrival <= k x 10 ms), so the admission sequence is
+    deterministic; value = generated tokens over the wall time of the whole run."""
+    rng = np.random.default_rng(33)
+    arrive = np.cumsum(rng.exponential(1 / 20.0, 50))
+    shared = rng.integers(0, 32000, 384).astype(np.int32)
+    prompts = []
+    for _ in range(50):
+        if rng.random() < 0.6:
+            n = int(rng.integers(385, 513))
+            prompts.append(np.concatenate([shared, rng.integers(0, 32000, n - 384).astype(np.int32)]))
+        else:
+            prompts.append(rng.integers(0, 32000, int(rng.integers(64, 513))).astype(np.int32))
+    model = synth.cached_model(synth.SHAPE_110M, seed=MODEL_SEED)
+    eng = NitroEngine(model, EngineConfig(total_blocks=4096, max_new_tokens=256, max_batch=64, max_prefill_tokens=256,
+                                          device=0))
+    dt = 0.010
+    k, nxt, gen, hits, steps = 0, 0, 0, 0, 0
+    t0 = time.perf_counter()
+    while nxt < 50 or eng.has_active_requests():
+        while nxt < 50 and arrive[nxt] <= k * dt:
+            eng.add_request(nxt, prompts[nxt])
+            nxt += 1
+        if eng.has_active_requests():
+            r = eng.step()
+            gen += len(r.emitted)
+            hits += r.prefill_hits
+            steps += 1
+        k += 1
+    wall = time.perf_counter() - t0
+    st = eng.stats()
+    eng.close()
+    return {"workload": "config3", "metric": "aggregate tok/s, 50 Poisson requests with a shared prefix (110M Q8_0)",
+            "value": round(gen / wall, 1), "unit": "tok/s", "generated_tokens": gen, "wall_s": round(wall, 3),
+            "steps": steps, "prefix_hit_pages": hits, "evictions": st["evictions"],
+            "note": "virtual clock 10 ms per step for admission; wall time includes the scheduler and copies"}
+
+
+def run_config4(args):
+    """Config 4: 32 prompts of 1024 tokens prefilled (one 1024-token chunk each through
+    nr_forward_prefill), then 16 decode steps at B = 32.  Positions reach 1039, so the
+    model header has seq_len 2048."""
+    import torch
+    model = synth.cached_model(synth.SHAPE_110M_LONG, seed=MODEL_SEED)
+    eng = NitroEngine(model, EngineConfig(total_blocks=33 * 66, max_new_tokens=100000, max_batch=32,
+                                          max_prefill_tokens=1024, device=0))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    rng = np.random.default_rng(44)
+    prompts = [rng.integers(0, 32000, 1024).astype(np.int32) for _ in range(32)]
+    warm = eng.seq_create(1000)
+    eng.forward_prefill_chunk(warm, prompts[0], 0, want_logits=False)
+    eng.release(warm)
+    seqs = [eng.seq_create(i) for i in range(32)]
+    torch.cuda.synchronize()
+    e0, e1 = _dev_events(torch, stream)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    toks = []
+    for s, p in zip(seqs, prompts):
+        toks.append(eng.forward_prefill_chunk(s, p, 0, want_logits=False)[1])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    prefill_dev_ms = e0.elapsed_time(e1)
+    pos = [1024] * 32
+    t0 = time.perf_counter()
+    for _ in range(16):
+        _, am = eng.forward_decode_batch(toks, pos, seqs, want_logits=False)
+        toks = am.tolist()
+        pos = [p + 1 for p in pos]
+    decode_s = time.perf_counter() - t0
+    eng.close()
+    linear = 2 * 84_934_656 * 32768
+    attn = 2 * 2 * 12 * 64 * 12 * 32 * (1024 * 1025 // 2)
+    flops = linear + attn
+    _, peak_src = load_peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tf_peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        tf_peak = 1590.0
+    tflops = flops / (prefill_dev_ms * 1e-3) / 1e12
+    issued = (3 * linear + attn) / (prefill_dev_ms * 1e-3) / 1e12  # tensor work incl. the hi/lo split
+    return {"workload": "config4", "metric": "prefill tok/s, 32 x 1024-token prompts (110M Q8_0)",
+            "value": round(32768 / (prefill_dev_ms * 1e-3), 1), "unit": "tok/s",
+            "prefill_ms": round(prefill_dev_ms, 3), "prefill_wall_ms": round(1000 * prefill_s, 3),
+            "model_tflops": round(tflops, 2),
+            "roofline": {"bound": "tensor", "achieved": round(issued, 2), "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": round(issued / tf_peak, 4), "peak_source": peak_src,
+                         "note": "bf16 tensor FLOPs issued: 3 x linear (hi/lo split) + attention on CUDA cores counted once"},
+            "decode_b32": {"value": round(32 * 16 / decode_s, 1), "unit": "tok/s", "steps": 16}}
+
+
+def run_config5(args):
+    """Config 5 (reduced): the 7B-shaped model, B requests (default 64) with 512-token
+    prompts prefilled one per call, then 32 decode steps at batch B through
+    nr_forward_decode.  The full 256-request run needs ~160 GiB of K/V on one GPU."""
+    import torch
+    B = args.batch or 64
+    model = synth.cached_model(synth.SHAPE_7B, seed=MODEL_SEED)
+    pages = B * (512 // 16 + 4) + 16
+    eng = NitroEngine(model, EngineConfig(total_blocks=pages, max_new_tokens=100000, max_batch=B,
+                                          max_prefill_tokens=512, device=0))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    rng = np.random.default_rng(55)
+    prompts = [rng.integers(0, 32000, 512).astype(np.int32) for _ in range(B)]
+    seqs = [eng.seq_create(i) for i in range(B)]
+    torch.cuda.synchronize()
+    e0, e1 = _dev_events(torch, stream)
+    e0.record(stream)
+    toks = [eng.forward_prefill_chunk(s, p, 0, want_logits=False)[1] for s, p in zip(seqs, prompts)]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    pos = [512] * B
+    for _ in range(2):
+        _, am = eng.forward_decode_batch(toks, pos, seqs, want_logits=False)
+        toks = am.tolist()
+        pos = [p + 1 for p in pos]
+    n = 30
+    t0 = time.perf_counter()
+    for _ in range(n):
+        _, am = eng.forward_decode_batch(toks, pos, seqs, want_logits=False)
+        toks = am.tolist()
+        pos = [p + 1 for p in pos]
+    dec_s = time.perf_counter() - t0
+    eng.replay_decode(3)
+    torch.cuda.synchronize()
+    d0, d1 = _dev_events(torch, stream)
+    d0.record(stream)
+    eng.replay_decode(10)
+    d1.record(stream)
+    torch.cuda.synchronize()
+    step_ms = d0.elapsed_time(d1) / 10
+    eng.close()
+    w_bytes = 7_810_859_008
+    kv = sum(p + 1 for p in pos) * 32 * 2 * 4096 * 4
+    peak, peak_src = load_peaks()
+    return {"workload": "config5", "metric": f"decode tok/s, 7B-shaped Q8_0, batch {B} (reduced config 5)",
+            "value": round(B / (step_ms * 1e-3), 1), "unit": "tok/s", "ms_per_step": round(step_ms, 3),
+            "e2e": {"value": round(B * n / dec_s, 1), "unit": "tok/s"},
+            "prefill": {"tokens": 512 * B, "ms": round(prefill_ms, 2), "tok_s": round(512 * B / (prefill_ms * 1e-3), 1)},
+            "roofline": {"bound": "hbm", "bytes_per_step": w_bytes + kv,
+                         "achieved": round((w_bytes + kv) / (step_ms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round((w_bytes + kv) / (step_ms * 1e-3) / 1e9 / peak, 4), "peak_source": peak_src}}
+
+
 # ------------------------------------------------------------------ GPU arm
 def engine_arm(args, rank, world, local_rank):
     import torch
@@ -380,6 +606,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="mark the timed device-resident replays as the CUDA profiler range")
+    ap.add_argument("--workload", choices=["decode64", "config1", "config3", "config4", "config5"],
+                    default="decode64", help="decode64 is the headline; the others print their own line")
+    ap.add_argument("--batch", type=int, default=0, help="config5: requests per GPU (default 64)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -392,6 +621,12 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         return reference_arm(args, rank)
+    if args.workload != "decode64":
+        if rank == 0:
+            fn = {"config1": run_config1, "config3": run_config3, "config4": run_config4,
+                  "config5": run_config5}[args.workload]
+            print(json.dumps(fn(args)), flush=True)
+        return 0
     return engine_arm(args, rank, world, local_rank)
 
 

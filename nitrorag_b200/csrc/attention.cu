@@ -527,10 +527,15 @@ void ensure_smem(K kernel, int bytes) {
 
 int decode_attn_chunk_pages(int head_dim) { return head_dim <= 64 ? NITRO_DEC_CHUNK64 : NITRO_DEC_CHUNK64 / 2; }
 
+// Small batches get shorter chunks (down to this many pages) so that there are enough
+// work items for every warp; the partial buffers are laid out for that many splits.
+constexpr int kMinChunkPages = 2;
+
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 size_t decode_attn_workspace_bytes(int B, int n_heads, int head_dim, int max_pages) {
-    const int cp = decode_attn_chunk_pages(head_dim);
+    (void)head_dim;
+    const int cp = kMinChunkPages;
     const int ms = (max_pages + cp - 1) / cp;
     size_t o = align_up((size_t)B * n_heads * ms * head_dim * 4, 256);
     size_t ml = align_up((size_t)B * n_heads * ms * 2 * 4, 256);
@@ -541,7 +546,7 @@ size_t decode_attn_workspace_bytes(int B, int n_heads, int head_dim, int max_pag
 void decode_attn_bind_workspace(DecodeAttnArgs& a, void* ws, int max_pages_capacity) {
     const int hd = a.geom.head_dim;
     a.chunk_pages = decode_attn_chunk_pages(hd);
-    a.max_splits = (max_pages_capacity + a.chunk_pages - 1) / a.chunk_pages;
+    a.max_splits = (max_pages_capacity + kMinChunkPages - 1) / kMinChunkPages;
     char* p = (char*)ws;
     a.part_o = (float*)p;
     p += align_up((size_t)a.B * a.n_heads * a.max_splits * hd * 4, 256);
@@ -562,10 +567,18 @@ static int sm_count() {
     return counts[dev] > 0 ? counts[dev] : 148;
 }
 
-void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t s) {
-    (void)max_ctx;
+void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream_t s) {
     count_launch();
     const int grid = sm_count();
+    // chunk length: the longest (default) that still gives every warp about two items,
+    // estimated from the longest context of the step
+    DecodeAttnArgs a = args;
+    {
+        const int warps = grid * (a.geom.head_dim == 64 ? DecCfg<64>::WARPS : DecCfg<128>::WARPS);
+        const int64_t pages = (int64_t)a.B * ((max_ctx + kPage - 1) / kPage);
+        while (a.chunk_pages > kMinChunkPages && pages / a.chunk_pages * a.n_heads < 2 * warps) a.chunk_pages /= 2;
+        if (a.chunk_pages < kMinChunkPages) a.chunk_pages = kMinChunkPages;
+    }
     const dim3 mgrid((unsigned)(((int64_t)a.B * a.n_heads + 7) / 8));
     count_launch();
     if (a.geom.head_dim == 64) {

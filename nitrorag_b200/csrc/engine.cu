@@ -207,31 +207,45 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
     }
     NR_CUDA(cudaMemcpy(w_.base, host.data(), total, cudaMemcpyHostToDevice));
 
-    // tiled hi/lo copies for the tensor-core path (made on the device from the above)
+    // Tiled hi/lo copies for the tensor-core path (made on the device from the above).
+    // They cost 4 B per weight instead of 1.125 B, so a Q8 projection gets them only while
+    // its kernel is latency-bound rather than HBM-bound: at most 8 M weights (32 MB of
+    // tiles, ~5 us of HBM).  The fp32 classifier always gets them (same 4 B per weight).
     const char* tiled_env = getenv("NITRO_TILED_WEIGHTS");
     if (!(tiled_env && tiled_env[0] == '0') && D % 64 == 0 && H % 64 == 0) {
-        w_.qkv_t_layer = align256(tc_tiled_weight_bytes(NQKV, D));
-        w_.wo_t_layer = align256(tc_tiled_weight_bytes(D, D));
-        w_.w13_t_layer = align256(tc_tiled_weight_bytes(2 * H, D));
-        w_.w2_t_layer = align256(tc_tiled_weight_bytes(D, H));
+        const int64_t kTileMax = (int64_t)8 << 20;
+        auto tiled = [&](int64_t n, int64_t k) { return n * k <= kTileMax ? align256(tc_tiled_weight_bytes((int)n, (int)k)) : 0; };
+        w_.qkv_t_layer = tiled(NQKV, D);
+        w_.wo_t_layer = tiled(D, D);
+        w_.w13_t_layer = tiled(2 * H, D);
+        w_.w2_t_layer = tiled(D, H);
         const size_t cls = align256(tc_tiled_weight_bytes(c.vocab, D));
         w_.tbytes = (size_t)L * (w_.qkv_t_layer + w_.wo_t_layer + w_.w13_t_layer + w_.w2_t_layer) + cls;
         NR_CUDA(cudaMalloc(&w_.tbase, w_.tbytes));
         uint8_t* p = (uint8_t*)w_.tbase;
-        w_.qkv_t = p; p += (size_t)L * w_.qkv_t_layer;
-        w_.wo_t = p; p += (size_t)L * w_.wo_t_layer;
-        w_.w13_t = p; p += (size_t)L * w_.w13_t_layer;
-        w_.w2_t = p; p += (size_t)L * w_.w2_t_layer;
+        auto carve = [&](size_t per_layer) {
+            uint8_t* r = per_layer ? p : nullptr;
+            p += (size_t)L * per_layer;
+            return r;
+        };
+        w_.qkv_t = carve(w_.qkv_t_layer);
+        w_.wo_t = carve(w_.wo_t_layer);
+        w_.w13_t = carve(w_.w13_t_layer);
+        w_.w2_t = carve(w_.w2_t_layer);
         w_.cls_t = p;
         for (int l = 0; l < L; l++) {
-            tc_tile_weights(w_.qkv_q + (int64_t)l * NQKV * D, w_.qkv_s + (int64_t)l * NQKV * (D / 32), nullptr, NQKV, D,
-                            w_.qkv_t + l * w_.qkv_t_layer, stream_);
-            tc_tile_weights(w_.wo_q + (int64_t)l * D * D, w_.wo_s + (int64_t)l * D * (D / 32), nullptr, D, D,
-                            w_.wo_t + l * w_.wo_t_layer, stream_);
-            tc_tile_weights(w_.w13_q + (int64_t)l * 2 * H * D, w_.w13_s + (int64_t)l * 2 * H * (D / 32), nullptr, 2 * H,
-                            D, w_.w13_t + l * w_.w13_t_layer, stream_);
-            tc_tile_weights(w_.w2_q + (int64_t)l * D * H, w_.w2_s + (int64_t)l * D * (H / 32), nullptr, D, H,
-                            w_.w2_t + l * w_.w2_t_layer, stream_);
+            if (w_.qkv_t)
+                tc_tile_weights(w_.qkv_q + (int64_t)l * NQKV * D, w_.qkv_s + (int64_t)l * NQKV * (D / 32), nullptr, NQKV,
+                                D, w_.qkv_t + l * w_.qkv_t_layer, stream_);
+            if (w_.wo_t)
+                tc_tile_weights(w_.wo_q + (int64_t)l * D * D, w_.wo_s + (int64_t)l * D * (D / 32), nullptr, D, D,
+                                w_.wo_t + l * w_.wo_t_layer, stream_);
+            if (w_.w13_t)
+                tc_tile_weights(w_.w13_q + (int64_t)l * 2 * H * D, w_.w13_s + (int64_t)l * 2 * H * (D / 32), nullptr,
+                                2 * H, D, w_.w13_t + l * w_.w13_t_layer, stream_);
+            if (w_.w2_t)
+                tc_tile_weights(w_.w2_q + (int64_t)l * D * H, w_.w2_s + (int64_t)l * D * (H / 32), nullptr, D, H,
+                                w_.w2_t + l * w_.w2_t_layer, stream_);
         }
         tc_tile_weights(nullptr, nullptr, w_.emb, c.vocab, D, w_.cls_t, stream_);
         NR_CUDA(cudaStreamSynchronize(stream_));

@@ -120,49 +120,148 @@ __device__ __forceinline__ void rms_rows(const float* x, int ldx, int K, int m0,
 }
 
 // ------------------------------------------------------------------ matvec, M <= 8
+// One warp per adjacent pair of output rows; lane l covers K positions l*16 + 512 i.
+// The weights of the first GV_PF steps (all of K up to 2048 for Q8, 1024 for fp32) and
+// the RMSNorm gain of the first GV_PG steps are requested before the grid-dependency
+// wait, i.e. while the previous kernel still runs; only the activations wait.  The
+// RMSNorm is folded into the dot product: every warp sees each whole input row anyway,
+// so it sums x^2 alongside w . (g * x) and scales by 1/rms at the end (the faithful
+// mode, which reads only the last block, computes the row sums separately).
+constexpr int GV_PF = 4;  // Q8 steps prefetched (2 for fp32 weights)
+constexpr int GV_PG = 2;  // gain steps prefetched
+
+template <bool F32W>
+struct GvW {  // one step's weights of the warp's two rows for this lane
+    int4 q[F32W ? 1 : 2];
+    float s[F32W ? 1 : 2];
+    float4 f[F32W ? 8 : 1];
+};
+
+template <bool F32W>
+__device__ __forceinline__ void gv_load(GvW<F32W>& w, const GemmArgs& a, int n, int k) {
+    if (F32W) {
+        const float4* r0 = reinterpret_cast<const float4*>(a.wf + (int64_t)n * a.K + k);
+        const float4* r1 = reinterpret_cast<const float4*>(a.wf + (int64_t)(n + 1) * a.K + k);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w.f[i] = __ldg(r0 + i);
+            w.f[4 + i] = __ldg(r1 + i);
+        }
+    } else {
+        w.q[0] = __ldg(reinterpret_cast<const int4*>(a.wq + (int64_t)n * a.K + k));
+        w.q[1] = __ldg(reinterpret_cast<const int4*>(a.wq + (int64_t)(n + 1) * a.K + k));
+        w.s[0] = __ldg(a.ws + (int64_t)n * (a.K >> 5) + (k >> 5));
+        w.s[1] = __ldg(a.ws + (int64_t)(n + 1) * (a.K >> 5) + (k >> 5));
+    }
+}
+
+template <bool F32W>
+__device__ __forceinline__ void gv_unpack(const GvW<F32W>& w, float* w0, float* w1) {
+    if (F32W) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w0[4 * i] = w.f[i].x; w0[4 * i + 1] = w.f[i].y; w0[4 * i + 2] = w.f[i].z; w0[4 * i + 3] = w.f[i].w;
+            w1[4 * i] = w.f[4 + i].x; w1[4 * i + 1] = w.f[4 + i].y; w1[4 * i + 2] = w.f[4 + i].z;
+            w1[4 * i + 3] = w.f[4 + i].w;
+        }
+    } else {
+        const int8_t* q0 = reinterpret_cast<const int8_t*>(&w.q[0]);
+        const int8_t* q1 = reinterpret_cast<const int8_t*>(&w.q[1]);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            w0[i] = (float)q0[i] * w.s[0];
+            w1[i] = (float)q1[i] * w.s[1];
+        }
+    }
+}
+
 template <int MT, bool F32W>
 __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
     constexpr int WARPS = 4;
+    constexpr int PF = F32W ? 2 : GV_PF;
     __shared__ float inv_rms[MT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool norm = a.norm_gain != nullptr;
-    grid_dependency_wait();
+    const bool fold = norm && a.kbegin == 0;  // 1/rms from this warp's own pass over x
+    const int n = (blockIdx.x * WARPS + warp) * 2;
+    const bool active = n < a.N;
+    const int k0 = a.kbegin + lane * 16;
+
+    // ---- before the wait: weights and gain (read-only)
+    GvW<F32W> wp[PF];
+    float4 gp[GV_PG][4];
+#pragma unroll
+    for (int i = 0; i < PF; i++)
+        if (active && k0 + 512 * i < a.K) gv_load<F32W>(wp[i], a, n, k0 + 512 * i);
     if (norm) {
+#pragma unroll
+        for (int i = 0; i < GV_PG; i++)
+            if (active && k0 + 512 * i < a.K) {
+                const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k0 + 512 * i);
+#pragma unroll
+                for (int j = 0; j < 4; j++) gp[i][j] = __ldg(g4 + j);
+            }
+    }
+    grid_dependency_wait();
+    if (norm && !fold) {
         rms_rows(a.x, a.ldx, a.K, 0, MT, a.M, inv_rms);
         __syncthreads();
     }
-    const int n = (blockIdx.x * WARPS + warp) * 2;
-    if (n >= a.N) return;
-    float acc0[MT], acc1[MT];
+    if (!active) return;
+    float acc0[MT], acc1[MT], ss[MT];
 #pragma unroll
-    for (int m = 0; m < MT; m++) acc0[m] = acc1[m] = 0.0f;
+    for (int m = 0; m < MT; m++) acc0[m] = acc1[m] = ss[m] = 0.0f;
 
-    for (int k = a.kbegin + lane * 16; k < a.K; k += 32 * 16) {
+#pragma unroll 1
+    for (int i = 0; k0 + 512 * i < a.K; i++) {
+        const int k = k0 + 512 * i;
         float w0[16], w1[16];
-        if (F32W) {
-            load16_f32(a.wf + (int64_t)n * a.K + k, w0);
-            load16_f32(a.wf + (int64_t)(n + 1) * a.K + k, w1);
+        if (i < PF) {
+            // prefetched (a switch keeps the register array statically indexed)
+#pragma unroll
+            for (int j = 0; j < PF; j++)
+                if (j == i) gv_unpack<F32W>(wp[j], w0, w1);
         } else {
-            load16_q8(a.wq, a.ws, n, a.K, k, w0);
-            load16_q8(a.wq, a.ws, n + 1, a.K, k, w1);
+            GvW<F32W> t;
+            gv_load<F32W>(t, a, n, k);
+            gv_unpack<F32W>(t, w0, w1);
         }
         float g[16];
-        if (norm) load16_f32(a.norm_gain + k, g);
+        if (norm) {
+            float4 g4[4];
+            if (i < GV_PG) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) g4[j] = i == 0 ? gp[0][j] : gp[GV_PG - 1][j];
+            } else {
+                const float4* src = reinterpret_cast<const float4*>(a.norm_gain + k);
+#pragma unroll
+                for (int j = 0; j < 4; j++) g4[j] = __ldg(src + j);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                g[4 * j] = g4[j].x; g[4 * j + 1] = g4[j].y; g[4 * j + 2] = g4[j].z; g[4 * j + 3] = g4[j].w;
+            }
+        }
 #pragma unroll
         for (int m = 0; m < MT; m++) {
             if (m < a.M) {
                 float xv[16];
                 load16_f32(a.x + (int64_t)m * a.ldx + k, xv);
                 if (norm) {
-                    float inv = inv_rms[m];
+                    const float sc = fold ? 1.0f : inv_rms[m];
+                    float q = 0.0f;
 #pragma unroll
-                    for (int i = 0; i < 16; i++) xv[i] = g[i] * (inv * xv[i]);
+                    for (int j = 0; j < 16; j++) {
+                        q = fmaf(xv[j], xv[j], q);
+                        xv[j] = g[j] * (sc * xv[j]);
+                    }
+                    ss[m] += q;
                 }
                 float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    s0 = fmaf(w0[i], xv[i], s0);
-                    s1 = fmaf(w1[i], xv[i], s1);
+                for (int j = 0; j < 16; j++) {
+                    s0 = fmaf(w0[j], xv[j], s0);
+                    s1 = fmaf(w1[j], xv[j], s1);
                 }
                 acc0[m] += s0;
                 acc1[m] += s1;
@@ -174,6 +273,11 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
     for (int m = 0; m < MT; m++) {
         acc0[m] = warp_sum(acc0[m]);
         acc1[m] = warp_sum(acc1[m]);
+        if (fold) {
+            const float inv = 1.0f / sqrtf(warp_sum(ss[m]) / (float)a.K + 1e-5f);
+            acc0[m] *= inv;
+            acc1[m] *= inv;
+        }
     }
 #pragma unroll
     for (int m = 0; m < MT; m++) {
