@@ -75,6 +75,7 @@ Engine::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
     cudaFree(w_.base);
     cudaFree(w_.tbase);
+    cudaFree(w_.rbase);
     cudaFree(kpool_);
     cudaFree(vpool_);
     cudaFree(d_x_);
@@ -213,7 +214,8 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
     // tiles, ~5 us of HBM).  The fp32 classifier always gets them (same 4 B per weight).
     const char* tiled_env = getenv("NITRO_TILED_WEIGHTS");
     if (!(tiled_env && tiled_env[0] == '0') && D % 64 == 0 && H % 64 == 0) {
-        const int64_t kTileMax = (int64_t)8 << 20;
+        int64_t kTileMax = (int64_t)8 << 20;  // NITRO_TILE_MAX_WEIGHTS overrides (tests use 0)
+        if (const char* tm = getenv("NITRO_TILE_MAX_WEIGHTS")) kTileMax = atoll(tm);
         auto tiled = [&](int64_t n, int64_t k) { return n * k <= kTileMax ? align256(tc_tiled_weight_bytes((int)n, (int)k)) : 0; };
         w_.qkv_t_layer = tiled(NQKV, D);
         w_.wo_t_layer = tiled(D, D);
@@ -250,6 +252,43 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
         tc_tile_weights(nullptr, nullptr, w_.emb, c.vocab, D, w_.cls_t, stream_);
         NR_CUDA(cudaStreamSynchronize(stream_));
         NR_CUDA(cudaGetLastError());
+
+        // the rest (HBM-bound projections) as raw Q8 tiles
+        auto raw = [&](int64_t n, int64_t k, size_t hilo) { return hilo ? 0 : align256(tc_raw_q8_bytes((int)n, (int)k)); };
+        w_.qkv_r_layer = raw(NQKV, D, w_.qkv_t_layer);
+        w_.wo_r_layer = raw(D, D, w_.wo_t_layer);
+        w_.w13_r_layer = raw(2 * H, D, w_.w13_t_layer);
+        w_.w2_r_layer = raw(D, H, w_.w2_t_layer);
+        w_.rbytes = (size_t)L * (w_.qkv_r_layer + w_.wo_r_layer + w_.w13_r_layer + w_.w2_r_layer);
+        if (w_.rbytes) {
+            NR_CUDA(cudaMalloc(&w_.rbase, w_.rbytes));
+            uint8_t* r = (uint8_t*)w_.rbase;
+            auto carve_r = [&](size_t per_layer) {
+                uint8_t* o = per_layer ? r : nullptr;
+                r += (size_t)L * per_layer;
+                return o;
+            };
+            w_.qkv_r = carve_r(w_.qkv_r_layer);
+            w_.wo_r = carve_r(w_.wo_r_layer);
+            w_.w13_r = carve_r(w_.w13_r_layer);
+            w_.w2_r = carve_r(w_.w2_r_layer);
+            for (int l = 0; l < L; l++) {
+                if (w_.qkv_r)
+                    tc_tile_q8_raw(w_.qkv_q + (int64_t)l * NQKV * D, w_.qkv_s + (int64_t)l * NQKV * (D / 32), NQKV, D,
+                                   w_.qkv_r + l * w_.qkv_r_layer, stream_);
+                if (w_.wo_r)
+                    tc_tile_q8_raw(w_.wo_q + (int64_t)l * D * D, w_.wo_s + (int64_t)l * D * (D / 32), D, D,
+                                   w_.wo_r + l * w_.wo_r_layer, stream_);
+                if (w_.w13_r)
+                    tc_tile_q8_raw(w_.w13_q + (int64_t)l * 2 * H * D, w_.w13_s + (int64_t)l * 2 * H * (D / 32), 2 * H, D,
+                                   w_.w13_r + l * w_.w13_r_layer, stream_);
+                if (w_.w2_r)
+                    tc_tile_q8_raw(w_.w2_q + (int64_t)l * D * H, w_.w2_s + (int64_t)l * D * (H / 32), D, H,
+                                   w_.w2_r + l * w_.w2_r_layer, stream_);
+            }
+            NR_CUDA(cudaStreamSynchronize(stream_));
+            NR_CUDA(cudaGetLastError());
+        }
     }
     return NR_OK;
 }
@@ -319,6 +358,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
         g.M = M; g.N = NQKV; g.K = D; g.kbegin = faithful ? D - 32 : 0;
         if (w_.qkv_t && !faithful) g.wt = w_.qkv_t + l * w_.qkv_t_layer;
+        if (w_.qkv_r) g.wr = w_.qkv_r + l * w_.qkv_r_layer;
         if (ss) { g.ss_in = d_ss_; g.ss_parts = ss_parts; g.ss_ld = max_rows_; }
         Epilogue e;
         e.kind = kEpiQKV; e.q_out = d_q_; e.kpool = kpool_; e.vpool = vpool_; e.geom = geom_; e.layer = l;
@@ -351,6 +391,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         go.x = d_att_; go.ldx = D; go.wq = w_.wo_q + (int64_t)l * D * D; go.ws = w_.wo_s + (int64_t)l * D * (D / 32);
         go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
         if (w_.wo_t && !faithful) go.wt = w_.wo_t + l * w_.wo_t_layer;
+        if (w_.wo_r) go.wr = w_.wo_r + l * w_.wo_r_layer;
         Epilogue eo;
         eo.kind = kEpiResidual; eo.out = d_x_; eo.ldo = D;
         if (ss) { eo.ss_out = d_ss_; eo.ss_ld = max_rows_; }
@@ -362,6 +403,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
         g13.M = M; g13.N = 2 * H; g13.K = D; g13.kbegin = faithful ? D - 32 : 0;
         if (w_.w13_t && !faithful) g13.wt = w_.w13_t + l * w_.w13_t_layer;
+        if (w_.w13_r) g13.wr = w_.w13_r + l * w_.w13_r_layer;
         if (ss) { g13.ss_in = d_ss_; g13.ss_parts = ss_parts; g13.ss_ld = max_rows_; }
         Epilogue e13;
         e13.kind = kEpiSwiGLU; e13.out = d_h_; e13.ldo = H;
@@ -372,6 +414,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g2.x = d_h_; g2.ldx = H; g2.wq = w_.w2_q + (int64_t)l * D * H; g2.ws = w_.w2_s + (int64_t)l * D * (H / 32);
         g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
         if (w_.w2_t && !faithful) g2.wt = w_.w2_t + l * w_.w2_t_layer;
+        if (w_.w2_r) g2.wr = w_.w2_r + l * w_.w2_r_layer;
         Epilogue e2;
         e2.kind = kEpiResidual; e2.out = d_x_; e2.ldo = D;
         if (ss) { e2.ss_out = d_ss_; e2.ss_ld = max_rows_; }

@@ -48,6 +48,12 @@ struct DeviceWeights {
     size_t qkv_t_layer = 0, wo_t_layer = 0, w13_t_layer = 0, w2_t_layer = 0;
     void* tbase = nullptr;
     size_t tbytes = 0;
+    // Projections too large for hi/lo tiles get raw Q8 tiles (tc_tile_q8_raw, 1.125 B per
+    // weight) that the tensor-core kernel streams through a ring of bulk copies.
+    uint8_t* qkv_r = nullptr; uint8_t* wo_r = nullptr; uint8_t* w13_r = nullptr; uint8_t* w2_r = nullptr;
+    size_t qkv_r_layer = 0, wo_r_layer = 0, w13_r_layer = 0, w2_r_layer = 0;
+    void* rbase = nullptr;
+    size_t rbytes = 0;
 };
 
 // Kernel classes timed by the engine's optional per-launch CUDA-event profiling.

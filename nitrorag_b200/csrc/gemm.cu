@@ -175,29 +175,37 @@ __device__ __forceinline__ void gv_unpack(const GvW<F32W>& w, float* w0, float* 
     }
 }
 
+// Long rows (K beyond 2048 / 4096) are split over 2 / 4 warps of the CTA, which then
+// join their partial sums through shared memory.
+__host__ __device__ inline int gv_ksplit(int k_len) { return k_len > 4096 ? 4 : (k_len > 2048 ? 2 : 1); }
+
 template <int MT, bool F32W>
 __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
     constexpr int WARPS = 4;
     constexpr int PF = F32W ? 2 : GV_PF;
     __shared__ float inv_rms[MT];
+    __shared__ float part[WARPS][MT][3];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool norm = a.norm_gain != nullptr;
-    const bool fold = norm && a.kbegin == 0;  // 1/rms from this warp's own pass over x
-    const int n = (blockIdx.x * WARPS + warp) * 2;
+    const bool fold = norm && a.kbegin == 0;  // 1/rms from the warps' own pass over x
+    const int KW = gv_ksplit(a.K - a.kbegin);
+    const int kw = warp % KW;                  // this warp's share of the row pair's K range
+    const int n = (blockIdx.x * (WARPS / KW) + warp / KW) * 2;
     const bool active = n < a.N;
-    const int k0 = a.kbegin + lane * 16;
+    const int k0 = a.kbegin + kw * 512 + lane * 16;
+    const int kstep = 512 * KW;
 
     // ---- before the wait: weights and gain (read-only)
     GvW<F32W> wp[PF];
     float4 gp[GV_PG][4];
 #pragma unroll
     for (int i = 0; i < PF; i++)
-        if (active && k0 + 512 * i < a.K) gv_load<F32W>(wp[i], a, n, k0 + 512 * i);
+        if (active && k0 + kstep * i < a.K) gv_load<F32W>(wp[i], a, n, k0 + kstep * i);
     if (norm) {
 #pragma unroll
         for (int i = 0; i < GV_PG; i++)
-            if (active && k0 + 512 * i < a.K) {
-                const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k0 + 512 * i);
+            if (active && k0 + kstep * i < a.K) {
+                const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k0 + kstep * i);
 #pragma unroll
                 for (int j = 0; j < 4; j++) gp[i][j] = __ldg(g4 + j);
             }
@@ -207,31 +215,28 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
         rms_rows(a.x, a.ldx, a.K, 0, MT, a.M, inv_rms);
         __syncthreads();
     }
-    if (!active) return;
     float acc0[MT], acc1[MT], ss[MT];
 #pragma unroll
     for (int m = 0; m < MT; m++) acc0[m] = acc1[m] = ss[m] = 0.0f;
 
+    // slot j of the register ring holds step i0 + j; after it is used it is refilled with
+    // step i0 + j + PF, so PF steps of weights stay in flight
 #pragma unroll 1
-    for (int i = 0; k0 + 512 * i < a.K; i++) {
-        const int k = k0 + 512 * i;
-        float w0[16], w1[16];
-        if (i < PF) {
-            // prefetched (a switch keeps the register array statically indexed)
+    for (int i0 = 0; active && k0 + kstep * i0 < a.K; i0 += PF)
 #pragma unroll
-            for (int j = 0; j < PF; j++)
-                if (j == i) gv_unpack<F32W>(wp[j], w0, w1);
-        } else {
-            GvW<F32W> t;
-            gv_load<F32W>(t, a, n, k);
-            gv_unpack<F32W>(t, w0, w1);
-        }
+    for (int j = 0; j < PF; j++) {
+        const int i = i0 + j;
+        const int k = k0 + kstep * i;
+        if (k >= a.K) break;
+        float w0[16], w1[16];
+        gv_unpack<F32W>(wp[j], w0, w1);
+        if (k + kstep * PF < a.K) gv_load<F32W>(wp[j], a, n, k + kstep * PF);
         float g[16];
         if (norm) {
             float4 g4[4];
             if (i < GV_PG) {
 #pragma unroll
-                for (int j = 0; j < 4; j++) g4[j] = i == 0 ? gp[0][j] : gp[GV_PG - 1][j];
+                for (int q4 = 0; q4 < 4; q4++) g4[q4] = i == 0 ? gp[0][q4] : gp[GV_PG - 1][q4];
             } else {
                 const float4* src = reinterpret_cast<const float4*>(a.norm_gain + k);
 #pragma unroll
@@ -273,12 +278,36 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
     for (int m = 0; m < MT; m++) {
         acc0[m] = warp_sum(acc0[m]);
         acc1[m] = warp_sum(acc1[m]);
-        if (fold) {
-            const float inv = 1.0f / sqrtf(warp_sum(ss[m]) / (float)a.K + 1e-5f);
+        if (fold) ss[m] = warp_sum(ss[m]);
+    }
+    if (KW > 1) {  // join the K shares of each row pair (uniform branch: every warp takes it)
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                part[warp][m][0] = acc0[m];
+                part[warp][m][1] = acc1[m];
+                part[warp][m][2] = ss[m];
+            }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            acc0[m] = acc1[m] = ss[m] = 0.0f;
+            for (int t = warp - kw; t < warp - kw + KW; t++) {  // in warp order: deterministic
+                acc0[m] += part[t][m][0];
+                acc1[m] += part[t][m][1];
+                ss[m] += part[t][m][2];
+            }
+        }
+    }
+    if (fold) {
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            const float inv = 1.0f / sqrtf(ss[m] / (float)a.K + 1e-5f);
             acc0[m] *= inv;
             acc1[m] *= inv;
         }
     }
+    if (!active || kw != 0) return;
 #pragma unroll
     for (int m = 0; m < MT; m++) {
         if (m < a.M && lane == m) {
@@ -421,7 +450,8 @@ __global__ void __launch_bounds__(128) gemm_tiled_kernel(GemmArgs a, Epilogue e)
 
 template <int MT>
 void gemv_dispatch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
-    dim3 grid((a.N / 2 + 3) / 4);
+    const int pairs_per_cta = 4 / gv_ksplit(a.K - a.kbegin);
+    dim3 grid((a.N / 2 + pairs_per_cta - 1) / pairs_per_cta);
     if (a.wf) launch_ex(gemv_kernel<MT, true>, grid, dim3(128), 0, s, 1, a, e);
     else launch_ex(gemv_kernel<MT, false>, grid, dim3(128), 0, s, 1, a, e);
 }
@@ -444,7 +474,7 @@ bool gemm_uses_tc(int M, int N, int K) {
 }
 
 void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
-    if (a.M > 8 && !tc_disabled() && tc_gemm_supported(a)) {
+    if (!tc_disabled() && tc_gemm_supported(a)) {
         launch_tc_gemm(a, e, s);
         return;
     }

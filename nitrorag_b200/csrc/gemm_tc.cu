@@ -52,6 +52,10 @@ constexpr int TC_WORKERS = 256;              // staging and epilogue threads: tw
 constexpr int TC_THREADS = TC_WORKERS + 32;  // + one warp that issues the MMAs
 constexpr int kIssuerWarp = TC_WORKERS / 32;
 constexpr uint32_t TC_TILE_BYTES = 2u * TC_M * TC_KC * 2u;  // hi + lo halves of one 128 x 64 weight tile
+// raw Q8 tile: int8 [half][16-byte piece][128 rows][16 B] (8 KB) then fp32 scales
+// [half][128 rows] (1 KB); a warp's 32 rows read 512 contiguous bytes per piece
+constexpr uint32_t TC_RAW_BYTES = TC_M * TC_KC + TC_M * 2 * 4;
+constexpr int TC_RAW_MAX = 12;  // ring slots of raw tiles
 
 // ------------------------------------------------------------------ tcgen05 wrappers
 // Shared-memory matrix descriptor, K-major without swizzle: core matrices of 8 rows x 16 B
@@ -214,6 +218,8 @@ struct SplitArgs {
     int recv_off;  // byte offset of the split-K receive buffer in dynamic shared memory
     int recv_pad;  // floats of padding per receive-buffer row (4, or 0 when short of space)
     int gain_off;  // byte offset of the staged RMSNorm gain slice in dynamic shared memory
+    int raw_off;   // raw Q8 tiles: byte offset and number of ring slots
+    int raw_slots;
 };
 
 // Thread roles.  Thread t owns weight row (t & 127) of the tile, which is also its TMEM
@@ -261,6 +267,34 @@ __device__ __forceinline__ void stage_w(const WRegs<F32W>& r, const GemmArgs& a,
             const int8_t* q = reinterpret_cast<const int8_t*>(r.q);
 #pragma unroll
             for (int j = 0; j < 32; j++) w[j] = (float)q[j] * r.s;
+        }
+        if (k < a.kbegin) {  // faithful mode: only k >= kbegin contributes
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (k + j < a.kbegin) w[j] = 0.0f;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++) w[j] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) split_store8(w + 8 * j, a_hi + core_off(row, half * 4 + j), a_lo + core_off(row, half * 4 + j));
+}
+
+// This thread's 32 weights of one chunk from a raw Q8 tile in shared memory (-> bf16 hi/lo).
+__device__ __forceinline__ void stage_w_raw(const uint8_t* raw, const GemmArgs& a, int n, int k, uint8_t* a_hi,
+                                            uint8_t* a_lo, int row, int half) {
+    float w[32];
+    if (n < a.N) {
+        const int4 p0 = *reinterpret_cast<const int4*>(raw + ((half * 2 + 0) * TC_M + row) * 16);
+        const int4 p1 = *reinterpret_cast<const int4*>(raw + ((half * 2 + 1) * TC_M + row) * 16);
+        const float sc = reinterpret_cast<const float*>(raw + TC_M * TC_KC)[half * TC_M + row];
+        const int8_t* q0 = reinterpret_cast<const int8_t*>(&p0);
+        const int8_t* q1 = reinterpret_cast<const int8_t*>(&p1);
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            w[j] = (float)q0[j] * sc;
+            w[16 + j] = (float)q1[j] * sc;
         }
         if (k < a.kbegin) {  // faithful mode: only k >= kbegin contributes
 #pragma unroll
@@ -337,6 +371,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t mma_bar[TC_MAX_STAGES];
     __shared__ uint64_t w_bar[TC_MAX_STAGES];  // tiled weights: the stage's bulk copy has landed
+    __shared__ uint64_t raw_bar[TC_RAW_MAX];   // raw Q8 tiles: the slot's bulk copy has landed
     __shared__ uint64_t done_bar;
     __shared__ uint64_t recv_bar;  // split K: the partials of this CTA's slice have all arrived
     __shared__ uint32_t tmem_slot;
@@ -361,9 +396,12 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     const int nch = max(0, c_end - c_first);
     const int stages = sp.stages;
     const int ks = sp.ksplit;
+    // raw Q8 tiles streamed through a ring of sp.raw_slots bulk copies (large matrices)
+    const bool use_raw = !F32W && a.wr != nullptr && a.wt == nullptr && sp.raw_slots >= 2;
+    const int RS = sp.raw_slots;
     // every chunk of this CTA has its own stage: all weights are staged before waiting for
     // the previous kernel (weights are read-only; activations are not)
-    const bool staged = nch <= stages;
+    const bool staged = nch <= stages && !use_raw;
     const int n = n_base + row;  // this thread's weight row
     auto stage_ptr = [&](int st, int part) { return smem + st * S::STAGE + (part < 2 ? part * S::A_BYTES : 2 * S::A_BYTES + (part - 2) * S::B_BYTES); };
     float* gain_s = reinterpret_cast<float*>(smem + sp.gain_off);  // [nch][64] when staged
@@ -388,6 +426,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             mbar_init(&mma_bar[st], 1);
             mbar_init(&w_bar[st], 1);
         }
+        for (int r = 0; r < TC_RAW_MAX; r++) mbar_init(&raw_bar[r], 1);
         mbar_init(&done_bar, 1);
         mbar_init(&recv_bar, 1);
         if (ks > 1) mbar_arrive_expect_tx(&recv_bar, (uint32_t)(TC_M * NT * 4));  // ks partials of slice x 128 rows
@@ -404,7 +443,17 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
         bulk_g2s(stage_ptr(st, 0), a.wt + ((size_t)n_tile * nchunk_total + c_first + i) * TC_TILE_BYTES, TC_TILE_BYTES,
                  &w_bar[st]);
     };
-    if (a.wt) {
+    uint8_t* raw_ring = smem + sp.raw_off;
+    auto fetch_raw = [&](int i) {  // chunk i -> slot i % RS
+        uint64_t* bar = &raw_bar[i % RS];
+        mbar_arrive_expect_tx(bar, TC_RAW_BYTES);
+        bulk_g2s(raw_ring + (size_t)(i % RS) * TC_RAW_BYTES,
+                 a.wr + ((size_t)n_tile * nchunk_total + c_first + i) * TC_RAW_BYTES, TC_RAW_BYTES, bar);
+    };
+    if (use_raw) {
+        if (tid == 0)
+            for (int i = 0; i < min(nch, RS); i++) fetch_raw(i);
+    } else if (a.wt) {
         if (tid == 0)
             for (int i = 0; i < min(nch, stages); i++) fetch_tile(i, i);
         if (staged && a.norm_gain)
@@ -430,7 +479,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
             stage_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32, stage_ptr(0, 0), stage_ptr(0, 1), row, wg);
         }
-    } else if (nch > 0 && worker) {
+    } else if (nch > 0 && worker && !use_raw) {
         load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
     }
     // QKV: where this thread's row goes (q row, or a K/V pool column) and the token
@@ -549,21 +598,56 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 named_arrive(1 + i, TC_THREADS);
             }
         } else {
+            // 64-token tiles: this thread's activation unit and gain slice of the next chunk
+            // are requested one chunk ahead
+            float4 xn[4], gn[4];
+            auto fetch_x = [&](int it) {
+                const int k = (c_first + it) * TC_KC + ukq * 16;
+                if (m_base + ur < a.M) {
+                    const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)(m_base + ur) * a.ldx + k);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) xn[j] = src[j];
+                }
+                if (a.norm_gain) {
+                    const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) gn[j] = __ldg(g4 + j);
+                }
+            };
+            if (NT == 64 && nch > 0) fetch_x(0);
             for (int it = 0; it < nch; it++) {
                 const int st = it % stages, use = it / stages;
                 const int k0 = (c_first + it) * TC_KC;
+                float4 xc[4], gc[4];
+                if (NT == 64) {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        xc[j] = xn[j];
+                        gc[j] = gn[j];
+                    }
+                    if (it + 1 < nch) fetch_x(it + 1);
+                }
                 WRegs<F32W> nxt;
-                if (!a.wt && it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
+                if (!a.wt && !use_raw && it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
                 // the stage was last read by the MMAs of chunk it - stages
                 if (ok && use > 0 && !mbar_wait(&mma_bar[st], (use - 1) & 1, a.err)) ok = false;
+                if (ok && use_raw && !mbar_wait(&raw_bar[it % RS], (it / RS) & 1, a.err)) ok = false;
                 if (ok) {
-                    if (!a.wt) stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
-                    stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2),
-                                      stage_ptr(st, 3), tid);
+                    if (use_raw)
+                        stage_w_raw(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, a, n, k0 + wg * 32, stage_ptr(st, 0),
+                                    stage_ptr(st, 1), row, wg);
+                    else if (!a.wt)
+                        stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
+                    if (NT == 64)
+                        stage_x16(xc, a.norm_gain ? reinterpret_cast<const float*>(gc) : nullptr, m_base + ur < a.M,
+                                  stage_ptr(st, 2), stage_ptr(st, 3), ur, ukq);
+                    else
+                        stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2),
+                                          stage_ptr(st, 3), tid);
                 }
                 fence_async_smem();
                 named_arrive(1 + st, TC_THREADS);
-                if (!a.wt && it + 1 < nch) cur = nxt;
+                if (!a.wt && !use_raw && it + 1 < nch) cur = nxt;
             }
         }
     } else {
@@ -576,6 +660,9 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 if (mbar_wait(&mma_bar[sp_], ((it - 1) / stages) & 1, a.err)) fetch_tile(it - 1 + stages, sp_);
                 else ok = false;
             }
+            // raw ring: the workers converted chunk it - 1 before the barrier this warp passed
+            // last iteration, so its slot takes chunk it - 1 + RS
+            if (use_raw && lane == 0 && it >= 1 && it - 1 + RS < nch) fetch_raw(it - 1 + RS);
             __syncwarp();
             named_sync(1 + st, TC_THREADS);
             if (lane == 0) {
@@ -896,6 +983,7 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
         kernel = tc_gemm_kernel<NT, false, -1>;
     }
     const int budget = tc_ensure_smem(kernel);
+    const bool raw = !a.wf && a.wr && !a.wt;
     // Stages and shared memory for a split: a stage per chunk when all of a CTA's chunks
     // fit (the receive buffer of a split, padded if there is room, and the RMSNorm gain
     // slice next to them), else a 2-stage ring: its loads run one chunk ahead in registers,
@@ -908,8 +996,15 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
             sp->recv_pad = pad;
             sp->recv_off = stages * TcSmem<NT>::STAGE;
             sp->gain_off = sp->recv_off + (ks > 1 ? (NT + pad * ks) * TC_M * 4 : 0);
-            return sp->gain_off + (a.norm_gain ? stages * TC_KC * 4 : 0);
+            sp->raw_off = sp->gain_off + (a.norm_gain ? stages * TC_KC * 4 : 0);
+            sp->raw_slots = 0;
+            return sp->raw_off;
         };
+        if (raw) {  // a 2-stage ring fed by as many raw-tile slots as fit
+            const int base = layout(TC_STAGES, 4);
+            sp->raw_slots = std::min(TC_RAW_MAX, (budget - base) / (int)TC_RAW_BYTES);
+            return base + sp->raw_slots * (int)TC_RAW_BYTES;
+        }
         if (per_cta <= TcSmem<NT>::MAX_STAGES) {
             const int st = std::max(TC_STAGES, per_cta);
             for (int pad = 4; pad >= 0; pad -= 4) {
@@ -964,7 +1059,36 @@ __global__ void tile_weights_kernel(const int8_t* q, const float* scales, const 
     split_store8(w, tile + o, tile + TC_TILE_BYTES / 2 + o);
 }
 
+// Raw Q8 tiles: one thread per (row, 16-byte group of a 64-column chunk).
+__global__ void tile_q8_raw_kernel(const int8_t* q, const float* scales, int N, int K, uint8_t* out) {
+    const int groups = K / 16;
+    const int64_t rows = (int64_t)((N + TC_M - 1) / TC_M) * TC_M;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= rows * groups) return;
+    const int n = (int)(t / groups), g = (int)(t % groups);
+    const int chunk = g / 4, piece = g % 4;  // piece = half * 2 + (16-byte part)
+    uint8_t* tile = out + ((int64_t)(n / TC_M) * (K / TC_KC) + chunk) * TC_RAW_BYTES;
+    const int r = n % TC_M;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (n < N) v = *reinterpret_cast<const int4*>(q + (int64_t)n * K + g * 16);
+    *reinterpret_cast<int4*>(tile + (piece * TC_M + r) * 16) = v;
+    if ((piece & 1) == 0) {
+        const int half = piece >> 1;
+        reinterpret_cast<float*>(tile + TC_M * TC_KC)[half * TC_M + r] =
+            n < N ? scales[(int64_t)n * (K / 32) + chunk * 2 + half] : 0.0f;
+    }
+}
+
 }  // namespace
+
+size_t tc_raw_q8_bytes(int N, int K) {
+    return (size_t)((N + TC_M - 1) / TC_M) * (size_t)(K / TC_KC) * TC_RAW_BYTES;
+}
+
+void tc_tile_q8_raw(const int8_t* q, const float* scales, int N, int K, uint8_t* out, cudaStream_t s) {
+    const int64_t n = (int64_t)((N + TC_M - 1) / TC_M) * TC_M * (K / 16);
+    tile_q8_raw_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, scales, N, K, out);
+}
 
 size_t tc_tiled_weight_bytes(int N, int K) {
     return (size_t)((N + TC_M - 1) / TC_M) * (size_t)(K / TC_KC) * TC_TILE_BYTES;
@@ -975,7 +1099,11 @@ void tc_tile_weights(const int8_t* q, const float* scales, const float* wf, int 
     tile_weights_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, scales, wf, N, K, out);
 }
 
-bool tc_gemm_supported(const GemmArgs& a) { return a.K % TC_KC == 0 && a.N % 2 == 0 && a.M > 8; }
+// Raw Q8 tiles send even single-token batches here: the tensor-core kernel streams large
+// matrices far better than the matvec.
+bool tc_gemm_supported(const GemmArgs& a) {
+    return a.K % TC_KC == 0 && a.N % 2 == 0 && (a.M > 8 || (a.wr != nullptr && !a.wf));
+}
 
 void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     count_launch();

@@ -61,6 +61,10 @@ struct GemmArgs {
     // kernel's shared-memory tile layout (tc_tile_weights); the kernel then fetches each
     // 128-row x 64-column tile with one bulk copy instead of converting q * scale itself.
     const uint8_t* wt = nullptr;
+    // Optional, for Q8 matrices without hi/lo tiles (large ones, HBM-bound): the int8 rows
+    // and scales regrouped per 128-row x 64-column tile (9 KB, tc_tile_q8_raw) so the
+    // kernel can stream them with bulk copies through a deep shared-memory ring.
+    const uint8_t* wr = nullptr;
 };
 
 // M <= 8: CUDA-core matvec; M > 8 with K % 64 == 0: tcgen05 GEMM (gemm_tc.cu); otherwise
@@ -75,6 +79,8 @@ void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s);
 // fp32 (wf) weights.
 size_t tc_tiled_weight_bytes(int N, int K);
 void tc_tile_weights(const int8_t* q, const float* scales, const float* wf, int N, int K, uint8_t* out, cudaStream_t s);
+size_t tc_raw_q8_bytes(int N, int K);
+void tc_tile_q8_raw(const int8_t* q, const float* scales, int N, int K, uint8_t* out, cudaStream_t s);
 
 // Decode attention over paged KV for one layer (see attention.cu).
 struct DecodeAttnArgs {

@@ -132,6 +132,67 @@ def write_model(path: str, shape: ModelShape, seed: int = 1234, std: float = 0.0
     return path
 
 
+def write_model_on_device(path: str, shape: ModelShape, seed: int = 1234, std: float = 0.02) -> str:
+    """The same file layout and Q8_0 quantisation as write_model, with the N(0, std) values
+    drawn by torch's CUDA generator (seeded) instead of PCG64: seconds instead of tens of
+    minutes for the 7B shape.  The values differ from write_model's, so this is for
+    throughput runs, not for parity against files written by write_model."""
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    D, H, L, KV = shape.dim, shape.hidden_dim, shape.n_layers, shape.kv_dim
+
+    def normal(n: int) -> "torch.Tensor":
+        return torch.randn(n, device="cuda", generator=g, dtype=torch.float32) * std
+
+    def q8(w: "torch.Tensor") -> bytes:
+        w = w.reshape(-1, Q_BLOCK)
+        amax = w.abs().amax(dim=1)
+        scale = torch.where(amax != 0, amax / 127.0, torch.full_like(amax, 1e-9))
+        q = torch.clamp(torch.round(w / scale[:, None]), -128, 127).to(torch.int8)
+        blk = torch.empty((w.shape[0], 36), dtype=torch.uint8, device="cuda")
+        blk[:, :4] = scale.contiguous().view(torch.uint8).reshape(-1, 4)
+        blk[:, 4:] = q.view(torch.uint8)
+        return blk.cpu().numpy().tobytes()
+
+    ones_ld = np.ones(L * D, np.float32).tobytes()
+    fr, fi = rope_tables(shape.seq_len, shape.head_dim)
+    with open(path, "wb") as f:
+        def q8_tensor(rows: int, cols: int):
+            for _ in range(L):
+                f.write(q8(normal(rows * cols)))
+
+        f.write(shape.header())
+        f.write(normal(shape.vocab_size * D).cpu().numpy().tobytes())
+        f.write(ones_ld)
+        q8_tensor(D, D)
+        q8_tensor(KV, D)
+        q8_tensor(KV, D)
+        q8_tensor(D, D)
+        f.write(ones_ld)
+        q8_tensor(H, D)
+        q8_tensor(D, H)
+        q8_tensor(H, D)
+        f.write(np.ones(D, np.float32).tobytes())
+        f.write(fr.tobytes())
+        f.write(fi.tobytes())
+    return path
+
+
+def cached_model_on_device(shape: ModelShape, seed: int = 1234, cache_dir: str | None = None) -> str:
+    """cached_model for write_model_on_device files (separate names)."""
+    cache_dir = cache_dir or os.environ.get("NITRO_MODEL_CACHE", "/tmp/nitro_models")
+    os.makedirs(cache_dir, exist_ok=True)
+    name = "q8dev_{}x{}x{}x{}x{}x{}x{}_s{}.bin".format(shape.dim, shape.hidden_dim, shape.n_layers, shape.n_heads,
+                                                       shape.n_kv_heads, shape.vocab_size, shape.seq_len, seed)
+    path = os.path.join(cache_dir, name)
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        write_model_on_device(tmp, shape, seed)
+        os.replace(tmp, path)
+    return path
+
+
 def cached_model(shape: ModelShape, seed: int = 1234, cache_dir: str | None = None) -> str:
     """Path of the synthetic model for (shape, seed), written on first use."""
     cache_dir = cache_dir or os.environ.get("NITRO_MODEL_CACHE", "/tmp/nitro_models")

@@ -248,3 +248,35 @@ def test_ingest_prompt_prefix_cache_hit(ref_fixed, tiny_model):
         assert eng.block_state(i) == ref.block_state(i)
     eng.close()
     ref.close()
+
+
+@pytest.mark.parametrize("B", [1, 5, 24])
+def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B):
+    """The large-model projection path: with the tile threshold at zero every Q8 projection
+    is streamed as raw Q8 tiles through the tensor-core kernel's bulk-copy ring, batches of
+    1-8 tokens included (the path the 7B shape takes).  Prefill and two decode steps must
+    match the reference."""
+    monkeypatch.setenv("NITRO_TILE_MAX_WEIGHTS", "0")
+    ref = ref_fixed
+    ref.open(m110_model, 256, 200)
+    eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=200)
+    prompts = synth.decode_workload(B, 20, 90, 32000, seed=12 + B)
+    rh, eh, toks, pos = [], [], [], []
+    for i, p in enumerate(prompts):
+        rh.append(ref.new_request(i, p))
+        eh.append(eng.seq_create(i))
+        lr = ref.forward_prefill(rh[i], p, 0)
+        le, am = eng.forward_prefill_chunk(eh[i], p, 0)
+        assert_close(le, lr, what=f"raw-tile prefill {i}")
+        toks.append(am)
+        pos.append(len(p))
+    for step in range(2):
+        lr = ref.forward_decode(toks, pos, rh)
+        le, am = eng.forward_decode_batch(toks, pos, eh)
+        assert_close(le, lr, what=f"raw-tile B={B} decode step {step}")
+        for i in range(B):
+            _check_tokens(int(am[i]), ref.argmax(lr[i]), lr[i], f"raw-tile B={B} step {step} row {i}")
+        toks = [int(t) for t in am]
+        pos = [p + 1 for p in pos]
+    eng.close()
+    ref.close()
