@@ -598,8 +598,10 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 named_arrive(1 + i, TC_THREADS);
             }
         } else {
-            // 64-token tiles: this thread's activation unit and gain slice of the next chunk
-            // are requested one chunk ahead
+            // 64-token tiles of the Q8 kernel: this thread's activation unit and gain slice of
+            // the next chunk are requested one chunk ahead (the fp32-weight classifier kernel,
+            // limited to 96 registers for two CTAs per SM, loads them per chunk)
+            constexpr bool XPF = NT == 64 && !F32W;
             float4 xn[4], gn[4];
             auto fetch_x = [&](int it) {
                 const int k = (c_first + it) * TC_KC + ukq * 16;
@@ -614,12 +616,12 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                     for (int j = 0; j < 4; j++) gn[j] = __ldg(g4 + j);
                 }
             };
-            if (NT == 64 && nch > 0) fetch_x(0);
+            if (XPF && nch > 0) fetch_x(0);
             for (int it = 0; it < nch; it++) {
                 const int st = it % stages, use = it / stages;
                 const int k0 = (c_first + it) * TC_KC;
                 float4 xc[4], gc[4];
-                if (NT == 64) {
+                if (XPF) {
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         xc[j] = xn[j];
@@ -638,7 +640,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                                     stage_ptr(st, 1), row, wg);
                     else if (!a.wt)
                         stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
-                    if (NT == 64)
+                    if (XPF)
                         stage_x16(xc, a.norm_gain ? reinterpret_cast<const float*>(gc) : nullptr, m_base + ur < a.M,
                                   stage_ptr(st, 2), stage_ptr(st, 3), ur, ukq);
                     else
