@@ -121,14 +121,13 @@ __device__ __forceinline__ void rms_rows(const float* x, int ldx, int K, int m0,
 
 // ------------------------------------------------------------------ matvec, M <= 8
 // One warp per adjacent pair of output rows; lane l covers K positions l*16 + 512 i.
-// The weights of the first GV_PF steps (all of K up to 2048 for Q8, 1024 for fp32) and
-// the RMSNorm gain of the first GV_PG steps are requested before the grid-dependency
-// wait, i.e. while the previous kernel still runs; only the activations wait.  The
+// The weights of the first GV_PF steps (all of K up to 2048 for Q8, 1024 for fp32) are
+// requested before the grid-dependency wait, i.e. while the previous kernel still runs,
+// and each step's slot is refilled GV_PF steps ahead; only the activations wait.  The
 // RMSNorm is folded into the dot product: every warp sees each whole input row anyway,
 // so it sums x^2 alongside w . (g * x) and scales by 1/rms at the end (the faithful
 // mode, which reads only the last block, computes the row sums separately).
 constexpr int GV_PF = 4;  // Q8 steps prefetched (2 for fp32 weights)
-constexpr int GV_PG = 2;  // gain steps prefetched
 
 template <bool F32W>
 struct GvW {  // one step's weights of the warp's two rows for this lane
@@ -155,24 +154,14 @@ __device__ __forceinline__ void gv_load(GvW<F32W>& w, const GemmArgs& a, int n, 
     }
 }
 
-template <bool F32W>
-__device__ __forceinline__ void gv_unpack(const GvW<F32W>& w, float* w0, float* w1) {
-    if (F32W) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            w0[4 * i] = w.f[i].x; w0[4 * i + 1] = w.f[i].y; w0[4 * i + 2] = w.f[i].z; w0[4 * i + 3] = w.f[i].w;
-            w1[4 * i] = w.f[4 + i].x; w1[4 * i + 1] = w.f[4 + i].y; w1[4 * i + 2] = w.f[4 + i].z;
-            w1[4 * i + 3] = w.f[4 + i].w;
-        }
-    } else {
-        const int8_t* q0 = reinterpret_cast<const int8_t*>(&w.q[0]);
-        const int8_t* q1 = reinterpret_cast<const int8_t*>(&w.q[1]);
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            w0[i] = (float)q0[i] * w.s[0];
-            w1[i] = (float)q1[i] * w.s[1];
-        }
-    }
+// Four int8 (one 32-bit word) -> exact floats: with the sign bit flipped each byte is
+// q + 128; placed in the low mantissa byte of 2^23 it reads 2^23 + q + 128.
+__device__ __forceinline__ void q8x4_to_f32(uint32_t w, float* f) {
+    const uint32_t u = w ^ 0x80808080u;
+    f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
+    f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
+    f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
+    f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
 }
 
 // Long rows (K beyond 2048 / 4096) are split over 2 / 4 warps of the CTA, which then
@@ -195,21 +184,11 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
     const int k0 = a.kbegin + kw * 512 + lane * 16;
     const int kstep = 512 * KW;
 
-    // ---- before the wait: weights and gain (read-only)
+    // ---- before the wait: weights (read-only)
     GvW<F32W> wp[PF];
-    float4 gp[GV_PG][4];
 #pragma unroll
     for (int i = 0; i < PF; i++)
         if (active && k0 + kstep * i < a.K) gv_load<F32W>(wp[i], a, n, k0 + kstep * i);
-    if (norm) {
-#pragma unroll
-        for (int i = 0; i < GV_PG; i++)
-            if (active && k0 + kstep * i < a.K) {
-                const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k0 + kstep * i);
-#pragma unroll
-                for (int j = 0; j < 4; j++) gp[i][j] = __ldg(g4 + j);
-            }
-    }
     grid_dependency_wait();
     if (norm && !fold) {
         rms_rows(a.x, a.ldx, a.K, 0, MT, a.M, inv_rms);
@@ -228,25 +207,10 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
         const int i = i0 + j;
         const int k = k0 + kstep * i;
         if (k >= a.K) break;
-        float w0[16], w1[16];
-        gv_unpack<F32W>(wp[j], w0, w1);
+        const GvW<F32W> wcur = wp[j];
         if (k + kstep * PF < a.K) gv_load<F32W>(wp[j], a, n, k + kstep * PF);
         float g[16];
-        if (norm) {
-            float4 g4[4];
-            if (i < GV_PG) {
-#pragma unroll
-                for (int q4 = 0; q4 < 4; q4++) g4[q4] = i == 0 ? gp[0][q4] : gp[GV_PG - 1][q4];
-            } else {
-                const float4* src = reinterpret_cast<const float4*>(a.norm_gain + k);
-#pragma unroll
-                for (int j = 0; j < 4; j++) g4[j] = __ldg(src + j);
-            }
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                g[4 * j] = g4[j].x; g[4 * j + 1] = g4[j].y; g[4 * j + 2] = g4[j].z; g[4 * j + 3] = g4[j].w;
-            }
-        }
+        if (norm) load16_f32(a.norm_gain + k, g);  // with the activations: no extra round trip
 #pragma unroll
         for (int m = 0; m < MT; m++) {
             if (m < a.M) {
@@ -263,10 +227,34 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
                     ss[m] += q;
                 }
                 float s0 = 0.0f, s1 = 0.0f;
+                if (F32W) {
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    s0 = fmaf(w0[j], xv[j], s0);
-                    s1 = fmaf(w1[j], xv[j], s1);
+                    for (int q4 = 0; q4 < 4; q4++) {
+                        const float4 a4 = wcur.f[q4], b4 = wcur.f[4 + q4];
+                        s0 = fmaf(a4.x, xv[4 * q4], s0); s0 = fmaf(a4.y, xv[4 * q4 + 1], s0);
+                        s0 = fmaf(a4.z, xv[4 * q4 + 2], s0); s0 = fmaf(a4.w, xv[4 * q4 + 3], s0);
+                        s1 = fmaf(b4.x, xv[4 * q4], s1); s1 = fmaf(b4.y, xv[4 * q4 + 1], s1);
+                        s1 = fmaf(b4.z, xv[4 * q4 + 2], s1); s1 = fmaf(b4.w, xv[4 * q4 + 3], s1);
+                    }
+                } else {
+                    // sum_k q_k x_k over this lane's 16 weights (one Q8 block), times the
+                    // block's scale; q -> float through the exponent trick (full-rate ALU
+                    // ops instead of the quarter-rate integer conversion)
+                    const uint32_t* w0 = reinterpret_cast<const uint32_t*>(&wcur.q[0]);
+                    const uint32_t* w1 = reinterpret_cast<const uint32_t*>(&wcur.q[1]);
+#pragma unroll
+                    for (int wi = 0; wi < 4; wi++) {
+                        float f0[4], f1[4];
+                        q8x4_to_f32(w0[wi], f0);
+                        q8x4_to_f32(w1[wi], f1);
+#pragma unroll
+                        for (int b = 0; b < 4; b++) {
+                            s0 = fmaf(f0[b], xv[4 * wi + b], s0);
+                            s1 = fmaf(f1[b], xv[4 * wi + b], s1);
+                        }
+                    }
+                    s0 *= wcur.s[0];
+                    s1 *= wcur.s[1];
                 }
                 acc0[m] += s0;
                 acc1[m] += s1;
