@@ -355,7 +355,7 @@ def run_config4(args):
     model header has seq_len 2048."""
     import torch
     model = synth.cached_model(synth.SHAPE_110M_LONG, seed=MODEL_SEED)
-    eng = NitroEngine(model, EngineConfig(total_blocks=33 * 66, max_new_tokens=100000, max_batch=32,
+    eng = NitroEngine(model, EngineConfig(total_blocks=36 * 66, max_new_tokens=100000, max_batch=32,
                                           max_prefill_tokens=1024, device=0))
     stream = torch.cuda.ExternalStream(eng.stream)
     rng = np.random.default_rng(44)
@@ -375,6 +375,13 @@ def run_config4(args):
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
     prefill_dev_ms = e0.elapsed_time(e1)
+    # per-kernel-class breakdown of one more prefill (CUDA events around every launch)
+    extra = eng.seq_create(2000)
+    eng.set_profiling(True)
+    eng.forward_prefill_chunk(extra, prompts[1], 0, want_logits=False)
+    kt = eng.kernel_times()
+    eng.set_profiling(False)
+    eng.release(extra)
     pos = [1024] * 32
     t0 = time.perf_counter()
     for _ in range(16):
@@ -401,7 +408,8 @@ def run_config4(args):
             "roofline": {"bound": "tensor", "achieved": round(issued, 2), "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": round(issued / tf_peak, 4), "peak_source": peak_src,
                          "note": "bf16 tensor FLOPs issued: 3 x linear (hi/lo split) + attention on CUDA cores counted once"},
-            "decode_b32": {"value": round(32 * 16 / decode_s, 1), "unit": "tok/s", "steps": 16}}
+            "decode_b32": {"value": round(32 * 16 / decode_s, 1), "unit": "tok/s", "steps": 16},
+            "prefill_kernel_ms_per_prompt": {k: round(v[0], 3) for k, v in kt.items()}}
 
 
 def run_config5(args):

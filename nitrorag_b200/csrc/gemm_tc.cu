@@ -1101,10 +1101,10 @@ void tc_tile_weights(const int8_t* q, const float* scales, const float* wf, int 
     tile_weights_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, scales, wf, N, K, out);
 }
 
-// Raw Q8 tiles send even single-token batches here: the tensor-core kernel streams large
-// matrices far better than the matvec.
+// Raw Q8 tiles send batches of 3-8 tokens here too: for large matrices the tensor-core
+// kernel streams them far better than the matvec (1-2 tokens take the streamed matvec).
 bool tc_gemm_supported(const GemmArgs& a) {
-    return a.K % TC_KC == 0 && a.N % 2 == 0 && (a.M > 8 || (a.wr != nullptr && !a.wf));
+    return a.K % TC_KC == 0 && a.N % 2 == 0 && (a.M > 8 || (a.wr != nullptr && !a.wf && a.M > 2));
 }
 
 void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {

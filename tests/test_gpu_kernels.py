@@ -31,7 +31,7 @@ def _aos_to_soa(w_aos: bytes, rows: int, K: int):
 @pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 17, 64, 65, 130, 300])
 @pytest.mark.parametrize("mode", [NR_Q8_FIXED, NR_Q8_FAITHFUL])
 @pytest.mark.parametrize("NK", [(768, 768), (256, 2048), (2304, 768), (4096, 768), (32000 // 250 * 2, 128),
-                                (128, 4608), (64, 11008)])
+                                (128, 4608), (64, 11008), (4096, 4096), (8192, 2048)])
 def test_q8_matmul(torch_cuda, restatement, M, mode, NK):
     """CUDA-core matvec (M <= 8) and tcgen05 GEMM (M > 8); the narrow shapes split K over a
     thread-block cluster (1 to 8 CTAs) and reduce through distributed shared memory."""
