@@ -431,27 +431,44 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(DecodeAttnArgs a) {
 }
 
 // ------------------------------------------------------------------ prefill
-// One CTA per (16-query tile, head).  Pages 0..last of the sequence stream through
-// kStages shared-memory stages; each warp carries the softmax state of 4 queries.
-constexpr int kPrefillQ = 16;
+// One CTA per (query tile, head); 4 warps of PQW queries each (8 at head_dim 64, 4 at
+// 128).  Pages 0..last of the sequence stream through kStages shared-memory stages.
+// Inside a warp, lane = (key group kg of 4 keys) x (dim group dg of head_dim / 8 dims):
+// each lane holds its queries' dims in registers, forms partial scores for 8 x 4
+// (query, key) pairs, joins them over the 8 dim groups with 3 shuffles, and accumulates
+// the output for its 4 keys and its dims; the 4 key groups' outputs are joined once at
+// the end.  FMA-dense, with independent chains across queries and keys.  Online softmax
+// in the exp2 domain as in the decode kernel (the reference's single-pass online softmax,
+// src/model_q8.cpp:485-523, up to fp32 rounding).
 constexpr int kStages = 4;
 
 template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAttnArgs a) {
-    constexpr int TILE = kPage * HD;
-    constexpr int QPW = kPrefillQ / kAttnWarps;  // queries per warp
-    constexpr int DPL = HD / 32;
-    extern __shared__ __align__(128) float smem[];  // [kStages][2][TILE] then q [kPrefillQ][HD]
-    __shared__ uint64_t full[kStages];
-    float* qs = smem + kStages * 2 * TILE;
+struct PrefillCfg {
+    static constexpr int QW = HD == 64 ? 8 : 4;  // queries per warp
+    static constexpr int QT = kAttnWarps * QW;   // queries per CTA
+    static constexpr int DG = HD / 8;            // dims per lane
+};
 
-    const int qt = blockIdx.x, h = blockIdx.y;
-    const int t0 = qt * kPrefillQ;
-    const int nq = min(kPrefillQ, a.T - t0);
+template <int HD>
+__global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAttnArgs a) {
+    using P = PrefillCfg<HD>;
+    constexpr int TILE = kPage * HD;
+    constexpr int QW = P::QW, DG = P::DG;
+    extern __shared__ __align__(128) float smem[];  // [kStages][2][TILE]
+    __shared__ uint64_t full[kStages];
+
+    // blocks in order of decreasing work (later query tiles attend more pages) so the
+    // longest start first: block b takes tile n_tiles - 1 - b / n_heads, head b % n_heads
+    const int n_tiles = (a.T + P::QT - 1) / P::QT;
+    const int qt = n_tiles - 1 - (int)blockIdx.x / a.n_heads, h = (int)blockIdx.x % a.n_heads;
+    const int t0 = qt * P::QT;
+    const int nq = min(P::QT, a.T - t0);
     const int last_pos = a.start_pos + t0 + nq - 1;
     const int n_pages = last_pos / kPage + 1;
     const int kvh = h / (a.n_heads / a.geom.n_kv_heads);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kg = lane >> 3, dg = lane & 7;  // keys kg*4.., dims dg*DG..
+    const int q0 = t0 + warp * QW;            // this warp's first query (token index)
 
     auto issue = [&](int page_idx) {
         const int s = page_idx % kStages;
@@ -467,29 +484,109 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
     grid_dependency_wait();  // q and this chunk's K/V rows come from the projection kernel
     if (threadIdx.x == 0)
         for (int i = 0; i < kStages && i < n_pages; i++) issue(i);
-    const float qscale = kLog2e / sqrtf((float)HD);
-    for (int i = threadIdx.x; i < kPrefillQ * HD; i += blockDim.x) {
-        const int qi = i / HD, d = i % HD;
-        qs[i] = qi < nq ? a.q[((int64_t)(t0 + qi) * a.n_heads + h) * HD + d] * qscale : 0.0f;
-    }
     __syncthreads();
 
-    QState<HD> st[QPW];
+    // this lane's dims of its warp's queries, pre-scaled for the exp2-domain softmax
+    const float qscale = kLog2e / sqrtf((float)HD);
+    float q[QW][DG];
 #pragma unroll
-    for (int j = 0; j < QPW; j++) st[j].init();
+    for (int i = 0; i < QW; i++) {
+        const int t = q0 + i;
+        const float4* src = reinterpret_cast<const float4*>(a.q + ((int64_t)min(t, a.T - 1) * a.n_heads + h) * HD + dg * DG);
+#pragma unroll
+        for (int j = 0; j < DG / 4; j++) {
+            const float4 v = src[j];
+            q[i][4 * j] = v.x * qscale; q[i][4 * j + 1] = v.y * qscale;
+            q[i][4 * j + 2] = v.z * qscale; q[i][4 * j + 3] = v.w * qscale;
+        }
+    }
+    float o[QW][DG], m[QW], l[QW];
+#pragma unroll
+    for (int i = 0; i < QW; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int d = 0; d < DG; d++) o[i][d] = 0.0f;
+    }
+    const int warp_last = a.start_pos + min(q0 + QW, a.T) - 1;  // position of the warp's last query
+
     bool ok = true;
     for (int p = 0; p < n_pages; p++) {
         const int s = p % kStages;
         if (ok && !mbar_wait(&full[s], (p / kStages) & 1, a.err)) ok = false;
-        if (ok) {
+        if (ok && p * kPage <= warp_last) {
+            const float* Kt = smem + (2 * s) * TILE;
+            const float* Vt = smem + (2 * s + 1) * TILE;
+            // scores of (query i, key kg*4 + j) over this lane's dims, then over all dims
+            float sc[QW][4];
 #pragma unroll
-            for (int j = 0; j < QPW; j++) {
-                const int qi = warp + j * kAttnWarps;
-                const int pos = a.start_pos + t0 + qi;
-                const int n_valid = min(kPage, pos - p * kPage + 1);
-                if (qi < nq && n_valid > 0)
-                    attend_page<HD>(st[j], qs + qi * HD, smem + (2 * s) * TILE, smem + (2 * s + 1) * TILE,
-                                    n_valid, lane);
+            for (int j = 0; j < 4; j++) {
+                float kr[DG];
+                const float4* k4 = reinterpret_cast<const float4*>(Kt + (kg * 4 + j) * HD + dg * DG);
+#pragma unroll
+                for (int c = 0; c < DG / 4; c++) {
+                    const float4 v = k4[c];
+                    kr[4 * c] = v.x; kr[4 * c + 1] = v.y; kr[4 * c + 2] = v.z; kr[4 * c + 3] = v.w;
+                }
+#pragma unroll
+                for (int i = 0; i < QW; i++) {
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int d = 0; d < DG; d++) acc = fmaf(q[i][d], kr[d], acc);
+                    sc[i][j] = acc;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < QW; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float v = sc[i][j];
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    v += __shfl_xor_sync(0xffffffffu, v, 4);
+                    sc[i][j] = v;
+                }
+            // causal mask, running max, probabilities, running sum
+#pragma unroll
+            for (int i = 0; i < QW; i++) {
+                const int qpos = a.start_pos + q0 + i;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (p * kPage + kg * 4 + j > qpos) sc[i][j] = -INFINITY;
+                    mx = fmaxf(mx, sc[i][j]);
+                }
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float m_new = fmaxf(m[i], mx);
+                const float corr = m_new == -INFINITY ? 1.0f : exp2f(m[i] - m_new);
+                float ps = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    sc[i][j] = m_new == -INFINITY ? 0.0f : exp2f(sc[i][j] - m_new);
+                    ps += sc[i][j];
+                }
+                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                l[i] = l[i] * corr + ps;
+                m[i] = m_new;
+#pragma unroll
+                for (int d = 0; d < DG; d++) o[i][d] *= corr;
+            }
+            // this lane's 4 keys times their value rows, its dims
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float vr[DG];
+                const float4* v4 = reinterpret_cast<const float4*>(Vt + (kg * 4 + j) * HD + dg * DG);
+#pragma unroll
+                for (int c = 0; c < DG / 4; c++) {
+                    const float4 v = v4[c];
+                    vr[4 * c] = v.x; vr[4 * c + 1] = v.y; vr[4 * c + 2] = v.z; vr[4 * c + 3] = v.w;
+                }
+#pragma unroll
+                for (int i = 0; i < QW; i++)
+#pragma unroll
+                    for (int d = 0; d < DG; d++) o[i][d] = fmaf(sc[i][j], vr[d], o[i][d]);
             }
         }
         // CTA-uniform: every thread leaves together if any wait gave up
@@ -498,14 +595,28 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
     }
     grid_dependents_launch();
     if (!ok) return;
+    // join the 4 key groups' outputs (same running max everywhere), normalise, store
 #pragma unroll
-    for (int j = 0; j < QPW; j++) {
-        const int qi = warp + j * kAttnWarps;
-        if (qi >= nq) continue;
-        float* out = a.out + ((int64_t)(t0 + qi) * a.n_heads + h) * HD + lane * DPL;
-        const float inv = 1.0f / st[j].l;
+    for (int i = 0; i < QW; i++)
 #pragma unroll
-        for (int i = 0; i < DPL; i++) out[i] = st[j].o[i] * inv;
+        for (int d = 0; d < DG; d++) {
+            float v = o[i][d];
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            o[i][d] = v;
+        }
+    if (kg == 0) {
+#pragma unroll
+        for (int i = 0; i < QW; i++) {
+            const int t = q0 + i;
+            if (t >= a.T) continue;
+            const float inv = 1.0f / l[i];
+            float4* dst = reinterpret_cast<float4*>(a.out + ((int64_t)t * a.n_heads + h) * HD + dg * DG);
+#pragma unroll
+            for (int c = 0; c < DG / 4; c++)
+                dst[c] = make_float4(o[i][4 * c] * inv, o[i][4 * c + 1] * inv, o[i][4 * c + 2] * inv,
+                                     o[i][4 * c + 3] * inv);
+        }
     }
 }
 
@@ -593,14 +704,15 @@ void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream
 }
 
 void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
-    dim3 grid((a.T + kPrefillQ - 1) / kPrefillQ, a.n_heads);
     count_launch();
     if (a.geom.head_dim == 64) {
-        const int smem = (kStages * 2 * kPage * 64 + kPrefillQ * 64) * 4;
+        dim3 grid((unsigned)(((a.T + PrefillCfg<64>::QT - 1) / PrefillCfg<64>::QT) * a.n_heads));
+        const int smem = kStages * 2 * kPage * 64 * 4;
         ensure_smem(prefill_attn_kernel<64>, smem);
         launch_ex(prefill_attn_kernel<64>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
     } else {
-        const int smem = (kStages * 2 * kPage * 128 + kPrefillQ * 128) * 4;
+        dim3 grid((unsigned)(((a.T + PrefillCfg<128>::QT - 1) / PrefillCfg<128>::QT) * a.n_heads));
+        const int smem = kStages * 2 * kPage * 128 * 4;
         ensure_smem(prefill_attn_kernel<128>, smem);
         launch_ex(prefill_attn_kernel<128>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
     }

@@ -5,6 +5,8 @@ Bit-exact: block tables, free lists, prefix-cache hits, greedy token ids.
 Within RTOL/ATOL (1e-3 relative, 1e-4 absolute): logits.
 `fixed` engine mode is checked against the ref_fixed build, `faithful` mode against the
 unmodified reference (whose batched Q8 matmul keeps only the last 32-wide block)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -276,6 +278,37 @@ def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B):
         assert_close(le, lr, what=f"raw-tile B={B} decode step {step}")
         for i in range(B):
             _check_tokens(int(am[i]), ref.argmax(lr[i]), lr[i], f"raw-tile B={B} step {step} row {i}")
+        toks = [int(t) for t in am]
+        pos = [p + 1 for p in pos]
+    eng.close()
+    ref.close()
+
+
+def test_head_dim_128_prefill_decode(ref_fixed, model_dir):
+    """head_dim 128 (the 7B shape's heads) on a small model: prefill chunks of 1-130 tokens
+    through the causal attention (4 queries per warp at this head size), then decode,
+    against the reference."""
+    shape = synth.ModelShape(256, 512, 2, 2, 2, 512, 512)
+    path = synth.write_model(os.path.join(model_dir, "hd128.bin"), shape, seed=21)
+    ref = ref_fixed
+    ref.open(path, 256, 96)
+    eng = _engine(path, NR_Q8_FIXED, total_blocks=96)
+    rng = np.random.default_rng(8)
+    lens = [1, 33, 130]
+    rh, eh, toks, pos = [], [], [], []
+    for i, n in enumerate(lens):
+        prompt = rng.integers(0, ref.vocab, n).astype(np.int32)
+        rh.append(ref.new_request(i, prompt))
+        eh.append(eng.seq_create(i))
+        lr = ref.forward_prefill(rh[i], prompt, 0)
+        le, am = eng.forward_prefill_chunk(eh[i], prompt, 0)
+        assert_close(le, lr, what=f"hd128 prefill logits seq {i}")
+        toks.append(am)
+        pos.append(n)
+    for step in range(3):
+        lr = ref.forward_decode(toks, pos, rh)
+        le, am = eng.forward_decode_batch(toks, pos, eh)
+        assert_close(le, lr, what=f"hd128 decode step {step}")
         toks = [int(t) for t in am]
         pos = [p + 1 for p in pos]
     eng.close()
