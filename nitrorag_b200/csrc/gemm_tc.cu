@@ -601,15 +601,19 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             // 64-token tiles of the Q8 kernel: this thread's activation unit and gain slice of
             // the next chunk are requested one chunk ahead (the fp32-weight classifier kernel,
             // limited to 96 registers for two CTAs per SM, loads them per chunk)
-            constexpr bool XPF = NT == 64 && !F32W;
-            float4 xn[4], gn[4];
+            constexpr bool XPF = NT <= 128 && !F32W;
+            constexpr int XU = NT <= 128 ? NT / 64 : 1;  // activation units per thread
+            float4 xn[XU][4], gn[4];
             auto fetch_x = [&](int it) {
                 const int k = (c_first + it) * TC_KC + ukq * 16;
-                if (m_base + ur < a.M) {
-                    const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)(m_base + ur) * a.ldx + k);
 #pragma unroll
-                    for (int j = 0; j < 4; j++) xn[j] = src[j];
-                }
+                for (int u = 0; u < XU; u++)
+                    if (m_base + ur + 64 * u < a.M) {
+                        const float4* src =
+                            reinterpret_cast<const float4*>(a.x + (int64_t)(m_base + ur + 64 * u) * a.ldx + k);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) xn[u][j] = src[j];
+                    }
                 if (a.norm_gain) {
                     const float4* g4 = reinterpret_cast<const float4*>(a.norm_gain + k);
 #pragma unroll
@@ -620,15 +624,6 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             for (int it = 0; it < nch; it++) {
                 const int st = it % stages, use = it / stages;
                 const int k0 = (c_first + it) * TC_KC;
-                float4 xc[4], gc[4];
-                if (XPF) {
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        xc[j] = xn[j];
-                        gc[j] = gn[j];
-                    }
-                    if (it + 1 < nch) fetch_x(it + 1);
-                }
                 WRegs<F32W> nxt;
                 if (!a.wt && !use_raw && it + 1 < nch) load_w<F32W>(nxt, a, n, k0 + TC_KC + wg * 32);
                 // the stage was last read by the MMAs of chunk it - stages
@@ -640,13 +635,19 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                                     stage_ptr(st, 1), row, wg);
                     else if (!a.wt)
                         stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
-                    if (XPF)
-                        stage_x16(xc, a.norm_gain ? reinterpret_cast<const float*>(gc) : nullptr, m_base + ur < a.M,
-                                  stage_ptr(st, 2), stage_ptr(st, 3), ur, ukq);
-                    else
+                    if (XPF) {
+#pragma unroll
+                        for (int u = 0; u < XU; u++)
+                            stage_x16(xn[u], a.norm_gain ? reinterpret_cast<const float*>(gn) : nullptr,
+                                      m_base + ur + 64 * u < a.M, stage_ptr(st, 2), stage_ptr(st, 3), ur + 64 * u, ukq);
+                    } else {
                         stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2),
                                           stage_ptr(st, 3), tid);
+                    }
                 }
+                // the next chunk's activations (and gain) load while this one goes through
+                // the barrier and the MMAs
+                if (XPF && it + 1 < nch) fetch_x(it + 1);
                 fence_async_smem();
                 named_arrive(1 + st, TC_THREADS);
                 if (!a.wt && !use_raw && it + 1 < nch) cur = nxt;
