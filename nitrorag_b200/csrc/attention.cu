@@ -387,6 +387,99 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
     }
 }
 
+// Small batches (B x n_heads up to the SM count): one CTA per (sequence, head), its warps
+// taking the sequence's pages round-robin through their own bulk-copy rings and joining
+// their softmax states in shared memory (in warp order), so neither split partials in
+// global memory nor the merge kernel are needed.
+template <int HD>
+struct DecSmall {
+    static constexpr int WARPS = HD == 64 ? 8 : 6;
+    static constexpr int STAGES = HD == 64 ? 3 : 2;
+    static constexpr int TILE = kPage * HD;
+    static constexpr int RING_FLOATS = WARPS * STAGES * 2 * TILE;
+    static constexpr int SMEM = RING_FLOATS * 4 + HD * 4 + WARPS * (HD + 2) * 4;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small_kernel(DecodeAttnArgs a) {
+    using C = DecSmall<HD>;
+    constexpr int DPL = HD / 32;
+    constexpr int W = C::WARPS, S = C::STAGES;
+    extern __shared__ __align__(128) float smem[];
+    __shared__ uint64_t bars[W][S];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x / a.n_heads, h = blockIdx.x % a.n_heads;
+    const int kvh = h / (a.n_heads / a.geom.n_kv_heads);
+    float* ring = smem + warp * S * 2 * C::TILE;
+    float* qs = smem + C::RING_FLOATS;
+    float* part = qs + HD;  // [W][HD + 2]: o, then m, l
+
+    // page ids of this warp's pages (descriptor data: read before the wait)
+    const int ctx = a.ctx_lens[b];
+    const int pages = (ctx + kPage - 1) / kPage;
+    const int mine = pages > warp ? (pages - warp + W - 1) / W : 0;  // pages warp, warp+W, ...
+    if (lane < S) mbar_init(&bars[warp][lane], 1);
+    fence_barrier_init();
+    __syncwarp();
+    grid_dependency_wait();  // q and the newest K/V rows come from the previous kernel
+    const float qscale = kLog2e / sqrtf((float)HD);
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) qs[i] = a.q[((int64_t)b * a.n_heads + h) * HD + i] * qscale;
+    auto issue = [&](int j) {  // the warp's j-th page -> slot j % S (lane 0)
+        const int p = warp + j * W;
+        const int page = a.block_tables[(int64_t)b * a.max_pages + p];
+        const int64_t off = a.geom.tile_offset(page, a.layer, kvh);
+        uint64_t* bar = &bars[warp][j % S];
+        mbar_arrive_expect_tx(bar, 2u * C::TILE * 4u);
+        bulk_g2s(ring + (2 * (j % S)) * C::TILE, a.kpool + off, C::TILE * 4, bar);
+        bulk_g2s(ring + (2 * (j % S) + 1) * C::TILE, a.vpool + off, C::TILE * 4, bar);
+    };
+    if (lane == 0)
+        for (int j = 0; j < S && j < mine; j++) issue(j);
+    __syncthreads();  // q in shared memory
+
+    QState<HD> st;
+    st.init();
+    bool ok = true;
+    for (int j = 0; j < mine; j++) {
+        const int slot = j % S;
+        if (ok && !mbar_wait(&bars[warp][slot], (j / S) & 1, a.err)) ok = false;
+        if (ok) {
+            const int first = (warp + j * W) * kPage;
+            attend_page<HD>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
+                            min(kPage, ctx - first), lane);
+        }
+        __syncwarp();  // every lane is done with the slot before it is refilled
+        if (lane == 0 && ok && j + S < mine) issue(j + S);
+    }
+    grid_dependents_launch();
+    float* pw = part + warp * (HD + 2);
+#pragma unroll
+    for (int i = 0; i < DPL; i++) pw[lane * DPL + i] = st.o[i];
+    if (lane == 0) {
+        pw[HD] = mine > 0 && ok ? st.m : -INFINITY;
+        pw[HD + 1] = mine > 0 && ok ? st.l : 0.0f;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float gm = -INFINITY;
+        for (int w = 0; w < W; w++) gm = fmaxf(gm, part[w * (HD + 2) + HD]);
+        float gl = 0.0f, go[DPL];
+#pragma unroll
+        for (int i = 0; i < DPL; i++) go[i] = 0.0f;
+        for (int w = 0; w < W; w++) {
+            const float mw = part[w * (HD + 2) + HD];
+            const float c = mw == -INFINITY ? 0.0f : exp2f(mw - gm);
+            gl += part[w * (HD + 2) + HD + 1] * c;
+#pragma unroll
+            for (int i = 0; i < DPL; i++) go[i] += part[w * (HD + 2) + lane * DPL + i] * c;
+        }
+        const float inv = 1.0f / gl;
+        float* out = a.out + ((int64_t)b * a.n_heads + h) * HD + lane * DPL;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) out[i] = go[i] * inv;
+    }
+}
+
 // Combine the splits of every (sequence, head) whose context spans more than one chunk:
 // one warp per (sequence, head), weights exp2(m_s - max) broadcast by shuffle.
 template <int HD>
@@ -681,6 +774,18 @@ static int sm_count() {
 void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream_t s) {
     count_launch();
     const int grid = sm_count();
+    if ((int64_t)args.B * args.n_heads <= grid) {  // small batch: one CTA per (sequence, head)
+        const dim3 g((unsigned)(args.B * args.n_heads));
+        if (args.geom.head_dim == 64) {
+            ensure_smem(decode_attn_small_kernel<64>, DecSmall<64>::SMEM);
+            launch_ex(decode_attn_small_kernel<64>, g, dim3(DecSmall<64>::WARPS * 32), DecSmall<64>::SMEM, s, 1, args);
+        } else {
+            ensure_smem(decode_attn_small_kernel<128>, DecSmall<128>::SMEM);
+            launch_ex(decode_attn_small_kernel<128>, g, dim3(DecSmall<128>::WARPS * 32), DecSmall<128>::SMEM, s, 1,
+                      args);
+        }
+        return;
+    }
     // chunk length: the longest (default) that still gives every warp about two items,
     // estimated from the longest context of the step
     DecodeAttnArgs a = args;
