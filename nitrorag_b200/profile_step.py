@@ -1,36 +1,60 @@
-"""One decode step of a 64-request batch inside a CUDA profiler range, for capturing
-individual kernels with a profiler started as `--profile-from-start off`:
+"""One engine step inside a CUDA profiler range, for capturing individual kernels with a
+profiler started as `--profile-from-start off`:
 
     ncu --profile-from-start off --set full --clock-control none -k regex:tc_gemm -c 1 \\
-        -o out python -m nitrorag_b200.profile_step
+        -o out python -m nitrorag_b200.profile_step [--batch B] [--prefill T]
 
-The case is the benchmark's decode step shape (110M Q8_0 model, 64 sequences) with short
-prompts (U[128, 200] tokens) and a 1024-page pool, so the device holds ~1.7 GB: small
-enough for multi-pass captures, with weights and K/V still far larger than L2.  The step
-runs eagerly (no CUDA graph) so each kernel is an ordinary launch.
+Default: one decode step of 64 sequences of the 110M Q8_0 model (contexts U[128, 200],
+1024-page pool, so the device holds ~1.7 GB: small enough for multi-pass captures, with
+weights and K/V still far larger than L2).  `--batch B` decodes B sequences instead;
+`--prefill T` instead profiles the prefill of one T-token prompt (T <= 1024, model
+header with seq_len 2048).  The step runs eagerly (no CUDA graph) so each kernel is an
+ordinary launch.
 """
 from __future__ import annotations
 
+import argparse
 import os
 import sys
 
 
 def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prefill", type=int, default=0)
+    args = ap.parse_args()
     os.environ.setdefault("NITRO_GRAPHS", "0")
     import numpy as np
     import torch
 
     from . import EngineConfig, NitroEngine, synth
 
+    rng = np.random.default_rng(3)
+    if args.prefill:
+        T = min(args.prefill, 1024)
+        model = synth.cached_model(synth.SHAPE_110M_LONG, seed=1234)
+        eng = NitroEngine(model, EngineConfig(total_blocks=256, max_new_tokens=100000, max_batch=8,
+                                              max_prefill_tokens=1024, device=0))
+        warm = eng.seq_create(0)
+        prompt = rng.integers(1, 32000, T).astype(np.int32)
+        eng.forward_prefill_chunk(warm, prompt, 0, want_logits=False)
+        seq = eng.seq_create(1)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        eng.forward_prefill_chunk(seq, prompt, 0, want_logits=False)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(f"profiled the prefill of one {T}-token prompt")
+        return 0
+    B = max(1, min(args.batch, 64))
     model = synth.cached_model(synth.SHAPE_110M, seed=1234)
     eng = NitroEngine(model, EngineConfig(total_blocks=1024, max_new_tokens=100000, max_batch=64,
                                           max_prefill_tokens=256, device=0))
-    rng = np.random.default_rng(3)
-    for i in range(64):
+    for i in range(B):
         eng.add_request(i, rng.integers(1, 32000, int(rng.integers(128, 201))).astype(np.int32))
     while True:  # admission, one prefill per step (the reference scheduler's order)
         r = eng.step()
-        if len(eng.running_batch()) == 64 and r.prefill_req_id < 0:
+        if len(eng.running_batch()) == B and r.prefill_req_id < 0:
             break
     eng.step()
     eng.replay_decode(3)
@@ -39,7 +63,7 @@ def main() -> int:
     eng.replay_decode(1)
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
-    print("profiled one decode step of 64 sequences")
+    print(f"profiled one decode step of {B} sequences")
     return 0
 
 
