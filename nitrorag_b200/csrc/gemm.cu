@@ -651,12 +651,10 @@ bool gemm_uses_tc(int M, int N, int K) {
 
 template <int MT, bool F32W>
 void launch_stream(const GemmArgs& a, const Epilogue& e, const StreamPlan& sp, cudaStream_t s) {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
+    if (sms <= 0) sms = 148;
     const int smem = sp.x_bytes + sp.warps * SG_SLOTS * sp.slot_bytes;
     cudaFuncSetAttribute(gemv_stream_kernel<MT, F32W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     const int pairs = a.N / 2;
