@@ -313,3 +313,34 @@ def test_head_dim_128_prefill_decode(ref_fixed, model_dir):
         pos = [p + 1 for p in pos]
     eng.close()
     ref.close()
+
+
+@pytest.mark.parametrize("shape_args", [(512, 1024, 2, 8, 2, 512, 1024), (256, 512, 2, 2, 1, 512, 1024)],
+                         ids=["hd64-gqa4", "hd128-gqa2"])
+def test_single_sequence_decode_grouped_kv(ref_fixed, model_dir, shape_args):
+    """Batch-1 decode (one attention CTA per head, matvec projections) with grouped KV heads
+    at both head sizes: a context that grows from 300 to 323 tokens (up to 21 pages, so the
+    attention warps cycle their page rings), 24 greedy steps with logits against the
+    reference."""
+    shape = synth.ModelShape(*shape_args)
+    path = synth.write_model(os.path.join(model_dir, f"b1_{shape.dim}_{shape.n_heads}.bin"), shape, seed=5)
+    ref = ref_fixed
+    ref.open(path, 512, 96)
+    eng = _engine(path, NR_Q8_FIXED, total_blocks=96, max_new=32, max_batch=4, max_prefill=512)
+    prompt = np.random.default_rng(12).integers(0, ref.vocab, 300).astype(np.int32)
+    rh = ref.new_request(0, prompt)
+    eh = eng.seq_create(0)
+    lr = ref.forward_prefill(rh, prompt, 0)
+    le, tok = eng.forward_prefill_chunk(eh, prompt, 0)
+    assert_close(le, lr, what="prefill logits")
+    pos = len(prompt)
+    for step in range(24):
+        lr = ref.forward_decode([tok], [pos], [rh])
+        le, am = eng.forward_decode_batch([tok], [pos], [eh])
+        assert_close(le[0], lr[0], what=f"decode step {step}")
+        _check_tokens(int(am[0]), ref.argmax(lr[0]), lr[0], f"decode step {step}")
+        tok = int(am[0])
+        pos += 1
+    assert eng.block_table(eh) == ref.block_table(rh)
+    eng.close()
+    ref.close()
