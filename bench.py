@@ -610,6 +610,73 @@ def engine_arm(args, rank, world, local_rank):
     return 0
 
 
+def run_quantize(args):
+    """The GPU Q8_0 quantizer (scripts/quantize.py's quantize_q8) on the 7B shape's
+    w1 + w3 of 4 layers as one flat tensor (4 x 2 x 11008 x 4096 = 360.7 M weights, 1.44 GB
+    fp32 in, 406 MB out: larger than L2, so no flush between launches).
+    value = weights/s of the device pass (CUDA events on the launching stream);
+    e2e = nr_quantize_q8 from/to host numpy buffers (pinned-slot pipeline, H2D/D2H in the
+    timed region); roofline: 5.125 algorithmic bytes per weight (4 read, 1.125 written)
+    against the measured HBM copy bandwidth; cpu_baseline: the CPU restatement
+    (oracle/nitro_oracle.cpp, one thread) on a bounded sample."""
+    import torch
+    from nitrorag_b200 import quantize_q8, quantized_size
+    from nitrorag_b200._lib import lib
+    peak, peak_src = load_peaks()
+    n = 4 * 2 * 11008 * 4096
+    g = torch.Generator(device="cuda").manual_seed(5)
+    w = torch.randn(n, generator=g, device="cuda", dtype=torch.float32) * 0.02
+    out = torch.empty(quantized_size(n), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def launch():
+        rc = lib().nr_quantize_q8_device(w.data_ptr(), n, out.data_ptr(), stream.cuda_stream)
+        assert rc == 0, rc
+
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = _dev_events(torch, stream)
+    e0.record(stream)
+    for _ in range(args.steps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    algo = 5.125 * n
+    # e2e through host buffers: a 64 M-weight tensor (256 MB in), two runs
+    n_h = 64 << 20
+    w_h = w[:n_h].cpu().numpy()
+    quantize_q8(w_h[: 1 << 20])
+    t0 = time.perf_counter()
+    reps = 2
+    for _ in range(reps):
+        host_out = quantize_q8(w_h)
+    e2e_s = (time.perf_counter() - t0) / reps
+    line = {"workload": "quantize", "metric": "Q8_0 quantize weights/s (scripts/quantize.py quantize_q8)",
+            "value": round(n / (ms * 1e-3) / 1e9, 2), "unit": "Gweights/s", "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "dtype": "f32->q8_0", "data": "synthetic",
+            "config": {"workload": "quantize", "weights": n, "flush": "inputs 1.44 GB > L2"},
+            "e2e": {"value": round(n_h / e2e_s / 1e9, 3), "unit": "Gweights/s", "weights": n_h,
+                    "h2d_bytes_per_step": 4 * n_h, "d2h_bytes_per_step": len(host_out)},
+            "roofline": {"bound": "hbm", "achieved": round(algo / (ms * 1e-3) / 1e9, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(algo / (ms * 1e-3) / 1e9 / peak, 4),
+                         "bytes_per_weight": 5.125, "peak_source": peak_src},
+            "gpu_launches": args.steps, "steps": args.steps, "warmup": args.warmup}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        r = oracle.Restatement()
+        n_c = 16 << 20
+        sample = w_h[:n_c]
+        t0 = time.perf_counter()
+        r.quantize_q8(sample)
+        cpu_s = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(n_c / cpu_s / 1e9, 4), "unit": "Gweights/s", "cores": 1,
+                                "kind": "port", "sample": f"{n_c} weights through orc_quantize_q8 (scalar C)"}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -619,7 +686,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="mark the timed device-resident replays as the CUDA profiler range")
-    ap.add_argument("--workload", choices=["decode64", "config1", "config3", "config4", "config5"],
+    ap.add_argument("--workload", choices=["decode64", "config1", "config3", "config4", "config5", "quantize"],
                     default="decode64", help="decode64 is the headline; the others print their own line")
     ap.add_argument("--batch", type=int, default=0, help="config5: requests per GPU (default 64)")
     args = ap.parse_args()
@@ -637,7 +704,7 @@ def main():
     if args.workload != "decode64":
         if rank == 0:
             fn = {"config1": run_config1, "config3": run_config3, "config4": run_config4,
-                  "config5": run_config5}[args.workload]
+                  "config5": run_config5, "quantize": run_quantize}[args.workload]
             print(json.dumps(fn(args)), flush=True)
         return 0
     return engine_arm(args, rank, world, local_rank)

@@ -251,6 +251,25 @@ int nr_paged_attention_decode_static(const float* q, const float* kpool, const f
 int nr_q8_matmul(const float* x, const int8_t* q, const float* scales, float* out,
                  int32_t M, int32_t N, int32_t K, int32_t q8_mode, void* stream);
 
+/* ------------------------------------------------------------------ Q8_0 quantizer
+ * scripts/quantize.py (quantize_q8, :7-23) byte for byte: per 32 consecutive weights (the
+ * last block of a tensor may be shorter) scale = max|w| / 127 in fp32 (1e-9 for an
+ * all-zero block), q = round-half-to-even(w / scale) clamped to [-128, 127]; each block
+ * is written as its scale (4 bytes, little-endian fp32) followed by its q bytes.  Weights
+ * must be finite (the script raises on NaN). */
+size_t nr_q8_quantized_size(int64_t n);
+/* Device buffers: w 16-byte aligned, out 4-byte aligned with nr_q8_quantized_size(n)
+ * bytes; enqueued on `stream` (a cudaStream_t; NULL = legacy default stream). */
+int nr_quantize_q8_device(const float* w, int64_t n, uint8_t* out, void* stream);
+/* Host buffers, on GPU `device`: streamed in 16 M-weight pieces through two pinned and
+ * two device slots (made on the first call on a device, ~164 MB each side, and kept), the
+ * copies of one piece overlapping the kernel of the other; returns when done. */
+int nr_quantize_q8(const float* w, int64_t n, uint8_t* out, int32_t device);
+/* The script's driver (quantize.py:27-60): read a llama2.c-format fp32 checkpoint, write
+ * the Q8_0 model file (header and fp32 tensors copied, wq wk wv wo w1 w2 w3 quantized,
+ * each as one flat array), on GPU `device`. */
+int nr_quantize_model_file(const char* in_path, const char* out_path, int32_t device);
+
 #ifdef __cplusplus
 }
 #endif

@@ -6,6 +6,8 @@ model/workload generators.  Importing the package does not require a GPU; creati
 GPU engine does, and fails loudly when the library or the device is missing."""
 from .engine import (FNV_OFFSET_BASIS, NR_Q8_FAITHFUL, NR_Q8_FIXED, EngineConfig, NitroEngine, NrError,
                      StepResult, argmax, hash_block_state)
+from .quantize import quantize_model_file, quantize_q8, quantized_size
 
 __all__ = ["NitroEngine", "EngineConfig", "StepResult", "NrError", "hash_block_state", "argmax",
-           "NR_Q8_FIXED", "NR_Q8_FAITHFUL", "FNV_OFFSET_BASIS"]
+           "NR_Q8_FIXED", "NR_Q8_FAITHFUL", "FNV_OFFSET_BASIS", "quantize_q8", "quantize_model_file",
+           "quantized_size"]

@@ -110,6 +110,10 @@ SIGNATURES = {
     "nr_paged_attention_decode": (C.c_int, [P, P, P, P, I32, P, I32, I32, I32, I32, I32, I32, P, P, P, P]),
     "nr_paged_attention_decode_static": (C.c_int, [P, P, P, P, I32, P, I32, I32, I32, I32, I32, I32, P, P, P]),
     "nr_q8_matmul": (C.c_int, [P, P, P, P, I32, I32, I32, I32, P]),
+    "nr_q8_quantized_size": (C.c_size_t, [C.c_int64]),
+    "nr_quantize_q8_device": (C.c_int, [P, C.c_int64, P, P]),
+    "nr_quantize_q8": (C.c_int, [P, C.c_int64, P, I32]),
+    "nr_quantize_model_file": (C.c_int, [C.c_char_p, C.c_char_p, I32]),
 }
 
 _lib = None

@@ -622,4 +622,32 @@ int nr_q8_matmul(const float* x, const int8_t* q, const float* scales, float* ou
     return cudaGetLastError() == cudaSuccess ? NR_OK : NR_ERR_CUDA;
 }
 
+size_t nr_q8_quantized_size(int64_t n) { return nitro::q8_quantized_bytes(n); }
+
+int nr_quantize_q8_device(const float* w, int64_t n, uint8_t* out, void* stream) {
+    if (n < 0 || (n > 0 && (!w || !out))) return NR_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(out) % 4) return NR_ERR_INVALID;
+    nitro::launch_quantize_q8(w, n, out, (cudaStream_t)stream);
+    return cudaGetLastError() == cudaSuccess ? NR_OK : NR_ERR_CUDA;
+}
+
+static int select_device(int32_t device) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) return NR_ERR_NO_DEVICE;
+    if (device < 0 || device >= count) return NR_ERR_INVALID;
+    return cudaSetDevice(device) == cudaSuccess ? NR_OK : NR_ERR_CUDA;
+}
+
+int nr_quantize_q8(const float* w, int64_t n, uint8_t* out, int32_t device) {
+    if (n < 0 || (n > 0 && (!w || !out))) return NR_ERR_INVALID;
+    const int rc = select_device(device);
+    return rc != NR_OK ? rc : nitro::quantize_q8_host(w, n, out);
+}
+
+int nr_quantize_model_file(const char* in_path, const char* out_path, int32_t device) {
+    if (!in_path || !out_path) return NR_ERR_INVALID;
+    const int rc = select_device(device);
+    return rc != NR_OK ? rc : nitro::quantize_model_file(in_path, out_path);
+}
+
 }  // extern "C"

@@ -38,16 +38,19 @@ inline int8_t blk_q(const uint8_t* w, int64_t blk, int k) { return (int8_t)w[blk
 extern "C" {
 
 // scripts/quantize.py:7-23: per 32 weights scale = absmax/127 (fp32), 1e-9 for an
-// all-zero block; q = round-half-even(w/scale) clamped to [-128,127].
+// all-zero block; q = round-half-even(w/scale) clamped to [-128,127].  The last block
+// of a tensor whose length is not a multiple of 32 is shorter (quantize.py:10-11): its
+// scale and its len q bytes follow the full blocks.
 void orc_quantize_q8(const float* w, int64_t n, uint8_t* out) {
-    for (int64_t b = 0; b < n / QB; b++) {
+    for (int64_t b = 0; b * QB < n; b++) {
         const float* blk = w + b * QB;
+        const int len = n - b * QB < QB ? (int)(n - b * QB) : QB;
         float amax = 0.0f;
-        for (int k = 0; k < QB; k++) amax = fmaxf(amax, fabsf(blk[k]));
+        for (int k = 0; k < len; k++) amax = fmaxf(amax, fabsf(blk[k]));
         float scale = amax != 0.0f ? amax / 127.0f : 1e-9f;
         uint8_t* o = out + b * 36;
         memcpy(o, &scale, 4);
-        for (int k = 0; k < QB; k++) {
+        for (int k = 0; k < len; k++) {
             float r = nearbyintf(blk[k] / scale);   // default rounding mode: half to even
             int q = (int)r;
             q = q < -128 ? -128 : (q > 127 ? 127 : q);

@@ -81,7 +81,8 @@ class Restatement:
     # kernels
     def quantize_q8(self, w) -> bytes:
         w = _f32(w).ravel()
-        out = np.zeros(len(w) // 32 * 36, np.uint8)
+        rem = len(w) % 32
+        out = np.zeros(len(w) // 32 * 36 + (4 + rem if rem else 0), np.uint8)
         self.L.orc_quantize_q8(_p(w, PF), len(w), _p(out, PU8))
         return out.tobytes()
 
