@@ -258,8 +258,8 @@ int nr_q8_matmul(const float* x, const int8_t* q, const float* scales, float* ou
  * is written as its scale (4 bytes, little-endian fp32) followed by its q bytes.  Weights
  * must be finite (the script raises on NaN). */
 size_t nr_q8_quantized_size(int64_t n);
-/* Device buffers: w 16-byte aligned, out 4-byte aligned with nr_q8_quantized_size(n)
- * bytes; enqueued on `stream` (a cudaStream_t; NULL = legacy default stream). */
+/* Device buffers: w and out 16-byte aligned, out of nr_q8_quantized_size(n) bytes;
+ * enqueued on `stream` (a cudaStream_t; NULL = legacy default stream). */
 int nr_quantize_q8_device(const float* w, int64_t n, uint8_t* out, void* stream);
 /* Host buffers, on GPU `device`: streamed in 16 M-weight pieces through two pinned and
  * two device slots (made on the first call on a device, ~164 MB each side, and kept), the

@@ -626,7 +626,7 @@ size_t nr_q8_quantized_size(int64_t n) { return nitro::q8_quantized_bytes(n); }
 
 int nr_quantize_q8_device(const float* w, int64_t n, uint8_t* out, void* stream) {
     if (n < 0 || (n > 0 && (!w || !out))) return NR_ERR_INVALID;
-    if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(out) % 4) return NR_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(out) % 16) return NR_ERR_INVALID;
     nitro::launch_quantize_q8(w, n, out, (cudaStream_t)stream);
     return cudaGetLastError() == cudaSuccess ? NR_OK : NR_ERR_CUDA;
 }

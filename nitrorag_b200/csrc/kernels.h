@@ -123,15 +123,7 @@ struct PrefillAttnArgs {
 void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
 
 // Q8_0 quantizer of scripts/quantize.py:7-23 (quantize.cu): bytes of n weights' blocks,
-// the device pass (w 16-byte aligned, out 4-byte aligned), the host-buffer pass through
-// pinned slots, and the script's whole-file conversion (NR_* status codes).
-size_t q8_quantized_bytes(int64_t n);
-void launch_quantize_q8(const float* w, int64_t n, uint8_t* out, cudaStream_t s);
-int quantize_q8_host(const float* w, int64_t n, uint8_t* out);
-int quantize_model_file(const char* in_path, const char* out_path);
-
-// Q8_0 quantizer of scripts/quantize.py:7-23 (quantize.cu): bytes of n weights' blocks,
-// the device pass (w 16-byte aligned, out 4-byte aligned), the host-buffer pass through
+// the device pass (w and out 16-byte aligned), the host-buffer pass through
 // pinned slots, and the script's whole-file conversion (NR_* status codes).
 size_t q8_quantized_bytes(int64_t n);
 void launch_quantize_q8(const float* w, int64_t n, uint8_t* out, cudaStream_t s);
