@@ -45,6 +45,13 @@ extern "C" {
 #define NR_Q8_FAITHFUL  1   /* last block only, as the shipped batched path computes     */
 
 #define NR_SCHED_REFERENCE   0  /* Continuous_Scheduler::step, src/pagedMemory.hpp:317-398 */
+/* Same release and decode rules; admission goes on past the FIFO head while token budget
+ * is left (a request whose prompt completes makes room for the next), each new request
+ * only if the pages of its whole remaining prompt fit in the free and reclaimable
+ * (cached, unreferenced) pages left after the step's decode rows and earlier chunks (or
+ * nothing else runs).  All chunks of a step run in one forward pass.  No reference
+ * counterpart. */
+#define NR_SCHED_PACKED      1
 
 typedef struct nr_config {
     int32_t total_blocks;          /* KV pool pages (reference TOTAL_BLOCKS, Server_Inference.cpp:85) */
@@ -105,17 +112,22 @@ typedef struct nr_step_out {
     int32_t* emitted_req_ids;  /* [emitted_cap] request id per emitted token (prefill first, then decode rows) */
     int32_t* emitted_tokens;   /* [emitted_cap] greedy token ids (argmax, src/model_q8.cpp:559) */
     float*   emitted_logits;   /* [emitted_cap * vocab] or NULL: logits row per emitted token */
+    /* filled by the engine */
+    int32_t n_prefill;         /* prompt chunks run this step (reference mode: 0 or 1); prefill_req_id
+                                  is the first one's request, prefill_tokens and prefill_hits the totals */
 } nr_step_out;
 
 /* One scheduler iteration: release finished requests, gather the decode batch, admit at
  * most one waiting request (prefix-cache scan then one prompt chunk within the token
- * budget), run the prefill chunk and the decode batch on the GPU, sample greedily. */
+ * budget; NR_SCHED_PACKED: several), run the prefill chunk(s) and the decode batch on the
+ * GPU, sample greedily. */
 int nr_step(nr_engine* e, nr_step_out* out);
 
 /* The same iteration split in two for a host-only engine or an external executor:
  * nr_step_plan does everything up to the forward passes (including every block
  * allocation the forwards would make, in the reference's order); nr_step_commit records
- * the sampled tokens (prefill token first if the plan has one, then one per decode row). */
+ * the sampled tokens (one per chunk that completes its prompt, in chunk order, then one
+ * per decode row). */
 typedef struct nr_plan {
     int32_t n_released;
     int32_t prefill_req_id;    /* -1 if none */
@@ -126,6 +138,13 @@ typedef struct nr_plan {
     int32_t n_decode;
     int32_t decode_cap;        /* caller: capacity of decode_req_ids */
     int32_t* decode_req_ids;   /* caller-owned [decode_cap] */
+    /* every prompt chunk of the step (the prefill_* fields above describe the first): */
+    int32_t n_prefill;
+    int32_t prefill_cap;       /* caller: capacity of the four arrays below (each may be NULL) */
+    int32_t* prefill_req_ids;
+    int32_t* prefill_starts;
+    int32_t* prefill_lens;
+    int32_t* prefill_dones;
 } nr_plan;
 int nr_step_plan(nr_engine* e, nr_plan* plan);
 int nr_step_commit(nr_engine* e, const nr_plan* plan, const int32_t* tokens, int32_t n_tokens);

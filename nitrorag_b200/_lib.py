@@ -18,6 +18,8 @@ NR_ERR = {
 KERNEL_CLASSES = ["embed", "qkv", "attention", "wo", "w13", "w2", "logits", "argmax"]
 NR_Q8_FIXED = 0
 NR_Q8_FAITHFUL = 1
+NR_SCHED_REFERENCE = 0
+NR_SCHED_PACKED = 1
 
 
 class EngineLibraryMissing(RuntimeError):
@@ -39,6 +41,7 @@ class NrStepOut(C.Structure):
         ("prefill_hits", C.c_int32), ("n_decode", C.c_int32), ("n_emitted", C.c_int32),
         ("emitted_cap", C.c_int32), ("emitted_req_ids", C.POINTER(C.c_int32)),
         ("emitted_tokens", C.POINTER(C.c_int32)), ("emitted_logits", C.POINTER(C.c_float)),
+        ("n_prefill", C.c_int32),
     ]
 
 
@@ -47,6 +50,9 @@ class NrPlan(C.Structure):
         ("n_released", C.c_int32), ("prefill_req_id", C.c_int32), ("prefill_start", C.c_int32),
         ("prefill_tokens", C.c_int32), ("prefill_done", C.c_int32), ("prefill_hits", C.c_int32),
         ("n_decode", C.c_int32), ("decode_cap", C.c_int32), ("decode_req_ids", C.POINTER(C.c_int32)),
+        ("n_prefill", C.c_int32), ("prefill_cap", C.c_int32), ("prefill_req_ids", C.POINTER(C.c_int32)),
+        ("prefill_starts", C.POINTER(C.c_int32)), ("prefill_lens", C.POINTER(C.c_int32)),
+        ("prefill_dones", C.POINTER(C.c_int32)),
     ]
 
 

@@ -551,12 +551,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
     __shared__ uint64_t full[kStages];
 
     // blocks in order of decreasing work (later query tiles attend more pages) so the
-    // longest start first: block b takes tile n_tiles - 1 - b / n_heads, head b % n_heads
-    const int n_tiles = (a.T + P::QT - 1) / P::QT;
-    const int qt = n_tiles - 1 - (int)blockIdx.x / a.n_heads, h = (int)blockIdx.x % a.n_heads;
+    // longest start first: block b takes tile n_tiles - 1 - b / n_heads, head b % n_heads;
+    // with several sequences the tile table holds that order (written with the descriptor,
+    // before the kernel chain of the step)
+    int T = a.T, start_pos = a.start_pos, row0 = 0, qt;
+    const int* bt = a.block_table;
+    const int h = (int)blockIdx.x % a.n_heads;
+    if (a.seg) {
+        const int j = (int)blockIdx.x / a.n_heads;
+        const int sg = a.tiles[2 * j];
+        qt = a.tiles[2 * j + 1];
+        row0 = a.seg[4 * sg];
+        T = a.seg[4 * sg + 1];
+        start_pos = a.seg[4 * sg + 2];
+        bt = a.block_table + a.seg[4 * sg + 3];
+    } else {
+        qt = (T + P::QT - 1) / P::QT - 1 - (int)blockIdx.x / a.n_heads;
+    }
     const int t0 = qt * P::QT;
-    const int nq = min(P::QT, a.T - t0);
-    const int last_pos = a.start_pos + t0 + nq - 1;
+    const int nq = min(P::QT, T - t0);
+    const int last_pos = start_pos + t0 + nq - 1;
     const int n_pages = last_pos / kPage + 1;
     const int kvh = h / (a.n_heads / a.geom.n_kv_heads);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -565,7 +579,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
 
     auto issue = [&](int page_idx) {
         const int s = page_idx % kStages;
-        const int64_t off = a.geom.tile_offset(a.block_table[page_idx], a.layer, kvh);
+        const int64_t off = a.geom.tile_offset(bt[page_idx], a.layer, kvh);
         mbar_arrive_expect_tx(&full[s], 2u * TILE * 4u);
         bulk_g2s(smem + (2 * s) * TILE, a.kpool + off, TILE * 4, &full[s]);
         bulk_g2s(smem + (2 * s + 1) * TILE, a.vpool + off, TILE * 4, &full[s]);
@@ -585,7 +599,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
 #pragma unroll
     for (int i = 0; i < QW; i++) {
         const int t = q0 + i;
-        const float4* src = reinterpret_cast<const float4*>(a.q + ((int64_t)min(t, a.T - 1) * a.n_heads + h) * HD + dg * DG);
+        const float4* src =
+            reinterpret_cast<const float4*>(a.q + ((int64_t)(row0 + min(t, T - 1)) * a.n_heads + h) * HD + dg * DG);
 #pragma unroll
         for (int j = 0; j < DG / 4; j++) {
             const float4 v = src[j];
@@ -601,7 +616,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
 #pragma unroll
         for (int d = 0; d < DG; d++) o[i][d] = 0.0f;
     }
-    const int warp_last = a.start_pos + min(q0 + QW, a.T) - 1;  // position of the warp's last query
+    const int warp_last = start_pos + min(q0 + QW, T) - 1;  // position of the warp's last query
 
     bool ok = true;
     for (int p = 0; p < n_pages; p++) {
@@ -642,7 +657,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
             // causal mask, running max, probabilities, running sum
 #pragma unroll
             for (int i = 0; i < QW; i++) {
-                const int qpos = a.start_pos + q0 + i;
+                const int qpos = start_pos + q0 + i;
                 float mx = -INFINITY;
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
@@ -702,9 +717,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
 #pragma unroll
         for (int i = 0; i < QW; i++) {
             const int t = q0 + i;
-            if (t >= a.T) continue;
+            if (t >= T) continue;
             const float inv = 1.0f / l[i];
-            float4* dst = reinterpret_cast<float4*>(a.out + ((int64_t)t * a.n_heads + h) * HD + dg * DG);
+            float4* dst = reinterpret_cast<float4*>(a.out + ((int64_t)(row0 + t) * a.n_heads + h) * HD + dg * DG);
 #pragma unroll
             for (int c = 0; c < DG / 4; c++)
                 dst[c] = make_float4(o[i][4 * c] * inv, o[i][4 * c + 1] * inv, o[i][4 * c + 2] * inv,
@@ -808,15 +823,17 @@ void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream
     }
 }
 
+int prefill_attn_query_tile(int head_dim) { return head_dim == 64 ? PrefillCfg<64>::QT : PrefillCfg<128>::QT; }
+
 void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
     count_launch();
     if (a.geom.head_dim == 64) {
-        dim3 grid((unsigned)(((a.T + PrefillCfg<64>::QT - 1) / PrefillCfg<64>::QT) * a.n_heads));
+        dim3 grid((unsigned)((a.seg ? a.n_tiles : (a.T + PrefillCfg<64>::QT - 1) / PrefillCfg<64>::QT) * a.n_heads));
         const int smem = kStages * 2 * kPage * 64 * 4;
         ensure_smem(prefill_attn_kernel<64>, smem);
         launch_ex(prefill_attn_kernel<64>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
     } else {
-        dim3 grid((unsigned)(((a.T + PrefillCfg<128>::QT - 1) / PrefillCfg<128>::QT) * a.n_heads));
+        dim3 grid((unsigned)((a.seg ? a.n_tiles : (a.T + PrefillCfg<128>::QT - 1) / PrefillCfg<128>::QT) * a.n_heads));
         const int smem = kStages * 2 * kPage * 128 * 4;
         ensure_smem(prefill_attn_kernel<128>, smem);
         launch_ex(prefill_attn_kernel<128>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);

@@ -58,7 +58,7 @@ int validate_cfg(const nr_config* c) {
     if (c->total_blocks <= 0 || c->max_tokens_per_batch <= 0 || c->max_new_tokens <= 0) return NR_ERR_INVALID;
     if (c->max_batch <= 0 || c->max_batch > 1024 || c->max_prefill_tokens <= 0) return NR_ERR_INVALID;
     if (c->q8_mode != NR_Q8_FIXED && c->q8_mode != NR_Q8_FAITHFUL) return NR_ERR_INVALID;
-    if (c->sched_mode != NR_SCHED_REFERENCE) return NR_ERR_INVALID;
+    if (c->sched_mode != NR_SCHED_REFERENCE && c->sched_mode != NR_SCHED_PACKED) return NR_ERR_INVALID;
     return NR_OK;
 }
 
@@ -230,18 +230,33 @@ int nr_step(nr_engine* e, nr_step_out* out) {
     std::vector<int> ids;
     const bool want_logits = out && out->emitted_logits;
     const int cap = out ? out->emitted_cap : 0;
-    if (p.prefill_req) {
-        int tok = 0;
-        float* lg = nullptr;
-        const bool emits = p.prefill_req->is_prefill_done;
-        if (want_logits && emits && (int)ids.size() < cap) lg = out->emitted_logits + ids.size() * (size_t)V;
-        rc = E.forward_prefill(p.prefill_req->seq, p.prefill_chunk.data(), (int)p.prefill_chunk.size(),
-                               p.prefill_start, lg, &tok);
-        if (rc) return rc;
-        if (emits) {
-            toks.push_back(tok);
-            ids.push_back(p.prefill_req->req_id);
+    int prefill_tokens = 0;
+    if (!p.prefills.empty()) {
+        // every chunk of the step in one forward pass; a token for each completed prompt
+        const int n = (int)p.prefills.size();
+        std::vector<nitro::PrefillSeg> segs(n);
+        int n_done = 0;
+        for (int i = 0; i < n; i++) {
+            const nitro::PrefillPart& part = p.prefills[i];
+            segs[i] = {&part.req->seq, part.chunk.data(), (int)part.chunk.size(), part.start, part.done};
+            prefill_tokens += segs[i].T;
+            n_done += part.done ? 1 : 0;
         }
+        std::vector<int> am(std::max(n_done, 1));
+        float* lg = nullptr;
+        std::vector<float> tmp;
+        if (want_logits && n_done > 0) {
+            if (n_done <= cap) lg = out->emitted_logits;
+            else { tmp.resize((size_t)n_done * V); lg = tmp.data(); }
+        }
+        rc = E.forward_prefill_batch(segs.data(), n, lg, am.data());
+        if (rc) return rc;
+        int k = 0;
+        for (const nitro::PrefillPart& part : p.prefills)
+            if (part.done) {
+                toks.push_back(am[k++]);
+                ids.push_back(part.req->req_id);
+            }
     }
     const int B = (int)p.decode_reqs.size();
     if (B > 0) {
@@ -264,9 +279,10 @@ int nr_step(nr_engine* e, nr_step_out* out) {
     E.sched().commit(p, toks.data(), (int)toks.size());
     if (out) {
         out->n_released = p.n_released;
-        out->prefill_req_id = p.prefill_req ? p.prefill_req->req_id : -1;
-        out->prefill_tokens = (int)p.prefill_chunk.size();
+        out->prefill_req_id = p.prefills.empty() ? -1 : p.prefills[0].req->req_id;
+        out->prefill_tokens = prefill_tokens;
         out->prefill_hits = p.prefill_hits;
+        out->n_prefill = (int)p.prefills.size();
         out->n_decode = B;
         out->n_emitted = (int)toks.size();
         for (int i = 0; i < (int)toks.size() && i < cap; i++) {
@@ -301,11 +317,20 @@ int nr_step_plan(nr_engine* e, nr_plan* plan) {
     pp.valid = true;
     const nitro::StepPlan& p = pp.plan;
     plan->n_released = p.n_released;
-    plan->prefill_req_id = p.prefill_req ? p.prefill_req->req_id : -1;
-    plan->prefill_start = p.prefill_start;
-    plan->prefill_tokens = (int)p.prefill_chunk.size();
-    plan->prefill_done = p.prefill_req && p.prefill_req->is_prefill_done ? 1 : 0;
+    const nitro::PrefillPart* first = p.prefills.empty() ? nullptr : &p.prefills[0];
+    plan->prefill_req_id = first ? first->req->req_id : -1;
+    plan->prefill_start = first ? first->start : 0;
+    plan->prefill_tokens = first ? (int)first->chunk.size() : 0;
+    plan->prefill_done = first && first->done ? 1 : 0;
     plan->prefill_hits = p.prefill_hits;
+    plan->n_prefill = (int)p.prefills.size();
+    for (int i = 0; i < plan->n_prefill && i < plan->prefill_cap; i++) {
+        const nitro::PrefillPart& part = p.prefills[i];
+        if (plan->prefill_req_ids) plan->prefill_req_ids[i] = part.req->req_id;
+        if (plan->prefill_starts) plan->prefill_starts[i] = part.start;
+        if (plan->prefill_lens) plan->prefill_lens[i] = (int)part.chunk.size();
+        if (plan->prefill_dones) plan->prefill_dones[i] = part.done ? 1 : 0;
+    }
     plan->n_decode = (int)p.decode_reqs.size();
     if (plan->decode_req_ids)
         for (int i = 0; i < plan->n_decode && i < plan->decode_cap; i++)
@@ -317,7 +342,8 @@ int nr_step_commit(nr_engine* e, const nr_plan* plan, const int32_t* tokens, int
     if (!e || !plan || (n_tokens > 0 && !tokens)) return NR_ERR_INVALID;
     PendingPlan& pp = pending_for(e);
     if (!pp.valid) return e->impl->fail(NR_ERR_INVALID, "no plan pending");
-    const int expect = plan->prefill_done + plan->n_decode;
+    int expect = (int)pp.plan.decode_reqs.size();
+    for (const nitro::PrefillPart& part : pp.plan.prefills) expect += part.done ? 1 : 0;
     if (n_tokens != expect) return e->impl->fail(NR_ERR_INVALID, "token count does not match the plan");
     e->impl->sched().commit(pp.plan, tokens, n_tokens);
     pp.valid = false;

@@ -11,6 +11,7 @@
 // and the classifier (final RMSNorm prologue, fp32 embedding^T, greedy argmax keys).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -66,7 +67,7 @@ void launch_argmax_finish(const unsigned long long* keys, int M, int* out, cudaS
 Engine::Engine(const nr_config& cfg, const ModelShape& shape) : cfg_(cfg), shape_(shape) {
     mem_.reset(new KVBlockManager(cfg.total_blocks));
     cache_.reset(new PrefixCacheManager(*mem_, cfg.total_blocks));
-    sched_.reset(new ContinuousScheduler(cfg.max_tokens_per_batch, cfg.max_new_tokens));
+    sched_.reset(new ContinuousScheduler(cfg.max_tokens_per_batch, cfg.max_new_tokens, cfg.sched_mode));
 }
 
 Engine::~Engine() {
@@ -327,7 +328,10 @@ int Engine::init_device(const uint8_t* file, size_t size) {
     const size_t ws = decode_attn_workspace_bytes(cfg_.max_batch, c.n_heads, c.head_dim(), c.max_pages());
     NR_CUDA(cudaMalloc(&d_attn_ws_, ws));
     NR_CUDA(cudaMemsetAsync(d_attn_ws_, 0, ws, stream_));
-    desc_ints_ = (size_t)3 * R + cfg_.max_batch + (size_t)std::max(cfg_.max_batch, 1) * c.max_pages();
+    // decode: tok pos page ctx [max_batch] + block tables; prefill of several chunks:
+    // tok pos page [R] + segments [max_batch][4] + query tiles + block tables
+    const size_t mb = (size_t)std::max(cfg_.max_batch, 1);
+    desc_ints_ = (size_t)3 * R + 4 * mb + 2 * ((size_t)R / 16 + mb) + mb * c.max_pages();
     NR_CUDA(cudaMalloc(&d_desc_, desc_ints_ * 4));
     NR_CUDA(cudaMallocHost(&h_desc_, desc_ints_ * 4));
     NR_CUDA(cudaMallocHost(&h_argmax_, (size_t)(R + 1) * 4));
@@ -371,6 +375,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
             a.q = d_q_; a.kpool = kpool_; a.vpool = vpool_; a.geom = geom_; a.layer = l;
             a.block_table = d_bt_; a.T = M; a.start_pos = start_pos; a.n_heads = c.n_heads;
             a.out = d_att_; a.err = d_err_;
+            a.seg = d_seg_; a.tiles = d_tiles_; a.n_tiles = n_tiles_;
             ProfScope ps(this, kKAttn);
             launch_prefill_attention(a, stream_);
         } else {
@@ -470,6 +475,105 @@ int Engine::forward_prefill(const Sequence& seq, const int* tokens, int T, int s
     NR_CUDA(cudaGetLastError());
     if (h_argmax_[0] != 0) return fail(NR_ERR_TIMEOUT, "device wait timed out");
     if (argmax_out) *argmax_out = h_argmax_[1];
+    stats.prefill_tokens += T;
+    if (profiling_) return prof_flush();
+    return NR_OK;
+}
+
+int Engine::forward_prefill_batch(const PrefillSeg* segs, int n, float* logits_out, int* argmax_out) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    if (n <= 0) return fail(NR_ERR_INVALID, "no prefill chunk");
+    if (n == 1) {
+        int tok = 0;
+        const int rc = forward_prefill(*segs[0].seq, segs[0].tokens, segs[0].T, segs[0].start_pos,
+                                       segs[0].emit ? logits_out : nullptr, &tok);
+        if (rc == NR_OK && segs[0].emit && argmax_out) argmax_out[0] = tok;
+        return rc;
+    }
+    if (n > cfg_.max_batch) return fail(NR_ERR_CAPACITY, "more prefill chunks than max_batch");
+    const ModelShape& c = shape_;
+    const int qt = prefill_attn_query_tile(c.head_dim());
+    int T = 0, n_emit = 0, n_tiles = 0;
+    size_t bt_ints = 0;
+    for (int i = 0; i < n; i++) {
+        const PrefillSeg& g = segs[i];
+        if (g.T <= 0) return fail(NR_ERR_INVALID, "empty prefill chunk");
+        if (g.start_pos < 0 || g.start_pos + g.T > c.seq_len) return fail(NR_ERR_INVALID, "positions exceed seq_len");
+        if ((g.start_pos + g.T - 1) / kBlockSize >= (int)g.seq->block_table.size())
+            return fail(NR_ERR_INVALID, "block table does not cover the chunk");
+        for (int t = 0; t < g.T; t++)
+            if (g.tokens[t] < 0 || g.tokens[t] >= c.vocab) return fail(NR_ERR_INVALID, "token id out of range");
+        T += g.T;
+        n_emit += g.emit ? 1 : 0;
+        n_tiles += (g.T + qt - 1) / qt;
+        bt_ints += g.seq->block_table.size();
+    }
+    if (T > cfg_.max_prefill_tokens) return fail(NR_ERR_CAPACITY, "prefill chunks exceed max_prefill_tokens");
+    // descriptor: tok[T] pos[T] page[T] seg[n][4] tiles[n_tiles][2] block tables
+    const size_t n_ints = (size_t)3 * T + 4 * (size_t)n + 2 * (size_t)n_tiles + bt_ints;
+    if (n_ints > desc_ints_) return fail(NR_ERR_CAPACITY, "descriptor overflow");
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    int* h = h_desc_;
+    int* h_seg = h + 3 * T;
+    int* h_tiles = h_seg + 4 * n;
+    int* h_bts = h_tiles + 2 * n_tiles;
+    struct Tile { int seg, qt, last; };
+    std::vector<Tile> tiles;
+    tiles.reserve(n_tiles);
+    int row = 0, bt_off = 0;
+    for (int i = 0; i < n; i++) {
+        const PrefillSeg& g = segs[i];
+        for (int t = 0; t < g.T; t++) {
+            const int pos = g.start_pos + t;
+            h[row + t] = g.tokens[t];
+            h[T + row + t] = pos;
+            h[2 * T + row + t] = g.seq->block_table[pos / kBlockSize];
+        }
+        h_seg[4 * i] = row; h_seg[4 * i + 1] = g.T; h_seg[4 * i + 2] = g.start_pos; h_seg[4 * i + 3] = bt_off;
+        for (size_t p = 0; p < g.seq->block_table.size(); p++) h_bts[bt_off + p] = g.seq->block_table[p];
+        for (int q = 0; q * qt < g.T; q++) tiles.push_back({i, q, g.start_pos + std::min(g.T, (q + 1) * qt) - 1});
+        row += g.T;
+        bt_off += (int)g.seq->block_table.size();
+    }
+    // query tiles by decreasing work (the last position a tile attends), stable
+    std::stable_sort(tiles.begin(), tiles.end(), [](const Tile& x, const Tile& y) { return x.last > y.last; });
+    for (int j = 0; j < n_tiles; j++) { h_tiles[2 * j] = tiles[j].seg; h_tiles[2 * j + 1] = tiles[j].qt; }
+    d_tok_ = d_desc_; d_pos_ = d_desc_ + T; d_page_ = d_desc_ + 2 * T;
+    d_seg_ = d_desc_ + 3 * T; d_tiles_ = d_seg_ + 4 * n; d_bt_ = d_desc_ + 3 * T + 4 * n + 2 * n_tiles;
+    n_tiles_ = n_tiles;
+    NR_CUDA(cudaMemcpyAsync(d_desc_, h_desc_, n_ints * 4, cudaMemcpyHostToDevice, stream_));
+    last_valid_ = false;  // the descriptor no longer holds a decode step
+    { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, T, c.dim, d_x_, d_keys_, use_ss(T) ? d_ss_ : nullptr, max_rows_, stream_); }
+    run_layers(T, true, nullptr, 0, 0, 0, false);
+    d_seg_ = nullptr; d_tiles_ = nullptr; n_tiles_ = 0;
+    if (n_emit > 0) {
+        // the emitting chunks' last rows, gathered, through the classifier (:553-556)
+        int k = 0;
+        row = 0;
+        for (int i = 0; i < n; i++) {
+            row += segs[i].T;
+            if (!segs[i].emit) continue;
+            NR_CUDA(cudaMemcpyAsync(d_att_ + (size_t)k * c.dim, d_x_ + (size_t)(row - 1) * c.dim, (size_t)c.dim * 4,
+                                    cudaMemcpyDeviceToDevice, stream_));
+            k++;
+        }
+        GemmArgs gl;
+        gl.err = d_err_;
+        gl.x = d_att_; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
+        gl.wt = w_.cls_t;
+        gl.M = n_emit; gl.N = c.vocab; gl.K = c.dim;
+        Epilogue el;
+        el.kind = kEpiLogits; el.out = logits_out ? d_logits_ : nullptr; el.ldo = c.vocab; el.argmax_keys = d_keys_;
+        { ProfScope ps(this, kKLogits); launch_gemm(gl, el, stream_); }
+        { ProfScope ps(this, kKArgmax); launch_argmax_finish(d_keys_, n_emit, d_argmax_, stream_); }
+    }
+    NR_CUDA(cudaMemcpyAsync(h_argmax_, d_err_, (size_t)(n_emit + 1) * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits_out && n_emit > 0)
+        NR_CUDA(cudaMemcpyAsync(logits_out, d_logits_, (size_t)n_emit * c.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+    NR_CUDA(cudaStreamSynchronize(stream_));
+    NR_CUDA(cudaGetLastError());
+    if (h_argmax_[0] != 0) return fail(NR_ERR_TIMEOUT, "device wait timed out");
+    if (argmax_out) memcpy(argmax_out, h_argmax_ + 1, (size_t)n_emit * 4);
     stats.prefill_tokens += T;
     if (profiling_) return prof_flush();
     return NR_OK;

@@ -56,6 +56,15 @@ struct DeviceWeights {
     size_t rbytes = 0;
 };
 
+// One prompt chunk of a multi-sequence prefill (Engine::forward_prefill_batch).
+struct PrefillSeg {
+    const Sequence* seq;
+    const int* tokens;
+    int T;
+    int start_pos;
+    bool emit;  // run the classifier on the chunk's last row (the chunk completes the prompt)
+};
+
 // Kernel classes timed by the engine's optional per-launch CUDA-event profiling.
 enum KernelClass : int { kKEmbed = 0, kKQKV, kKAttn, kKWo, kKW13, kKW2, kKLogits, kKArgmax, kKClasses };
 
@@ -85,6 +94,10 @@ public:
     // forward passes over already-allocated tokens (block tables complete)
     int forward_prefill(const Sequence& seq, const int* tokens, int T, int start_pos, float* logits_out,
                         int* argmax_out);
+    // Prompt chunks of several sequences in one forward pass: their rows concatenated
+    // through every projection, causal attention per chunk; the classifier runs for the
+    // chunks with emit set, whose logits rows / token ids are written in chunk order.
+    int forward_prefill_batch(const PrefillSeg* segs, int n, float* logits_out, int* argmax_out);
     int forward_decode(int B, const int* tokens, const int* positions, const Sequence* const* seqs,
                        float* logits_out, int* argmax_out, bool force_fixed = false);
     int read_page(int block, float* k_out, float* v_out);
@@ -137,6 +150,10 @@ private:
     int* d_argmax_ = nullptr;  // [max_rows]
     int* d_err_ = nullptr;
     void* d_attn_ws_ = nullptr;
+    // set while a multi-sequence prefill runs: its segment and tile tables on the device
+    const int* d_seg_ = nullptr;
+    const int* d_tiles_ = nullptr;
+    int n_tiles_ = 0;
     // step descriptor: tokens, positions, pages, ctx, block tables (device + pinned host)
     int* d_desc_ = nullptr;
     int* h_desc_ = nullptr;

@@ -108,19 +108,28 @@ size_t decode_attn_workspace_bytes(int B, int n_heads, int head_dim, int max_pag
 void decode_attn_bind_workspace(DecodeAttnArgs& a, void* ws, int max_pages_capacity);
 void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t s);
 
-// Causal prefill attention for T consecutive tokens of one sequence (see attention.cu).
+// Causal prefill attention for T consecutive tokens of one sequence, or (seg != null) for
+// chunks of several sequences whose rows are concatenated in q/out (see attention.cu).
 struct PrefillAttnArgs {
     const float* q = nullptr;  // [T][n_heads*head_dim]
     const float* kpool = nullptr;
     const float* vpool = nullptr;
     PoolGeom geom{};
     int layer = 0;
-    const int* block_table = nullptr;  // pages of the sequence
+    const int* block_table = nullptr;  // pages of the sequence (seg: all block tables, concatenated)
     int T = 0, start_pos = 0, n_heads = 0;
     float* out = nullptr;  // [T][n_heads*head_dim]
     int* err = nullptr;
+    // several sequences: seg[4*i..] = first row, rows, position of the first row, offset of
+    // the sequence's block table in block_table; tiles[2*j..] = (segment, query tile),
+    // ordered by decreasing work; T, start_pos unused
+    const int* seg = nullptr;
+    const int* tiles = nullptr;
+    int n_tiles = 0;
 };
 void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
+// Queries per prefill attention CTA (the unit of the tile table).
+int prefill_attn_query_tile(int head_dim);
 
 // Q8_0 quantizer of scripts/quantize.py:7-23 (quantize.cu): bytes of n weights' blocks,
 // the device pass (w and out 16-byte aligned), the host-buffer pass through

@@ -151,6 +151,13 @@ int PrefixCacheManager::evict_lru_blocks() {
     return 0;
 }
 
+int PrefixCacheManager::reclaimable() const {
+    int n = 0;
+    for (int id = 0; id < (int)cached_.size(); id++)
+        if (cached_[id] && mem_.block(id).ref_count == 0) n++;
+    return n;
+}
+
 // ---------------------------------------------------------------- Sequence
 int Sequence::allocate_next_token(int token, KVBlockManager& mm, PrefixCacheManager& cache) {
     if ((int)token_buffer.size() == kBlockSize) {
@@ -194,6 +201,35 @@ void ContinuousScheduler::add_request(Request* r) {
     waiting_.push_back(r);
 }
 
+int ContinuousScheduler::scan_prefix(Request* r, PrefixCacheManager& cache, KVBlockManager& mm, bool mutate,
+                                     int* unreferenced) {
+    const int n = (int)r->prompt_tokens.size();
+    int idx = r->prefill_idx, hits = 0;
+    uint64_t h = r->seq.current_hash;
+    if (unreferenced) *unreferenced = 0;
+    while (idx + kBlockSize <= n && r->seq.token_buffer.empty()) {
+        const uint64_t nh = hash_block_state(h, r->prompt_tokens.data() + idx, kBlockSize);
+        const int hit = cache.check_cache(nh);
+        if (hit == -1) break;
+        if (unreferenced && mm.block(hit).ref_count == 0) (*unreferenced)++;
+        if (mutate) {
+            mm.inc_ref_count(hit, cache);
+            r->seq.block_table.push_back(hit);
+            r->seq.logical_token_count += kBlockSize;
+            r->seq.current_hash = nh;
+            r->prefill_idx += kBlockSize;
+        }
+        h = nh;
+        idx += kBlockSize;
+        hits++;
+    }
+    return hits;
+}
+
+namespace {
+int pages_for(int count) { return (count + kBlockSize - 1) / kBlockSize; }
+}  // namespace
+
 int ContinuousScheduler::plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManager& cache) {
     p = StepPlan();
     // 1. release finished requests (:318-327)
@@ -208,50 +244,66 @@ int ContinuousScheduler::plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManage
     }
     int budget = max_tokens_per_batch_;
     // 2. decode batch: every running request, one token each (:334-341)
+    int reserved = 0;  // pages this step's decode rows and admitted chunks will take
     for (Request* r : running_) {
         if (r->is_prefill_done) {
             p.decode_tokens.push_back(r->next_token_to_process);
             p.decode_positions.push_back(r->seq.logical_token_count);
             p.decode_reqs.push_back(r);
             budget -= 1;
+            if (r->seq.logical_token_count % kBlockSize == 0) reserved++;
         }
     }
-    // 3. admit the FIFO head: prefix-cache scan, then one chunk within the budget (:344-375)
-    if (!waiting_.empty() && budget > 0) {
+    // 3. admission (:344-375): the FIFO head's prefix-cache scan, then one chunk within the
+    // budget; packed mode goes on to the next request while budget and pages last
+    int available = mode_ == kSchedPacked ? mm.free_count() + cache.reclaimable() : 0;
+    while (!waiting_.empty() && budget > 0) {
         Request* r = waiting_.front();
-        int n = (int)r->prompt_tokens.size();
-        while (r->prefill_idx + kBlockSize <= n && r->seq.token_buffer.empty()) {
-            const int* chunk = r->prompt_tokens.data() + r->prefill_idx;
-            uint64_t h = hash_block_state(r->seq.current_hash, chunk, kBlockSize);
-            int hit = cache.check_cache(h);
-            if (hit == -1) break;
-            mm.inc_ref_count(hit, cache);
-            r->seq.block_table.push_back(hit);
-            r->seq.logical_token_count += kBlockSize;
-            r->seq.current_hash = h;
-            r->prefill_idx += kBlockSize;
-            p.prefill_hits++;
+        const int n = (int)r->prompt_tokens.size();
+        if (mode_ == kSchedPacked && !(running_.empty() && p.prefills.empty())) {
+            int unref = 0;
+            const int hits = scan_prefix(r, cache, mm, false, &unref);
+            const int count = r->seq.logical_token_count + hits * kBlockSize;
+            const int rest = n - r->prefill_idx - hits * kBlockSize;
+            const int need = r->prefill_idx == 0 ? pages_for(count + rest) - pages_for(count)
+                                                 : pages_for(count + std::min(rest, budget)) - pages_for(count);
+            if (available - unref - reserved < need) break;  // wait for pages to come back
         }
-        int remaining = n - r->prefill_idx;
-        int chunk_size = std::min(remaining, budget);
+        PrefillPart part;
+        part.req = r;
+        part.hits = scan_prefix(r, cache, mm, true, nullptr);
+        p.prefill_hits += part.hits;
+        const int remaining = n - r->prefill_idx;
+        const int chunk_size = std::min(remaining, budget);
         if (chunk_size > 0) {
-            p.prefill_chunk.assign(r->prompt_tokens.begin() + r->prefill_idx,
-                                   r->prompt_tokens.begin() + r->prefill_idx + chunk_size);
-            p.prefill_req = r;
+            part.chunk.assign(r->prompt_tokens.begin() + r->prefill_idx,
+                              r->prompt_tokens.begin() + r->prefill_idx + chunk_size);
+            budget -= chunk_size;
         }
-        if (r->prefill_idx + chunk_size == n) {
+        const bool completes = r->prefill_idx + chunk_size == n;
+        if (completes) {
             r->is_prefill_done = true;
             running_.push_back(r);
             waiting_.pop_front();
         } else {
             r->prefill_idx += chunk_size;
         }
+        part.done = completes;
+        if (mode_ == kSchedPacked) {
+            const int count = r->seq.logical_token_count;
+            reserved += pages_for(count + chunk_size) - pages_for(count);
+            available = mm.free_count() + cache.reclaimable();
+        }
+        // no chunk when the whole prompt was prefix hits (n a multiple of 16): the request
+        // then runs without a sampled token, as in the reference
+        if (!part.chunk.empty()) p.prefills.push_back(std::move(part));
+        if (mode_ != kSchedPacked || !completes) break;
     }
-    // 4. the allocations forward_prefill_chunk makes before computing (:428-430)
-    if (p.prefill_req) {
-        Sequence& s = p.prefill_req->seq;
-        p.prefill_start = s.logical_token_count;
-        for (int t : p.prefill_chunk)
+    // 4. the allocations forward_prefill_chunk makes before computing (:428-430), per chunk
+    for (PrefillPart& part : p.prefills) {
+        Sequence& s = part.req->seq;
+        part.start = s.logical_token_count;
+        for (int t : part.chunk)
             if (s.allocate_next_token(t, mm, cache) != 0) return -1;
     }
     // 5. the allocations forward_decode_batch makes, in row order (:578-582)
@@ -262,9 +314,10 @@ int ContinuousScheduler::plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManage
 
 void ContinuousScheduler::commit(const StepPlan& p, const int* tokens, int n_tokens) {
     int k = 0;
-    // the greedy token of a prefill that completed the prompt (:380-384)
-    if (p.prefill_req && p.prefill_req->is_prefill_done && k < n_tokens) {
-        Request* r = p.prefill_req;
+    // the greedy token of each prefill that completed its prompt (:380-384), in plan order
+    for (const PrefillPart& part : p.prefills) {
+        if (!part.done || k >= n_tokens) continue;
+        Request* r = part.req;
         r->next_token_to_process = tokens[k];
         r->generated_tokens.push_back(tokens[k]);
         k++;

@@ -69,6 +69,8 @@ public:
     int evict_lru_blocks();
     bool is_cached(int id) const { return cached_[id] != 0; }  // :168-170
     int cache_size() const { return (int)cache_map_.size(); }
+    // cached pages nobody references: eviction can return each of them to the free list
+    int reclaimable() const;
     std::vector<int> lru_front_to_back() const;
     const std::unordered_map<uint64_t, int>& entries() const { return cache_map_; }
     int64_t evictions() const { return evictions_; }
@@ -116,26 +118,47 @@ struct Request {
     Sequence seq;
 };
 
+// One prompt chunk of a step.
+struct PrefillPart {
+    Request* req = nullptr;
+    int start = 0;            // logical position of the first chunk token
+    std::vector<int> chunk;
+    int hits = 0;             // prefix-cache pages mapped for this request this step
+    bool done = false;        // the chunk completes the prompt (a token is sampled)
+};
+
 // What one scheduler iteration will compute, after its allocations have been made.
 struct StepPlan {
     int n_released = 0;
-    Request* prefill_req = nullptr;
-    int prefill_start = 0;            // logical position of the first chunk token
-    std::vector<int> prefill_chunk;
-    int prefill_hits = 0;
+    std::vector<PrefillPart> prefills;  // reference mode: at most one
+    int prefill_hits = 0;               // over all parts
     std::vector<Request*> decode_reqs;
     std::vector<int> decode_tokens;
     std::vector<int> decode_positions;
+};
+
+// Scheduling policies (nr_config.sched_mode).
+enum SchedMode : int {
+    kSchedReference = 0,  // Continuous_Scheduler::step as shipped: one prompt chunk per step
+    kSchedPacked = 1,     // prompt chunks of several waiting requests per step, admission by pages
 };
 
 // Continuous_Scheduler, src/pagedMemory.hpp:303-398, split into plan (release, batch,
 // admission, and every allocation the forward passes make, in the reference's order:
 // prefill chunk tokens first, :428-430, then decode rows in batch order, :578-582) and
 // commit (record sampled tokens, finish at max_new_tokens instead of the fixed 20, :393).
+//
+// kSchedPacked keeps the release and decode-batch rules and extends admission: while
+// token budget is left after the decode rows, the FIFO head gets its prefix-cache scan
+// and a chunk, and a request whose prompt completes makes room for the next one; a new
+// request is admitted only if the pages its whole remaining prompt needs fit in the
+// free plus reclaimable (cached, unreferenced) pages left after this step's decode rows
+// and earlier chunks (always, when nothing else runs).  Prompt chunks are allocated in
+// admission order, then the decode rows.
 class ContinuousScheduler {
 public:
-    ContinuousScheduler(int max_tokens_per_batch, int max_new_tokens)
-        : max_tokens_per_batch_(max_tokens_per_batch), max_new_tokens_(max_new_tokens) {}
+    ContinuousScheduler(int max_tokens_per_batch, int max_new_tokens, int mode = kSchedReference)
+        : max_tokens_per_batch_(max_tokens_per_batch), max_new_tokens_(max_new_tokens), mode_(mode) {}
     void add_request(Request* r);                    // :310-313
     bool has_active_requests() const { return !waiting_.empty() || !running_.empty(); }
     int plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManager& cache);
@@ -144,10 +167,14 @@ public:
     size_t waiting() const { return waiting_.size(); }
 
 private:
+    // the FIFO head's prefix-cache scan (:344-357): mutate = false only counts the hits
+    // and how many of the hit pages are unreferenced (they stop being reclaimable)
+    int scan_prefix(Request* r, PrefixCacheManager& cache, KVBlockManager& mm, bool mutate, int* unreferenced);
     std::deque<Request*> waiting_;
     std::vector<Request*> running_;
     int max_tokens_per_batch_;
     int max_new_tokens_;
+    int mode_;
 };
 
 }  // namespace nitro

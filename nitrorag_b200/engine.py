@@ -16,10 +16,12 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from ._lib import NR_Q8_FAITHFUL, NR_Q8_FIXED, NrConfig, NrError, NrPlan, NrStats, NrStepOut, check, lib
+from ._lib import (NR_Q8_FAITHFUL, NR_Q8_FIXED, NR_SCHED_PACKED, NR_SCHED_REFERENCE, NrConfig, NrError, NrPlan,
+                   NrStats, NrStepOut, check, lib)
 
 __all__ = ["NitroEngine", "EngineConfig", "StepResult", "hash_block_state", "argmax",
-           "NR_Q8_FIXED", "NR_Q8_FAITHFUL", "NrError", "FNV_OFFSET_BASIS"]
+           "NR_Q8_FIXED", "NR_Q8_FAITHFUL", "NR_SCHED_REFERENCE", "NR_SCHED_PACKED", "NrError",
+           "FNV_OFFSET_BASIS"]
 
 FNV_OFFSET_BASIS = 14695981039346656037
 
@@ -55,6 +57,7 @@ class EngineConfig:
     max_batch: int = 256
     max_prefill_tokens: int = 1024
     device: int = 0
+    sched_mode: int = 0  # NR_SCHED_REFERENCE; 1 = NR_SCHED_PACKED
 
     def to_c(self) -> NrConfig:
         c = NrConfig()
@@ -66,6 +69,7 @@ class EngineConfig:
         c.max_batch = self.max_batch
         c.max_prefill_tokens = self.max_prefill_tokens
         c.device = self.device
+        c.sched_mode = self.sched_mode
         return c
 
 
@@ -78,6 +82,7 @@ class StepResult:
     n_decode: int
     emitted: list  # [(req_id, token)]
     logits: np.ndarray | None
+    n_prefill: int = 0  # prompt chunks this step (prefill_tokens / prefill_hits are totals)
 
 
 class NitroEngine:
@@ -169,19 +174,25 @@ class NitroEngine:
         n = out.n_emitted
         return StepResult(out.n_released, out.prefill_req_id, out.prefill_tokens, out.prefill_hits,
                           out.n_decode, list(zip(ids[:n].tolist(), toks[:n].tolist())),
-                          None if lg is None else lg[:n].copy())
+                          None if lg is None else lg[:n].copy(), out.n_prefill)
 
     def step_plan(self, cap: int = 4096) -> dict:
         ids = np.zeros(cap, np.int32)
+        rows = [np.zeros(cap, np.int32) for _ in range(4)]  # req ids, starts, lengths, done flags
         p = NrPlan()
         p.decode_cap = cap
         p.decode_req_ids = _pi32(ids)
+        p.prefill_cap = cap
+        p.prefill_req_ids, p.prefill_starts, p.prefill_lens, p.prefill_dones = (_pi32(r) for r in rows)
         self._check(lib().nr_step_plan(self._h, C.byref(p)), "nr_step_plan")
         self._plan = p
-        self._plan_ids = ids
+        self._plan_ids = (ids, rows)
+        k = p.n_prefill
         return dict(n_released=p.n_released, prefill_req_id=p.prefill_req_id, prefill_start=p.prefill_start,
                     prefill_tokens=p.prefill_tokens, prefill_done=bool(p.prefill_done),
-                    prefill_hits=p.prefill_hits, decode_req_ids=ids[:p.n_decode].tolist())
+                    prefill_hits=p.prefill_hits, decode_req_ids=ids[:p.n_decode].tolist(),
+                    prefills=[dict(req_id=int(rows[0][i]), start=int(rows[1][i]), tokens=int(rows[2][i]),
+                                   done=bool(rows[3][i])) for i in range(k)])
 
     def step_commit(self, tokens) -> None:
         t = _i32(tokens)

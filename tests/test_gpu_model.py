@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 from conftest import assert_close
-from nitrorag_b200 import NR_Q8_FAITHFUL, NR_Q8_FIXED, EngineConfig, NitroEngine, synth
+from nitrorag_b200 import NR_Q8_FAITHFUL, NR_Q8_FIXED, NR_SCHED_PACKED, EngineConfig, NitroEngine, synth
 
 pytestmark = pytest.mark.gpu
 
@@ -342,5 +342,71 @@ def test_single_sequence_decode_grouped_kv(ref_fixed, model_dir, shape_args):
         tok = int(am[0])
         pos += 1
     assert eng.block_table(eh) == ref.block_table(rh)
+    eng.close()
+    ref.close()
+
+
+def _packed_vs_reference(ref, eng, prompts, max_new, what):
+    """Run the engine's NR_SCHED_PACKED steps to completion; every emitted logits row and
+    token is checked against the reference computing that request alone (its prompt in
+    one prefill, then one decode per token)."""
+    rh = {}
+    for i, p in enumerate(prompts):
+        eng.add_request(i, p)
+        rh[i] = ref.new_request(i, p)
+    n_tok = {i: 0 for i in range(len(prompts))}
+    steps = multi = 0
+    while eng.has_active_requests():
+        res = eng.step(want_logits=True)
+        multi = max(multi, res.n_prefill)
+        for k, (rid, tok) in enumerate(res.emitted):
+            p = prompts[rid]
+            if n_tok[rid] == 0:
+                lr = ref.forward_prefill(rh[rid], p, 0)
+            else:
+                prev = eng.request_tokens(rid)[n_tok[rid] - 1]
+                lr = ref.forward_decode([prev], [len(p) + n_tok[rid] - 1], [rh[rid]])[0]
+            assert_close(res.logits[k], lr, what=f"{what}: step {steps} req {rid} token {n_tok[rid]}")
+            _check_tokens(tok, ref.argmax(lr), lr, f"{what}: step {steps} req {rid} token {n_tok[rid]}")
+            n_tok[rid] += 1
+        steps += 1
+        assert steps < 1000
+    assert all(n == max_new for n in n_tok.values()), n_tok
+    return multi
+
+
+@pytest.mark.parametrize("shape_args", [None, (256, 512, 2, 2, 1, 512, 1024)], ids=["tiny-hd64", "hd128-gqa2"])
+def test_packed_scheduler_multi_prompt_prefill(ref_fixed, tiny_model, model_dir, shape_args):
+    """NR_SCHED_PACKED: several prompt chunks per step in one forward pass (rows
+    concatenated through the projections, causal attention per chunk from a tile table),
+    a prompt longer than the budget split across steps, against the reference run one
+    request at a time."""
+    if shape_args is None:
+        path = tiny_model
+    else:
+        path = synth.write_model(os.path.join(model_dir, "packed_hd128.bin"), synth.ModelShape(*shape_args), seed=4)
+    ref = ref_fixed
+    ref.open(path, 512, 256)
+    eng = NitroEngine(path, EngineConfig(total_blocks=256, max_new_tokens=6, max_batch=64, max_prefill_tokens=256,
+                                         sched_mode=NR_SCHED_PACKED))
+    rng = np.random.default_rng(31)
+    lens = [5, 17, 33, 60, 300, 1, 48, 90, 130, 16]
+    prompts = [rng.integers(0, ref.vocab, n).astype(np.int32) for n in lens]
+    multi = _packed_vs_reference(ref, eng, prompts, 6, "packed")
+    assert multi >= 3  # several chunks shared a forward pass
+    eng.close()
+    ref.close()
+
+
+def test_packed_scheduler_110m(ref_fixed, m110_model):
+    """The 110M model: chunks of up to 256 concatenated rows on the tensor-core projections."""
+    ref = ref_fixed
+    ref.open(m110_model, 512, 256)
+    eng = NitroEngine(m110_model, EngineConfig(total_blocks=256, max_new_tokens=4, max_batch=64,
+                                               max_prefill_tokens=256, sched_mode=NR_SCHED_PACKED))
+    rng = np.random.default_rng(32)
+    prompts = [rng.integers(0, 32000, n).astype(np.int32) for n in (40, 100, 70, 200, 23, 64)]
+    multi = _packed_vs_reference(ref, eng, prompts, 4, "packed 110M")
+    assert multi >= 2
     eng.close()
     ref.close()

@@ -1,0 +1,109 @@
+"""NR_SCHED_PACKED on a host-only engine: several prompt chunks per step within the token
+budget, FIFO order, and admission by free pages (a request whose prompt does not fit
+waits instead of exhausting the pool).  No reference counterpart: the reference admits one
+chunk per step (src/pagedMemory.hpp:344-375), whose behaviour NR_SCHED_REFERENCE keeps
+(tests/test_host_engine.py)."""
+import pytest
+
+from nitrorag_b200 import NR_SCHED_PACKED, NR_SCHED_REFERENCE, EngineConfig, NitroEngine, NrError
+
+TINY_SHAPE = (128, 256, 2, 2, 2, 512, 512)
+
+
+def host_engine(total_blocks, mode, max_new=20, budget=256):
+    cfg = EngineConfig(total_blocks=total_blocks, max_new_tokens=max_new, max_tokens_per_batch=budget, device=-1,
+                       sched_mode=mode)
+    return NitroEngine(config=cfg, shape=TINY_SHAPE)
+
+
+def _commit_all(eng, p, tok=1):
+    n = sum(1 for part in p["prefills"] if part["done"]) + len(p["decode_req_ids"])
+    eng.step_commit([tok] * n)
+
+
+def test_several_chunks_per_step_within_budget():
+    eng = host_engine(160, NR_SCHED_PACKED, max_new=4)
+    for rid, n in enumerate([30, 40, 50, 300]):
+        eng.add_request(rid, [rid + 3] * n)
+    p = eng.step_plan()
+    assert [(x["req_id"], x["start"], x["tokens"], x["done"]) for x in p["prefills"]] == [
+        (0, 0, 30, True), (1, 0, 40, True), (2, 0, 50, True), (3, 0, 136, False)]
+    assert p["prefill_req_id"] == 0 and p["prefill_tokens"] == 30 and p["decode_req_ids"] == []
+    with pytest.raises(NrError):
+        eng.step_commit([1, 2])  # three prompts completed: three tokens
+    eng.step_commit([5, 6, 7])
+    p = eng.step_plan()
+    # decode rows take budget first; the last prompt's remaining 164 tokens fit in 253
+    assert p["decode_req_ids"] == [0, 1, 2]
+    assert [(x["req_id"], x["start"], x["tokens"], x["done"]) for x in p["prefills"]] == [(3, 136, 164, True)]
+    _commit_all(eng, p)
+    assert eng.request_tokens(3) == [1] and eng.request_tokens(0) == [5, 1]
+    eng.close()
+
+
+def test_reference_mode_admits_one_chunk():
+    eng = host_engine(160, NR_SCHED_REFERENCE)
+    for rid, n in enumerate([30, 40]):
+        eng.add_request(rid, [9] * n)
+    p = eng.step_plan()
+    assert [(x["req_id"], x["tokens"]) for x in p["prefills"]] == [(0, 30)]
+    eng.close()
+
+
+def _run(eng, limit=200):
+    steps = 0
+    while eng.has_active_requests():
+        _commit_all(eng, eng.step_plan())
+        steps += 1
+        assert steps < limit
+    return steps
+
+
+def test_admission_waits_for_pages():
+    """12 pages; two 100-token prompts need 7 pages each.  Packed mode admits the second
+    only after the first finished and released its pages; the reference's one-chunk-per-
+    step admission runs out of pages instead."""
+    eng = host_engine(12, NR_SCHED_PACKED, max_new=5)
+    eng.add_request(0, list(range(100)))
+    eng.add_request(1, list(range(200, 300)))
+    p = eng.step_plan()
+    assert [x["req_id"] for x in p["prefills"]] == [0]
+    _commit_all(eng, p)
+    for _ in range(4):  # request 0 decodes; request 1 still does not fit
+        p = eng.step_plan()
+        assert p["prefills"] == [] and p["decode_req_ids"] == [0]
+        _commit_all(eng, p)
+    _run(eng)
+    assert len(eng.request_tokens(0)) == 5 and len(eng.request_tokens(1)) == 5
+
+    ref = host_engine(12, NR_SCHED_REFERENCE, max_new=5)
+    ref.add_request(0, list(range(100)))
+    ref.add_request(1, list(range(200, 300)))
+    with pytest.raises(NrError) as ei:
+        _run(ref)
+    assert ei.value.code == -5  # NR_ERR_NO_BLOCKS
+    ref.close()
+    eng.close()
+
+
+def test_lone_request_is_admitted_even_if_it_cannot_fit():
+    """With nothing running the head is admitted regardless of the estimate (otherwise it
+    would wait forever); the allocation then reports the exhausted pool."""
+    eng = host_engine(4, NR_SCHED_PACKED)
+    eng.add_request(0, list(range(100)))
+    with pytest.raises(NrError) as ei:
+        eng.step_plan()
+    assert ei.value.code == -5
+    eng.close()
+
+
+def test_many_small_requests_drain():
+    eng = host_engine(64, NR_SCHED_PACKED, max_new=3, budget=64)
+    for rid in range(40):
+        eng.add_request(rid, [rid % 50 + 1] * (5 + rid % 13))
+    steps = _run(eng)
+    assert all(len(eng.request_tokens(r)) == 3 for r in range(40))
+    assert steps < 40 * 3  # several admissions per step
+    # every page is back: free, or cached and unreferenced
+    assert len(eng.free_list()) + len(set(eng.cache_entries().values())) == 64
+    eng.close()
