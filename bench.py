@@ -349,6 +349,43 @@ def run_config3(args):
             "note": "virtual clock 10 ms per step for admission; wall time includes the scheduler and copies"}
 
 
+def _config4_packed(model, prompts):
+    """The same 32 prompts through nr_step in NR_SCHED_PACKED with a 4096-token budget:
+    four 1024-token prompts per step in one forward pass (max_new_tokens 1, so every step
+    is pure prefill: the four finish and are released at the next step)."""
+    import torch
+    from nitrorag_b200 import NR_SCHED_PACKED
+    eng = NitroEngine(model, EngineConfig(total_blocks=36 * 66, max_new_tokens=1, max_batch=32,
+                                          max_tokens_per_batch=4096, max_prefill_tokens=4096, device=0,
+                                          sched_mode=NR_SCHED_PACKED))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    # warm-up round (kernel set-up, one packed step) on other prompts: the timed prompts
+    # must not find their pages in the prefix cache
+    warm = np.random.default_rng(45).integers(0, 32000, (4, 1024)).astype(np.int32)
+    for i in range(4):
+        eng.add_request(1000 + i, warm[i])
+    while eng.has_active_requests():
+        eng.step()
+    for i, p in enumerate(prompts):
+        eng.add_request(i, p)
+    torch.cuda.synchronize()
+    e0, e1 = _dev_events(torch, stream)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    steps = chunks = 0
+    while eng.has_active_requests():
+        r = eng.step()
+        steps += 1
+        chunks += r.n_prefill
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    eng.close()
+    return {"value": round(32768 / (ms * 1e-3), 1), "unit": "tok/s", "prefill_ms": round(ms, 3),
+            "wall_ms": round(1000 * wall, 3), "steps": steps, "chunks": chunks, "budget": 4096}
+
+
 def run_config4(args):
     """Config 4: 32 prompts of 1024 tokens prefilled (one 1024-token chunk each through
     nr_forward_prefill), then 16 decode steps at B = 32.  Positions reach 1039, so the
@@ -390,6 +427,7 @@ def run_config4(args):
         pos = [p + 1 for p in pos]
     decode_s = time.perf_counter() - t0
     eng.close()
+    packed = _config4_packed(model, prompts)
     linear = 2 * 84_934_656 * 32768
     attn = 2 * 2 * 12 * 64 * 12 * 32 * (1024 * 1025 // 2)
     flops = linear + attn
@@ -409,6 +447,7 @@ def run_config4(args):
                          "frac": round(issued / tf_peak, 4), "peak_source": peak_src,
                          "note": "bf16 tensor FLOPs issued: 3 x linear (hi/lo split) + attention on CUDA cores counted once"},
             "decode_b32": {"value": round(32 * 16 / decode_s, 1), "unit": "tok/s", "steps": 16},
+            "packed_scheduler": packed,
             "prefill_kernel_ms_per_prompt": {k: round(v[0], 3) for k, v in kt.items()}}
 
 
