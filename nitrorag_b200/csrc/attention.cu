@@ -823,11 +823,16 @@ void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream
     }
 }
 
-int prefill_attn_query_tile(int head_dim) { return head_dim == 64 ? PrefillCfg<64>::QT : PrefillCfg<128>::QT; }
+int prefill_attn_query_tile(int head_dim) {
+    if (prefill_attn_tc_enabled(head_dim)) return 128;
+    return head_dim == 64 ? PrefillCfg<64>::QT : PrefillCfg<128>::QT;
+}
 
 void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
     count_launch();
-    if (a.geom.head_dim == 64) {
+    if (prefill_attn_tc_enabled(a.geom.head_dim)) {
+        launch_prefill_attention_tc(a, s);
+    } else if (a.geom.head_dim == 64) {
         dim3 grid((unsigned)((a.seg ? a.n_tiles : (a.T + PrefillCfg<64>::QT - 1) / PrefillCfg<64>::QT) * a.n_heads));
         const int smem = kStages * 2 * kPage * 64 * 4;
         ensure_smem(prefill_attn_kernel<64>, smem);

@@ -130,6 +130,10 @@ struct PrefillAttnArgs {
 void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
 // Queries per prefill attention CTA (the unit of the tile table).
 int prefill_attn_query_tile(int head_dim);
+// The tcgen05 causal prefill attention (attention_tc.cu): head_dim 64, 128 queries per
+// CTA; launch_prefill_attention takes it when enabled (NITRO_DISABLE_TC_ATTN=1 turns it off).
+bool prefill_attn_tc_enabled(int head_dim);
+void launch_prefill_attention_tc(const PrefillAttnArgs& a, cudaStream_t s);
 
 // Q8_0 quantizer of scripts/quantize.py:7-23 (quantize.cu): bytes of n weights' blocks,
 // the device pass (w and out 16-byte aligned), the host-buffer pass through

@@ -410,3 +410,26 @@ def test_packed_scheduler_110m(ref_fixed, m110_model):
     assert multi >= 2
     eng.close()
     ref.close()
+
+
+def test_110m_long_prompt_in_chunks(ref_fixed, m110_model):
+    """Causal prefill attention over chunks that start mid-page and mid query tile: a
+    700-token prompt as chunks of 1, 299 and 400 tokens (positions 0, 1 and 300), the last
+    logits of each chunk against the reference's prefill of the same chunks."""
+    ref = ref_fixed
+    ref.open(m110_model, 512, 64)
+    eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=64, max_prefill=512)
+    prompt = np.random.default_rng(5).integers(0, 32000, 700).astype(np.int32)
+    rh = ref.new_request(0, prompt)
+    eh = eng.seq_create(0)
+    start = 0
+    for n in (1, 299, 400):
+        chunk = prompt[start:start + n]
+        lr = ref.forward_prefill(rh, chunk, start)
+        le, tok = eng.forward_prefill_chunk(eh, chunk, start)
+        assert_close(le, lr, what=f"chunk at {start}")
+        _check_tokens(tok, ref.argmax(lr), lr, f"chunk at {start}")
+        start += n
+    assert eng.block_table(eh) == ref.block_table(rh)
+    eng.close()
+    ref.close()
