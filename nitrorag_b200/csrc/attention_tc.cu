@@ -1,7 +1,8 @@
 // Causal prefill attention on the 5th-generation tensor cores (tcgen05), head_dim 64.
 //
-// One CTA per (128-query tile, head): 128 threads, thread t owns query row t, which is
-// also TMEM lane t.  Keys are taken 64 at a time (4 pages):
+// One CTA per (128-query tile, head): 256 threads, two per query row (TMEM lane r is read
+// by warp r/32 of both warpgroups, each taking half of the row's keys and output dims).
+// Keys are taken 64 at a time (4 pages):
 //
 //   1. the block's K and V page tiles (fp32, bulk copies issued one block ahead) are
 //      split into bf16 hi/lo halves in the UMMA K-major layout: K as the B operand of
@@ -9,11 +10,12 @@
 //      (rows = dims, K = keys); pages past the context are zero;
 //   2. one thread issues S = Qhi Khi + Qhi Klo + Qlo Khi (4 x 3 MMAs, M=128, N=64, K=64)
 //      into TMEM columns 0-63;
-//   3. every thread loads its row of S, applies the causal mask and the online softmax
-//      (running max and sum in the exp2 domain, the scores already scaled by
-//      log2(e)/sqrt(64) through Q) and writes its row of P as bf16 hi/lo;
+//   3. every thread loads its half row of S, applies the causal mask, joins the row maximum
+//      with its partner through shared memory and applies the online softmax (running max
+//      and sum in the exp2 domain, the scores already scaled by log2(e)/sqrt(64) through
+//      Q), then writes its half row of P as bf16 hi/lo;
 //   4. one thread issues O_blk = P V the same way into TMEM columns 64-127; every thread
-//      adds its row of O_blk into its running output (rescaled by the max correction).
+//      adds its half row of O_blk into its running output (rescaled by the max correction).
 //
 // The hi/lo split keeps ~17 significant bits per operand and the dropped lo*lo term is
 // ~2^-17 relative, so scores and outputs agree with fp32 to ~1e-5 relative, the same
@@ -34,7 +36,8 @@ namespace nitro {
 
 namespace {
 
-constexpr int FA_M = 128;                     // queries per CTA = UMMA M = threads
+constexpr int FA_M = 128;                     // queries per CTA = UMMA M = TMEM lanes
+constexpr int FA_THREADS = 2 * FA_M;          // two warpgroups: each row's keys and dims split in halves
 constexpr int FA_N = 64;                      // keys per block = UMMA N of S
 constexpr int FA_HD = 64;                     // head_dim = K of S = N of O
 constexpr int FA_PAGES = FA_N / kPage;        // pages per key block
@@ -47,11 +50,14 @@ constexpr int OFF_QH = 0, OFF_QL = 16384, OFF_KH = 32768, OFF_KL = 40960, OFF_PH
 constexpr int FA_SMEM = OFF_RAW + 2 * FA_RAW;
 constexpr uint32_t FA_TMEM_COLS = 128;  // S in columns 0-63, O_blk in 64-127
 
-__global__ void __launch_bounds__(FA_M, 1) prefill_attn_tc_kernel(PrefillAttnArgs a) {
+__global__ void __launch_bounds__(FA_THREADS, 1) prefill_attn_tc_kernel(PrefillAttnArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t raw_bar[2], s_bar, o_bar;
     __shared__ uint32_t tmem_slot;
+    __shared__ float red[2][FA_M];  // per-row partial maxima (and, at the end, sums) of the two halves
     const int tid = threadIdx.x, warp = tid >> 5;
+    const int r = tid & (FA_M - 1);  // query row = TMEM lane
+    const int c = tid >> 7;          // warpgroup: keys / output dims c*32..c*32+31
 
     // (segment, query tile) of this CTA: longest tiles first (see prefill_attn_kernel)
     int T = a.T, start_pos = a.start_pos, row0 = 0, qt;
@@ -100,31 +106,32 @@ __global__ void __launch_bounds__(FA_M, 1) prefill_attn_tc_kernel(PrefillAttnArg
     grid_dependency_wait();  // q and this chunk's K/V rows come from the projection kernel
     if (tid == 0) issue(0);
 
-    // this thread's query row, pre-scaled for the exp2-domain softmax, as bf16 hi/lo
+    // half of this row's query (dims c*32..+31), pre-scaled for the exp2-domain softmax,
+    // as bf16 hi/lo
     {
         const float qscale = 1.4426950408889634f / 8.0f;  // log2(e) / sqrt(64)
         const float4* src = reinterpret_cast<const float4*>(
-            a.q + ((int64_t)(row0 + t0 + min(tid, nq - 1)) * a.n_heads + h) * FA_HD);
+            a.q + ((int64_t)(row0 + t0 + min(r, nq - 1)) * a.n_heads + h) * FA_HD + c * 32);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < 4; j++) {
             const float4 x0 = src[2 * j], x1 = src[2 * j + 1];
             const float v[8] = {x0.x * qscale, x0.y * qscale, x0.z * qscale, x0.w * qscale,
                                 x1.x * qscale, x1.y * qscale, x1.z * qscale, x1.w * qscale};
-            split_store8(v, smem + OFF_QH + core_off(tid, j), smem + OFF_QL + core_off(tid, j));
+            split_store8(v, smem + OFF_QH + core_off(r, c * 4 + j), smem + OFF_QL + core_off(r, c * 4 + j));
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t idesc = umma_idesc_bf16(FA_M, FA_N);
-    const int qpos = tid < nq ? start_pos + t0 + tid : -1;  // rows past the chunk attend nothing
+    const int qpos = r < nq ? start_pos + t0 + r : -1;  // rows past the chunk attend nothing
 
-    float o[FA_HD];
+    float o[32];  // output dims c*32..c*32+31 of row r
 #pragma unroll
-    for (int i = 0; i < FA_HD; i++) o[i] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
+    for (int i = 0; i < 32; i++) o[i] = 0.0f;
+    float m = -INFINITY, l = 0.0f;  // running max (shared by both halves) and this half's sum
     bool ok = true;
     for (int b = 0; b < n_blocks; b++) {
         const int st = b & 1;
@@ -133,40 +140,37 @@ __global__ void __launch_bounds__(FA_M, 1) prefill_attn_tc_kernel(PrefillAttnArg
         if (ok && !mbar_wait(&raw_bar[st], (uint32_t)(b >> 1) & 1, a.err)) ok = false;
         const uint8_t* raw = smem + OFF_RAW + st * FA_RAW;
         const int valid_keys = min(FA_N, (n_pages - b * FA_PAGES) * kPage);
-        // K: thread t converts half a key row (key t/2, dims (t&1)*32..+31); groups are
-        // taken in a rotated order so a warp's loads spread over the banks
+        // K: thread t converts a quarter key row (key t/4, dims (t&3)*16..+15)
         {
-            const int key = tid >> 1, half = tid & 1;
-            const float* krow = reinterpret_cast<const float*>(raw) + key * FA_HD + half * 32;
+            const int key = tid >> 2, qd = tid & 3;
+            const float4* krow = reinterpret_cast<const float4*>(raw) + key * (FA_HD / 4) + qd * 4;
 #pragma unroll
-            for (int jj = 0; jj < 4; jj++) {
-                const int j = (jj + (tid >> 1)) & 3;
+            for (int g = 0; g < 2; g++) {
                 float v[8];
                 if (key < valid_keys) {
-                    const float4 x0 = reinterpret_cast<const float4*>(krow + 8 * j)[0];
-                    const float4 x1 = reinterpret_cast<const float4*>(krow + 8 * j)[1];
+                    const float4 x0 = krow[2 * g], x1 = krow[2 * g + 1];
                     v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
                     v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
                 } else {
 #pragma unroll
                     for (int i = 0; i < 8; i++) v[i] = 0.0f;
                 }
-                split_store8(v, smem + OFF_KH + core_off(key, half * 4 + j), smem + OFF_KL + core_off(key, half * 4 + j));
+                split_store8(v, smem + OFF_KH + core_off(key, qd * 2 + g), smem + OFF_KL + core_off(key, qd * 2 + g));
             }
         }
-        // V transposed: thread t converts dim t/2 of keys (t&1)*32..+31
+        // V transposed: thread t converts dim t/4 of keys (t&3)*16..+15
         {
-            const int dim = tid >> 1, half = tid & 1;
+            const int dim = tid >> 2, qk = tid & 3;
             const float* vbase = reinterpret_cast<const float*>(raw + FA_PAGES * FA_PAGE_BYTES);
 #pragma unroll
-            for (int g = 0; g < 4; g++) {
+            for (int g = 0; g < 2; g++) {
                 float v[8];
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const int key = half * 32 + g * 8 + i;  // page tiles are contiguous: key * 64 + dim
+                    const int key = qk * 16 + g * 8 + i;  // page tiles are contiguous: key * 64 + dim
                     v[i] = key < valid_keys ? vbase[key * FA_HD + dim] : 0.0f;
                 }
-                split_store8(v, smem + OFF_VH + core_off(dim, half * 4 + g), smem + OFF_VL + core_off(dim, half * 4 + g));
+                split_store8(v, smem + OFF_VH + core_off(dim, qk * 2 + g), smem + OFF_VL + core_off(dim, qk * 2 + g));
             }
         }
         fence_async_smem();  // the operands are read by the tensor cores (async proxy)
@@ -188,32 +192,33 @@ __global__ void __launch_bounds__(FA_M, 1) prefill_attn_tc_kernel(PrefillAttnArg
         }
         if (ok && !mbar_wait(&s_bar, (uint32_t)b & 1, a.err)) ok = false;
         tc_fence_after();
-        float corr = 1.0f;
-        {
-            float s[FA_N];
-            tmem_ld32(tmem + lane_base, s);
-            tmem_ld32(tmem + lane_base + 32, s + 32);
-            const int kpos0 = b * FA_N;
-            float mx = -INFINITY;
+        // this half's 32 scores of row r; the row maximum joins both halves in shared memory
+        float sc[32];
+        tmem_ld32(tmem + lane_base + c * 32, sc);
+        const int kpos0 = b * FA_N + c * 32;
+        float mx = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < FA_N; j++) {
-                if (kpos0 + j > qpos) s[j] = -INFINITY;  // causal (and rows past the chunk)
-                mx = fmaxf(mx, s[j]);
-            }
-            const float m_new = fmaxf(m, mx);
-            corr = m_new == -INFINITY ? 1.0f : exp2f(m - m_new);
-            float ps = 0.0f;
-#pragma unroll
-            for (int j = 0; j < FA_N; j++) {
-                s[j] = m_new == -INFINITY ? 0.0f : exp2f(s[j] - m_new);
-                ps += s[j];
-            }
-            l = l * corr + ps;
-            m = m_new;
-#pragma unroll
-            for (int j = 0; j < 8; j++)
-                split_store8(s + 8 * j, smem + OFF_PH + core_off(tid, j), smem + OFF_PL + core_off(tid, j));
+        for (int j = 0; j < 32; j++) {
+            if (kpos0 + j > qpos) sc[j] = -INFINITY;  // causal (and rows past the chunk)
+            mx = fmaxf(mx, sc[j]);
         }
+        red[c][r] = mx;
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        const float m_new = fmaxf(m, fmaxf(mx, red[c ^ 1][r]));
+        const float corr = m_new == -INFINITY ? 1.0f : exp2f(m - m_new);
+        float ps = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            sc[j] = m_new == -INFINITY ? 0.0f : exp2f(sc[j] - m_new);
+            ps += sc[j];
+        }
+        l = l * corr + ps;
+        m = m_new;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            split_store8(sc + 8 * j, smem + OFF_PH + core_off(r, c * 4 + j), smem + OFF_PL + core_off(r, c * 4 + j));
         fence_async_smem();
         tc_fence_before();
         ok = __syncthreads_and(ok);
@@ -234,26 +239,27 @@ __global__ void __launch_bounds__(FA_M, 1) prefill_attn_tc_kernel(PrefillAttnArg
         if (ok && !mbar_wait(&o_bar, (uint32_t)b & 1, a.err)) ok = false;
         tc_fence_after();
         {
-            float ob[FA_HD];
-            tmem_ld32(tmem + lane_base + 64, ob);
-            tmem_ld32(tmem + lane_base + 96, ob + 32);
+            float ob[32];
+            tmem_ld32(tmem + lane_base + 64 + c * 32, ob);
 #pragma unroll
-            for (int i = 0; i < FA_HD; i++) o[i] = fmaf(o[i], corr, ob[i]);
+            for (int i = 0; i < 32; i++) o[i] = fmaf(o[i], corr, ob[i]);
         }
-        // the next block's operands overwrite K, V^T and P, and its MMAs overwrite S and
-        // O_blk: every thread's loads above are complete at the next block's barrier
+        // the next block's operands overwrite K, V^T, P and red, and its MMAs overwrite S
+        // and O_blk: every thread's reads above are complete at the next block's barrier
         tc_fence_before();
     }
     grid_dependents_launch();
+    // the row's sum over both halves
+    red[c][r] = l;
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, FA_TMEM_COLS);
-    if (!ok || tid >= nq) return;
-    const float inv = 1.0f / l;
-    float4* dst = reinterpret_cast<float4*>(a.out + ((int64_t)(row0 + t0 + tid) * a.n_heads + h) * FA_HD);
+    if (!ok || r >= nq) return;
+    const float inv = 1.0f / (l + red[c ^ 1][r]);
+    float4* dst = reinterpret_cast<float4*>(a.out + ((int64_t)(row0 + t0 + r) * a.n_heads + h) * FA_HD + c * 32);
 #pragma unroll
-    for (int c = 0; c < FA_HD / 4; c++)
-        dst[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+    for (int i = 0; i < 8; i++)
+        dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
 }
 
 }  // namespace
@@ -276,7 +282,7 @@ void launch_prefill_attention_tc(const PrefillAttnArgs& a, cudaStream_t s) {
         configured_dev = dev;
     }
     const int tiles = a.seg ? a.n_tiles : (a.T + FA_M - 1) / FA_M;
-    launch_ex(prefill_attn_tc_kernel, dim3((unsigned)(tiles * a.n_heads)), dim3(FA_M), FA_SMEM, s, 1, a);
+    launch_ex(prefill_attn_tc_kernel, dim3((unsigned)(tiles * a.n_heads)), dim3(FA_THREADS), FA_SMEM, s, 1, a);
 }
 
 }  // namespace nitro
