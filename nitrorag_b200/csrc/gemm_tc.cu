@@ -57,6 +57,9 @@ constexpr uint32_t TC_TILE_BYTES = 2u * TC_M * TC_KC * 2u;  // hi + lo halves of
 // [half][128 rows] (1 KB); a warp's 32 rows read 512 contiguous bytes per piece
 constexpr uint32_t TC_RAW_BYTES = TC_M * TC_KC + TC_M * 2 * 4;
 constexpr int TC_RAW_MAX = 12;  // ring slots of raw tiles
+#ifndef NITRO_TC_MAX_KSPLIT
+#define NITRO_TC_MAX_KSPLIT 8  // largest K split (CTAs per cluster)
+#endif
 
 // Named CTA barriers between the staging warps (arrive) and the MMA-issuing warp (sync).
 __device__ __forceinline__ void named_arrive(int id, int count) {
@@ -933,7 +936,7 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     int ksplit = 1;
     const int tiles = n_tiles * m_tiles;
     if (a.kbegin == 0 && NT <= 128)
-        while (ksplit < 8 && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
+        while (ksplit < NITRO_TC_MAX_KSPLIT && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
     SplitArgs sp;
     int smem = plan(ksplit, &sp);
     while (ksplit > 1 && tc_max_clusters(kernel, ksplit, smem, n_tiles, m_tiles) < tiles) {
