@@ -213,11 +213,31 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
     // They cost 4 B per weight instead of 1.125 B, so a Q8 projection gets them only while
     // its kernel is latency-bound rather than HBM-bound: at most 8 M weights (32 MB of
     // tiles, ~5 us of HBM).  The fp32 classifier always gets them (same 4 B per weight).
+    // Larger projections get raw Q8 tiles (below) and, when HBM has room beside the K/V
+    // pools, hi/lo tiles as well, which wide batches read instead (run_layers): at 64 rows
+    // the on-chip conversion of raw tiles costs more than the extra bytes.
     const char* tiled_env = getenv("NITRO_TILED_WEIGHTS");
     if (!(tiled_env && tiled_env[0] == '0') && D % 64 == 0 && H % 64 == 0) {
         int64_t kTileMax = (int64_t)8 << 20;  // NITRO_TILE_MAX_WEIGHTS overrides (tests use 0)
         if (const char* tm = getenv("NITRO_TILE_MAX_WEIGHTS")) kTileMax = atoll(tm);
-        auto tiled = [&](int64_t n, int64_t k) { return n * k <= kTileMax ? align256(tc_tiled_weight_bytes((int)n, (int)k)) : 0; };
+        auto small = [&](int64_t n, int64_t k) { return n * k <= kTileMax; };
+        size_t wide_bytes = 0;
+        for (auto nk : {std::make_pair((int64_t)NQKV, (int64_t)D), std::make_pair((int64_t)D, (int64_t)D),
+                        std::make_pair((int64_t)2 * H, (int64_t)D), std::make_pair((int64_t)D, (int64_t)H)})
+            if (!small(nk.first, nk.second)) wide_bytes += (size_t)L * align256(tc_tiled_weight_bytes((int)nk.first, (int)nk.second));
+        bool wide = false;
+        const char* wide_env = getenv("NITRO_WIDE_TILES");
+        if (wide_bytes && !(wide_env && wide_env[0] == '0')) {
+            size_t free_b = 0, total_b = 0;
+            NR_CUDA(cudaMemGetInfo(&free_b, &total_b));
+            const size_t pools = (size_t)2 * cfg_.total_blocks * (size_t)c.n_layers * c.n_kv_heads * kBlockSize * hd * 4;
+            const size_t raw_b = (size_t)L * ((size_t)NQKV * D + (size_t)D * D + (size_t)2 * H * D + (size_t)D * H) * 9 / 8;
+            wide = free_b > wide_bytes + raw_b + pools + ((size_t)4 << 30);  // 4 GB for activations and slack
+        }
+        wide_tiles_ = wide;
+        auto tiled = [&](int64_t n, int64_t k) {
+            return small(n, k) || wide ? align256(tc_tiled_weight_bytes((int)n, (int)k)) : 0;
+        };
         w_.qkv_t_layer = tiled(NQKV, D);
         w_.wo_t_layer = tiled(D, D);
         w_.w13_t_layer = tiled(2 * H, D);
@@ -255,11 +275,11 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
         NR_CUDA(cudaGetLastError());
 
         // the rest (HBM-bound projections) as raw Q8 tiles
-        auto raw = [&](int64_t n, int64_t k, size_t hilo) { return hilo ? 0 : align256(tc_raw_q8_bytes((int)n, (int)k)); };
-        w_.qkv_r_layer = raw(NQKV, D, w_.qkv_t_layer);
-        w_.wo_r_layer = raw(D, D, w_.wo_t_layer);
-        w_.w13_r_layer = raw(2 * H, D, w_.w13_t_layer);
-        w_.w2_r_layer = raw(D, H, w_.w2_t_layer);
+        auto raw = [&](int64_t n, int64_t k) { return small(n, k) ? 0 : align256(tc_raw_q8_bytes((int)n, (int)k)); };
+        w_.qkv_r_layer = raw(NQKV, D);
+        w_.wo_r_layer = raw(D, D);
+        w_.w13_r_layer = raw(2 * H, D);
+        w_.w2_r_layer = raw(D, H);
         w_.rbytes = (size_t)L * (w_.qkv_r_layer + w_.wo_r_layer + w_.w13_r_layer + w_.w2_r_layer);
         if (w_.rbytes) {
             NR_CUDA(cudaMalloc(&w_.rbase, w_.rbytes));
@@ -361,7 +381,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g.x = d_x_; g.ldx = D; g.norm_gain = w_.rms_att + (int64_t)l * D;
         g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
         g.M = M; g.N = NQKV; g.K = D; g.kbegin = faithful ? D - 32 : 0;
-        if (w_.qkv_t && !faithful) g.wt = w_.qkv_t + l * w_.qkv_t_layer;
+        if (w_.qkv_t && !faithful && (!w_.qkv_r || M >= kWideTileRows)) g.wt = w_.qkv_t + l * w_.qkv_t_layer;
         if (w_.qkv_r) g.wr = w_.qkv_r + l * w_.qkv_r_layer;
         if (ss) { g.ss_in = d_ss_; g.ss_parts = ss_parts; g.ss_ld = max_rows_; }
         Epilogue e;
@@ -395,7 +415,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         go.err = d_err_;
         go.x = d_att_; go.ldx = D; go.wq = w_.wo_q + (int64_t)l * D * D; go.ws = w_.wo_s + (int64_t)l * D * (D / 32);
         go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
-        if (w_.wo_t && !faithful) go.wt = w_.wo_t + l * w_.wo_t_layer;
+        if (w_.wo_t && !faithful && (!w_.wo_r || M >= kWideTileRows)) go.wt = w_.wo_t + l * w_.wo_t_layer;
         if (w_.wo_r) go.wr = w_.wo_r + l * w_.wo_r_layer;
         Epilogue eo;
         eo.kind = kEpiResidual; eo.out = d_x_; eo.ldo = D;
@@ -407,7 +427,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g13.x = d_x_; g13.ldx = D; g13.norm_gain = w_.rms_ffn + (int64_t)l * D;
         g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
         g13.M = M; g13.N = 2 * H; g13.K = D; g13.kbegin = faithful ? D - 32 : 0;
-        if (w_.w13_t && !faithful) g13.wt = w_.w13_t + l * w_.w13_t_layer;
+        if (w_.w13_t && !faithful && (!w_.w13_r || M >= kWideTileRows)) g13.wt = w_.w13_t + l * w_.w13_t_layer;
         if (w_.w13_r) g13.wr = w_.w13_r + l * w_.w13_r_layer;
         if (ss) { g13.ss_in = d_ss_; g13.ss_parts = ss_parts; g13.ss_ld = max_rows_; }
         Epilogue e13;
@@ -418,7 +438,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g2.err = d_err_;
         g2.x = d_h_; g2.ldx = H; g2.wq = w_.w2_q + (int64_t)l * D * H; g2.ws = w_.w2_s + (int64_t)l * D * (H / 32);
         g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
-        if (w_.w2_t && !faithful) g2.wt = w_.w2_t + l * w_.w2_t_layer;
+        if (w_.w2_t && !faithful && (!w_.w2_r || M >= kWideTileRows)) g2.wt = w_.w2_t + l * w_.w2_t_layer;
         if (w_.w2_r) g2.wr = w_.w2_r + l * w_.w2_r_layer;
         Epilogue e2;
         e2.kind = kEpiResidual; e2.out = d_x_; e2.ldo = D;

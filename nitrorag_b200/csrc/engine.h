@@ -150,6 +150,10 @@ private:
     int* d_argmax_ = nullptr;  // [max_rows]
     int* d_err_ = nullptr;
     void* d_attn_ws_ = nullptr;
+    // large projections have both raw Q8 tiles and hi/lo tiles; batches of at least
+    // kWideTileRows rows read the hi/lo tiles
+    bool wide_tiles_ = false;
+    static constexpr int kWideTileRows = 32;
     // set while a multi-sequence prefill runs: its segment and tile tables on the device
     const int* d_seg_ = nullptr;
     const int* d_tiles_ = nullptr;
