@@ -50,7 +50,7 @@ extern "C" {
  * only if the pages of its whole remaining prompt fit in the free and reclaimable
  * (cached, unreferenced) pages left after the step's decode rows and earlier chunks (or
  * nothing else runs).  All chunks of a step run in one forward pass.  No reference
- * counterpart. */
+ * counterpart: the reference admits one chunk per step. */
 #define NR_SCHED_PACKED      1
 
 typedef struct nr_config {
