@@ -107,3 +107,41 @@ def test_many_small_requests_drain():
     # every page is back: free, or cached and unreferenced
     assert len(eng.free_list()) + len(set(eng.cache_entries().values())) == 64
     eng.close()
+
+
+def test_prefix_hits_for_several_admissions_in_one_step():
+    """Two requests sharing a finished request's 48-token prefix are admitted in the same
+    step; both map its three cached pages (the dry-run scan of the admission rule and the
+    real scan agree), and neither sees the other's pages, allocated after admission."""
+    eng = host_engine(64, NR_SCHED_PACKED, max_new=2)
+    shared = list(range(100, 148))
+    eng.add_request(0, shared + [7] * 20)
+    _run(eng)  # request 0 finishes; its full pages stay in the prefix cache
+    eng.add_request(1, shared + [8] * 10)
+    eng.add_request(2, shared + [9] * 30)
+    p = eng.step_plan()
+    assert [(x["req_id"], x["start"], x["tokens"]) for x in p["prefills"]] == [(1, 48, 10), (2, 48, 30)]
+    assert p["prefill_hits"] == 6
+    t1, t2 = eng.request_block_table(1), eng.request_block_table(2)
+    assert t1[:3] == t2[:3] and len(set(t1[3:]) & set(t2[3:])) == 0
+    _commit_all(eng, p)
+    eng.close()
+
+
+def test_budget_split_between_decode_rows_and_chunks():
+    """Decode rows take their budget first; the FIFO head then gets what is left and
+    admission stops at a head it cannot finish."""
+    eng = host_engine(256, NR_SCHED_PACKED, max_new=50, budget=64)
+    for rid in range(3):
+        eng.add_request(rid, [rid + 1] * 10)
+    _commit_all(eng, eng.step_plan())  # three prompts of 10 in one step
+    eng.add_request(3, [5] * 100)
+    eng.add_request(4, [6] * 5)
+    p = eng.step_plan()
+    assert p["decode_req_ids"] == [0, 1, 2]
+    assert [(x["req_id"], x["tokens"], x["done"]) for x in p["prefills"]] == [(3, 61, False)]
+    _commit_all(eng, p)
+    p = eng.step_plan()
+    assert [(x["req_id"], x["start"], x["tokens"], x["done"]) for x in p["prefills"]] == [
+        (3, 61, 39, True), (4, 0, 5, True)]
+    eng.close()
