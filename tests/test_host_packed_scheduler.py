@@ -145,3 +145,50 @@ def test_budget_split_between_decode_rows_and_chunks():
     assert [(x["req_id"], x["start"], x["tokens"], x["done"]) for x in p["prefills"]] == [
         (3, 61, 39, True), (4, 0, 5, True)]
     eng.close()
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_packed_invariants_fuzz(seed):
+    """Random workloads (prompt lengths, shared prefixes, budget, pool size, generation
+    length): every step stays within the token budget, chunks are admitted in FIFO order
+    and each request's chunks are contiguous, and a run either drains every request or
+    stops with NR_ERR_NO_BLOCKS (decode growth can still exhaust a small pool)."""
+    import random
+    rnd = random.Random(seed)
+    budget = rnd.choice([16, 64, 256])
+    total = rnd.choice([24, 64, 400])
+    max_new = rnd.choice([1, 3, 9])
+    eng = host_engine(total, NR_SCHED_PACKED, max_new=max_new, budget=budget)
+    shared = [rnd.randrange(512) for _ in range(32)]
+    n_req = rnd.randint(5, 25)
+    prompts = {}
+    for rid in range(n_req):
+        n = rnd.randint(1, 150)
+        p = (shared + [rnd.randrange(512) for _ in range(n)]) if rnd.random() < 0.4 else [rnd.randrange(512) for _ in range(n)]
+        prompts[rid] = p
+        eng.add_request(rid, p)
+    next_start = {rid: None for rid in prompts}
+    admitted_order = []
+    steps = 0
+    try:
+        while eng.has_active_requests():
+            p = eng.step_plan()
+            used = sum(x["tokens"] for x in p["prefills"]) + len(p["decode_req_ids"])
+            assert used <= budget, (steps, used)
+            for x in p["prefills"]:
+                rid = x["req_id"]
+                if rid not in admitted_order:
+                    admitted_order.append(rid)
+                if next_start[rid] is not None:
+                    assert x["start"] == next_start[rid], (steps, rid)
+                next_start[rid] = x["start"] + x["tokens"]
+                assert x["done"] == (next_start[rid] == len(prompts[rid])), (steps, rid)
+            _commit_all(eng, p, tok=rnd.randrange(512))
+            steps += 1
+            assert steps < 5000
+    except NrError as err:
+        assert err.code == -5, err
+    else:
+        assert all(len(eng.request_tokens(r)) == max_new for r in prompts if next_start[r] is not None)
+    assert admitted_order == sorted(admitted_order)  # FIFO
+    eng.close()
