@@ -131,28 +131,55 @@ def prompts_for(rank: int):
     return synth.decode_workload(N_REQ, PROMPT_LO, PROMPT_HI, 32000, seed=100 + rank)
 
 
+# A decoder as narrow as the reference harness allows with the 110M model's vocabulary,
+# sequence length and scheduler budget: its Continuous_Scheduler admits and decodes the
+# decode64 requests in the same steps as the 110M model (admission and positions are
+# count-driven, src/pagedMemory.hpp:317-398), in seconds on the CPU.
+SCHED_SHAPE = synth.ModelShape(32, 64, 1, 1, 1, 32000, 1024)
+
+
 def schedule_contexts(prompts, extra_steps: int):
-    """Context length of every request at the first decode step after all requests are
-    running plus `extra_steps` more steps, from a host-only engine replaying the
-    reference scheduler (positions do not depend on the sampled token values)."""
-    shape = (768, 2048, 12, 12, 12, 32000, 1024)
-    eng = NitroEngine(config=EngineConfig(total_blocks=8192, max_new_tokens=100000, device=-1), shape=shape)
+    """Context length of every request (in running-batch order) at the first decode step
+    after all requests are running plus `extra_steps` more steps, from the reference's own
+    Continuous_Scheduler::step (oracle/_ref, ref_fixed build) on SCHED_SHAPE: one prompt
+    chunk of at most 256 tokens per step, every running request decoded per step."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    ref = oracle.Reference("fixed")
+    ref.set_threads(os.cpu_count() or 1)
+    pages = sum((len(p) + extra_steps + 300) // 16 + 2 for p in prompts) + 64
+    ref.open(synth.cached_model(SCHED_SHAPE, seed=MODEL_SEED), 256, pages)
+    ref.sched_reset()
+    handles = []
     for i, p in enumerate(prompts):
-        eng.add_request(i, p)
-    while True:
-        plan = eng.step_plan()
-        eng.step_commit([0] * (int(plan["prefill_done"]) + len(plan["decode_req_ids"])))
-        if len(eng.running_batch()) == len(prompts) and plan["prefill_req_id"] < 0:
+        h = ref.new_request(i, p)
+        ref.sched_add(h)
+        handles.append(h)
+    for _ in range(4 * len(prompts) + 64):
+        before = ref.L.ref_sched_waiting()
+        ref.sched_step(100000)
+        if before == 0 and len(ref.sched_running()) == len(prompts) and all(
+                ref.req_flags(h)["is_prefill_done"] for h in handles):
             break
+    else:
+        raise RuntimeError("reference scheduler did not admit every request")
     for _ in range(extra_steps):
-        plan = eng.step_plan()
-        eng.step_commit([0] * (int(plan["prefill_done"]) + len(plan["decode_req_ids"])))
-    order = eng.running_batch()
-    ctx = []
-    for rid in order:
-        ctx.append(len(prompts[rid]) + len(eng.request_tokens(rid)) - 1)
-    eng.close()
+        ref.sched_step(100000)
+    order = ref.sched_running()
+    ctx = [len(prompts[rid]) + len(ref.generated(handles[rid])) - 1 for rid in order]
+    ref.close()
     return order, ctx
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def attn_bytes(ctx, kv_dim=768, dim=768, B=N_REQ):
@@ -203,17 +230,20 @@ def run_cpu_reference(prompts, ctx_order, ctx, n_steps: int, warmup: int = 0, bu
 
 
 def reference_arm(args, rank):
+    """The reference's own CPU path (oracle/_ref only: its scheduler for the contexts, its
+    forward_decode_batch for the timed steps); no library of this repository is loaded."""
     if rank != 0:
         return 0
     prompts = prompts_for(0)
     order, ctx = schedule_contexts(prompts, args.warmup + args.steps)
-    tps, threads, done, dt = run_cpu_reference(prompts, order, ctx, args.steps, warmup=min(args.warmup, 1))
+    tps, threads, done, dt = run_cpu_reference(prompts, order, ctx, args.steps, warmup=args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": done, "warmup": min(args.warmup, 1), "ms_per_step": round(1000 * dt / max(done, 1), 3),
+        "steps": done, "warmup": args.warmup, "ms_per_step": round(1000 * dt / max(done, 1), 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(ctx),
         "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "cpu_model": cpu_model(),
                          "sample": f"{done} forward_decode_batch calls at B=64 (ref_fixed build, "
                                    f"{threads} OpenMP threads)"},
         "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

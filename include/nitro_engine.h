@@ -236,7 +236,10 @@ int nr_engine_stats(nr_engine* e, nr_stats* out);
 
 /* Decode paged attention for one layer (the per-(b,h) loop of src/model_q8.cpp:625-662 with
  * softmax :142-159).  q, out: [B][n_heads*head_dim]; kpool/vpool as above with n_layers
- * layers per page; block_tables: [B][max_pages] int32; ctx_lens[B] = pos+1 tokens to read.
+ * layers per page; block_tables: [B][max_pages] int32; ctx_lens[B] = pos+1 tokens to read,
+ * each in [1, max_pages * 16] (the tokens the block table row can address).  A length
+ * outside that range sets *error_flag to 2 and is clamped into [0, max_pages * 16] (a row
+ * left with no tokens gets a zero output); a bounded wait that gives up sets it to 1.
  * workspace: device scratch of nr_paged_attention_workspace_size() bytes whose counter
  * region must be zero before the first call (each call leaves it zero again). */
 size_t nr_paged_attention_workspace_size(int32_t B, int32_t n_heads, int32_t head_dim, int32_t max_pages);
@@ -253,8 +256,10 @@ int nr_paged_attention_decode(const float* q, const float* kpool, const float* v
  * NR_ATTN_STATIC_SCRATCH_BYTES in the library's device image, shared by every call on a
  * device: calls needing nr_paged_attention_workspace_size() above that return
  * NR_ERR_CAPACITY; the call clears the counters it needs, and two calls that overlap on
- * the device race on the array.  The first call on each device resolves the array's
- * address and sets kernel attributes: make it before any stream capture. */
+ * the device race on the array.  Every call resolves the array's address; the first call
+ * on each device also sets kernel attributes, so make it before any stream capture, and
+ * do not use the library across a cudaDeviceReset (those attributes are set once per
+ * device for the life of the process).  Context lengths and error_flag as above. */
 #define NR_ATTN_STATIC_SCRATCH_BYTES ((size_t)8 << 20)
 int nr_paged_attention_decode_static(const float* q, const float* kpool, const float* vpool,
                                      const int32_t* block_tables, int32_t max_pages, const int32_t* ctx_lens,

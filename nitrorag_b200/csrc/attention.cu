@@ -140,6 +140,15 @@ struct DecItem {
     float q[4];    // lane l: query dims l + 32 j (pre-scaled), j < head_dim / 32
 };
 
+// Context length of row b clamped into [0, max_pages * 16] (what the block table can
+// address); with `report`, a length outside [1, max_pages * 16] sets kErrBadContext.
+__device__ __forceinline__ int checked_ctx(const DecodeAttnArgs& a, int b, bool report) {
+    const int ctx = a.ctx_lens[b];
+    const int cap = a.max_pages * kPage;
+    if (report && (ctx < 1 || ctx > cap) && a.err) atomicCAS(a.err, 0, kErrBadContext);
+    return min(max(ctx, 0), cap);
+}
+
 // Work items are numbered longest first: every full chunk (chunk_pages pages) of every
 // (sequence, head) in sequence order, then the shorter last chunks, longest remainder
 // first, so that the items still running when the counter runs dry are the short ones.
@@ -216,7 +225,7 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
         const int b = base + threadIdx.x;
         int cnt = 0;
         if (b < a.B) {
-            const int ctx = a.ctx_lens[b];
+            const int ctx = checked_ctx(a, b, blockIdx.x == 0);
             tab.ctx[b] = ctx;
             const int pages = (ctx + kPage - 1) / kPage;
             cnt = (pages / cp) * a.n_heads;
@@ -415,7 +424,7 @@ __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small
     float* part = qs + HD;  // [W][HD + 2]: o, then m, l
 
     // page ids of this warp's pages (descriptor data: read before the wait)
-    const int ctx = a.ctx_lens[b];
+    const int ctx = checked_ctx(a, b, h == 0 && threadIdx.x == 0);
     const int pages = (ctx + kPage - 1) / kPage;
     const int mine = pages > warp ? (pages - warp + W - 1) / W : 0;  // pages warp, warp+W, ...
     if (lane < S) mbar_init(&bars[warp][lane], 1);
@@ -473,7 +482,7 @@ __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small
 #pragma unroll
             for (int i = 0; i < DPL; i++) go[i] += part[w * (HD + 2) + lane * DPL + i] * c;
         }
-        const float inv = 1.0f / gl;
+        const float inv = gl > 0.0f ? 1.0f / gl : 0.0f;  // no tokens: zero output
         float* out = a.out + ((int64_t)b * a.n_heads + h) * HD + lane * DPL;
 #pragma unroll
         for (int i = 0; i < DPL; i++) out[i] = go[i] * inv;
@@ -491,8 +500,14 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(DecodeAttnArgs a) {
     grid_dependents_launch();
     if (bh >= (int64_t)a.B * a.n_heads) return;
     const int b = (int)(bh / a.n_heads);
-    const int pages = (a.ctx_lens[b] + kPage - 1) / kPage;
+    const int pages = (checked_ctx(a, b, false) + kPage - 1) / kPage;
     const int nsplit = (pages + a.chunk_pages - 1) / a.chunk_pages;
+    if (nsplit == 0) {  // a row with no tokens (flagged by the attention kernel): zero output
+        float* out = a.out + bh * HD + lane * DPL;
+#pragma unroll
+        for (int i = 0; i < DPL; i++) out[i] = 0.0f;
+        return;
+    }
     if (nsplit <= 1) return;
     float GM = -INFINITY;
     for (int base = 0; base < nsplit; base += 32)
@@ -861,26 +876,23 @@ void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
 // it: the work counters are cleared on the stream before each launch, the partials are
 // always written before they are read.  Two calls whose kernels overlap (different
 // streams, or different host threads on one stream without ordering) race on it.
-// The first call on each device resolves the array's address (cudaGetSymbolAddress, which
-// may load the module) and sets the kernels' shared-memory limits; make that first call
-// outside any stream capture.
+// Every call resolves the array's address with cudaGetSymbolAddress (the first call on a
+// device may load the module there); the first call on each device also sets the kernels'
+// shared-memory limits, so make it outside any stream capture.  Those limits are recorded
+// once per device for the life of the process, like every other kernel of this library:
+// do not use the library across a cudaDeviceReset.
 namespace nitro {
 
 static constexpr size_t kStaticScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 
+// The array's device address on the current device.  Resolved on every call (cheap once
+// the module is loaded) rather than cached, so a context torn down and created again
+// never gets an address from the old one.
 static int static_scratch(void** out) {
-    static std::mutex mu;
-    static void* ptrs[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!ptrs[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p) return -1;
-        ptrs[dev] = p;
-    }
-    *out = ptrs[dev];
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p) return -1;
+    *out = p;
     return 0;
 }
 

@@ -13,6 +13,9 @@ constexpr int kPage = 16;  // tokens per KV page (src/pagedMemory.hpp:9)
 
 // Error codes a kernel records in its error flag (first writer wins).
 constexpr int kErrWaitTimeout = 1;
+// A decode context length outside [1, max_pages * 16]: the kernel clamps it into
+// [0, max_pages * 16] (a row with no tokens left gets a zero output) and goes on.
+constexpr int kErrBadContext = 2;
 
 // Time limit of every mbarrier wait (nanoseconds of %globaltimer).  A wait that gives up
 // sets the kernel's error flag; the kernel then skips the work that needed the data.

@@ -179,9 +179,16 @@ def write_model_on_device(path: str, shape: ModelShape, seed: int = 1234, std: f
     return path
 
 
+def model_cache_dir() -> str:
+    """NITRO_MODEL_CACHE if set, else ``.model_cache`` at the top of the source tree
+    (git-ignored; generated model files are never committed)."""
+    return os.environ.get("NITRO_MODEL_CACHE") or os.path.join(
+        os.path.dirname(os.path.dirname(os.path.abspath(__file__))), ".model_cache")
+
+
 def cached_model_on_device(shape: ModelShape, seed: int = 1234, cache_dir: str | None = None) -> str:
     """cached_model for write_model_on_device files (separate names)."""
-    cache_dir = cache_dir or os.environ.get("NITRO_MODEL_CACHE", "/tmp/nitro_models")
+    cache_dir = cache_dir or model_cache_dir()
     os.makedirs(cache_dir, exist_ok=True)
     name = "q8dev_{}x{}x{}x{}x{}x{}x{}_s{}.bin".format(shape.dim, shape.hidden_dim, shape.n_layers, shape.n_heads,
                                                        shape.n_kv_heads, shape.vocab_size, shape.seq_len, seed)
@@ -195,7 +202,7 @@ def cached_model_on_device(shape: ModelShape, seed: int = 1234, cache_dir: str |
 
 def cached_model(shape: ModelShape, seed: int = 1234, cache_dir: str | None = None) -> str:
     """Path of the synthetic model for (shape, seed), written on first use."""
-    cache_dir = cache_dir or os.environ.get("NITRO_MODEL_CACHE", "/tmp/nitro_models")
+    cache_dir = cache_dir or model_cache_dir()
     os.makedirs(cache_dir, exist_ok=True)
     name = "q8_{}x{}x{}x{}x{}x{}x{}_s{}.bin".format(shape.dim, shape.hidden_dim, shape.n_layers, shape.n_heads,
                                                     shape.n_kv_heads, shape.vocab_size, shape.seq_len, seed)

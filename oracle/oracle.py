@@ -37,13 +37,22 @@ def _p(a, t):
     return None if a is None else a.ctypes.data_as(t)
 
 
+def reference_dir():
+    """The reference checkout (nvivek17/NitroRAG): NITRO_REFERENCE_DIR if set, else a
+    directory named ``reference`` beside this repository; None where neither holds its
+    sources (the GPU hosts, which use the libraries built beforehand)."""
+    d = os.environ.get("NITRO_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return d if os.path.isdir(os.path.join(d, "src")) else None
+
+
 def build(quiet: bool = True) -> None:
     """Run oracle/Makefile (the reference builds only where its sources exist)."""
     import subprocess
-    targets = ["oracle"]
-    if os.path.isdir("/root/reference/src"):
-        targets.append("ref")
-    subprocess.run(["make", "-C", HERE, *targets], check=True,
+    args = ["oracle"]
+    ref = reference_dir()
+    if ref:
+        args += ["ref", f"REF_SRC={os.path.join(ref, 'src')}"]
+    subprocess.run(["make", "-C", HERE, *args], check=True,
                    stdout=subprocess.DEVNULL if quiet else None)
 
 

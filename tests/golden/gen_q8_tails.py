@@ -4,7 +4,8 @@ not a multiple of 32 (and a few edge-valued full blocks), from the reference's o
 scripts/quantize.py runs its file conversion at import time, so this script takes the
 `quantize_q8` function (quantize.py:7-23) out of the file with `ast` and executes only
 that definition, with the module's own imports and Q_BLOCK_SIZE.  Run where a checkout of
-the reference (nvivek17/NitroRAG) is present, its location in NITRO_REFERENCE_DIR; NumPy's
+the reference (nvivek17/NitroRAG) is present: NITRO_REFERENCE_DIR, or a directory named
+`reference` beside this repository; NumPy's
 version is recorded because quantize.py's float32 arithmetic relies on NumPy's scalar
 promotion rules (NumPy 2: a Python float operand keeps float32)."""
 from __future__ import annotations
@@ -16,7 +17,9 @@ import struct
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_QUANTIZE = os.path.join(os.environ.get("NITRO_REFERENCE_DIR", "/root/reference"), "scripts", "quantize.py")
+REF_DIR = os.environ.get("NITRO_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))),
+                                                                "reference")
+REF_QUANTIZE = os.path.join(REF_DIR, "scripts", "quantize.py")
 LENGTHS = [1, 5, 31, 32, 33, 64, 70, 127, 128, 129, 200, 1000]
 
 

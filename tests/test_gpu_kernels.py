@@ -130,3 +130,44 @@ def test_paged_attention_microbench_config(torch_cuda, restatement):
     k_eng, v_eng = _engine_pools(kref, vref, 1, H, hd)
     got = _run_decode_attention(torch, q, k_eng, v_eng, bt, ctx, H, H, hd, 1, 0, repeat=3)
     assert_close(got, want, rtol=1e-4, atol=1e-5, what="paged attention config 2")
+
+
+@pytest.mark.parametrize("B,n_heads", [(8, 4), (64, 12)])
+def test_paged_attention_context_out_of_range(torch_cuda, restatement, B, n_heads):
+    """A context length beyond what the block-table row can address (max_pages * 16) and a
+    zero length: the call sets the error flag to 2, the too-long row attends to its
+    max_pages * 16 tokens, the empty row gets a zero output, every other row is unchanged.
+    The block table has one spare row of valid page ids and the workspace is oversized, so
+    every read and write of the call stays inside its buffers."""
+    torch = torch_cuda
+    hd, n_kv, n_layers, max_pages = 64, n_heads, 1, 8
+    cap = max_pages * 16
+    rng = np.random.default_rng(B + n_heads)
+    ctx = rng.integers(1, cap + 1, B).astype(np.int32)
+    ctx[1], ctx[2] = cap + 20, 0
+    P = (B + 1) * max_pages
+    bt = rng.permutation(P).astype(np.int32).reshape(B + 1, max_pages)
+    kv_dim = n_kv * hd
+    kref = rng.standard_normal((P, n_layers, 16, kv_dim)).astype(np.float32)
+    vref = rng.standard_normal((P, n_layers, 16, kv_dim)).astype(np.float32)
+    q = rng.standard_normal((B, n_heads * hd)).astype(np.float32)
+    clamped = np.clip(ctx, 0, cap).astype(np.int32)
+    clamped[2] = 1  # the oracle needs a non-empty row; its output is replaced below
+    want = restatement.paged_decode_attention(q, kref, vref, n_layers * 16 * kv_dim, 0, bt[:B], clamped, n_heads,
+                                              n_kv, hd)
+    want[2] = 0.0
+    k_eng, v_eng = _engine_pools(kref, vref, n_layers, n_kv, hd)
+    dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k_eng, v_eng))
+    dbt, dctx = torch.from_numpy(bt).cuda(), torch.from_numpy(ctx).cuda()
+    out = torch.full((B, n_heads * hd), float("nan"), dtype=torch.float32, device="cuda")
+    ws_bytes = 2 * lib().nr_paged_attention_workspace_size(B, n_heads, hd, 2 * max_pages)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = lib().nr_paged_attention_decode(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dbt.data_ptr(), max_pages,
+                                         dctx.data_ptr(), B, n_heads, n_kv, hd, n_layers, 0, out.data_ptr(),
+                                         ws.data_ptr(), err.data_ptr(),
+                                         C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 2
+    assert_close(out.cpu().numpy(), want, rtol=1e-4, atol=1e-5, what="paged attention, clamped contexts")

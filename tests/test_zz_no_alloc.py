@@ -63,7 +63,8 @@ def _static(torch, d, out, err, B, n_heads, n_kv, hd, n_layers, layer, max_pages
 
 
 @pytest.mark.parametrize("hd,n_heads,n_kv,ctx_kind", [(64, 12, 12, "config2"), (64, 8, 2, "ragged"),
-                                                      (128, 4, 4, "ragged")])
+                                                      (128, 4, 4, "ragged"), (128, 8, 2, "wide"),
+                                                      (64, 16, 4, "wide")])
 def test_static_scratch_matches_workspace_entry(torch_cuda, hd, n_heads, n_kv, ctx_kind):
     """Two calls in a row on different layers and queries (the second reuses the scratch the
     first left behind), each equal to the workspace entry point; a third call shows the
@@ -74,6 +75,14 @@ def test_static_scratch_matches_workspace_entry(torch_cuda, hd, n_heads, n_kv, c
         ctx, _, _ = synth.paged_attention_case(seed=3)
         ctx = ctx.astype(np.int32)
         max_pages, P, n_layers = 64, 4608, 2
+    elif ctx_kind == "wide":
+        # more (sequence, head) pairs than SMs: the split kernel and the merge kernel, whose
+        # partials live in the static array (head_dim 128 doubles their rows)
+        B = 24 if hd == 128 else 48
+        ctx = rng.integers(1, 1025, B).astype(np.int32)
+        ctx[:3] = [1, 16, 1024]
+        max_pages, n_layers = 64, 2
+        P = int(sum((c + 15) // 16 for c in ctx)) + 8
     else:
         ctx = np.array([1, 15, 16, 17, 128, 129, 300, 513], np.int32)
         max_pages, P, n_layers = 40, 96, 3
