@@ -41,7 +41,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from nitrorag_b200 import EngineConfig, NitroEngine, synth  # noqa: E402
+from nitrorag_b200 import EngineConfig, NitroEngine, replicas, synth  # noqa: E402
 
 METRIC = "decode tok/s per GPU (110M Q8_0, 64 reqs); paged-attn achieved HBM GB/s"
 N_REQ = 64
@@ -127,8 +127,50 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
-def prompts_for(rank: int):
-    return synth.decode_workload(N_REQ, PROMPT_LO, PROMPT_HI, 32000, seed=100 + rank)
+def prompts_for(rank: int, world: int = 1):
+    """Replica `rank`'s 64 requests: request i of one stream of 64 x world prompts (seed 100)
+    goes to replica i mod world (nitrorag_b200.replicas.partition)."""
+    stream = synth.decode_workload(N_REQ * world, PROMPT_LO, PROMPT_HI, 32000, seed=100)
+    return [stream[i] for i in replicas.partition(len(stream), world, rank)]
+
+
+class Comm:
+    """The benchmark's only cross-rank steps (gloo on the host; the data path has none):
+    barrier, max and sum of scalars over the ranks."""
+
+    def __init__(self, world: int):
+        self.world = world
+        self.dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def _reduce(self, v: float, op: str) -> float:
+        if not self.dist:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64)
+        self.dist.all_reduce(t, op=getattr(self.dist.ReduceOp, op))
+        return float(t.item())
+
+    def max(self, v: float) -> float:
+        return self._reduce(v, "MAX")
+
+    def sum(self, v: float) -> float:
+        return self._reduce(v, "SUM")
+
+    def close(self):
+        if self.dist:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+            self.dist = None
 
 
 # A decoder as narrow as the reference harness allows with the 110M model's vocabulary,
@@ -259,7 +301,8 @@ def workload_config(ctx):
             "batch": N_REQ, "prompt_tokens": f"U[{PROMPT_LO},{PROMPT_HI}]",
             "ctx_mean": round(float(np.mean(ctx)), 1), "ctx_min": int(min(ctx)), "ctx_max": int(max(ctx)),
             "l2": "inputs larger than L2 (194 MB weights + ~2.7 GB K/V read per step)",
-            "parallelism": "replicas (one engine per GPU, no collectives)"}
+            "parallelism": "replicas (one engine per GPU, no collectives); one stream of 64 x n_gpus requests, "
+                           "request i on replica i mod n_gpus"}
 
 
 # ------------------------------------------------------------------ other configs
@@ -338,45 +381,134 @@ def run_config1(args):
             "kernels": kernels, "steps": args.steps}
 
 
-def run_config3(args):
+def _config3_trace_bytes(arrive, prompts, ids, max_new):
+    """Roofline bytes of a replica's config-3 run, from a host-only replay of the same
+    request stream (block allocation and prefix hits do not depend on generated token
+    values): per step, one weight pass per forward pass (the prompt chunk and the decode
+    batch run separately), the unique KV pages read (valid tokens x 73,728 B; a prefix
+    page shared by several rows counts once) and the K/V rows written."""
+    eng = NitroEngine(config=EngineConfig(total_blocks=4096, max_new_tokens=max_new, device=-1),
+                      shape=(768, 2048, 12, 12, 12, 32000, 1024))
+    total = {"bytes": 0, "steps": 0}
+
+    def on_step(k, plan):
+        pages = {}
+        rows = 0
+        for rid in plan["decode_req_ids"]:
+            ctx = len(prompts[rid]) + len(eng.request_tokens(rid)) - 1
+            bt = eng.request_block_table(rid)
+            for j in range((ctx + 15) // 16):
+                pages[bt[j]] = max(pages.get(bt[j], 0), min(16, ctx - 16 * j))
+            rows += 1
+        for c in plan["prefills"]:
+            end = c["start"] + c["tokens"]
+            bt = eng.request_block_table(c["req_id"])
+            for j in range((end + 15) // 16):
+                pages[bt[j]] = max(pages.get(bt[j], 0), min(16, end - 16 * j))
+            rows += c["tokens"]
+        passes = (1 if plan["decode_req_ids"] else 0) + (1 if plan["prefills"] else 0)
+        total["bytes"] += passes * W110_BYTES + (sum(pages.values()) + rows) * KV110_PER_TOKEN
+        total["steps"] += 1
+
+    def tokens(plan):
+        return [0] * (sum(1 for c in plan["prefills"] if c["done"]) + len(plan["decode_req_ids"]))
+
+    replicas.run_stream(eng, arrive, prompts, ids, host_tokens=tokens, on_step=on_step)
+    eng.close()
+    return total
+
+
+def _config3_cpu_baseline(arrive, prompts, budget_s=20.0):
+    """The reference's own Continuous_Scheduler::step (ref_fixed build, all host threads)
+    on the config-3 stream from its start, for about budget_s seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    ref = oracle.Reference("fixed")
+    threads = os.cpu_count() or 1
+    ref.set_threads(threads)
+    ref.open(synth.cached_model(synth.SHAPE_110M, seed=MODEL_SEED), 256, 4096)
+    ref.sched_reset()
+    handles = {}
+    steps = 0
+    t0 = time.perf_counter()
+    for admitted in synth.virtual_clock_admissions(arrive):
+        for i in admitted:
+            handles[i] = ref.new_request(i, prompts[i])
+            ref.sched_add(handles[i])
+        if not ref.sched_has_active():
+            if len(handles) == len(prompts):
+                break
+            continue
+        ref.sched_step(256)
+        steps += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    gen = sum(len(ref.generated(h)) for h in handles.values())
+    ref.close()
+    return {"value": round(gen / dt, 2), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "cpu_model": cpu_model(),
+            "sample": f"the first {steps} Continuous_Scheduler::step iterations of the same stream ({gen} tokens, "
+                      f"{dt:.1f} s; ref_fixed build, {threads} OpenMP threads)"}
+
+
+def run_config3(args, rank, world, comm):
     """Config 3: 50 requests arriving by a seeded Poisson process (mean 20 req/s), prompts
     U[64, 512], 60 % of them sharing a 384-token prefix, 256 greedy tokens each, through
     nr_step (reference scheduler, prefix cache on).  Arrivals are mapped to steps by a
     virtual clock (step k admits every arrival <= k x 10 ms), so the admission sequence is
-    deterministic; value = generated tokens over the wall time of the whole run."""
-    rng = np.random.default_rng(33)
-    arrive = np.cumsum(rng.exponential(1 / 20.0, 50))
-    shared = rng.integers(0, 32000, 384).astype(np.int32)
-    prompts = []
-    for _ in range(50):
-        if rng.random() < 0.6:
-            n = int(rng.integers(385, 513))
-            prompts.append(np.concatenate([shared, rng.integers(0, 32000, n - 384).astype(np.int32)]))
-        else:
-            prompts.append(rng.integers(0, 32000, int(rng.integers(64, 513))).astype(np.int32))
+    deterministic.  With N ranks, request i goes to replica i mod N (each its own engine,
+    pool and prefix cache).  value = generated tokens of all replicas over the longest
+    replica's time (CUDA events on its stream, or its wall clock if longer: host
+    scheduling included); warm-up: one stream of the same shape from another seed."""
+    import torch
+    arrive, prompts = synth.poisson_prefix_workload()
+    ids = replicas.partition(len(prompts), world, rank)
     model = synth.cached_model(synth.SHAPE_110M, seed=MODEL_SEED)
     eng = NitroEngine(model, EngineConfig(total_blocks=4096, max_new_tokens=256, max_batch=64, max_prefill_tokens=256,
-                                          device=0))
-    dt = 0.010
-    k, nxt, gen, hits, steps = 0, 0, 0, 0, 0
+                                          device=torch.cuda.current_device()))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    w_arrive, w_prompts = synth.poisson_prefix_workload(seed=34)
+    replicas.run_stream(eng, w_arrive, w_prompts, replicas.partition(50, world, rank), id_offset=1000)
+    warm_evictions = eng.stats()["evictions"]
+    torch.cuda.synchronize()
+    comm.barrier()
+    e0, e1 = _dev_events(torch, stream)
     t0 = time.perf_counter()
-    while nxt < 50 or eng.has_active_requests():
-        while nxt < 50 and arrive[nxt] <= k * dt:
-            eng.add_request(nxt, prompts[nxt])
-            nxt += 1
-        if eng.has_active_requests():
-            r = eng.step()
-            gen += len(r.emitted)
-            hits += r.prefill_hits
-            steps += 1
-        k += 1
+    e0.record(stream)
+    res = replicas.run_stream(eng, arrive, prompts, ids)
+    e1.record(stream)
+    torch.cuda.synchronize()
     wall = time.perf_counter() - t0
-    st = eng.stats()
+    mine = max(wall, e0.elapsed_time(e1) * 1e-3)
+    evictions = eng.stats()["evictions"] - warm_evictions
     eng.close()
-    return {"workload": "config3", "metric": "aggregate tok/s, 50 Poisson requests with a shared prefix (110M Q8_0)",
-            "value": round(gen / wall, 1), "unit": "tok/s", "generated_tokens": gen, "wall_s": round(wall, 3),
-            "steps": steps, "prefix_hit_pages": hits, "evictions": st["evictions"],
-            "note": "virtual clock 10 ms per step for admission; wall time includes the scheduler and copies"}
+    t_max = comm.max(mine)
+    gen = comm.sum(res.generated)
+    hits = comm.sum(res.prefill_hits)
+    steps = comm.max(res.steps)
+    trace = _config3_trace_bytes(arrive, prompts, ids, 256)
+    bytes_all = comm.sum(trace["bytes"])
+    if rank != 0:
+        return None
+    peak, peak_src = load_peaks()
+    achieved = bytes_all / t_max / 1e9
+    line = {"workload": "config3", "metric": "aggregate tok/s, 50 Poisson requests with a shared prefix (110M Q8_0)",
+            "value": round(gen / t_max, 1), "unit": "tok/s", "n_gpus": world, "value_per_gpu": round(gen / t_max / world, 1),
+            "higher_is_better": True, "scaling": "strong", "generated_tokens": int(gen), "seconds": round(t_max, 3),
+            "steps_longest_replica": int(steps), "prefix_hit_pages": int(hits), "evictions": evictions,
+            "config": {"workload": "config3", "requests": 50, "arrivals": "Poisson 20 req/s, virtual clock 10 ms/step",
+                       "shared_prefix": "60 % share 384 tokens", "new_tokens": 256,
+                       "partition": "request i on replica i mod n_gpus"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peak * world, 1), "unit": "GB/s",
+                         "frac": round(achieved / (peak * world), 4), "peak_source": peak_src,
+                         "bytes": int(bytes_all),
+                         "note": "per step: one weight pass (193.9 MB) per forward pass + unique KV pages read + "
+                                 "K/V rows written, from a host-only replay of each replica's trace; over the "
+                                 "whole run's time, host scheduling included"}}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = _config3_cpu_baseline(arrive, prompts)
+    return line
 
 
 def _config4_packed(model, prompts):
@@ -481,10 +613,83 @@ def run_config4(args):
             "prefill_kernel_ms_per_prompt": {k: round(v[0], 3) for k, v in kt.items()}}
 
 
-def run_config5(args):
-    """Config 5 (reduced): the 7B-shaped model, B requests (default 64) with 512-token
-    prompts prefilled one per call, then 32 decode steps at batch B through
-    nr_forward_decode.  The full 256-request run needs ~160 GiB of K/V on one GPU."""
+W7B_BYTES = 7_810_859_008          # Q8 projections + fp32 classifier + RMS gains, 7B shape
+KV7B_PER_TOKEN = 32 * 2 * 4096 * 4  # K and V of every layer, 7B shape
+PAGE7B_BYTES = 16 * KV7B_PER_TOKEN
+
+
+def run_config5(args, rank, world, comm):
+    """Config 5: 256 concurrent requests (all arriving at once) with 512-token uniform-random
+    prompts and 128 greedy tokens each on the 7B-shaped model, request i on replica
+    i mod N.  Each replica runs nr_step in NR_SCHED_PACKED (prompt chunks of several
+    requests per step within a 4096-token budget; a request is admitted only when every
+    page it can take until it finishes fits), its page pool sized from the HBM left after
+    the weights: on one GPU the 256 requests' 160 GiB of K/V does not fit, so requests
+    wait for pages.  value = generated tokens of all replicas over the longest replica's
+    time (CUDA events or wall clock, whichever is longer)."""
+    import torch
+    from nitrorag_b200 import NR_SCHED_PACKED
+    n_req, plen, new_tok = 256, 512, 128
+    rng = np.random.default_rng(57)
+    prompts = [rng.integers(0, 32000, plen).astype(np.int32) for _ in range(n_req)]
+    arrive = np.zeros(n_req)
+    ids = replicas.partition(n_req, world, rank)
+    model = synth.cached_model_on_device(synth.SHAPE_7B, seed=MODEL_SEED)
+    pages_wanted = len(ids) * ((plen + new_tok + 15) // 16) + 8
+    free_b, _ = torch.cuda.mem_get_info()
+    # weights (SoA + raw tiles ~16 GB) and hi/lo tiles (~26 GB) and ~10 GB of activations
+    # and slack come out of what is free before the engine loads
+    fit = int((free_b - 52e9) // PAGE7B_BYTES)
+    pages = max(64, min(pages_wanted, fit))
+    budget = 4096
+    eng = NitroEngine(model, EngineConfig(total_blocks=pages, max_new_tokens=new_tok, max_batch=min(len(ids), 1024),
+                                          max_tokens_per_batch=budget, max_prefill_tokens=budget,
+                                          sched_mode=NR_SCHED_PACKED, device=torch.cuda.current_device()))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    # warm-up: a few requests of the same shape under other ids
+    w_rng = np.random.default_rng(58)
+    w_prompts = [w_rng.integers(0, 32000, plen).astype(np.int32) for _ in range(8)]
+    replicas.run_stream(eng, np.zeros(8), w_prompts, range(8), id_offset=100000)
+    torch.cuda.synchronize()
+    comm.barrier()
+    e0, e1 = _dev_events(torch, stream)
+    most = [0]
+
+    def on_step(k, r):
+        most[0] = max(most[0], r.n_decode)
+
+    t0 = time.perf_counter()
+    e0.record(stream)
+    res = replicas.run_stream(eng, arrive, prompts, ids, on_step=on_step)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    mine = max(wall, e0.elapsed_time(e1) * 1e-3)
+    eng.close()
+    t_max = comm.max(mine)
+    gen = comm.sum(res.generated)
+    pages_all = comm.sum(pages)
+    most_all = comm.max(most[0])
+    if rank != 0:
+        return None
+    return {"workload": "config5", "metric": "aggregate tok/s, 256 requests x (512 + 128) tokens, 7B-shaped Q8_0",
+            "value": round(gen / t_max, 1), "unit": "tok/s", "n_gpus": world,
+            "value_per_gpu": round(gen / t_max / world, 1), "higher_is_better": True, "scaling": "strong",
+            "generated_tokens": int(gen), "seconds": round(t_max, 3), "prefill_tokens": n_req * plen,
+            "pages_per_replica": pages, "pages_all_replicas": int(pages_all),
+            "largest_decode_batch": int(most_all),
+            "config": {"workload": "config5", "model": "7B-shaped (dim 4096, 32 layers, 32x128 heads, ffn 11008), "
+                                                       "Q8_0, synthetic N(0,0.02) weights",
+                       "requests": n_req, "prompt_tokens": plen, "new_tokens": new_tok,
+                       "scheduler": "NR_SCHED_PACKED, 4096-token budget, admission by pages to finish",
+                       "partition": "request i on replica i mod n_gpus"}}
+
+
+def run_config5_decode(args):
+    """Config 5 (reduced, one GPU): the 7B-shaped model, B requests (default 64) with
+    512-token prompts prefilled one per call, then 32 decode steps at batch B through
+    nr_forward_decode; the decode step's roofline counts the Q8 model's bytes plus the
+    K/V the step reads."""
     import torch
     B = args.batch or 64
     t0 = time.perf_counter()
@@ -526,10 +731,10 @@ def run_config5(args):
     step_ms = d0.elapsed_time(d1) / 10
     prof = _profile_classes(eng, 3)
     eng.close()
-    w_bytes = 7_810_859_008
-    kv = sum(p + 1 for p in pos) * 32 * 2 * 4096 * 4
+    w_bytes = W7B_BYTES
+    kv = sum(p + 1 for p in pos) * KV7B_PER_TOKEN
     peak, peak_src = load_peaks()
-    return {"workload": "config5", "metric": f"decode tok/s, 7B-shaped Q8_0, batch {B} (reduced config 5)",
+    return {"workload": "config5_decode", "metric": f"decode tok/s, 7B-shaped Q8_0, batch {B} (reduced config 5)",
             "value": round(B / (step_ms * 1e-3), 1), "unit": "tok/s", "ms_per_step": round(step_ms, 3),
             "e2e": {"value": round(B * n / dec_s, 1), "unit": "tok/s"},
             "prefill": {"tokens": 512 * B, "ms": round(prefill_ms, 2), "tok_s": round(512 * B / (prefill_ms * 1e-3), 1)},
@@ -541,33 +746,16 @@ def run_config5(args):
 
 
 # ------------------------------------------------------------------ GPU arm
-def engine_arm(args, rank, world, local_rank):
+def engine_arm(args, rank, world, local_rank, comm):
     import torch
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     torch.cuda.set_device(local_rank)
-
-    def barrier():
-        if dist:
-            dist.barrier()
-
-    def max_over_ranks(v: float) -> float:
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier, max_over_ranks = comm.barrier, comm.max
 
     model = synth.cached_model(synth.SHAPE_110M, seed=MODEL_SEED)
     eng = NitroEngine(model, EngineConfig(total_blocks=4096, max_new_tokens=100000, max_batch=N_REQ,
                                           max_prefill_tokens=256, device=local_rank))
     stream = torch.cuda.ExternalStream(eng.stream)
-    prompts = prompts_for(rank)
+    prompts = prompts_for(rank, world)
     for i, p in enumerate(prompts):
         eng.add_request(i, p)
     # admission (untimed): until every request is running
@@ -660,6 +848,7 @@ def engine_arm(args, rank, world, local_rank):
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "value_per_gpu": round(value / world, 2),
             "ms_per_step": round(value_ms / K, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(ctx),
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -673,9 +862,6 @@ def engine_arm(args, rank, world, local_rank):
         }
         print(json.dumps(line), flush=True)
     eng.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
     return 0
 
 
@@ -755,7 +941,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="mark the timed device-resident replays as the CUDA profiler range")
-    ap.add_argument("--workload", choices=["decode64", "config1", "config3", "config4", "config5", "quantize"],
+    ap.add_argument("--workload", choices=["decode64", "config1", "config3", "config4", "config5", "config5_decode",
+                                           "quantize"],
                     default="decode64", help="decode64 is the headline; the others print their own line")
     ap.add_argument("--batch", type=int, default=0, help="config5: requests per GPU (default 64)")
     args = ap.parse_args()
@@ -770,13 +957,34 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         return reference_arm(args, rank)
-    if args.workload != "decode64":
+    comm = Comm(world)
+    try:
+        # rank 0 writes the synthetic model file of the workload once; the others wait
         if rank == 0:
-            fn = {"config1": run_config1, "config3": run_config3, "config4": run_config4,
-                  "config5": run_config5, "quantize": run_quantize}[args.workload]
-            print(json.dumps(fn(args)), flush=True)
-        return 0
-    return engine_arm(args, rank, world, local_rank)
+            if args.workload == "config5":
+                import torch
+                torch.cuda.set_device(local_rank)
+                synth.cached_model_on_device(synth.SHAPE_7B, seed=MODEL_SEED)
+            elif args.workload in ("decode64", "config3"):
+                synth.cached_model(synth.SHAPE_110M, seed=MODEL_SEED)
+        comm.barrier()
+        if args.workload in ("config3", "config5"):
+            import torch
+            torch.cuda.set_device(local_rank)
+            fn = run_config3 if args.workload == "config3" else run_config5
+            line = fn(args, rank, world, comm)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+            return 0
+        if args.workload != "decode64":
+            if rank == 0:
+                fn = {"config1": run_config1, "config4": run_config4, "config5_decode": run_config5_decode,
+                      "quantize": run_quantize}[args.workload]
+                print(json.dumps(fn(args)), flush=True)
+            return 0
+        return engine_arm(args, rank, world, local_rank, comm)
+    finally:
+        comm.close()
 
 
 if __name__ == "__main__":

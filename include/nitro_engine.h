@@ -46,11 +46,13 @@ extern "C" {
 
 #define NR_SCHED_REFERENCE   0  /* Continuous_Scheduler::step, src/pagedMemory.hpp:317-398 */
 /* Same release and decode rules; admission goes on past the FIFO head while token budget
- * is left (a request whose prompt completes makes room for the next), each new request
- * only if the pages of its whole remaining prompt fit in the free and reclaimable
- * (cached, unreferenced) pages left after the step's decode rows and earlier chunks (or
- * nothing else runs).  All chunks of a step run in one forward pass.  No reference
- * counterpart: the reference admits one chunk per step. */
+ * is left (a request whose prompt completes makes room for the next), each request only if
+ * every page it can take until it finishes (its prompt and max_new_tokens - 1 generated
+ * tokens, at most seq_len tokens) fits in the free and reclaimable (cached, unreferenced)
+ * pages left after what the running and earlier admitted requests can still take (or
+ * nothing else runs), so a packed run does not exhaust the pool while decoding.  All
+ * chunks of a step run in one forward pass.  No reference counterpart: the reference
+ * admits one chunk per step. */
 #define NR_SCHED_PACKED      1
 
 typedef struct nr_config {
@@ -220,9 +222,13 @@ int nr_engine_kernel_times(nr_engine* e, double ms[NR_KERNEL_CLASSES], int64_t l
 
 /* Enqueue the kernels of the engine's last decode step n more times on its stream, from
  * the step descriptor still resident in HBM (same tokens, positions and pages; the K/V
- * append rewrites the same rows), without host copies or synchronisation.  For timing the
- * device-resident decode step. */
+ * append rewrites the same rows; logits written if that step wrote them), without host
+ * copies or synchronisation.  For timing the device-resident decode step. */
 int nr_replay_decode(nr_engine* e, int32_t n);
+/* Outputs of the most recent decode step or replay: *B_out rows; argmax_out (if not NULL,
+ * [B]) the greedy ids, logits_out (if not NULL, [B x vocab]) the logits, which only a step
+ * that computed them has (NR_ERR_INVALID otherwise).  Synchronises the engine stream. */
+int nr_decode_last_outputs(nr_engine* e, int32_t* argmax_out, float* logits_out, int32_t* B_out);
 
 typedef struct nr_stats {
     int64_t steps, prefill_tokens, decode_tokens, cache_hit_pages, evictions, kernel_launches;

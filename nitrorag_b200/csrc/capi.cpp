@@ -597,6 +597,11 @@ int nr_replay_decode(nr_engine* e, int32_t n) {
     return e->impl->replay_decode(n);
 }
 
+int nr_decode_last_outputs(nr_engine* e, int32_t* argmax_out, float* logits_out, int32_t* B_out) {
+    if (!e) return NR_ERR_INVALID;
+    return e->impl->last_decode_outputs(argmax_out, logits_out, B_out);
+}
+
 int nr_engine_stats(nr_engine* e, nr_stats* out) {
     if (!e || !out) return NR_ERR_INVALID;
     *out = e->impl->stats;

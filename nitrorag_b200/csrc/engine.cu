@@ -67,7 +67,7 @@ void launch_argmax_finish(const unsigned long long* keys, int M, int* out, cudaS
 Engine::Engine(const nr_config& cfg, const ModelShape& shape) : cfg_(cfg), shape_(shape) {
     mem_.reset(new KVBlockManager(cfg.total_blocks));
     cache_.reset(new PrefixCacheManager(*mem_, cfg.total_blocks));
-    sched_.reset(new ContinuousScheduler(cfg.max_tokens_per_batch, cfg.max_new_tokens, cfg.sched_mode));
+    sched_.reset(new ContinuousScheduler(cfg.max_tokens_per_batch, cfg.max_new_tokens, cfg.sched_mode, shape.seq_len));
 }
 
 Engine::~Engine() {
@@ -720,7 +720,7 @@ int Engine::replay_decode(int n) {
     NR_CUDA(cudaSetDevice(cfg_.device));
     for (int i = 0; i < n; i++) {
         {
-            int rc = launch_decode_step(last_B_, last_max_ctx_, last_force_fixed_, false);
+            int rc = launch_decode_step(last_B_, last_max_ctx_, last_force_fixed_, last_logits_);
             if (rc) return rc;
         }
         if (profiling_ && ev_used_ + 512 > ev_pool_.size()) {
@@ -729,6 +729,22 @@ int Engine::replay_decode(int n) {
         }
     }
     NR_CUDA(cudaGetLastError());
+    return NR_OK;
+}
+
+int Engine::last_decode_outputs(int* argmax_out, float* logits_out, int* B_out) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    if (!last_valid_) return fail(NR_ERR_INVALID, "no decode step ran");
+    if (logits_out && !last_logits_) return fail(NR_ERR_INVALID, "the last decode step computed no logits");
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    NR_CUDA(cudaMemcpyAsync(h_argmax_, d_err_, (size_t)(last_B_ + 1) * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits_out)
+        NR_CUDA(cudaMemcpyAsync(logits_out, d_logits_, (size_t)last_B_ * shape_.vocab * 4, cudaMemcpyDeviceToHost,
+                                stream_));
+    NR_CUDA(cudaStreamSynchronize(stream_));
+    if (h_argmax_[0] != 0) return fail(NR_ERR_TIMEOUT, "device wait timed out");
+    if (argmax_out) memcpy(argmax_out, h_argmax_ + 1, (size_t)last_B_ * 4);
+    if (B_out) *B_out = last_B_;
     return NR_OK;
 }
 

@@ -104,6 +104,9 @@ public:
     // Enqueue the kernels of the last decode step again, n times, on the engine stream
     // (its descriptor is still resident); returns without synchronising.
     int replay_decode(int n);
+    // Outputs of the most recent decode step or replay: B argmax ids, and the B x vocab
+    // logits when that step computed them (synchronises the engine stream).
+    int last_decode_outputs(int* argmax_out, float* logits_out, int* B_out);
 
     // profiling: CUDA events around every launch, accumulated per KernelClass
     int set_profiling(bool on);

@@ -230,6 +230,12 @@ namespace {
 int pages_for(int count) { return (count + kBlockSize - 1) / kBlockSize; }
 }  // namespace
 
+int ContinuousScheduler::pages_to_finish(const Request* r, int extra_held) const {
+    int64_t final_count = (int64_t)r->prompt_tokens.size() + std::max(max_new_tokens_, 1) - 1;
+    if (seq_len_ > 0) final_count = std::min<int64_t>(final_count, seq_len_);
+    return std::max(0, pages_for((int)final_count) - (int)r->seq.block_table.size() - extra_held);
+}
+
 int ContinuousScheduler::plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManager& cache) {
     p = StepPlan();
     // 1. release finished requests (:318-327)
@@ -243,31 +249,30 @@ int ContinuousScheduler::plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManage
         }
     }
     int budget = max_tokens_per_batch_;
+    const bool packed = mode_ == kSchedPacked;
     // 2. decode batch: every running request, one token each (:334-341)
-    int reserved = 0;  // pages this step's decode rows and admitted chunks will take
+    int reserved = 0;  // packed: pages the running and newly admitted requests can still take
     for (Request* r : running_) {
         if (r->is_prefill_done) {
             p.decode_tokens.push_back(r->next_token_to_process);
             p.decode_positions.push_back(r->seq.logical_token_count);
             p.decode_reqs.push_back(r);
             budget -= 1;
-            if (r->seq.logical_token_count % kBlockSize == 0) reserved++;
         }
+        if (packed) reserved += pages_to_finish(r);
     }
     // 3. admission (:344-375): the FIFO head's prefix-cache scan, then one chunk within the
-    // budget; packed mode goes on to the next request while budget and pages last
-    int available = mode_ == kSchedPacked ? mm.free_count() + cache.reclaimable() : 0;
+    // budget; packed mode goes on to the next request while budget and pages last, and
+    // admits a request only if every page it can take until it finishes fits beside what
+    // the requests already running can still take, so decode never runs the pool dry
+    int available = packed ? mm.free_count() + cache.reclaimable() : 0;
     while (!waiting_.empty() && budget > 0) {
         Request* r = waiting_.front();
         const int n = (int)r->prompt_tokens.size();
-        if (mode_ == kSchedPacked && !(running_.empty() && p.prefills.empty())) {
+        if (packed && !(running_.empty() && p.prefills.empty())) {
             int unref = 0;
             const int hits = scan_prefix(r, cache, mm, false, &unref);
-            const int count = r->seq.logical_token_count + hits * kBlockSize;
-            const int rest = n - r->prefill_idx - hits * kBlockSize;
-            const int need = r->prefill_idx == 0 ? pages_for(count + rest) - pages_for(count)
-                                                 : pages_for(count + std::min(rest, budget)) - pages_for(count);
-            if (available - unref - reserved < need) break;  // wait for pages to come back
+            if (available - unref - reserved < pages_to_finish(r, hits)) break;  // wait for pages
         }
         PrefillPart part;
         part.req = r;
@@ -289,15 +294,14 @@ int ContinuousScheduler::plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManage
             r->prefill_idx += chunk_size;
         }
         part.done = completes;
-        if (mode_ == kSchedPacked) {
-            const int count = r->seq.logical_token_count;
-            reserved += pages_for(count + chunk_size) - pages_for(count);
+        if (packed) {
+            reserved += pages_to_finish(r);
             available = mm.free_count() + cache.reclaimable();
         }
         // no chunk when the whole prompt was prefix hits (n a multiple of 16): the request
         // then runs without a sampled token, as in the reference
         if (!part.chunk.empty()) p.prefills.push_back(std::move(part));
-        if (mode_ != kSchedPacked || !completes) break;
+        if (!packed || !completes) break;
     }
     // 4. the allocations forward_prefill_chunk makes before computing (:428-430), per chunk
     for (PrefillPart& part : p.prefills) {

@@ -157,8 +157,10 @@ enum SchedMode : int {
 // admission order, then the decode rows.
 class ContinuousScheduler {
 public:
-    ContinuousScheduler(int max_tokens_per_batch, int max_new_tokens, int mode = kSchedReference)
-        : max_tokens_per_batch_(max_tokens_per_batch), max_new_tokens_(max_new_tokens), mode_(mode) {}
+    // seq_len caps a request's final length in the packed mode's page reservation (0: none)
+    ContinuousScheduler(int max_tokens_per_batch, int max_new_tokens, int mode = kSchedReference, int seq_len = 0)
+        : max_tokens_per_batch_(max_tokens_per_batch), max_new_tokens_(max_new_tokens), mode_(mode),
+          seq_len_(seq_len) {}
     void add_request(Request* r);                    // :310-313
     bool has_active_requests() const { return !waiting_.empty() || !running_.empty(); }
     int plan(StepPlan& p, KVBlockManager& mm, PrefixCacheManager& cache);
@@ -170,11 +172,15 @@ private:
     // the FIFO head's prefix-cache scan (:344-357): mutate = false only counts the hits
     // and how many of the hit pages are unreferenced (they stop being reclaimable)
     int scan_prefix(Request* r, PrefixCacheManager& cache, KVBlockManager& mm, bool mutate, int* unreferenced);
+    // pages request r can still take before it finishes: its whole prompt and
+    // max_new_tokens - 1 generated tokens (the last one is never fed back), capped at seq_len
+    int pages_to_finish(const Request* r, int extra_held = 0) const;
     std::deque<Request*> waiting_;
     std::vector<Request*> running_;
     int max_tokens_per_batch_;
     int max_new_tokens_;
     int mode_;
+    int seq_len_;
 };
 
 }  // namespace nitro

@@ -152,6 +152,15 @@ class NitroEngine:
     def replay_decode(self, n: int) -> None:
         self._check(lib().nr_replay_decode(self._h, n), "nr_replay_decode")
 
+    def last_decode_outputs(self, want_logits: bool = False):
+        """(argmax ids, logits or None) of the most recent decode step or replay."""
+        cap = self.config.max_batch
+        am = np.zeros(cap, np.int32)
+        lg = np.zeros((cap, self.vocab_size), np.float32) if want_logits else None
+        B = C.c_int32(0)
+        self._check(lib().nr_decode_last_outputs(self._h, _pi32(am), _pf(lg), C.byref(B)), "nr_decode_last_outputs")
+        return am[:B.value].copy(), (None if lg is None else lg[:B.value].copy())
+
     # ------------------------------------------------------------ scheduler
     def add_request(self, req_id: int, prompt) -> None:
         p = _i32(prompt)

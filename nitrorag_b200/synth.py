@@ -242,3 +242,36 @@ def paged_attention_case(seed: int = 2, B: int = 64, n_heads: int = 12, head_dim
         at += n
     q = rng.standard_normal((B, n_heads * head_dim), dtype=np.float32)
     return ctx, bt, q
+
+
+def poisson_prefix_workload(n: int = 50, rate: float = 20.0, shared_len: int = 384, shared_frac: float = 0.6,
+                            lo: int = 64, hi: int = 512, vocab: int = 32000, seed: int = 33):
+    """Config 3: n requests arriving by a Poisson process of `rate` per second (arrival
+    times, seconds); a fraction `shared_frac` of them (a seeded Bernoulli draw) are one
+    shared `shared_len`-token prefix plus a random suffix, total length U[shared_len + 1,
+    hi]; the others U[lo, hi] random tokens.  Returns (arrivals, prompts)."""
+    rng = np.random.default_rng(seed)
+    arrive = np.cumsum(rng.exponential(1 / rate, n))
+    shared = rng.integers(0, vocab, shared_len).astype(np.int32)
+    prompts = []
+    for _ in range(n):
+        if rng.random() < shared_frac:
+            m = int(rng.integers(shared_len + 1, hi + 1))
+            prompts.append(np.concatenate([shared, rng.integers(0, vocab, m - shared_len).astype(np.int32)]))
+        else:
+            prompts.append(rng.integers(0, vocab, int(rng.integers(lo, hi + 1))).astype(np.int32))
+    return arrive, prompts
+
+
+def virtual_clock_admissions(arrive, step_s: float = 0.010):
+    """Admission schedule of a request stream under a virtual clock: step k admits every
+    request with arrival time <= k * step_s.  Yields, per scheduler iteration k, the
+    indices admitted before it; the caller stops when nothing is left to run."""
+    nxt, k = 0, 0
+    while True:
+        batch = []
+        while nxt < len(arrive) and arrive[nxt] <= k * step_s:
+            batch.append(nxt)
+            nxt += 1
+        yield batch
+        k += 1

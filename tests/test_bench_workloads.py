@@ -31,13 +31,14 @@ def _engine_contexts(prompts, extra_steps):
     return order, ctx
 
 
-@pytest.mark.parametrize("rank,extra", [(0, 25), (3, 0)])
-def test_decode64_contexts_reference_scheduler(rank, extra):
+@pytest.mark.parametrize("rank,world,extra", [(0, 1, 25), (3, 4, 0)])
+def test_decode64_contexts_reference_scheduler(rank, world, extra):
     import oracle
     if not oracle.reference_available("fixed"):
         pytest.skip("reference build absent")
     import bench
-    prompts = bench.prompts_for(rank)
+    prompts = bench.prompts_for(rank, world)
+    assert len(prompts) == 64
     want = _engine_contexts(prompts, extra)
     got = bench.schedule_contexts(prompts, extra)
     assert got == want

@@ -1,0 +1,285 @@
+"""Parity at the sizes the benchmark reports: every BASELINE configuration that bench.py
+measures is run here at its own size (or, for the 7B shape, the reduced subset the CPU
+reference can finish), through the C ABI, against the reference's own code (ref_fixed).
+
+Bit-exact: running batches, block tables, free lists, prefix-cache entries and greedy
+token ids.  Within 1e-3 relative + 1e-4 absolute: logits.  A token mismatch inside the
+logit tolerance is reported as a near tie (top-2 margin), never accepted silently."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, assert_close
+from nitrorag_b200 import NR_Q8_FIXED, NR_SCHED_PACKED, EngineConfig, NitroEngine, synth
+from test_gpu_model import _check_tokens, _engine, _packed_vs_reference
+
+pytestmark = pytest.mark.gpu
+
+sys.path.insert(0, ROOT)
+
+
+def _compare_step(ref, eng, res, B, handles, steps, check_logits):
+    assert res.n_decode == B, steps
+    assert eng.running_batch() == ref.sched_running(), steps
+    dec = res.emitted[len(res.emitted) - B:] if B else []
+    lr = ref.sched_decode_logits(B) if B and check_logits else None
+    if lr is not None:
+        le = res.logits[len(res.emitted) - B:]
+        for r in range(B):
+            assert_close(le[r], lr[r], what=f"step {steps} decode row {r}")
+    for r, (rid, tok) in enumerate(dec):
+        want = ref.generated(handles[rid])[-1]
+        if tok != want:
+            row = lr[r] if lr is not None else ref.sched_decode_logits(B)[r]
+            _check_tokens(tok, want, row, f"step {steps} req {rid}")
+    for rid, h in handles.items():
+        assert eng.request_tokens(rid) == ref.generated(h), (steps, rid)
+        assert eng.request_block_table(rid) == ref.block_table(h), (steps, rid)
+    assert eng.free_list() == ref.free_list(), steps
+
+
+def _cache_state(x):
+    return x.cache_entries(), x.lru()
+
+
+# ------------------------------------------------------------------ config 1
+def test_config1_full_128_tokens(ref_fixed, m110_model):
+    """Config 1 exactly as bench.py runs it: the 256-token prompt (seed 11) through nr_step
+    (one prefill step, then 127 decode steps at B = 1), all 128 greedy tokens and every
+    step's logits against the reference scheduler."""
+    ref = ref_fixed
+    ref.open(m110_model, 256, 64)
+    eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=64, max_new=128, max_batch=1)
+    prompt = np.random.default_rng(11).integers(0, 32000, 256).astype(np.int32)
+    handles = {0: ref.new_request(0, prompt)}
+    ref.sched_add(handles[0])
+    eng.add_request(0, prompt)
+    steps = 0
+    while ref.sched_has_active():
+        B = ref.sched_step(128)
+        res = eng.step(want_logits=True)
+        _compare_step(ref, eng, res, B, handles, steps, True)
+        steps += 1
+    assert not eng.has_active_requests()
+    assert len(eng.request_tokens(0)) == 128 and steps >= 128
+    eng.close()
+    ref.close()
+
+
+# ------------------------------------------------------------------ config 3
+def test_config3_poisson_prefix_cache_full_run(ref_fixed, m110_model):
+    """Config 3 at its benchmarked size: 50 requests arriving by the seeded Poisson process
+    (virtual clock, 10 ms per step), 60 % sharing a 384-token prefix, 256 greedy tokens
+    each, through nr_step against the reference's Continuous_Scheduler::step.  Every step:
+    running batch, tokens, block tables of all requests and the free list; every 8th step
+    and the last: decode logits; at the end: the prefix cache's entries and LRU order."""
+    ref = ref_fixed
+    arrive, prompts = synth.poisson_prefix_workload()
+    ref.open(m110_model, 256, 4096)
+    eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=4096, max_new=256, max_batch=64)
+    handles = {}
+    steps = hits = 0
+    for admitted in synth.virtual_clock_admissions(arrive):
+        for i in admitted:
+            handles[i] = ref.new_request(i, prompts[i])
+            ref.sched_add(handles[i])
+            eng.add_request(i, prompts[i])
+        if len(handles) == len(prompts) and not ref.sched_has_active():
+            break
+        if not ref.sched_has_active():
+            assert not eng.has_active_requests()
+            continue
+        check = steps % 8 == 0
+        B = ref.sched_step(256)
+        res = eng.step(want_logits=check)
+        hits += res.prefill_hits
+        _compare_step(ref, eng, res, B, handles, steps, check)
+        steps += 1
+        assert steps < 5000
+    assert not eng.has_active_requests()
+    assert all(len(eng.request_tokens(i)) == 256 for i in range(len(prompts)))
+    assert hits > 0 and eng.stats()["cache_hit_pages"] == hits
+    assert _cache_state(eng) == _cache_state(ref)
+    eng.close()
+    ref.close()
+
+
+# ------------------------------------------------------------------ config 4
+@pytest.fixture(scope="module")
+def long_model():
+    return synth.cached_model(synth.SHAPE_110M_LONG, seed=1234)
+
+
+def test_config4_prefill_1024_then_decode_past_1024(ref_fixed, long_model):
+    """Config 4's shapes: two 1024-token prompts, each prefilled in ONE chunk (seq_len 2048
+    in the header), plus ten short ones so the decode batch (12 rows) runs on the tensor
+    cores; then 16 decode steps, the long rows at positions 1024-1039 (RoPE rows and
+    block-table entries past the 110M model's 1024)."""
+    ref = ref_fixed
+    ref.open(long_model, 1024, 320)
+    eng = _engine(long_model, NR_Q8_FIXED, total_blocks=320, max_new=64, max_batch=32, max_prefill=1024)
+    rng = np.random.default_rng(44)
+    lens = [1024, 1024] + [int(n) for n in rng.integers(16, 101, 10)]
+    rh, eh, toks, pos = [], [], [], []
+    for i, n in enumerate(lens):
+        prompt = rng.integers(0, 32000, n).astype(np.int32)
+        rh.append(ref.new_request(i, prompt))
+        eh.append(eng.seq_create(i))
+        lr = ref.forward_prefill(rh[i], prompt, 0)
+        le, am = eng.forward_prefill_chunk(eh[i], prompt, 0)
+        assert eng.block_table(eh[i]) == ref.block_table(rh[i])
+        assert_close(le, lr, what=f"{n}-token prefill logits, seq {i}")
+        _check_tokens(am, ref.argmax(lr), lr, f"prefill token seq {i}")
+        toks.append(am)
+        pos.append(n)
+    for step in range(16):
+        lr = ref.forward_decode(toks, pos, rh)
+        le, am = eng.forward_decode_batch(toks, pos, eh)
+        assert_close(le, lr, what=f"decode step {step} (positions up to {max(pos)})")
+        for i in range(len(lens)):
+            _check_tokens(int(am[i]), ref.argmax(lr[i]), lr[i], f"decode step {step} row {i}")
+        toks = [int(t) for t in am]
+        pos = [p + 1 for p in pos]
+    assert max(pos) == 1040
+    for i in range(len(lens)):
+        assert eng.block_table(eh[i]) == ref.block_table(rh[i])
+    assert eng.free_list() == ref.free_list()
+    eng.close()
+    ref.close()
+
+
+def test_config4_packed_step_4096(ref_fixed, long_model):
+    """Config 4 through nr_step in NR_SCHED_PACKED with a 4096-token budget: four
+    1024-token prompts in ONE forward pass (4096 rows through every projection, causal
+    attention per prompt), then a decode step; each request's logits and tokens against
+    the reference computing it alone."""
+    ref = ref_fixed
+    ref.open(long_model, 1024, 300)
+    eng = NitroEngine(long_model, EngineConfig(total_blocks=300, max_new_tokens=2, max_batch=32,
+                                               max_tokens_per_batch=4096, max_prefill_tokens=4096,
+                                               sched_mode=NR_SCHED_PACKED))
+    rng = np.random.default_rng(45)
+    prompts = [rng.integers(0, 32000, 1024).astype(np.int32) for _ in range(4)]
+    multi = _packed_vs_reference(ref, eng, prompts, 2, "packed 4096")
+    assert multi == 4
+    eng.close()
+    ref.close()
+
+
+# ------------------------------------------------------------------ config 5 (reduced)
+@pytest.fixture(scope="module")
+def model_7b():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for gpu tests")
+    return synth.cached_model_on_device(synth.SHAPE_7B, seed=1234)
+
+
+def test_config5_7b_two_requests_16_tokens(ref_fixed, model_7b):
+    """Config 5's reduced subset on the 7B shape (dim 4096, 32 layers, 32 x 128 heads, FFN
+    11008): 2 requests (a 40-token prompt, whose prefill reads the hi/lo weight tiles, and
+    a 24-token one, which reads the raw Q8 tiles), then 16 greedy decode steps at B = 2
+    (the streamed matvec)."""
+    ref = ref_fixed
+    ref.open(model_7b, 64, 16)
+    eng = _engine(model_7b, NR_Q8_FIXED, total_blocks=16, max_new=32, max_batch=64, max_prefill=64)
+    rng = np.random.default_rng(55)
+    rh, eh, toks, pos = [], [], [], []
+    for i, n in enumerate((40, 24)):
+        prompt = rng.integers(0, 32000, n).astype(np.int32)
+        rh.append(ref.new_request(i, prompt))
+        eh.append(eng.seq_create(i))
+        lr = ref.forward_prefill(rh[i], prompt, 0)
+        le, am = eng.forward_prefill_chunk(eh[i], prompt, 0)
+        assert_close(le, lr, what=f"7B prefill logits seq {i}")
+        _check_tokens(am, ref.argmax(lr), lr, f"7B prefill token seq {i}")
+        toks.append(am)
+        pos.append(n)
+    for step in range(16):
+        lr = ref.forward_decode(toks, pos, rh)
+        le, am = eng.forward_decode_batch(toks, pos, eh)
+        assert_close(le, lr, what=f"7B decode step {step}")
+        for i in range(2):
+            _check_tokens(int(am[i]), ref.argmax(lr[i]), lr[i], f"7B decode step {step} row {i}")
+        toks = [int(t) for t in am]
+        pos = [p + 1 for p in pos]
+    for i in range(2):
+        assert eng.block_table(eh[i]) == ref.block_table(rh[i])
+    eng.close()
+    ref.close()
+
+
+def test_config5_7b_decode_batch_32_wide_tiles(ref_fixed, model_7b):
+    """The 7B shape's wide-batch path: 32 sequences (4-token prompts, prefill on raw Q8
+    tiles), then two decode steps at B = 32, which read the pre-split hi/lo weight tiles
+    that large projections keep beside the raw tiles."""
+    ref = ref_fixed
+    ref.open(model_7b, 64, 40)
+    eng = _engine(model_7b, NR_Q8_FIXED, total_blocks=40, max_new=32, max_batch=64, max_prefill=64)
+    rng = np.random.default_rng(56)
+    rh, eh, toks, pos = [], [], [], []
+    for i in range(32):
+        prompt = rng.integers(0, 32000, 4).astype(np.int32)
+        rh.append(ref.new_request(i, prompt))
+        eh.append(eng.seq_create(i))
+        lr = ref.forward_prefill(rh[i], prompt, 0)
+        le, am = eng.forward_prefill_chunk(eh[i], prompt, 0)
+        assert_close(le, lr, what=f"7B prefill logits seq {i}")
+        toks.append(am)
+        pos.append(4)
+    for step in range(2):
+        lr = ref.forward_decode(toks, pos, rh)
+        le, am = eng.forward_decode_batch(toks, pos, eh)
+        assert_close(le, lr, what=f"7B B=32 decode step {step}")
+        for i in range(32):
+            _check_tokens(int(am[i]), ref.argmax(lr[i]), lr[i], f"7B B=32 step {step} row {i}")
+        toks = [int(t) for t in am]
+        pos = [p + 1 for p in pos]
+    eng.close()
+    ref.close()
+
+
+# ------------------------------------------------------------------ headline decode64
+def test_decode64_bench_workload_and_replay(ref_fixed, m110_model):
+    """The headline workload exactly as bench.py builds it: the 64 decode64 prompts
+    (U[128, 768], seed 100) admitted through nr_step against the reference scheduler, then
+    decode steps at the bench's contexts (~190-930), every step checked; logits on every
+    8th step and the last.  Then the step that nr_replay_decode repeats (the bench's
+    `value`): three replays of the last step must reproduce its logits and tokens."""
+    import bench
+    ref = ref_fixed
+    prompts = bench.prompts_for(0)
+    ref.open(m110_model, 256, 4096)
+    eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=4096, max_new=100000, max_batch=64)
+    handles = {}
+    for i, p in enumerate(prompts):
+        handles[i] = ref.new_request(i, p)
+        ref.sched_add(handles[i])
+        eng.add_request(i, p)
+    steps, after = 0, None
+    while after is None or steps < after + 25:
+        waiting = ref.L.ref_sched_waiting()
+        check = steps % 8 == 0 or (after is not None and steps == after + 24)
+        B = ref.sched_step(100000)
+        res = eng.step(want_logits=check)
+        _compare_step(ref, eng, res, B, handles, steps, check)
+        if after is None and waiting == 0 and B == 64:
+            after = steps
+        steps += 1
+        assert steps < 2000
+    ctx = [len(prompts[r]) + len(eng.request_tokens(r)) - 1 for r in eng.running_batch()]
+    assert min(ctx) >= 150 and max(ctx) >= 900
+    # the replayed step
+    res = eng.step(want_logits=True)
+    B = ref.sched_step(100000)
+    _compare_step(ref, eng, res, B, handles, steps, True)
+    step_logits = res.logits[len(res.emitted) - B:]
+    step_tokens = np.array([t for _, t in res.emitted[len(res.emitted) - B:]], np.int32)
+    eng.replay_decode(3)
+    am, lg = eng.last_decode_outputs(want_logits=True)
+    assert np.array_equal(am, step_tokens)
+    assert_close(lg, step_logits, rtol=1e-6, atol=1e-7, what="replayed decode step")
+    eng.close()
+    ref.close()

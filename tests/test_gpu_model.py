@@ -252,11 +252,12 @@ def test_ingest_prompt_prefix_cache_hit(ref_fixed, tiny_model):
     ref.close()
 
 
-@pytest.mark.parametrize("B", [1, 5, 24])
+@pytest.mark.parametrize("B", [1, 5, 24, 40])
 def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B):
     """The large-model projection path: with the tile threshold at zero every Q8 projection
-    is streamed as raw Q8 tiles through the tensor-core kernel's bulk-copy ring, batches of
-    1-8 tokens included (the path the 7B shape takes).  Prefill and two decode steps must
+    gets raw Q8 tiles, streamed through the tensor-core kernel's bulk-copy ring by batches
+    of 1-31 tokens (1-8 included: the path the 7B shape takes), and hi/lo tiles beside them,
+    which batches of 32 or more rows read (B = 40 here).  Prefill and two decode steps must
     match the reference."""
     monkeypatch.setenv("NITRO_TILE_MAX_WEIGHTS", "0")
     ref = ref_fixed

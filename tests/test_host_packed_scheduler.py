@@ -192,3 +192,35 @@ def test_packed_invariants_fuzz(seed):
         assert all(len(eng.request_tokens(r)) == max_new for r in prompts if next_start[r] is not None)
     assert admitted_order == sorted(admitted_order)  # FIFO
     eng.close()
+
+
+def test_admission_reserves_pages_to_finish():
+    """Ten 60-token prompts generating 40 tokens each end at 99 tokens, 7 pages, so a
+    40-page pool holds five at a time.  Their prompts alone (4 pages each) would all fit;
+    packed admission reserves the pages each admitted request can still take, so at most
+    five run at once and the run drains without NR_ERR_NO_BLOCKS."""
+    eng = host_engine(40, NR_SCHED_PACKED, max_new=40, budget=1024)
+    for rid in range(10):
+        eng.add_request(rid, [rid + 1] * 60)
+    most = 0
+    steps = 0
+    while eng.has_active_requests():
+        _commit_all(eng, eng.step_plan())
+        most = max(most, len(eng.running_batch()))
+        steps += 1
+        assert steps < 500
+    assert most == 5
+    assert all(len(eng.request_tokens(r)) == 40 for r in range(10))
+    eng.close()
+
+
+def test_reservation_capped_at_seq_len():
+    """A generation length beyond the model's sequence length (512 here) reserves only up
+    to seq_len: two 100-token prompts with max_new_tokens 100000 reserve 32 pages each,
+    so a 64-page pool admits both in one step."""
+    eng = host_engine(64, NR_SCHED_PACKED, max_new=100000, budget=1024)
+    eng.add_request(0, [3] * 100)
+    eng.add_request(1, [4] * 100)
+    p = eng.step_plan()
+    assert [x["req_id"] for x in p["prefills"]] == [0, 1]
+    eng.close()
