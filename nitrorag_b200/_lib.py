@@ -67,7 +67,11 @@ PI32 = C.POINTER(C.c_int32)
 PF = C.POINTER(C.c_float)
 U64 = C.c_uint64
 
-# name -> (restype, argtypes); every symbol declared in include/nitro_engine.h
+# nr_step_fn of include/nitro_server.h: int (*)(void* ctx, nr_engine*, nr_step_out*)
+STEP_FN = C.CFUNCTYPE(C.c_int, P, P, C.POINTER(NrStepOut))
+
+# name -> (restype, argtypes); every symbol declared in include/nitro_engine.h and
+# include/nitro_server.h
 SIGNATURES = {
     "nr_config_default": (None, [C.POINTER(NrConfig)]),
     "nr_engine_create": (C.c_int, [C.POINTER(NrConfig), C.c_char_p, C.POINTER(P)]),
@@ -121,6 +125,13 @@ SIGNATURES = {
     "nr_quantize_q8_device": (C.c_int, [P, C.c_int64, P, P]),
     "nr_quantize_q8": (C.c_int, [P, C.c_int64, P, I32]),
     "nr_quantize_model_file": (C.c_int, [C.c_char_p, C.c_char_p, I32]),
+    "nr_server_create": (C.c_int, [P, C.c_char_p, I32, STEP_FN, P, C.POINTER(P)]),
+    "nr_server_port": (C.c_int, [P]),
+    "nr_server_poll": (C.c_int, [P, I32]),
+    "nr_server_run": (C.c_int, [P]),
+    "nr_server_stop": (C.c_int, [P]),
+    "nr_server_counters": (C.c_int, [P, C.POINTER(C.c_int64)]),
+    "nr_server_destroy": (C.c_int, [P]),
 }
 
 _lib = None

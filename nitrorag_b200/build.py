@@ -10,6 +10,8 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, "libnitro_engine.so")
+SERVER = os.path.join(PKG, "nitro_server")        # the inference server process
+SERVER_SRC = os.path.join(PKG, "nitro_server.cc")
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",
@@ -37,13 +39,20 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
-        return LIB
     nvcc = os.environ.get("NVCC", "nvcc")
-    cmd = [nvcc, *NVCC_FLAGS, "-o", LIB, *sources()]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True, cwd=ROOT)
+    if force or not up_to_date():
+        cmd = [nvcc, *NVCC_FLAGS, "-o", LIB, *sources()]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True, cwd=ROOT)
+    if force or not os.path.exists(SERVER) or os.path.getmtime(SERVER) < max(
+            os.path.getmtime(LIB), os.path.getmtime(SERVER_SRC)):
+        # host-only executable linked against the library, found next to it at run time
+        cmd = [os.environ.get("CXX_HOST", "g++"), "-O2", "-std=c++17", "-Wall", "-o", SERVER, SERVER_SRC,
+               "-L", PKG, "-lnitro_engine", "-Wl,-rpath,$ORIGIN"]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True, cwd=ROOT)
     return LIB
 
 

@@ -11,7 +11,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import ROOT, assert_close
+from conftest import ATOL, ROOT, RTOL, assert_close
 from nitrorag_b200 import NR_Q8_FIXED, NR_SCHED_PACKED, EngineConfig, NitroEngine, synth
 from test_gpu_model import _check_tokens, _engine, _packed_vs_reference
 
@@ -20,28 +20,42 @@ pytestmark = pytest.mark.gpu
 sys.path.insert(0, ROOT)
 
 
-def _compare_step(ref, eng, res, B, handles, steps, check_logits):
+def _near_tie(row, got, want):
+    """True when the two tokens' reference logits are within the logits tolerance of each
+    other (a different fp32 summation order may then pick either)."""
+    a, b = float(row[got]), float(row[want])
+    return abs(a - b) <= ATOL + RTOL * max(abs(a), abs(b))
+
+
+def _compare_step(ref, eng, res, B, handles, steps, check_logits, diverged=None):
+    """One scheduler step of the engine against the reference.  With `diverged` (a dict),
+    a greedy-token flip between two logits inside the tolerance is recorded there as a
+    near tie (request -> (step, engine token, reference token, top-2 margin)) instead of
+    failing; that request's later tokens and logits then follow a different input and are
+    no longer compared, while its block table (count-driven) still is."""
     assert res.n_decode == B, steps
     assert eng.running_batch() == ref.sched_running(), steps
+    skip = diverged if diverged is not None else {}
     dec = res.emitted[len(res.emitted) - B:] if B else []
     lr = ref.sched_decode_logits(B) if B and check_logits else None
     if lr is not None:
         le = res.logits[len(res.emitted) - B:]
-        for r in range(B):
-            assert_close(le[r], lr[r], what=f"step {steps} decode row {r}")
+        for r, (rid, _) in enumerate(dec):
+            if rid not in skip:
+                assert_close(le[r], lr[r], what=f"step {steps} decode row {r}")
     for r, (rid, tok) in enumerate(dec):
         want = ref.generated(handles[rid])[-1]
-        if tok != want:
+        if tok != want and rid not in skip:
             row = lr[r] if lr is not None else ref.sched_decode_logits(B)[r]
+            if diverged is not None and _near_tie(row, tok, want):
+                diverged[rid] = (steps, tok, want, float(abs(row[tok] - row[want])))
+                continue
             _check_tokens(tok, want, row, f"step {steps} req {rid}")
     for rid, h in handles.items():
-        assert eng.request_tokens(rid) == ref.generated(h), (steps, rid)
+        if rid not in skip:
+            assert eng.request_tokens(rid) == ref.generated(h), (steps, rid)
         assert eng.request_block_table(rid) == ref.block_table(h), (steps, rid)
     assert eng.free_list() == ref.free_list(), steps
-
-
-def _cache_state(x):
-    return x.cache_entries(), x.lru()
 
 
 # ------------------------------------------------------------------ config 1
@@ -80,6 +94,7 @@ def test_config3_poisson_prefix_cache_full_run(ref_fixed, m110_model):
     ref.open(m110_model, 256, 4096)
     eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=4096, max_new=256, max_batch=64)
     handles = {}
+    diverged = {}
     steps = hits = 0
     for admitted in synth.virtual_clock_admissions(arrive):
         for i in admitted:
@@ -95,13 +110,25 @@ def test_config3_poisson_prefix_cache_full_run(ref_fixed, m110_model):
         B = ref.sched_step(256)
         res = eng.step(want_logits=check)
         hits += res.prefill_hits
-        _compare_step(ref, eng, res, B, handles, steps, check)
+        _compare_step(ref, eng, res, B, handles, steps, check, diverged)
         steps += 1
         assert steps < 5000
     assert not eng.has_active_requests()
     assert all(len(eng.request_tokens(i)) == 256 for i in range(len(prompts)))
     assert hits > 0 and eng.stats()["cache_hit_pages"] == hits
-    assert _cache_state(eng) == _cache_state(ref)
+    # near ties: reported, and rare (each is a flip between logits within the tolerance)
+    if diverged:
+        print(f"config 3 near-tie token flips (req: step, engine, reference, |logit gap|): {diverged}")
+    assert len(diverged) <= 3, diverged
+    # the prefix cache: same pages in the same LRU order; a hash can differ only for pages
+    # holding a diverged request's generated tokens
+    e_map, r_map = eng.cache_entries(), ref.cache_entries()
+    assert eng.lru() == ref.lru()
+    assert sorted(e_map.values()) == sorted(r_map.values())
+    if not diverged:
+        assert e_map == r_map
+    else:
+        assert sum(1 for h, b in r_map.items() if e_map.get(h) != b) <= 16 * len(diverged)
     eng.close()
     ref.close()
 
