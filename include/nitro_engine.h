@@ -44,6 +44,14 @@ extern "C" {
 #define NR_Q8_FIXED     0   /* sum all blocks (the reference's matmul definition, default) */
 #define NR_Q8_FAITHFUL  1   /* last block only, as the shipped batched path computes     */
 
+/* Element type of the K/V pages.  The reference keeps them fp32 (src/pagedMemory.hpp:90-94,
+ * src/model_q8.cpp:616-623), which NR_KV_F32 reproduces.  NR_KV_BF16 stores each K/V value
+ * rounded to bf16 (half the page bytes, so half the bytes decode attention reads); the
+ * attention still computes in fp32.  It changes the arithmetic (values carry 8 significant
+ * bits), so it is never the default and never used for parity with the reference. */
+#define NR_KV_F32   0
+#define NR_KV_BF16  1
+
 #define NR_SCHED_REFERENCE   0  /* Continuous_Scheduler::step, src/pagedMemory.hpp:317-398 */
 /* Same release and decode rules; admission goes on past the FIFO head while token budget
  * is left (a request whose prompt completes makes room for the next), each request only if
@@ -65,7 +73,8 @@ typedef struct nr_config {
     int32_t max_batch;             /* decode rows per forward call (scratch sizing), default 256, <= 1024 */
     int32_t max_prefill_tokens;    /* tokens per prefill call (scratch sizing), default 1024     */
     int32_t device;                /* CUDA device ordinal; -1 = host-only (metadata, no GPU)      */
-    int32_t reserved[7];
+    int32_t kv_dtype;              /* NR_KV_*: element type of the K/V pages, default fp32        */
+    int32_t reserved[6];
 } nr_config;
 
 typedef struct nr_engine nr_engine;
@@ -204,7 +213,7 @@ int nr_cache_is_cached(nr_engine* e, int32_t block);                       /* is
 int nr_cache_lru(nr_engine* e, int32_t* out, int32_t cap, int32_t* n);     /* evictable leaves, front to back */
 int nr_cache_entries(nr_engine* e, uint64_t* hashes, int32_t* blocks, int32_t cap, int32_t* n);
 /* Copy one page of the device K/V pools to host, converted to the reference's page
- * layout [layer][16][kv_dim] (src/pagedMemory.hpp:90). */
+ * layout [layer][16][kv_dim] (src/pagedMemory.hpp:90) and to fp32. */
 int nr_pool_read_page(nr_engine* e, int32_t block, float* k_out, float* v_out);
 
 /* hash_block_state, src/pagedMemory.hpp:14-24 (FNV-1a 64 over 4 LE bytes per token). */

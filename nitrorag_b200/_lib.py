@@ -20,6 +20,8 @@ NR_Q8_FIXED = 0
 NR_Q8_FAITHFUL = 1
 NR_SCHED_REFERENCE = 0
 NR_SCHED_PACKED = 1
+NR_KV_F32 = 0
+NR_KV_BF16 = 1
 
 
 class EngineLibraryMissing(RuntimeError):
@@ -31,7 +33,7 @@ class NrConfig(C.Structure):
         ("total_blocks", C.c_int32), ("max_tokens_per_batch", C.c_int32),
         ("max_new_tokens", C.c_int32), ("block_size", C.c_int32), ("sched_mode", C.c_int32),
         ("q8_mode", C.c_int32), ("max_batch", C.c_int32), ("max_prefill_tokens", C.c_int32),
-        ("device", C.c_int32), ("reserved", C.c_int32 * 7),
+        ("device", C.c_int32), ("kv_dtype", C.c_int32), ("reserved", C.c_int32 * 6),
     ]
 
 

@@ -18,6 +18,7 @@
 // covers a whole context writes its output, the others write their partial (max, sum,
 // unnormalised output) and a small merge kernel, chained behind it with programmatic
 // dependent launch, combines them.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,6 +33,7 @@ namespace nitro {
 namespace {
 
 constexpr int kAttnWarps = 4;
+
 
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -54,12 +56,12 @@ struct QState {
 // Fold the 16 rows of one K/V page tile (in shared memory) into a query's state.
 // qs: the query (head_dim floats, shared memory, pre-scaled by log2(e)/sqrt(head_dim));
 // n_valid: how many leading rows of the page are attended (1..16).
-template <int HD>
-__device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, const float* Kt, const float* Vt,
+template <int HD, typename KT>
+__device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, const KT* Kt, const KT* Vt,
                                             int n_valid, int lane) {
-    constexpr int HALF4 = HD / 8;  // float4s per half row
+    constexpr int HALF4 = HD / 8;  // groups of 4 values per half row
     const int t = lane >> 1, half = lane & 1;
-    const float4* krow = reinterpret_cast<const float4*>(Kt + t * HD + half * (HD / 2));
+    const KT* krow = Kt + t * HD + half * (HD / 2);
     const float4* qrow = reinterpret_cast<const float4*>(qs + half * (HD / 2));
     float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;  // four short FMA chains
 #pragma unroll
@@ -67,7 +69,7 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
         // rotate the float4 index with the lane so the 8 lanes of each shared-memory
         // phase hit 8 different bank groups
         const int jj = (j + lane) & (HALF4 - 1);
-        float4 kv = krow[jj];
+        float4 kv = ldkv4(krow + 4 * jj);
         float4 qv = qrow[jj];
         s0 = fmaf(qv.x, kv.x, s0);
         s1 = fmaf(qv.y, kv.y, s1);
@@ -90,16 +92,16 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
     st.m = m_new;
 #pragma unroll
     for (int i = 0; i < QState<HD>::DPL; i++) st.o[i] *= corr;
-    const float* vbase = Vt + lane * QState<HD>::DPL;
+    const KT* vbase = Vt + lane * QState<HD>::DPL;
 #pragma unroll
     for (int tt = 0; tt < kPage; tt++) {
         const float pt = __shfl_sync(0xffffffffu, p, 2 * tt);
         if (QState<HD>::DPL == 2) {
-            float2 v = *reinterpret_cast<const float2*>(vbase + tt * HD);
+            float2 v = ldkv2(vbase + tt * HD);
             st.o[0] = fmaf(pt, v.x, st.o[0]);
             st.o[1] = fmaf(pt, v.y, st.o[1]);
         } else {
-            float4 v = *reinterpret_cast<const float4*>(vbase + tt * HD);
+            float4 v = ldkv4(vbase + tt * HD);
             st.o[0] = fmaf(pt, v.x, st.o[0]);
             st.o[1] = fmaf(pt, v.y, st.o[1]);
             st.o[2] = fmaf(pt, v.z, st.o[2]);
@@ -125,12 +127,13 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
 #endif
 constexpr int kDecStages = NITRO_DEC_STAGES;
 
-template <int HD>
+template <int HD, typename KT = float>
 struct DecCfg {
     static constexpr int WARPS = HD == 64 ? NITRO_DEC_WARPS64 : NITRO_DEC_WARPS64 / 2;
-    static constexpr int TILE = kPage * HD;                              // floats per K or V tile
-    static constexpr int RING_FLOATS = WARPS * kDecStages * 2 * TILE;
-    static constexpr int SMEM = RING_FLOATS * 4 + WARPS * HD * 4;        // + one query per warp
+    static constexpr int TILE = kPage * HD;                              // elements per K or V tile
+    static constexpr int TILE_BYTES = TILE * (int)sizeof(KT);
+    static constexpr int RING_BYTES = WARPS * kDecStages * 2 * TILE_BYTES;
+    static constexpr int SMEM = RING_BYTES + WARPS * HD * 4;             // + one query per warp
 };
 
 struct DecItem {
@@ -205,11 +208,13 @@ __device__ __forceinline__ DecItem dec_item(int idx, int total, const DecTable& 
     return it;
 }
 
-template <int HD>
+template <int HD, typename KT>
 __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(DecodeAttnArgs a) {
-    using C = DecCfg<HD>;
+    using C = DecCfg<HD, KT>;
     constexpr int DPL = HD / 32;
-    extern __shared__ __align__(128) float smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const KT* kpool = reinterpret_cast<const KT*>(a.kpool);
+    const KT* vpool = reinterpret_cast<const KT*>(a.vpool);
     __shared__ uint64_t bars[C::WARPS][kDecStages];
     __shared__ DecTable tab;
 
@@ -294,8 +299,8 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
     __syncthreads();
     const int total = tab.full_prefix[a.B] + tab.bucket[0] * a.n_heads;
 
-    float* ring = smem + warp * kDecStages * 2 * C::TILE;
-    float* qs = smem + C::RING_FLOATS + warp * HD;
+    KT* ring = reinterpret_cast<KT*>(smem_raw + warp * kDecStages * 2 * C::TILE_BYTES);
+    float* qs = reinterpret_cast<float*>(smem_raw + C::RING_BYTES) + warp * HD;
     uint64_t* wb = bars[warp];
     if (lane == 0) {
         for (int s = 0; s < kDecStages; s++) mbar_init(&wb[s], 1);
@@ -327,9 +332,9 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
                 // that ended its processing, so the copy cannot overwrite live data
                 const int slot = issued % kDecStages;
                 const int64_t off = a.geom.tile_offset(page, a.layer, src.h / kvmul);
-                mbar_arrive_expect_tx(&wb[slot], 2u * C::TILE * 4u);
-                bulk_g2s(ring + (2 * slot) * C::TILE, a.kpool + off, C::TILE * 4, &wb[slot]);
-                bulk_g2s(ring + (2 * slot + 1) * C::TILE, a.vpool + off, C::TILE * 4, &wb[slot]);
+                mbar_arrive_expect_tx(&wb[slot], 2u * C::TILE_BYTES);
+                bulk_g2s(ring + (2 * slot) * C::TILE, kpool + off, C::TILE_BYTES, &wb[slot]);
+                bulk_g2s(ring + (2 * slot + 1) * C::TILE, vpool + off, C::TILE_BYTES, &wb[slot]);
             }
             issued++;
             ip++;
@@ -351,8 +356,8 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
             if (ok && !mbar_wait(&wb[slot], (consumed / kDecStages) & 1, a.err)) ok = false;
             if (ok) {
                 const int first = (cur.p0 + pg) * kPage;
-                attend_page<HD>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
-                                min(kPage, cur.ctx - first), lane);
+                attend_page<HD, KT>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
+                                    min(kPage, cur.ctx - first), lane);
             }
             __syncwarp();  // every lane is done with the slot before it is refilled
             consumed++;
@@ -400,27 +405,30 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
 // taking the sequence's pages round-robin through their own bulk-copy rings and joining
 // their softmax states in shared memory (in warp order), so neither split partials in
 // global memory nor the merge kernel are needed.
-template <int HD>
+template <int HD, typename KT = float>
 struct DecSmall {
     static constexpr int WARPS = HD == 64 ? 8 : 6;
     static constexpr int STAGES = HD == 64 ? 3 : 2;
     static constexpr int TILE = kPage * HD;
-    static constexpr int RING_FLOATS = WARPS * STAGES * 2 * TILE;
-    static constexpr int SMEM = RING_FLOATS * 4 + HD * 4 + WARPS * (HD + 2) * 4;
+    static constexpr int TILE_BYTES = TILE * (int)sizeof(KT);
+    static constexpr int RING_BYTES = WARPS * STAGES * 2 * TILE_BYTES;
+    static constexpr int SMEM = RING_BYTES + HD * 4 + WARPS * (HD + 2) * 4;
 };
 
-template <int HD>
+template <int HD, typename KT>
 __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small_kernel(DecodeAttnArgs a) {
-    using C = DecSmall<HD>;
+    using C = DecSmall<HD, KT>;
     constexpr int DPL = HD / 32;
     constexpr int W = C::WARPS, S = C::STAGES;
-    extern __shared__ __align__(128) float smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
     __shared__ uint64_t bars[W][S];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.x / a.n_heads, h = blockIdx.x % a.n_heads;
     const int kvh = h / (a.n_heads / a.geom.n_kv_heads);
-    float* ring = smem + warp * S * 2 * C::TILE;
-    float* qs = smem + C::RING_FLOATS;
+    const KT* kpool = reinterpret_cast<const KT*>(a.kpool);
+    const KT* vpool = reinterpret_cast<const KT*>(a.vpool);
+    KT* ring = reinterpret_cast<KT*>(smem_raw + warp * S * 2 * C::TILE_BYTES);
+    float* qs = reinterpret_cast<float*>(smem_raw + C::RING_BYTES);
     float* part = qs + HD;  // [W][HD + 2]: o, then m, l
 
     // page ids of this warp's pages (descriptor data: read before the wait)
@@ -438,9 +446,9 @@ __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small
         const int page = a.block_tables[(int64_t)b * a.max_pages + p];
         const int64_t off = a.geom.tile_offset(page, a.layer, kvh);
         uint64_t* bar = &bars[warp][j % S];
-        mbar_arrive_expect_tx(bar, 2u * C::TILE * 4u);
-        bulk_g2s(ring + (2 * (j % S)) * C::TILE, a.kpool + off, C::TILE * 4, bar);
-        bulk_g2s(ring + (2 * (j % S) + 1) * C::TILE, a.vpool + off, C::TILE * 4, bar);
+        mbar_arrive_expect_tx(bar, 2u * C::TILE_BYTES);
+        bulk_g2s(ring + (2 * (j % S)) * C::TILE, kpool + off, C::TILE_BYTES, bar);
+        bulk_g2s(ring + (2 * (j % S) + 1) * C::TILE, vpool + off, C::TILE_BYTES, bar);
     };
     if (lane == 0)
         for (int j = 0; j < S && j < mine; j++) issue(j);
@@ -454,8 +462,8 @@ __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small
         if (ok && !mbar_wait(&bars[warp][slot], (j / S) & 1, a.err)) ok = false;
         if (ok) {
             const int first = (warp + j * W) * kPage;
-            attend_page<HD>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
-                            min(kPage, ctx - first), lane);
+            attend_page<HD, KT>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
+                                min(kPage, ctx - first), lane);
         }
         __syncwarp();  // every lane is done with the slot before it is refilled
         if (lane == 0 && ok && j + S < mine) issue(j + S);
@@ -557,12 +565,16 @@ struct PrefillCfg {
     static constexpr int DG = HD / 8;            // dims per lane
 };
 
-template <int HD>
+template <int HD, typename KT>
 __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAttnArgs a) {
     using P = PrefillCfg<HD>;
     constexpr int TILE = kPage * HD;
+    constexpr int TILE_BYTES = TILE * (int)sizeof(KT);
     constexpr int QW = P::QW, DG = P::DG;
-    extern __shared__ __align__(128) float smem[];  // [kStages][2][TILE]
+    extern __shared__ __align__(128) uint8_t smem_raw[];  // [kStages][2][TILE] page elements
+    KT* smem = reinterpret_cast<KT*>(smem_raw);
+    const KT* kpool = reinterpret_cast<const KT*>(a.kpool);
+    const KT* vpool = reinterpret_cast<const KT*>(a.vpool);
     __shared__ uint64_t full[kStages];
 
     // blocks in order of decreasing work (later query tiles attend more pages) so the
@@ -595,9 +607,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
     auto issue = [&](int page_idx) {
         const int s = page_idx % kStages;
         const int64_t off = a.geom.tile_offset(bt[page_idx], a.layer, kvh);
-        mbar_arrive_expect_tx(&full[s], 2u * TILE * 4u);
-        bulk_g2s(smem + (2 * s) * TILE, a.kpool + off, TILE * 4, &full[s]);
-        bulk_g2s(smem + (2 * s + 1) * TILE, a.vpool + off, TILE * 4, &full[s]);
+        mbar_arrive_expect_tx(&full[s], 2u * TILE_BYTES);
+        bulk_g2s(smem + (2 * s) * TILE, kpool + off, TILE_BYTES, &full[s]);
+        bulk_g2s(smem + (2 * s + 1) * TILE, vpool + off, TILE_BYTES, &full[s]);
     };
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
@@ -638,17 +650,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
         const int s = p % kStages;
         if (ok && !mbar_wait(&full[s], (p / kStages) & 1, a.err)) ok = false;
         if (ok && p * kPage <= warp_last) {
-            const float* Kt = smem + (2 * s) * TILE;
-            const float* Vt = smem + (2 * s + 1) * TILE;
+            const KT* Kt = smem + (2 * s) * TILE;
+            const KT* Vt = smem + (2 * s + 1) * TILE;
             // scores of (query i, key kg*4 + j) over this lane's dims, then over all dims
             float sc[QW][4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 float kr[DG];
-                const float4* k4 = reinterpret_cast<const float4*>(Kt + (kg * 4 + j) * HD + dg * DG);
+                const KT* k4 = Kt + (kg * 4 + j) * HD + dg * DG;
 #pragma unroll
                 for (int c = 0; c < DG / 4; c++) {
-                    const float4 v = k4[c];
+                    const float4 v = ldkv4(k4 + 4 * c);
                     kr[4 * c] = v.x; kr[4 * c + 1] = v.y; kr[4 * c + 2] = v.z; kr[4 * c + 3] = v.w;
                 }
 #pragma unroll
@@ -700,10 +712,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) prefill_attn_kernel(PrefillAt
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 float vr[DG];
-                const float4* v4 = reinterpret_cast<const float4*>(Vt + (kg * 4 + j) * HD + dg * DG);
+                const KT* v4 = Vt + (kg * 4 + j) * HD + dg * DG;
 #pragma unroll
                 for (int c = 0; c < DG / 4; c++) {
-                    const float4 v = v4[c];
+                    const float4 v = ldkv4(v4 + 4 * c);
                     vr[4 * c] = v.x; vr[4 * c + 1] = v.y; vr[4 * c + 2] = v.z; vr[4 * c + 3] = v.w;
                 }
 #pragma unroll
@@ -801,18 +813,39 @@ static int sm_count() {
     return counts[dev] > 0 ? counts[dev] : 148;
 }
 
+template <int HD, typename KT>
+static void launch_small(const DecodeAttnArgs& a, dim3 g, cudaStream_t s) {
+    using C = DecSmall<HD, KT>;
+    ensure_smem(decode_attn_small_kernel<HD, KT>, C::SMEM);
+    launch_ex(decode_attn_small_kernel<HD, KT>, g, dim3(C::WARPS * 32), C::SMEM, s, 1, a);
+}
+
+template <int HD, typename KT>
+static void launch_split(const DecodeAttnArgs& a, int grid, cudaStream_t s) {
+    using C = DecCfg<HD, KT>;
+    ensure_smem(decode_attn_kernel<HD, KT>, C::SMEM);
+    launch_ex(decode_attn_kernel<HD, KT>, dim3(grid), dim3(C::WARPS * 32), C::SMEM, s, 1, a);
+}
+
+template <int HD, typename KT>
+static void launch_prefill(const PrefillAttnArgs& a, cudaStream_t s) {
+    dim3 grid((unsigned)((a.seg ? a.n_tiles : (a.T + PrefillCfg<HD>::QT - 1) / PrefillCfg<HD>::QT) * a.n_heads));
+    const int smem = kStages * 2 * kPage * HD * (int)sizeof(KT);
+    ensure_smem(prefill_attn_kernel<HD, KT>, smem);
+    launch_ex(prefill_attn_kernel<HD, KT>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
+}
+
 void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream_t s) {
     count_launch();
     const int grid = sm_count();
     if ((int64_t)args.B * args.n_heads <= grid) {  // small batch: one CTA per (sequence, head)
         const dim3 g((unsigned)(args.B * args.n_heads));
         if (args.geom.head_dim == 64) {
-            ensure_smem(decode_attn_small_kernel<64>, DecSmall<64>::SMEM);
-            launch_ex(decode_attn_small_kernel<64>, g, dim3(DecSmall<64>::WARPS * 32), DecSmall<64>::SMEM, s, 1, args);
+            if (args.geom.kv_bf16) launch_small<64, __nv_bfloat16>(args, g, s);
+            else launch_small<64, float>(args, g, s);
         } else {
-            ensure_smem(decode_attn_small_kernel<128>, DecSmall<128>::SMEM);
-            launch_ex(decode_attn_small_kernel<128>, g, dim3(DecSmall<128>::WARPS * 32), DecSmall<128>::SMEM, s, 1,
-                      args);
+            if (args.geom.kv_bf16) launch_small<128, __nv_bfloat16>(args, g, s);
+            else launch_small<128, float>(args, g, s);
         }
         return;
     }
@@ -828,12 +861,12 @@ void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream
     const dim3 mgrid((unsigned)(((int64_t)a.B * a.n_heads + 7) / 8));
     count_launch();
     if (a.geom.head_dim == 64) {
-        ensure_smem(decode_attn_kernel<64>, DecCfg<64>::SMEM);
-        launch_ex(decode_attn_kernel<64>, dim3(grid), dim3(DecCfg<64>::WARPS * 32), DecCfg<64>::SMEM, s, 1, a);
+        if (a.geom.kv_bf16) launch_split<64, __nv_bfloat16>(a, grid, s);
+        else launch_split<64, float>(a, grid, s);
         launch_ex(decode_merge_kernel<64>, mgrid, dim3(256), 0, s, 1, a);
     } else {
-        ensure_smem(decode_attn_kernel<128>, DecCfg<128>::SMEM);
-        launch_ex(decode_attn_kernel<128>, dim3(grid), dim3(DecCfg<128>::WARPS * 32), DecCfg<128>::SMEM, s, 1, a);
+        if (a.geom.kv_bf16) launch_split<128, __nv_bfloat16>(a, grid, s);
+        else launch_split<128, float>(a, grid, s);
         launch_ex(decode_merge_kernel<128>, mgrid, dim3(256), 0, s, 1, a);
     }
 }
@@ -848,15 +881,11 @@ void launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
     if (prefill_attn_tc_enabled(a.geom.head_dim)) {
         launch_prefill_attention_tc(a, s);
     } else if (a.geom.head_dim == 64) {
-        dim3 grid((unsigned)((a.seg ? a.n_tiles : (a.T + PrefillCfg<64>::QT - 1) / PrefillCfg<64>::QT) * a.n_heads));
-        const int smem = kStages * 2 * kPage * 64 * 4;
-        ensure_smem(prefill_attn_kernel<64>, smem);
-        launch_ex(prefill_attn_kernel<64>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
+        if (a.geom.kv_bf16) launch_prefill<64, __nv_bfloat16>(a, s);
+        else launch_prefill<64, float>(a, s);
     } else {
-        dim3 grid((unsigned)((a.seg ? a.n_tiles : (a.T + PrefillCfg<128>::QT - 1) / PrefillCfg<128>::QT) * a.n_heads));
-        const int smem = kStages * 2 * kPage * 128 * 4;
-        ensure_smem(prefill_attn_kernel<128>, smem);
-        launch_ex(prefill_attn_kernel<128>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
+        if (a.geom.kv_bf16) launch_prefill<128, __nv_bfloat16>(a, s);
+        else launch_prefill<128, float>(a, s);
     }
 }
 

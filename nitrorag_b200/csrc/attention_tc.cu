@@ -24,9 +24,12 @@
 //
 // Every mbarrier wait is bounded; a CTA whose wait gave up sets the error flag, releases
 // its tensor memory and writes nothing.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <mutex>
+#include <set>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -41,16 +44,20 @@ constexpr int FA_THREADS = 2 * FA_M;          // two warpgroups: each row's keys
 constexpr int FA_N = 64;                      // keys per block = UMMA N of S
 constexpr int FA_HD = 64;                     // head_dim = K of S = N of O
 constexpr int FA_PAGES = FA_N / kPage;        // pages per key block
-constexpr int FA_PAGE_BYTES = kPage * FA_HD * 4;  // one fp32 K (or V) page tile
+constexpr int FA_PAGE_BYTES = kPage * FA_HD * 4;  // one fp32 K (or V) page tile (bf16 pages: half)
 constexpr int FA_RAW = 2 * FA_PAGES * FA_PAGE_BYTES;  // K and V tiles of one block (32 KB)
 // dynamic shared memory, bytes: bf16 halves of Q [128][64], K [64][64], P [128][64],
-// V^T [64][64], then two stages of raw fp32 page tiles
+// V^T [64][64], then two stages of raw page tiles (laid out for fp32 pages)
 constexpr int OFF_QH = 0, OFF_QL = 16384, OFF_KH = 32768, OFF_KL = 40960, OFF_PH = 49152, OFF_PL = 65536,
               OFF_VH = 81920, OFF_VL = 90112, OFF_RAW = 98304;
 constexpr int FA_SMEM = OFF_RAW + 2 * FA_RAW;
 constexpr uint32_t FA_TMEM_COLS = 128;  // S in columns 0-63, O_blk in 64-127
 
+template <typename KT>
 __global__ void __launch_bounds__(FA_THREADS, 1) prefill_attn_tc_kernel(PrefillAttnArgs a) {
+    constexpr int PAGE_BYTES = kPage * FA_HD * (int)sizeof(KT);  // one K (or V) page tile
+    const KT* kpool = reinterpret_cast<const KT*>(a.kpool);
+    const KT* vpool = reinterpret_cast<const KT*>(a.vpool);
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t raw_bar[2], s_bar, o_bar;
     __shared__ uint32_t tmem_slot;
@@ -96,11 +103,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1) prefill_attn_tc_kernel(PrefillA
         uint8_t* raw = smem + OFF_RAW + (b & 1) * FA_RAW;
         const int p0 = b * FA_PAGES, np = min(FA_PAGES, n_pages - p0);
         uint64_t* bar = &raw_bar[b & 1];
-        mbar_arrive_expect_tx(bar, (uint32_t)(2 * np * FA_PAGE_BYTES));
+        mbar_arrive_expect_tx(bar, (uint32_t)(2 * np * PAGE_BYTES));
         for (int p = 0; p < np; p++) {
             const int64_t off = a.geom.tile_offset(bt[p0 + p], a.layer, kvh);
-            bulk_g2s(raw + p * FA_PAGE_BYTES, a.kpool + off, FA_PAGE_BYTES, bar);
-            bulk_g2s(raw + (FA_PAGES + p) * FA_PAGE_BYTES, a.vpool + off, FA_PAGE_BYTES, bar);
+            bulk_g2s(raw + p * PAGE_BYTES, kpool + off, PAGE_BYTES, bar);
+            bulk_g2s(raw + (FA_PAGES + p) * PAGE_BYTES, vpool + off, PAGE_BYTES, bar);
         }
     };
     grid_dependency_wait();  // q and this chunk's K/V rows come from the projection kernel
@@ -143,12 +150,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1) prefill_attn_tc_kernel(PrefillA
         // K: thread t converts a quarter key row (key t/4, dims (t&3)*16..+15)
         {
             const int key = tid >> 2, qd = tid & 3;
-            const float4* krow = reinterpret_cast<const float4*>(raw) + key * (FA_HD / 4) + qd * 4;
+            const KT* krow = reinterpret_cast<const KT*>(raw) + key * FA_HD + qd * 16;
 #pragma unroll
             for (int g = 0; g < 2; g++) {
                 float v[8];
                 if (key < valid_keys) {
-                    const float4 x0 = krow[2 * g], x1 = krow[2 * g + 1];
+                    const float4 x0 = ldkv4(krow + 8 * g), x1 = ldkv4(krow + 8 * g + 4);
                     v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
                     v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
                 } else {
@@ -161,14 +168,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1) prefill_attn_tc_kernel(PrefillA
         // V transposed: thread t converts dim t/4 of keys (t&3)*16..+15
         {
             const int dim = tid >> 2, qk = tid & 3;
-            const float* vbase = reinterpret_cast<const float*>(raw + FA_PAGES * FA_PAGE_BYTES);
+            const KT* vbase = reinterpret_cast<const KT*>(raw + FA_PAGES * PAGE_BYTES);
 #pragma unroll
             for (int g = 0; g < 2; g++) {
                 float v[8];
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     const int key = qk * 16 + g * 8 + i;  // page tiles are contiguous: key * 64 + dim
-                    v[i] = key < valid_keys ? vbase[key * FA_HD + dim] : 0.0f;
+                    v[i] = key < valid_keys ? ldkv1(vbase + key * FA_HD + dim) : 0.0f;
                 }
                 split_store8(v, smem + OFF_VH + core_off(dim, qk * 2 + g), smem + OFF_VL + core_off(dim, qk * 2 + g));
             }
@@ -274,15 +281,23 @@ bool prefill_attn_tc_enabled(int head_dim) {
 }
 
 void launch_prefill_attention_tc(const PrefillAttnArgs& a, cudaStream_t s) {
-    static int configured_dev = -1;
+    static std::mutex mu;
+    static std::set<int> configured;  // devices whose kernels have their shared-memory limit set
     int dev = 0;
     cudaGetDevice(&dev);
-    if (configured_dev != dev) {
-        cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
-        configured_dev = dev;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured.count(dev)) {
+            cudaFuncSetAttribute(prefill_attn_tc_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+            cudaFuncSetAttribute(prefill_attn_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 FA_SMEM);
+            configured.insert(dev);
+        }
     }
     const int tiles = a.seg ? a.n_tiles : (a.T + FA_M - 1) / FA_M;
-    launch_ex(prefill_attn_tc_kernel, dim3((unsigned)(tiles * a.n_heads)), dim3(FA_THREADS), FA_SMEM, s, 1, a);
+    const dim3 grid((unsigned)(tiles * a.n_heads));
+    if (a.geom.kv_bf16) launch_ex(prefill_attn_tc_kernel<__nv_bfloat16>, grid, dim3(FA_THREADS), FA_SMEM, s, 1, a);
+    else launch_ex(prefill_attn_tc_kernel<float>, grid, dim3(FA_THREADS), FA_SMEM, s, 1, a);
 }
 
 }  // namespace nitro

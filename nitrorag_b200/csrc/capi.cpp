@@ -59,6 +59,7 @@ int validate_cfg(const nr_config* c) {
     if (c->max_batch <= 0 || c->max_batch > 1024 || c->max_prefill_tokens <= 0) return NR_ERR_INVALID;
     if (c->q8_mode != NR_Q8_FIXED && c->q8_mode != NR_Q8_FAITHFUL) return NR_ERR_INVALID;
     if (c->sched_mode != NR_SCHED_REFERENCE && c->sched_mode != NR_SCHED_PACKED) return NR_ERR_INVALID;
+    if (c->kv_dtype != NR_KV_F32 && c->kv_dtype != NR_KV_BF16) return NR_ERR_INVALID;
     return NR_OK;
 }
 

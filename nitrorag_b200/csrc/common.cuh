@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <utility>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 namespace nitro {
@@ -21,12 +22,15 @@ constexpr int kErrBadContext = 2;
 // sets the kernel's error flag; the kernel then skips the work that needed the data.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
-// Page layout of the device K and V pools: [page][layer][kv_head][16][head_dim] fp32, so
-// the 16 rows of one (page, layer, kv_head) form one contiguous tile of 16*head_dim floats.
+// Page layout of the device K and V pools: [page][layer][kv_head][16][head_dim] elements
+// (fp32, or bf16 with kv_bf16 = 1), so the 16 rows of one (page, layer, kv_head) form one
+// contiguous tile of 16*head_dim elements.  Offsets below count elements.
 struct PoolGeom {
     int n_layers;
     int n_kv_heads;
     int head_dim;
+    int kv_bf16 = 0;
+    __host__ __device__ int elem_bytes() const { return kv_bf16 ? 2 : 4; }
     __host__ __device__ int64_t page_floats() const { return (int64_t)n_layers * n_kv_heads * kPage * head_dim; }
     __host__ __device__ int64_t tile_offset(int64_t page, int layer, int kvh) const {
         return page * page_floats() + ((int64_t)layer * n_kv_heads + kvh) * kPage * head_dim;
@@ -34,6 +38,30 @@ struct PoolGeom {
 };
 
 #if defined(__CUDACC__)
+// K/V page elements (from shared memory) as fp32: fp32 pages load as they are; bf16 pages
+// hold the upper 16 bits of an fp32, so a shift widens them exactly.
+__device__ __forceinline__ float4 ldkv4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ldkv4(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+}
+__device__ __forceinline__ float2 ldkv2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 ldkv2(const __nv_bfloat16* p) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+__device__ __forceinline__ float ldkv1(const float* p) { return *p; }
+__device__ __forceinline__ float ldkv1(const __nv_bfloat16* p) {
+    return __uint_as_float((uint32_t)*reinterpret_cast<const uint16_t*>(p) << 16);
+}
+
+// Store one K or V value at element index idx of a pool of geometry g (the K/V append).
+__device__ __forceinline__ void store_kv(float* pool, const PoolGeom& g, int64_t idx, float v) {
+    if (g.kv_bf16) reinterpret_cast<__nv_bfloat16*>(pool)[idx] = __float2bfloat16_rn(v);
+    else pool[idx] = v;
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }

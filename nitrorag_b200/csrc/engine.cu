@@ -326,8 +326,8 @@ int Engine::init_device(const uint8_t* file, size_t size) {
     int rc = upload_weights(file, size);
     if (rc != NR_OK) return rc;
 
-    geom_ = PoolGeom{c.n_layers, c.n_kv_heads, c.head_dim()};
-    const size_t pool_bytes = (size_t)cfg_.total_blocks * geom_.page_floats() * 4;
+    geom_ = PoolGeom{c.n_layers, c.n_kv_heads, c.head_dim(), cfg_.kv_dtype == NR_KV_BF16 ? 1 : 0};
+    const size_t pool_bytes = (size_t)cfg_.total_blocks * geom_.page_floats() * geom_.elem_bytes();
     NR_CUDA(cudaMalloc(&kpool_, pool_bytes));
     NR_CUDA(cudaMalloc(&vpool_, pool_bytes));
     NR_CUDA(cudaMemsetAsync(kpool_, 0, pool_bytes, stream_));
@@ -812,14 +812,22 @@ int Engine::read_page(int block, float* k_out, float* v_out) {
     const ModelShape& c = shape_;
     const int hd = c.head_dim(), KV = c.kv_dim();
     const size_t pf = (size_t)geom_.page_floats();
+    const size_t eb = (size_t)geom_.elem_bytes();
     std::vector<float> tmp(pf);
+    std::vector<uint16_t> raw16(geom_.kv_bf16 ? pf : 0);
     NR_CUDA(cudaSetDevice(cfg_.device));
     for (int which = 0; which < 2; which++) {
         float* dst = which == 0 ? k_out : v_out;
         if (!dst) continue;
-        const float* src = (which == 0 ? kpool_ : vpool_) + (size_t)block * pf;
-        NR_CUDA(cudaMemcpyAsync(tmp.data(), src, pf * 4, cudaMemcpyDeviceToHost, stream_));
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(which == 0 ? kpool_ : vpool_) + (size_t)block * pf * eb;
+        NR_CUDA(cudaMemcpyAsync(geom_.kv_bf16 ? (void*)raw16.data() : (void*)tmp.data(), src, pf * eb,
+                                cudaMemcpyDeviceToHost, stream_));
         NR_CUDA(cudaStreamSynchronize(stream_));
+        if (geom_.kv_bf16)  // bf16 is the upper half of an fp32
+            for (size_t i = 0; i < pf; i++) {
+                const uint32_t u = (uint32_t)raw16[i] << 16;
+                memcpy(&tmp[i], &u, 4);
+            }
         // [layer][kv_head][16][hd] -> [layer][16][kv_dim]
         for (int l = 0; l < c.n_layers; l++)
             for (int h = 0; h < c.n_kv_heads; h++)

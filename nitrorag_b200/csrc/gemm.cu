@@ -65,17 +65,17 @@ __device__ __forceinline__ void epi_pair(const Epilogue& e, int m, int n, float 
                 e.q_out[(int64_t)m * D + n] = r0;
                 e.q_out[(int64_t)m * D + n + 1] = r1;
             } else {
-                float* dst = e.kpool + e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
-                             (int64_t)(pos & (kPage - 1)) * hd + (c % hd);
-                dst[0] = r0;
-                dst[1] = r1;
+                const int64_t at = e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
+                                   (int64_t)(pos & (kPage - 1)) * hd + (c % hd);
+                store_kv(e.kpool, e.geom, at, r0);
+                store_kv(e.kpool, e.geom, at + 1, r1);
             }
         } else {
             int c = n - D - KV;
-            float* dst = e.vpool + e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
-                         (int64_t)(pos & (kPage - 1)) * hd + (c % hd);
-            dst[0] = v0;
-            dst[1] = v1;
+            const int64_t at = e.geom.tile_offset(e.tok_page[m], e.layer, c / hd) +
+                               (int64_t)(pos & (kPage - 1)) * hd + (c % hd);
+            store_kv(e.vpool, e.geom, at, v0);
+            store_kv(e.vpool, e.geom, at + 1, v1);
         }
         break;
     }

@@ -800,7 +800,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                     if (qkv_kind == 0)
                         e.q_out[(int64_t)m * D + row_off] = r;
                     else
-                        pool[(int64_t)page[j] * pf + (int64_t)(pos[j] & (kPage - 1)) * hd + row_off] = r;
+                        store_kv(pool, e.geom, (int64_t)page[j] * pf + (int64_t)(pos[j] & (kPage - 1)) * hd + row_off, r);
                 }
             }
         }

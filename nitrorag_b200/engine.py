@@ -16,12 +16,12 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from ._lib import (NR_Q8_FAITHFUL, NR_Q8_FIXED, NR_SCHED_PACKED, NR_SCHED_REFERENCE, NrConfig, NrError, NrPlan,
-                   NrStats, NrStepOut, check, lib)
+from ._lib import (NR_KV_BF16, NR_KV_F32, NR_Q8_FAITHFUL, NR_Q8_FIXED, NR_SCHED_PACKED, NR_SCHED_REFERENCE, NrConfig,
+                   NrError, NrPlan, NrStats, NrStepOut, check, lib)
 
 __all__ = ["NitroEngine", "EngineConfig", "StepResult", "hash_block_state", "argmax",
-           "NR_Q8_FIXED", "NR_Q8_FAITHFUL", "NR_SCHED_REFERENCE", "NR_SCHED_PACKED", "NrError",
-           "FNV_OFFSET_BASIS"]
+           "NR_Q8_FIXED", "NR_Q8_FAITHFUL", "NR_SCHED_REFERENCE", "NR_SCHED_PACKED", "NR_KV_F32", "NR_KV_BF16",
+           "NrError", "FNV_OFFSET_BASIS"]
 
 FNV_OFFSET_BASIS = 14695981039346656037
 
@@ -58,6 +58,7 @@ class EngineConfig:
     max_prefill_tokens: int = 1024
     device: int = 0
     sched_mode: int = 0  # NR_SCHED_REFERENCE; 1 = NR_SCHED_PACKED
+    kv_dtype: int = 0    # NR_KV_F32; 1 = NR_KV_BF16 (bf16 K/V pages)
 
     def to_c(self) -> NrConfig:
         c = NrConfig()
@@ -70,6 +71,7 @@ class EngineConfig:
         c.max_prefill_tokens = self.max_prefill_tokens
         c.device = self.device
         c.sched_mode = self.sched_mode
+        c.kv_dtype = self.kv_dtype
         return c
 
 

@@ -230,7 +230,19 @@ struct OrcModel {
     std::vector<float> kpool, vpool;
     int64_t page_floats;
     int total_pages;
+    int kv_bf16 = 0;  // pages hold K/V rounded to bf16 (the engine's NR_KV_BF16 option)
 };
+
+// Round to the nearest bf16 (8 significant bits), ties to even, kept as fp32: IEEE
+// round-to-nearest-even on the upper 16 bits of the fp32 pattern (finite values).
+static float round_bf16(float v) {
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    u &= 0xFFFF0000u;
+    memcpy(&v, &u, 4);
+    return v;
+}
 
 void* orc_model_open(const char* path, int total_pages) {
     FILE* f = fopen(path, "rb");
@@ -272,6 +284,10 @@ void* orc_model_open(const char* path, int total_pages) {
 
 void orc_model_close(void* h) { delete (OrcModel*)h; }
 
+// Pages store K/V rounded to bf16 from now on (no reference counterpart: the reference's
+// pages are fp32, src/pagedMemory.hpp:90-94).
+void orc_model_set_kv_bf16(void* h, int on) { ((OrcModel*)h)->kv_bf16 = on != 0; }
+
 int orc_model_page(void* h, int page, float* k_out, float* v_out) {
     OrcModel* m = (OrcModel*)h;
     if (page < 0 || page >= m->total_pages) return -1;
@@ -306,6 +322,11 @@ void run_layers(OrcModel* m, int R, const int* pos, BT bt_row, ATT attend, std::
             int64_t off = pg * m->page_floats + layer_off + (int64_t)(pos[r] % PAGE) * kv_dim;
             memcpy(&m->kpool[off], &k[(size_t)r * kv_dim], kv_dim * 4);
             memcpy(&m->vpool[off], &v[(size_t)r * kv_dim], kv_dim * 4);
+            if (m->kv_bf16)
+                for (int i = 0; i < kv_dim; i++) {
+                    m->kpool[off + i] = round_bf16(m->kpool[off + i]);
+                    m->vpool[off + i] = round_bf16(m->vpool[off + i]);
+                }
         }
         attend(q.data(), att.data(), layer_off);
         orc_q8_matmul(tmp.data(), att.data(), m->wo + (int64_t)l * D * D / QB * 36, R, D, D, lbo);

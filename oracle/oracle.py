@@ -83,6 +83,7 @@ class Restatement:
         L.orc_model_open.restype = C.c_void_p
         L.orc_model_close.argtypes = [C.c_void_p]
         L.orc_model_page.argtypes = [C.c_void_p, C.c_int, PF, PF]
+        L.orc_model_set_kv_bf16.argtypes = [C.c_void_p, C.c_int]
         L.orc_forward_prefill.argtypes = [C.c_void_p, PI32, PI32, C.c_int, C.c_int, PF, C.c_int]
         L.orc_forward_decode.argtypes = [C.c_void_p, PI32, C.c_int, C.c_int, PI32, PI32, PF, C.c_int]
         self.L = L
@@ -162,6 +163,10 @@ class RestatedModel:
             hdr = np.frombuffer(f.read(28), np.int32)
         self.dim, self.hidden, self.n_layers, self.n_heads, self.n_kv_heads, self.vocab, self.seq_len = map(int, hdr)
         self.kv_dim = self.n_kv_heads * (self.dim // self.n_heads)
+
+    def set_kv_bf16(self, on: bool = True):
+        """Round K/V to bf16 as they are appended to the pages (the engine's NR_KV_BF16)."""
+        self.o.L.orc_model_set_kv_bf16(self.h, int(on))
 
     def close(self):
         if self.h:

@@ -1,0 +1,116 @@
+"""K/V pages in bf16 (NR_KV_BF16, off by default): every K/V value rounded to bf16 when it
+is appended, attention still in fp32.  The reference keeps fp32 pages, so this option is
+not parity with it; it is checked two ways:
+
+* against the CPU restatement run with the same rounding (orc_model_set_kv_bf16): logits
+  within the usual 1e-3 relative + 1e-4 absolute, pages equal value for value, greedy
+  tokens equal (a mismatch is reported with its top-2 margin);
+* against the fp32 reference (ref_fixed): logits within 2e-2 of the logits' RMS, the
+  error bf16 pages bring (8 significant bits per K/V value, ~4e-3 relative per value)."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import assert_close
+from nitrorag_b200 import NR_KV_BF16, NR_SCHED_PACKED, EngineConfig, NitroEngine, synth
+from test_gpu_model import _check_tokens
+
+pytestmark = pytest.mark.gpu
+
+
+def _rms(x):
+    return float(np.sqrt(np.mean(np.asarray(x, np.float64) ** 2)))
+
+
+def _greedy(row):
+    return int(np.argmax(np.where(row > 0, row, -np.inf))) if row.max() > 0 else 0
+
+
+def _run(path, restatement, ref, lens, decode_steps, seed, pages=256):
+    eng = NitroEngine(path, EngineConfig(total_blocks=pages, max_new_tokens=64, max_batch=128, max_prefill_tokens=512,
+                                         kv_dtype=NR_KV_BF16))
+    model = restatement.model(path, pages)
+    model.set_kv_bf16(True)
+    ref.open(path, 512, pages)
+    rng = np.random.default_rng(seed)
+    V = eng.vocab_size
+    seqs, rh, toks, pos = [], [], [], []
+    for i, n in enumerate(lens):
+        prompt = rng.integers(0, V, n).astype(np.int32)
+        s = eng.seq_create(i)
+        seqs.append(s)
+        rh.append(ref.new_request(i, prompt))
+        le, tok = eng.forward_prefill_chunk(s, prompt, 0)
+        want = model.forward_prefill(eng.block_table(s), prompt, 0)
+        assert_close(le, want, what=f"bf16-page prefill seq {i} ({n} tokens)")
+        lr = ref.forward_prefill(rh[i], prompt, 0)
+        assert np.max(np.abs(le - lr)) <= 2e-2 * _rms(lr), f"bf16 pages vs fp32 reference, seq {i}"
+        toks.append(tok)
+        pos.append(n)
+    for step in range(decode_steps):
+        want = model.forward_decode([eng.block_table(s) for s in seqs], toks, pos)
+        le, am = eng.forward_decode_batch(toks, pos, seqs)
+        assert_close(le, want, what=f"bf16-page decode step {step} (B={len(seqs)})")
+        for i in range(len(seqs)):
+            _check_tokens(int(am[i]), _greedy(want[i]), want[i], f"bf16-page decode step {step} row {i}")
+        toks = [int(t) for t in am]
+        pos = [p + 1 for p in pos]
+    for blk in eng.block_table(seqs[0])[:3]:
+        k1, v1 = model.page(blk)
+        k2, v2 = eng.read_page(blk)
+        assert np.array_equal(k2, k1) and np.array_equal(v2, v1), blk
+    eng.close()
+    model.close()
+    ref.close()
+
+
+@pytest.mark.parametrize("shape_args", [None, (256, 512, 2, 2, 1, 512, 1024)], ids=["tiny-hd64", "hd128-gqa2"])
+def test_bf16_pages_many_rows(restatement, ref_fixed, tiny_model, model_dir, shape_args):
+    """80 prompts of 1-60 tokens (prefill on the matvec and the tensor-core projections, K/V
+    appended by both), then decode at B = 80: more (sequence, head) pairs than SMs, so the
+    split decode kernel and its merge read the bf16 pages."""
+    if shape_args is None:
+        path = tiny_model
+    else:
+        path = synth.write_model(os.path.join(model_dir, "bf16_hd128.bin"), synth.ModelShape(*shape_args), seed=6)
+    lens = [int(n) for n in np.random.default_rng(3).integers(1, 61, 80)]
+    _run(path, restatement, ref_fixed, lens, 3, seed=70, pages=512)
+
+
+@pytest.mark.parametrize("shape_args", [None, (256, 512, 2, 2, 1, 512, 1024)], ids=["tiny-hd64", "hd128-gqa2"])
+def test_bf16_pages_small_batch(restatement, ref_fixed, tiny_model, model_dir, shape_args):
+    """A 300-token prompt and two short ones, then decode at B = 3 (one attention CTA per
+    (sequence, head) reading bf16 pages)."""
+    if shape_args is None:
+        path = tiny_model
+    else:
+        path = synth.write_model(os.path.join(model_dir, "bf16_hd128.bin"), synth.ModelShape(*shape_args), seed=6)
+    _run(path, restatement, ref_fixed, [300, 17, 64], 8, seed=71)
+
+
+def test_bf16_pages_110m(restatement, ref_fixed, m110_model):
+    """The 110M model: a 24-token prompt on the tensor-core path, then decode at B = 1."""
+    _run(m110_model, restatement, ref_fixed, [24], 3, seed=72, pages=64)
+
+
+def test_bf16_pages_packed_scheduler(restatement, tiny_model):
+    """NR_SCHED_PACKED with bf16 pages: several prompts in one forward pass (the tensor-core
+    prefill attention over a segment table reads bf16 pages), each request's logits
+    against the restatement with bf16 rounding."""
+    eng = NitroEngine(tiny_model, EngineConfig(total_blocks=256, max_new_tokens=2, max_batch=32,
+                                               max_tokens_per_batch=1024, max_prefill_tokens=1024,
+                                               sched_mode=NR_SCHED_PACKED, kv_dtype=NR_KV_BF16))
+    model = restatement.model(tiny_model, 256)
+    model.set_kv_bf16(True)
+    rng = np.random.default_rng(73)
+    prompts = [rng.integers(0, 512, n).astype(np.int32) for n in (300, 200, 150, 40)]
+    for i, p in enumerate(prompts):
+        eng.add_request(i, p)
+    res = eng.step(want_logits=True)
+    assert res.n_prefill == 4
+    for k, (rid, _) in enumerate(res.emitted):
+        want = model.forward_prefill(eng.request_block_table(rid), prompts[rid], 0)
+        assert_close(res.logits[k], want, what=f"packed bf16-page prefill req {rid}")
+    eng.close()
+    model.close()
