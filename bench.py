@@ -324,6 +324,50 @@ def _profile_classes(eng, n):
     return {k: (v[0] / n, v[1] // max(n, 1)) for k, v in kt.items()}
 
 
+def _ref_cpu(model_path, max_tokens, pages):
+    """The reference's ref_fixed build (oracle/_ref) opened on a model, all host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    ref = oracle.Reference("fixed")
+    threads = os.cpu_count() or 1
+    ref.set_threads(threads)
+    ref.open(model_path, max_tokens, pages)
+    return ref, threads
+
+
+def _cpu_baseline_prefill_decode(model_path, prompt_lens, decode_steps, seed, max_tokens, label):
+    """Reference prefill of each prompt (one forward_prefill_chunk each, as the reference
+    does) and then `decode_steps` forward_decode_batch steps over all of them; returns a
+    cpu_baseline dict with the decode tok/s and the prefill tok/s."""
+    pages = sum((n + decode_steps + 15) // 16 + 1 for n in prompt_lens) + 8
+    ref, threads = _ref_cpu(model_path, max_tokens, pages)
+    rng = np.random.default_rng(seed)
+    handles, toks, pos = [], [], []
+    t0 = time.perf_counter()
+    for i, n in enumerate(prompt_lens):
+        prompt = rng.integers(0, 32000, n).astype(np.int32)
+        h = ref.new_request(i, prompt)
+        lg = ref.forward_prefill(h, prompt, 0)
+        handles.append(h)
+        toks.append(ref.argmax(lg))
+        pos.append(n)
+    prefill_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    for _ in range(decode_steps):
+        lg = ref.forward_decode(toks, pos, handles)
+        toks = [ref.argmax(row) for row in lg]
+        pos = [p + 1 for p in pos]
+    decode_s = time.perf_counter() - t0
+    ref.close()
+    B = len(prompt_lens)
+    return {"value": round(B * decode_steps / decode_s, 3) if decode_steps else None, "unit": "tok/s",
+            "prefill_tok_s": round(sum(prompt_lens) / prefill_s, 2), "prefill_s": round(prefill_s, 3),
+            "cores": threads, "kind": "reference", "cpu_model": cpu_model(),
+            "sample": f"{label}: {B} prompt(s) of {sorted(set(prompt_lens))} tokens through forward_prefill_chunk, "
+                      f"then {decode_steps} forward_decode_batch steps at B={B} (ref_fixed build, "
+                      f"{threads} OpenMP threads)"}
+
+
 def run_config1(args):
     """Config 1: one request, 256-token prompt, 128 greedy tokens (B = 1 decode: the Q8_0
     matvec path).  value = device-resident decode step at the end of the run;
@@ -378,7 +422,9 @@ def run_config1(args):
                        "achieved": round(matvec_bytes / (matvec_ms * 1e-3) / 1e9, 1),
                        "frac": round(matvec_bytes / (matvec_ms * 1e-3) / 1e9 / peak, 4),
                        "note": "per-launch CUDA events around every matvec launch (second pass)"},
-            "kernels": kernels, "steps": args.steps}
+            "kernels": kernels, "steps": args.steps,
+            "cpu_baseline": None if args.no_cpu_baseline else _cpu_baseline_prefill_decode(
+                model, [256], 127, 11, 256, "the whole config-1 run")}
 
 
 def _config3_trace_bytes(arrive, prompts, ids, max_new):
@@ -610,7 +656,9 @@ def run_config4(args):
                          "note": "bf16 tensor FLOPs issued: 3 x (linear + causal attention), the hi/lo split"},
             "decode_b32": {"value": round(32 * 16 / decode_s, 1), "unit": "tok/s", "steps": 16},
             "packed_scheduler": packed,
-            "prefill_kernel_ms_per_prompt": {k: round(v[0], 3) for k, v in kt.items()}}
+            "prefill_kernel_ms_per_prompt": {k: round(v[0], 3) for k, v in kt.items()},
+            "cpu_baseline": None if args.no_cpu_baseline else _cpu_baseline_prefill_decode(
+                model, [1024] * 4, 4, 44, 1024, "a bounded sample of config 4 (4 of its 32 prompts, 4 decode steps)")}
 
 
 W7B_BYTES = 7_810_859_008          # Q8 projections + fp32 classifier + RMS gains, 7B shape
@@ -734,7 +782,11 @@ def run_config5_decode(args):
     w_bytes = W7B_BYTES
     kv = sum(p + 1 for p in pos) * KV7B_PER_TOKEN
     peak, peak_src = load_peaks()
-    return {"workload": "config5_decode", "metric": f"decode tok/s, 7B-shaped Q8_0, batch {B} (reduced config 5)",
+    cpu = None if args.no_cpu_baseline else _cpu_baseline_prefill_decode(
+        model, [32, 32], 16, 55, 64, "the reduced config-5 subset (2 requests x 16 tokens; the 512-token prompts "
+                                     "are cut to 32, and per-token cost at B = 64 is extrapolated from B = 2)")
+    return {"workload": "config5_decode", "cpu_baseline": cpu,
+            "metric": f"decode tok/s, 7B-shaped Q8_0, batch {B} (reduced config 5)",
             "value": round(B / (step_ms * 1e-3), 1), "unit": "tok/s", "ms_per_step": round(step_ms, 3),
             "e2e": {"value": round(B * n / dec_s, 1), "unit": "tok/s"},
             "prefill": {"tokens": 512 * B, "ms": round(prefill_ms, 2), "tok_s": round(512 * B / (prefill_ms * 1e-3), 1)},
