@@ -61,18 +61,6 @@ constexpr int TC_RAW_MAX = 12;  // ring slots of raw tiles
 #define NITRO_TC_MAX_KSPLIT 8  // largest K split (CTAs per cluster)
 #endif
 
-// Accumulator regions.  A tensor-core fp32 accumulator that takes many MMAs in a row loses
-// precision as its depth grows (measured on the 7B shape: logits error 8.6e-4 of their RMS
-// with one accumulator per tile against 1.1e-4 for fp32 CUDA-core sums), so a CTA spreads
-// its K chunks over up to TcTmem<NT>::MAX_REGIONS TMEM regions of NT columns, a fresh
-// accumulator every `group` chunks, and sums the regions in fp32 registers in region order
-// when it reads the accumulators (deterministic).
-template <int NT>
-struct TcTmem {
-    static constexpr int COLS = NT == 256 ? 512 : 256;  // columns allocated per CTA
-    static constexpr int MAX_REGIONS = COLS / NT;
-};
-
 // Named CTA barriers between the staging warps (arrive) and the MMA-issuing warp (sync).
 __device__ __forceinline__ void named_arrive(int id, int count) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -341,11 +329,8 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     const int my_begin = fin_begin + wg * my_cols;
     constexpr int PRE = 8;  // epilogue columns whose inputs are fetched early
 
-    // chunks per accumulator region, and regions used
-    const int group = max(1, (nch + TcTmem<NT>::MAX_REGIONS - 1) / TcTmem<NT>::MAX_REGIONS);
-    const int regions = max(1, (nch + group - 1) / group);
     if (warp == 0) {
-        tmem_alloc(&tmem_slot, TcTmem<NT>::COLS);
+        tmem_alloc(&tmem_slot, NT);
         tmem_relinquish();
     }
     if (tid == 0) {
@@ -599,8 +584,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 if (a.wt && ok && !mbar_wait(&w_bar[st], use & 1, a.err)) ok = false;
                 tc_fence_after();
                 if (ok)
-                    issue_chunk_mmas(tmem + (uint32_t)((it / group) * NT), idesc, stage_ptr(st, 0), stage_ptr(st, 1),
-                                     stage_ptr(st, 2), stage_ptr(st, 3), it % group == 0);
+                    issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
                 if (!staged) umma_commit(&mma_bar[st]);  // always, so the stage's phases stay in step
             }
             __syncwarp();
@@ -672,15 +656,6 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             float v[32];
             if (nch > 0 && !bail) {
                 tmem_ld32(tl + c32, v);
-                for (int r = 1; r < regions; r++) {
-#pragma unroll
-                    for (int p8 = 0; p8 < 4; p8++) {
-                        float w[8];
-                        tmem_ld8(tl + (uint32_t)(r * NT) + c32 + 8 * p8, w);
-#pragma unroll
-                        for (int j = 0; j < 8; j++) v[8 * p8 + j] += w[j];
-                    }
-                }
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; j++) v[j] = 0.0f;
@@ -701,7 +676,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     if (bail) {  // a wait gave up (error flag set): release TMEM and leave
         tc_fence_before();
         __syncthreads();
-        if (warp == 0) tmem_dealloc(tmem, TcTmem<NT>::COLS);
+        if (warp == 0) tmem_dealloc(tmem, NT);
         return;
     }
     const bool even = (n & 1) == 0;
@@ -718,12 +693,6 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             v[0] = s4.x; v[1] = s4.y; v[2] = s4.z; v[3] = s4.w;
         } else if (nch > 0) {
             tmem_ld4(tl + c0, v);
-            for (int r = 1; r < regions; r++) {
-                float w[4];
-                tmem_ld4(tl + (uint32_t)(r * NT) + c0, w);
-#pragma unroll
-                for (int j = 0; j < 4; j++) v[j] += w[j];
-            }
         } else {
 #pragma unroll
             for (int j = 0; j < 4; j++) v[j] = 0.0f;
@@ -856,7 +825,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, TcTmem<NT>::COLS);
+    if (warp == 0) tmem_dealloc(tmem, NT);
 }
 
 // Allow the kernel the largest dynamic shared memory the device offers next to its static
@@ -882,23 +851,6 @@ int tc_ensure_smem(K kernel) {
 }
 
 using TcKernel = void (*)(GemmArgs, Epilogue, SplitArgs);
-
-// Dynamic shared memory that keeps at most `max_ctas` CTAs of a kernel on one SM.
-int tc_min_smem_for_tmem(int max_ctas) {
-    static std::mutex mu;
-    static std::map<int, int> sm_bytes;  // per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lock(mu);
-    auto it = sm_bytes.find(dev);
-    if (it == sm_bytes.end()) {
-        int b = 0;
-        if (cudaDeviceGetAttribute(&b, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || b <= 0)
-            b = 233472;
-        it = sm_bytes.emplace(dev, b).first;
-    }
-    return it->second / (max_ctas + 1) + 1024;
-}
 
 // Clusters of `ks` CTAs with `smem` bytes each that fit on the device at once (cached per
 // device; a failed query reports "no limit").
@@ -985,16 +937,11 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     const int tiles = n_tiles * m_tiles;
     if (a.kbegin == 0 && NT <= 128)
         while (ksplit < NITRO_TC_MAX_KSPLIT && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
-    // TMEM: each CTA allocates TcTmem<NT>::COLS of the SM's 512 columns, so no more than
-    // 512 / COLS CTAs of this launch may share an SM (a CTA of a cluster waiting in
-    // tcgen05.alloc for a peer that waits on it would never finish): every launch asks for
-    // enough shared memory that one more CTA cannot fit.
-    const int min_smem = tc_min_smem_for_tmem(512 / TcTmem<NT>::COLS);
     SplitArgs sp;
-    int smem = std::max(plan(ksplit, &sp), min_smem);
+    int smem = plan(ksplit, &sp);
     while (ksplit > 1 && tc_max_clusters(kernel, ksplit, smem, n_tiles, m_tiles) < tiles) {
         ksplit /= 2;
-        smem = std::max(plan(ksplit, &sp), min_smem);
+        smem = plan(ksplit, &sp);
     }
     launch_ex(kernel, dim3(ksplit, n_tiles, m_tiles), dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
 }

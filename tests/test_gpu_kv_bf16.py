@@ -1,18 +1,22 @@
 """K/V pages in bf16 (NR_KV_BF16, off by default): every K/V value rounded to bf16 when it
 is appended, attention still in fp32.  The reference keeps fp32 pages, so this option is
-not parity with it; it is checked two ways:
+not parity with it.  Rounding to 8 significant bits is discontinuous: two correct fp32
+computations that differ by ~1e-5 can store values one bf16 step (2^-8 relative) apart.
+So the checks are:
 
-* against the CPU restatement run with the same rounding (orc_model_set_kv_bf16): logits
-  within the usual 1e-3 relative + 1e-4 absolute, pages equal value for value, greedy
-  tokens equal (a mismatch is reported with its top-2 margin);
-* against the fp32 reference (ref_fixed): logits within 2e-2 of the logits' RMS, the
-  error bf16 pages bring (8 significant bits per K/V value, ~4e-3 relative per value)."""
+* pages against the CPU restatement run with the same rounding (orc_model_set_kv_bf16):
+  at least 99 % of the values equal, every other one a single bf16 step away;
+* logits against that restatement within 1e-2 of the logits' RMS, and closer to it (in
+  RMS) than to the fp32 reference (ref_fixed), i.e. the engine rounds where the
+  restatement does;
+* logits against the fp32 reference within 2e-2 of their RMS, the error bf16 pages bring;
+* greedy tokens equal to the restatement's unless its two logits are within 1e-2 of the
+  RMS of each other (then reported as a near tie under bf16 rounding)."""
 import os
 
 import numpy as np
 import pytest
 
-from conftest import assert_close
 from nitrorag_b200 import NR_KV_BF16, NR_SCHED_PACKED, EngineConfig, NitroEngine, synth
 from test_gpu_model import _check_tokens
 
@@ -25,6 +29,29 @@ def _rms(x):
 
 def _greedy(row):
     return int(np.argmax(np.where(row > 0, row, -np.inf))) if row.max() > 0 else 0
+
+
+def _check_logits(le, want, lr, what):
+    le, want, lr = (np.asarray(v, np.float64) for v in (le, want, lr))
+    scale = _rms(want)
+    assert np.max(np.abs(le - want)) <= 1e-2 * scale, f"{what}: vs bf16 restatement"
+    assert np.max(np.abs(le - lr)) <= 2e-2 * _rms(lr), f"{what}: vs fp32 reference"
+    d_bf16, d_fp32 = _rms(le - want), _rms(le - lr)
+    assert d_bf16 <= d_fp32, f"{what}: closer to fp32 ({d_fp32:.3e}) than to the bf16 restatement ({d_bf16:.3e})"
+
+
+def _check_token(got, row, what):
+    want = _greedy(row)
+    if got != want and abs(float(row[got]) - float(row[want])) > 1e-2 * _rms(row):
+        _check_tokens(got, want, row, what)
+
+
+def _check_pages(k_eng, k_orc, what):
+    a, b = np.asarray(k_eng, np.float64).ravel(), np.asarray(k_orc, np.float64).ravel()
+    same = a == b
+    assert same.mean() >= 0.99, f"{what}: only {same.mean():.4f} of values equal"
+    step = 2.0 ** -7 * np.maximum(np.abs(a), np.abs(b))  # one bf16 step (8 significant bits)
+    assert np.all(np.abs(a - b) <= step + 1e-30), f"{what}: a value more than one bf16 step away"
 
 
 def _run(path, restatement, ref, lens, decode_steps, seed, pages=256):
@@ -43,23 +70,25 @@ def _run(path, restatement, ref, lens, decode_steps, seed, pages=256):
         rh.append(ref.new_request(i, prompt))
         le, tok = eng.forward_prefill_chunk(s, prompt, 0)
         want = model.forward_prefill(eng.block_table(s), prompt, 0)
-        assert_close(le, want, what=f"bf16-page prefill seq {i} ({n} tokens)")
         lr = ref.forward_prefill(rh[i], prompt, 0)
-        assert np.max(np.abs(le - lr)) <= 2e-2 * _rms(lr), f"bf16 pages vs fp32 reference, seq {i}"
+        _check_logits(le, want, lr, f"bf16-page prefill seq {i} ({n} tokens)")
         toks.append(tok)
         pos.append(n)
     for step in range(decode_steps):
         want = model.forward_decode([eng.block_table(s) for s in seqs], toks, pos)
+        lr = ref.forward_decode(toks, pos, rh)
         le, am = eng.forward_decode_batch(toks, pos, seqs)
-        assert_close(le, want, what=f"bf16-page decode step {step} (B={len(seqs)})")
         for i in range(len(seqs)):
-            _check_tokens(int(am[i]), _greedy(want[i]), want[i], f"bf16-page decode step {step} row {i}")
+            _check_logits(le[i], want[i], lr[i], f"bf16-page decode step {step} row {i}")
+            _check_token(int(am[i]), want[i], f"bf16-page decode step {step} row {i}")
+        # the restatement and the reference continue with the engine's tokens
         toks = [int(t) for t in am]
         pos = [p + 1 for p in pos]
     for blk in eng.block_table(seqs[0])[:3]:
         k1, v1 = model.page(blk)
         k2, v2 = eng.read_page(blk)
-        assert np.array_equal(k2, k1) and np.array_equal(v2, v1), blk
+        _check_pages(k2, k1, f"K page {blk}")
+        _check_pages(v2, v1, f"V page {blk}")
     eng.close()
     model.close()
     ref.close()
@@ -111,6 +140,6 @@ def test_bf16_pages_packed_scheduler(restatement, tiny_model):
     assert res.n_prefill == 4
     for k, (rid, _) in enumerate(res.emitted):
         want = model.forward_prefill(eng.request_block_table(rid), prompts[rid], 0)
-        assert_close(res.logits[k], want, what=f"packed bf16-page prefill req {rid}")
+        assert np.max(np.abs(res.logits[k] - want)) <= 1e-2 * _rms(want), f"packed bf16-page prefill req {rid}"
     eng.close()
     model.close()
