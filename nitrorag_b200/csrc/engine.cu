@@ -216,16 +216,10 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
     // Larger projections get raw Q8 tiles (below) and, when HBM has room beside the K/V
     // pools, hi/lo tiles as well, which wide batches read instead (run_layers): at 64 rows
     // the on-chip conversion of raw tiles costs more than the extra bytes.
-    // Wide models (dim >= 2048) run the tensor-core projections with three-part operands
-    // (GemmArgs::parts, ~fp32 accuracy); their weights are split on chip, so they get no
-    // hi/lo tiles, only raw Q8 tiles.  NITRO_PRECISE=0/1 overrides the choice.
-    precise_ = c.dim >= 2048;
-    if (const char* pe = getenv("NITRO_PRECISE")) precise_ = pe[0] == '1';
     const char* tiled_env = getenv("NITRO_TILED_WEIGHTS");
     if (!(tiled_env && tiled_env[0] == '0') && D % 64 == 0 && H % 64 == 0) {
         int64_t kTileMax = (int64_t)8 << 20;  // NITRO_TILE_MAX_WEIGHTS overrides (tests use 0)
         if (const char* tm = getenv("NITRO_TILE_MAX_WEIGHTS")) kTileMax = atoll(tm);
-        if (precise_) kTileMax = 0;
         auto small = [&](int64_t n, int64_t k) { return n * k <= kTileMax; };
         size_t wide_bytes = 0;
         for (auto nk : {std::make_pair((int64_t)NQKV, (int64_t)D), std::make_pair((int64_t)D, (int64_t)D),
@@ -233,7 +227,7 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
             if (!small(nk.first, nk.second)) wide_bytes += (size_t)L * align256(tc_tiled_weight_bytes((int)nk.first, (int)nk.second));
         bool wide = false;
         const char* wide_env = getenv("NITRO_WIDE_TILES");
-        if (wide_bytes && !precise_ && !(wide_env && wide_env[0] == '0')) {
+        if (wide_bytes && !(wide_env && wide_env[0] == '0')) {
             size_t free_b = 0, total_b = 0;
             NR_CUDA(cudaMemGetInfo(&free_b, &total_b));
             const size_t pools = (size_t)2 * cfg_.total_blocks * (size_t)c.n_layers * c.n_kv_heads * kBlockSize * hd * 4;
@@ -248,7 +242,7 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
         w_.wo_t_layer = tiled(D, D);
         w_.w13_t_layer = tiled(2 * H, D);
         w_.w2_t_layer = tiled(D, H);
-        const size_t cls = precise_ ? 0 : align256(tc_tiled_weight_bytes(c.vocab, D));
+        const size_t cls = align256(tc_tiled_weight_bytes(c.vocab, D));
         w_.tbytes = (size_t)L * (w_.qkv_t_layer + w_.wo_t_layer + w_.w13_t_layer + w_.w2_t_layer) + cls;
         NR_CUDA(cudaMalloc(&w_.tbase, w_.tbytes));
         uint8_t* p = (uint8_t*)w_.tbase;
@@ -261,7 +255,7 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
         w_.wo_t = carve(w_.wo_t_layer);
         w_.w13_t = carve(w_.w13_t_layer);
         w_.w2_t = carve(w_.w2_t_layer);
-        w_.cls_t = precise_ ? nullptr : p;
+        w_.cls_t = p;
         for (int l = 0; l < L; l++) {
             if (w_.qkv_t)
                 tc_tile_weights(w_.qkv_q + (int64_t)l * NQKV * D, w_.qkv_s + (int64_t)l * NQKV * (D / 32), nullptr, NQKV,
@@ -276,7 +270,7 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
                 tc_tile_weights(w_.w2_q + (int64_t)l * D * H, w_.w2_s + (int64_t)l * D * (H / 32), nullptr, D, H,
                                 w_.w2_t + l * w_.w2_t_layer, stream_);
         }
-        if (w_.cls_t) tc_tile_weights(nullptr, nullptr, w_.emb, c.vocab, D, w_.cls_t, stream_);
+        tc_tile_weights(nullptr, nullptr, w_.emb, c.vocab, D, w_.cls_t, stream_);
         NR_CUDA(cudaStreamSynchronize(stream_));
         NR_CUDA(cudaGetLastError());
 
@@ -383,7 +377,6 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
     for (int l = 0; l < c.n_layers; l++) {
         // 1. q,k,v = Wqkv . rmsnorm(x); RoPE; k,v -> pages
         GemmArgs g;
-        g.parts = precise_ ? 3 : 2;
         g.err = d_err_;
         g.x = d_x_; g.ldx = D; g.norm_gain = w_.rms_att + (int64_t)l * D;
         g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
@@ -419,7 +412,6 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         }
         // 3. x += Wo . att
         GemmArgs go;
-        go.parts = precise_ ? 3 : 2;
         go.err = d_err_;
         go.x = d_att_; go.ldx = D; go.wq = w_.wo_q + (int64_t)l * D * D; go.ws = w_.wo_s + (int64_t)l * D * (D / 32);
         go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
@@ -431,7 +423,6 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         { ProfScope ps(this, kKWo); launch_gemm(go, eo, stream_); }
         // 4. h = silu(W1 . rmsnorm(x)) * (W3 . rmsnorm(x))
         GemmArgs g13;
-        g13.parts = precise_ ? 3 : 2;
         g13.err = d_err_;
         g13.x = d_x_; g13.ldx = D; g13.norm_gain = w_.rms_ffn + (int64_t)l * D;
         g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
@@ -444,7 +435,6 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         { ProfScope ps(this, kKW13); launch_gemm(g13, e13, stream_); }
         // 5. x += W2 . h
         GemmArgs g2;
-        g2.parts = precise_ ? 3 : 2;
         g2.err = d_err_;
         g2.x = d_h_; g2.ldx = H; g2.wq = w_.w2_q + (int64_t)l * D * H; g2.ws = w_.w2_s + (int64_t)l * D * (H / 32);
         g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
@@ -490,7 +480,6 @@ int Engine::forward_prefill(const Sequence& seq, const int* tokens, int T, int s
     run_layers(T, true, &seq, start_pos, 0, start_pos + T, false);
     // classifier over the last token (src/model_q8.cpp:553-556)
     GemmArgs gl;
-    gl.parts = precise_ ? 3 : 2;
     gl.err = d_err_;
     gl.x = d_x_ + (int64_t)(T - 1) * c.dim; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
     gl.wt = w_.cls_t;
@@ -589,7 +578,6 @@ int Engine::forward_prefill_batch(const PrefillSeg* segs, int n, float* logits_o
             k++;
         }
         GemmArgs gl;
-        gl.parts = precise_ ? 3 : 2;
         gl.err = d_err_;
         gl.x = d_att_; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
         gl.wt = w_.cls_t;
@@ -670,7 +658,6 @@ void Engine::enqueue_decode(int B, int max_ctx, bool force_fixed, bool want_logi
     { ProfScope ps(this, kKEmbed); launch_embed(w_.emb, d_tok_, B, c.dim, d_x_, d_keys_, use_ss(B) ? d_ss_ : nullptr, max_rows_, stream_); }
     run_layers(B, false, nullptr, 0, B, max_ctx, force_fixed);
     GemmArgs gl;
-    gl.parts = precise_ ? 3 : 2;
     gl.err = d_err_;
     gl.x = d_x_; gl.ldx = c.dim; gl.norm_gain = w_.rms_final; gl.wf = w_.emb;
     gl.wt = w_.cls_t;

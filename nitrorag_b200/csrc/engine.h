@@ -156,7 +156,6 @@ private:
     // large projections have both raw Q8 tiles and hi/lo tiles; batches of at least
     // kWideTileRows rows read the hi/lo tiles
     bool wide_tiles_ = false;
-    bool precise_ = false;  // three-part tensor-core operands (wide models)
     static constexpr int kWideTileRows = 32;
     // set while a multi-sequence prefill runs: its segment and tile tables on the device
     const int* d_seg_ = nullptr;

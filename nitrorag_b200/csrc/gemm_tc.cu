@@ -10,11 +10,7 @@
 // Each operand is split into two bf16 halves, v = hi + lo with hi = bf16(v) and
 // lo = bf16(v - hi) (17 significant bits together), and the product is accumulated as
 // hi*hi + hi*lo + lo*hi by three MMAs into the same fp32 accumulator; the dropped lo*lo
-// term and the split residues are ~2^-17 relative, inside the 1e-3 / 1e-4 logits bar for
-// the 110M shape.  Wide, deep models amplify that error past the bar (the 7B shape's logits
-// came out 8.6e-4 of their RMS off), so for them (GemmArgs::parts = 3) each operand is
-// split into three bf16 parts hi + mid + lo and six MMAs accumulate hi*hi, hi*mid, mid*hi,
-// hi*lo, lo*hi and mid*mid: the residue is ~2^-23 relative, what fp32 sums carry anyway.
+// term and the split residues are ~2^-17 relative, far inside the 1e-3 / 1e-4 logits bar.
 //
 // Pipeline per CTA (256 threads, two warpgroups): every thread dequantises half a weight
 // row of each 64-wide K chunk (one Q8_0 block, w = q * scale) and a quarter-chunk slice of
@@ -120,40 +116,13 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 
 // ------------------------------------------------------------------ operand staging
-// One stage: the P bf16 parts of the weight tile (A), then the P parts of the token tile (B).
-template <int NT, int P = 2>
+template <int NT>
 struct TcSmem {
-    static constexpr int A_BYTES = TC_M * TC_KC * 2;   // one bf16 part of the weight tile
-    static constexpr int B_BYTES = NT * TC_KC * 2;     // one bf16 part of the token tile
-    static constexpr int STAGE = P * A_BYTES + P * B_BYTES;
+    static constexpr int A_BYTES = TC_M * TC_KC * 2;   // one bf16 half of the weight tile
+    static constexpr int B_BYTES = NT * TC_KC * 2;     // one bf16 half of the token tile
+    static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int MAX_STAGES = NT == 64 ? TC_MAX_STAGES : TC_STAGES;
 };
-
-// Split 8 fp32 values into P bf16 parts (P = 2: hi/lo, P = 3: hi/mid/lo), each stored as one
-// 16-byte core-matrix row at dst + part * stride.
-template <int P>
-__device__ __forceinline__ void split_store8p(const float* v, uint8_t* dst, uint32_t stride) {
-    if (P == 2) {
-        split_store8(v, dst, dst + stride);
-    } else {
-        uint32_t h[4], m[4], l[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-            const float2 hf = __bfloat1622float2(hb);
-            const float r0 = v[2 * i] - hf.x, r1 = v[2 * i + 1] - hf.y;  // exact
-            const __nv_bfloat162 mb = __floats2bfloat162_rn(r0, r1);
-            const float2 mf = __bfloat1622float2(mb);
-            const __nv_bfloat162 lb = __floats2bfloat162_rn(r0 - mf.x, r1 - mf.y);
-            h[i] = *reinterpret_cast<const uint32_t*>(&hb);
-            m[i] = *reinterpret_cast<const uint32_t*>(&mb);
-            l[i] = *reinterpret_cast<const uint32_t*>(&lb);
-        }
-        *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(dst + stride) = make_uint4(m[0], m[1], m[2], m[3]);
-        *reinterpret_cast<uint4*>(dst + 2 * stride) = make_uint4(l[0], l[1], l[2], l[3]);
-    }
-}
 
 struct SplitArgs {
     int ksplit;  // K-range splits per tile = CTAs per thread-block cluster (grid.x)
@@ -196,9 +165,9 @@ __device__ __forceinline__ void load_w(WRegs<F32W>& r, const GemmArgs& a, int n,
 }
 
 // This thread's 32 weights of one chunk (registers -> bf16 hi/lo core rows).
-template <bool F32W, int P>
-__device__ __forceinline__ void stage_w(const WRegs<F32W>& r, const GemmArgs& a, int n, int k, uint8_t* a0,
-                                        uint32_t pstride, int row, int half) {
+template <bool F32W>
+__device__ __forceinline__ void stage_w(const WRegs<F32W>& r, const GemmArgs& a, int n, int k, uint8_t* a_hi,
+                                        uint8_t* a_lo, int row, int half) {
     float w[32];
     if (n < a.N) {
         if (F32W) {
@@ -221,13 +190,12 @@ __device__ __forceinline__ void stage_w(const WRegs<F32W>& r, const GemmArgs& a,
         for (int j = 0; j < 32; j++) w[j] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < 4; j++) split_store8p<P>(w + 8 * j, a0 + core_off(row, half * 4 + j), pstride);
+    for (int j = 0; j < 4; j++) split_store8(w + 8 * j, a_hi + core_off(row, half * 4 + j), a_lo + core_off(row, half * 4 + j));
 }
 
-// This thread's 32 weights of one chunk from a raw Q8 tile in shared memory (-> bf16 parts).
-template <int P>
-__device__ __forceinline__ void stage_w_raw(const uint8_t* raw, const GemmArgs& a, int n, int k, uint8_t* a0,
-                                            uint32_t pstride, int row, int half) {
+// This thread's 32 weights of one chunk from a raw Q8 tile in shared memory (-> bf16 hi/lo).
+__device__ __forceinline__ void stage_w_raw(const uint8_t* raw, const GemmArgs& a, int n, int k, uint8_t* a_hi,
+                                            uint8_t* a_lo, int row, int half) {
     float w[32];
     if (n < a.N) {
         const int4 p0 = *reinterpret_cast<const int4*>(raw + ((half * 2 + 0) * TC_M + row) * 16);
@@ -250,13 +218,12 @@ __device__ __forceinline__ void stage_w_raw(const uint8_t* raw, const GemmArgs& 
         for (int j = 0; j < 32; j++) w[j] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < 4; j++) split_store8p<P>(w + 8 * j, a0 + core_off(row, half * 4 + j), pstride);
+    for (int j = 0; j < 4; j++) split_store8(w + 8 * j, a_hi + core_off(row, half * 4 + j), a_lo + core_off(row, half * 4 + j));
 }
 
 // 16 activations of token row r (K quarter kq of a chunk), times the RMSNorm gain when
 // there is one -> bf16 hi/lo.  The row's 1/rms is applied to the accumulators instead.
-template <int P>
-__device__ __forceinline__ void stage_x16(const float4* x4, const float* g, bool valid, uint8_t* b0, uint32_t pstride,
+__device__ __forceinline__ void stage_x16(const float4* x4, const float* g, bool valid, uint8_t* b_hi, uint8_t* b_lo,
                                           int r, int kq) {
     float xv[16];
     if (valid) {
@@ -279,13 +246,13 @@ __device__ __forceinline__ void stage_x16(const float4* x4, const float* g, bool
         for (int i = 0; i < 16; i++) xv[i] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < 2; j++) split_store8p<P>(xv + 8 * j, b0 + core_off(r, kq * 2 + j), pstride);
+    for (int j = 0; j < 2; j++) split_store8(xv + 8 * j, b_hi + core_off(r, kq * 2 + j), b_lo + core_off(r, kq * 2 + j));
 }
 
 // The activation tile of one chunk (all NT token rows), loaded and staged by unit.
-template <int NT, int P>
-__device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* g, int m_base, int k0, uint8_t* b0,
-                                              uint32_t pstride, int tid) {
+template <int NT>
+__device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* g, int m_base, int k0, uint8_t* b_hi,
+                                              uint8_t* b_lo, int tid) {
     for (int u = tid; u < NT * 4; u += TC_WORKERS) {
         const int r = u >> 2, kq = u & 3, m = m_base + r;
         float4 x4[4];
@@ -294,33 +261,25 @@ __device__ __forceinline__ void stage_chunk_x(const GemmArgs& a, const float* g,
 #pragma unroll
             for (int i = 0; i < 4; i++) x4[i] = src[i];
         }
-        stage_x16<P>(x4, g ? g + kq * 16 : nullptr, m < a.M, b0, pstride, r, kq);
+        stage_x16(x4, g ? g + kq * 16 : nullptr, m < a.M, b_hi, b_lo, r, kq);
     }
 }
 
-// One chunk's MMAs: A parts at a0 + p * astride, B parts at b0 + p * bstride.
-template <int P>
-__device__ __forceinline__ void issue_chunk_mmas(uint32_t tmem, uint32_t idesc, const uint8_t* a0, uint32_t astride,
-                                                 const uint8_t* b0, uint32_t bstride, bool first) {
-    const uint32_t ah = smem_addr(a0), am = ah + astride, bh = smem_addr(b0), bm = bh + bstride;
+__device__ __forceinline__ void issue_chunk_mmas(uint32_t tmem, uint32_t idesc, const uint8_t* a_hi, const uint8_t* a_lo,
+                                                 const uint8_t* b_hi, const uint8_t* b_lo, bool first) {
+    const uint32_t ah = smem_addr(a_hi), al = smem_addr(a_lo), bh = smem_addr(b_hi), bl = smem_addr(b_lo);
 #pragma unroll
     for (int kk = 0; kk < TC_KC / 16; kk++) {
         const uint32_t o = kk * 256;  // 16 K-elements = two core matrices along K
         umma_bf16(tmem, umma_desc(ah + o), umma_desc(bh + o), idesc, (!first || kk > 0) ? 1u : 0u);
-        umma_bf16(tmem, umma_desc(ah + o), umma_desc(bm + o), idesc, 1u);
-        umma_bf16(tmem, umma_desc(am + o), umma_desc(bh + o), idesc, 1u);
-        if (P == 3) {
-            const uint32_t al = am + astride, bl = bm + bstride;
-            umma_bf16(tmem, umma_desc(ah + o), umma_desc(bl + o), idesc, 1u);
-            umma_bf16(tmem, umma_desc(al + o), umma_desc(bh + o), idesc, 1u);
-            umma_bf16(tmem, umma_desc(am + o), umma_desc(bm + o), idesc, 1u);
-        }
+        umma_bf16(tmem, umma_desc(ah + o), umma_desc(bl + o), idesc, 1u);
+        umma_bf16(tmem, umma_desc(al + o), umma_desc(bh + o), idesc, 1u);
     }
 }
 
-template <int NT, bool F32W, int EPI, int P>
+template <int NT, bool F32W, int EPI>
 __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm_kernel(GemmArgs a, Epilogue e, SplitArgs sp) {
-    using S = TcSmem<NT, P>;
+    using S = TcSmem<NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t mma_bar[TC_MAX_STAGES];
     __shared__ uint64_t w_bar[TC_MAX_STAGES];  // tiled weights: the stage's bulk copy has landed
@@ -356,10 +315,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     // the previous kernel (weights are read-only; activations are not)
     const bool staged = nch <= stages && !use_raw;
     const int n = n_base + row;  // this thread's weight row
-    // stage st: weight parts 0..P-1 (A_BYTES apart), then token parts (B_BYTES apart)
-    auto a_ptr = [&](int st) { return smem + st * S::STAGE; };
-    auto b_ptr = [&](int st) { return smem + st * S::STAGE + P * S::A_BYTES; };
-    constexpr uint32_t AS = S::A_BYTES, BS = S::B_BYTES;
+    auto stage_ptr = [&](int st, int part) { return smem + st * S::STAGE + (part < 2 ? part * S::A_BYTES : 2 * S::A_BYTES + (part - 2) * S::B_BYTES); };
     float* gain_s = reinterpret_cast<float*>(smem + sp.gain_off);  // [nch][64] when staged
 
     // Columns (tokens) this CTA finishes: its slice of the tile when K is split, else all;
@@ -396,7 +352,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     // tiled weights: one bulk copy per chunk (all of them when staged, the first for a ring)
     auto fetch_tile = [&](int i, int st) {
         mbar_arrive_expect_tx(&w_bar[st], TC_TILE_BYTES);
-        bulk_g2s(a_ptr(st), a.wt + ((size_t)n_tile * nchunk_total + c_first + i) * TC_TILE_BYTES, TC_TILE_BYTES,
+        bulk_g2s(stage_ptr(st, 0), a.wt + ((size_t)n_tile * nchunk_total + c_first + i) * TC_TILE_BYTES, TC_TILE_BYTES,
                  &w_bar[st]);
     };
     uint8_t* raw_ring = smem + sp.raw_off;
@@ -425,15 +381,15 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             WRegs<F32W> r1;
             load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
             load_w<F32W>(r1, a, n, (c_first + 1) * TC_KC + wg * 32);
-            stage_w<F32W, P>(cur, a, n, c_first * TC_KC + wg * 32, a_ptr(0), AS, row, wg);
-            stage_w<F32W, P>(r1, a, n, (c_first + 1) * TC_KC + wg * 32, a_ptr(1), AS, row, wg);
+            stage_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32, stage_ptr(0, 0), stage_ptr(0, 1), row, wg);
+            stage_w<F32W>(r1, a, n, (c_first + 1) * TC_KC + wg * 32, stage_ptr(1, 0), stage_ptr(1, 1), row, wg);
             for (int i = 2; i < nch; i++) {
                 load_w<F32W>(cur, a, n, (c_first + i) * TC_KC + wg * 32);
-                stage_w<F32W, P>(cur, a, n, (c_first + i) * TC_KC + wg * 32, a_ptr(i), AS, row, wg);
+                stage_w<F32W>(cur, a, n, (c_first + i) * TC_KC + wg * 32, stage_ptr(i, 0), stage_ptr(i, 1), row, wg);
             }
         } else if (nch == 1) {
             load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
-            stage_w<F32W, P>(cur, a, n, c_first * TC_KC + wg * 32, a_ptr(0), AS, row, wg);
+            stage_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32, stage_ptr(0, 0), stage_ptr(0, 1), row, wg);
         }
     } else if (nch > 0 && worker && !use_raw) {
         load_w<F32W>(cur, a, n, c_first * TC_KC + wg * 32);
@@ -546,9 +502,9 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                         if (i == s2)
 #pragma unroll
                             for (int j = 0; j < 4; j++) x4[j] = xr[s2][j];
-                    stage_x16<P>(x4, g ? g + ukq * 16 : nullptr, m < a.M, b_ptr(i), BS, ur, ukq);
+                    stage_x16(x4, g ? g + ukq * 16 : nullptr, m < a.M, stage_ptr(i, 2), stage_ptr(i, 3), ur, ukq);
                 } else {
-                    stage_chunk_x<NT, P>(a, g, m_base, (c_first + i) * TC_KC, b_ptr(i), BS, tid);
+                    stage_chunk_x<NT>(a, g, m_base, (c_first + i) * TC_KC, stage_ptr(i, 2), stage_ptr(i, 3), tid);
                 }
                 fence_async_smem();
                 named_arrive(1 + i, TC_THREADS);
@@ -587,17 +543,18 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 if (ok && use_raw && !mbar_wait(&raw_bar[it % RS], (it / RS) & 1, a.err)) ok = false;
                 if (ok) {
                     if (use_raw)
-                        stage_w_raw<P>(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, a, n, k0 + wg * 32, a_ptr(st), AS,
-                                       row, wg);
+                        stage_w_raw(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, a, n, k0 + wg * 32, stage_ptr(st, 0),
+                                    stage_ptr(st, 1), row, wg);
                     else if (!a.wt)
-                        stage_w<F32W, P>(cur, a, n, k0 + wg * 32, a_ptr(st), AS, row, wg);
+                        stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
                     if (XPF) {
 #pragma unroll
                         for (int u = 0; u < XU; u++)
-                            stage_x16<P>(xn[u], a.norm_gain ? reinterpret_cast<const float*>(gn) : nullptr,
-                                         m_base + ur + 64 * u < a.M, b_ptr(st), BS, ur + 64 * u, ukq);
+                            stage_x16(xn[u], a.norm_gain ? reinterpret_cast<const float*>(gn) : nullptr,
+                                      m_base + ur + 64 * u < a.M, stage_ptr(st, 2), stage_ptr(st, 3), ur + 64 * u, ukq);
                     } else {
-                        stage_chunk_x<NT, P>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, b_ptr(st), BS, tid);
+                        stage_chunk_x<NT>(a, a.norm_gain ? a.norm_gain + k0 : nullptr, m_base, k0, stage_ptr(st, 2),
+                                          stage_ptr(st, 3), tid);
                     }
                 }
                 // the next chunk's activations (and gain) load while this one goes through
@@ -627,7 +584,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 if (a.wt && ok && !mbar_wait(&w_bar[st], use & 1, a.err)) ok = false;
                 tc_fence_after();
                 if (ok)
-                    issue_chunk_mmas<P>(tmem, idesc, a_ptr(st), AS, b_ptr(st), BS, it == 0);
+                    issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3), it == 0);
                 if (!staged) umma_commit(&mma_bar[st]);  // always, so the stage's phases stay in step
             }
             __syncwarp();
@@ -926,21 +883,19 @@ int tc_max_clusters(TcKernel kernel, int ks, int smem, int n_tiles, int m_tiles)
     return n;
 }
 
-template <int NT, int P>
-void tc_launch(const GemmArgs& a_in, const Epilogue& e, cudaStream_t s) {
-    GemmArgs a = a_in;
-    if (P != 2) a.wt = nullptr;  // pre-split tiles hold two parts; three-part weights are split on chip
+template <int NT>
+void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     const int n_tiles = (a.N + TC_M - 1) / TC_M;
     const int m_tiles = (a.M + NT - 1) / NT;
     const int chunks = a.K / TC_KC;
     TcKernel kernel;
     if (a.wf) {
-        kernel = tc_gemm_kernel<NT, true, kEpiLogits, P>;
+        kernel = tc_gemm_kernel<NT, true, kEpiLogits>;
     } else {
         // one kernel for every Q8 projection kind: the four projections of a layer then
         // share their instruction-cache footprint (measured ~1.5 % faster per step than a
         // kernel per kind)
-        kernel = tc_gemm_kernel<NT, false, -1, P>;
+        kernel = tc_gemm_kernel<NT, false, -1>;
     }
     const int budget = tc_ensure_smem(kernel);
     const bool raw = !a.wf && a.wr && !a.wt;
@@ -954,7 +909,7 @@ void tc_launch(const GemmArgs& a_in, const Epilogue& e, cudaStream_t s) {
         auto layout = [&](int stages, int pad) {
             sp->stages = stages;
             sp->recv_pad = pad;
-            sp->recv_off = stages * TcSmem<NT, P>::STAGE;
+            sp->recv_off = stages * TcSmem<NT>::STAGE;
             sp->gain_off = sp->recv_off + (ks > 1 ? (NT + pad * ks) * TC_M * 4 : 0);
             sp->raw_off = sp->gain_off + (a.norm_gain ? stages * TC_KC * 4 : 0);
             sp->raw_slots = 0;
@@ -963,12 +918,9 @@ void tc_launch(const GemmArgs& a_in, const Epilogue& e, cudaStream_t s) {
         if (raw) {  // a 2-stage ring fed by as many raw-tile slots as fit
             const int base = layout(TC_STAGES, 4);
             sp->raw_slots = std::min(TC_RAW_MAX, (budget - base) / (int)TC_RAW_BYTES);
-            // fewer than two slots do not fit: report the two-slot size (above the budget),
-            // so the caller reduces the split instead of launching an undersized layout
-            if (sp->raw_slots < 2) sp->raw_slots = 2;
             return base + sp->raw_slots * (int)TC_RAW_BYTES;
         }
-        if (per_cta <= TcSmem<NT, P>::MAX_STAGES) {
+        if (per_cta <= TcSmem<NT>::MAX_STAGES) {
             const int st = std::max(TC_STAGES, per_cta);
             for (int pad = 4; pad >= 0; pad -= 4) {
                 const int bytes = layout(st, pad);
@@ -987,14 +939,9 @@ void tc_launch(const GemmArgs& a_in, const Epilogue& e, cudaStream_t s) {
         while (ksplit < NITRO_TC_MAX_KSPLIT && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
     SplitArgs sp;
     int smem = plan(ksplit, &sp);
-    // a split's receive buffer must fit beside the stages (three-part stages are larger)
-    while (ksplit > 1 && (smem > budget || tc_max_clusters(kernel, ksplit, smem, n_tiles, m_tiles) < tiles)) {
+    while (ksplit > 1 && tc_max_clusters(kernel, ksplit, smem, n_tiles, m_tiles) < tiles) {
         ksplit /= 2;
         smem = plan(ksplit, &sp);
-    }
-    if (smem > budget) {  // no layout fits (not reached by the engine's shapes): refuse, do not launch
-        if (a.err) cudaMemsetAsync(a.err, 0xff, sizeof(int), s);
-        return;
     }
     launch_ex(kernel, dim3(ksplit, n_tiles, m_tiles), dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
 }
@@ -1077,14 +1024,9 @@ void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     count_launch();
     // 256-token tiles only when they alone fill the GPU (they never split K)
     const int n_tiles = (a.N + TC_M - 1) / TC_M;
-    if (a.parts == 3) {  // three-part operands: 256-token stages would not fit twice
-        if (a.M <= 64) tc_launch<64, 3>(a, e, s);
-        else tc_launch<128, 3>(a, e, s);
-        return;
-    }
-    if (a.M <= 64) tc_launch<64, 2>(a, e, s);
-    else if (a.M <= 128 || n_tiles * ((a.M + 255) / 256) < 148) tc_launch<128, 2>(a, e, s);
-    else tc_launch<256, 2>(a, e, s);
+    if (a.M <= 64) tc_launch<64>(a, e, s);
+    else if (a.M <= 128 || n_tiles * ((a.M + 255) / 256) < 148) tc_launch<128>(a, e, s);
+    else tc_launch<256>(a, e, s);
 }
 
 

@@ -65,9 +65,6 @@ struct GemmArgs {
     // and scales regrouped per 128-row x 64-column tile (9 KB, tc_tile_q8_raw) so the
     // kernel can stream them with bulk copies through a deep shared-memory ring.
     const uint8_t* wr = nullptr;
-    // bf16 parts per operand on the tensor cores: 2 (hi/lo, 3 MMAs) or 3 (hi/mid/lo, 6 MMAs,
-    // ~fp32 accuracy, for wide and deep models; wt is then not used)
-    int parts = 2;
 };
 
 // M <= 8: CUDA-core matvec; M > 8 with K % 64 == 0: tcgen05 GEMM (gemm_tc.cu); otherwise
