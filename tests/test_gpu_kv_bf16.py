@@ -5,9 +5,9 @@ computations that differ by ~1e-5 can store values one bf16 step (2^-8 relative)
 So the checks are:
 
 * pages: every stored value exactly a bf16 number (the rounding happened), and within
-  one bf16 step of the CPU restatement run with the same rounding
-  (orc_model_set_kv_bf16) - deeper layers differ by ~1e-4 relative before rounding, so a
-  share of the values round the other way;
+  one bf16 step (plus 1e-3 of the page's RMS, for values near zero) of the CPU restatement
+  run with the same rounding (orc_model_set_kv_bf16) - deeper layers differ by ~1e-4
+  relative before rounding, so a share of the values round the other way;
 * logits against that restatement within 1e-2 of the logits' RMS, and closer to it (in
   RMS) than to the fp32 reference (ref_fixed), i.e. the engine rounds where the
   restatement does;
@@ -53,8 +53,10 @@ def _check_pages(k_eng, k_orc, what):
     assert np.all((bits & 0xFFFF) == 0), f"{what}: a stored value is not a bf16 number"
     a, b = np.asarray(k_eng, np.float64).ravel(), np.asarray(k_orc, np.float64).ravel()
     assert (a == b).mean() >= 0.5, f"{what}: only {(a == b).mean():.4f} of values equal"
-    step = 2.0 ** -7 * np.maximum(np.abs(a), np.abs(b))  # one bf16 step (8 significant bits)
-    assert np.all(np.abs(a - b) <= step + 1e-30), f"{what}: a value more than one bf16 step away"
+    # one bf16 step (8 significant bits) of the value, plus 1e-3 of the page's RMS for values
+    # near zero, whose pre-rounding difference (an absolute ~1e-5 of the RMS) spans steps
+    step = 2.0 ** -7 * np.maximum(np.abs(a), np.abs(b)) + 1e-3 * float(np.sqrt(np.mean(b ** 2)))
+    assert np.all(np.abs(a - b) <= step), f"{what}: a value more than one bf16 step away"
 
 
 def _run(path, restatement, ref, lens, decode_steps, seed, pages=256):
