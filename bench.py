@@ -877,6 +877,7 @@ def engine_arm(args, rank, world, local_rank, comm):
     eng.set_profiling(False)
     attn_ms_total, attn_n = kt["attention"]
     attn_ms = attn_ms_total / max(attn_n, 1)
+    merge_ms = kt["attn_merge"][0] / max(kt["attn_merge"][1], 1)
     peak, peak_src = load_peaks()
     algo = attn_bytes(ctx)
     achieved = algo / (attn_ms * 1e-3) / 1e9
@@ -914,6 +915,7 @@ def engine_arm(args, rank, world, local_rank, comm):
             "roofline": {"bound": "hbm", "kernel": "decode_attn_kernel<64>", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": algo, "launch_ms": round(attn_ms, 5),
+                         "merge_kernel_ms": round(merge_ms, 5),
                          "traffic": (round(ratio * algo) if ratio else None)},
             "kernel_ms_per_step": kernel_share, "profiled_step_ms": round(step_ms_prof, 4),
             "cpu_baseline": cpu, "clocks": dict(clocks, window=f"{soak} untimed replays of the same step (~1.5 s) "

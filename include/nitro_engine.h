@@ -223,9 +223,10 @@ int32_t nr_argmax(const float* x, int32_t n);
 
 /* Per-kernel-class profiling: when enabled, every launch is bracketed by CUDA events on the
  * engine stream and the elapsed times are accumulated per class.  Classes, in order:
- * 0 embed, 1 qkv, 2 attention, 3 wo, 4 w13, 5 w2, 6 logits, 7 argmax.  Enabling resets
- * the accumulators; nr_engine_kernel_times synchronises and reports ms and launch counts. */
-#define NR_KERNEL_CLASSES 8
+ * 0 embed, 1 qkv, 2 attention, 3 wo, 4 w13, 5 w2, 6 logits, 7 argmax, 8 the merge of
+ * split decode attention.  Enabling resets the accumulators; nr_engine_kernel_times
+ * synchronises and reports ms and launch counts. */
+#define NR_KERNEL_CLASSES 9
 int nr_engine_set_profiling(nr_engine* e, int32_t enable);
 int nr_engine_kernel_times(nr_engine* e, double ms[NR_KERNEL_CLASSES], int64_t launches[NR_KERNEL_CLASSES]);
 

@@ -15,7 +15,7 @@ NR_ERR = {
     -5: "NR_ERR_NO_BLOCKS", -6: "NR_ERR_NO_DEVICE", -7: "NR_ERR_UNKNOWN_SEQ",
     -8: "NR_ERR_CAPACITY", -9: "NR_ERR_TIMEOUT",
 }
-KERNEL_CLASSES = ["embed", "qkv", "attention", "wo", "w13", "w2", "logits", "argmax"]
+KERNEL_CLASSES = ["embed", "qkv", "attention", "wo", "w13", "w2", "logits", "argmax", "attn_merge"]
 NR_Q8_FIXED = 0
 NR_Q8_FAITHFUL = 1
 NR_SCHED_REFERENCE = 0

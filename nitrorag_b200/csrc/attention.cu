@@ -835,40 +835,57 @@ static void launch_prefill(const PrefillAttnArgs& a, cudaStream_t s) {
     launch_ex(prefill_attn_kernel<HD, KT>, grid, dim3(kAttnWarps * 32), smem, s, 1, a);
 }
 
-void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream_t s) {
+// Small batches (B x heads up to the SM count) take one CTA per (sequence, head) and
+// need no merge; larger ones take the persistent split kernel and the merge kernel.
+bool decode_attn_splits(const DecodeAttnArgs& a) { return (int64_t)a.B * a.n_heads > sm_count(); }
+
+DecodeAttnArgs plan_decode_attention(const DecodeAttnArgs& args, int max_ctx) {
+    DecodeAttnArgs a = args;
+    if (!decode_attn_splits(a)) return a;
+    // chunk length: the longest (default) that still gives every warp about two items,
+    // estimated from the longest context of the step
+    const int warps = sm_count() * (a.geom.head_dim == 64 ? DecCfg<64>::WARPS : DecCfg<128>::WARPS);
+    const int64_t pages = (int64_t)a.B * ((max_ctx + kPage - 1) / kPage);
+    while (a.chunk_pages > kMinChunkPages && pages / a.chunk_pages * a.n_heads < 2 * warps) a.chunk_pages /= 2;
+    if (a.chunk_pages < kMinChunkPages) a.chunk_pages = kMinChunkPages;
+    return a;
+}
+
+void launch_decode_attention_main(const DecodeAttnArgs& a, cudaStream_t s) {
     count_launch();
     const int grid = sm_count();
-    if ((int64_t)args.B * args.n_heads <= grid) {  // small batch: one CTA per (sequence, head)
-        const dim3 g((unsigned)(args.B * args.n_heads));
-        if (args.geom.head_dim == 64) {
-            if (args.geom.kv_bf16) launch_small<64, __nv_bfloat16>(args, g, s);
-            else launch_small<64, float>(args, g, s);
+    if (!decode_attn_splits(a)) {
+        const dim3 g((unsigned)(a.B * a.n_heads));
+        if (a.geom.head_dim == 64) {
+            if (a.geom.kv_bf16) launch_small<64, __nv_bfloat16>(a, g, s);
+            else launch_small<64, float>(a, g, s);
         } else {
-            if (args.geom.kv_bf16) launch_small<128, __nv_bfloat16>(args, g, s);
-            else launch_small<128, float>(args, g, s);
+            if (a.geom.kv_bf16) launch_small<128, __nv_bfloat16>(a, g, s);
+            else launch_small<128, float>(a, g, s);
         }
         return;
     }
-    // chunk length: the longest (default) that still gives every warp about two items,
-    // estimated from the longest context of the step
-    DecodeAttnArgs a = args;
-    {
-        const int warps = grid * (a.geom.head_dim == 64 ? DecCfg<64>::WARPS : DecCfg<128>::WARPS);
-        const int64_t pages = (int64_t)a.B * ((max_ctx + kPage - 1) / kPage);
-        while (a.chunk_pages > kMinChunkPages && pages / a.chunk_pages * a.n_heads < 2 * warps) a.chunk_pages /= 2;
-        if (a.chunk_pages < kMinChunkPages) a.chunk_pages = kMinChunkPages;
-    }
-    const dim3 mgrid((unsigned)(((int64_t)a.B * a.n_heads + 7) / 8));
-    count_launch();
     if (a.geom.head_dim == 64) {
         if (a.geom.kv_bf16) launch_split<64, __nv_bfloat16>(a, grid, s);
         else launch_split<64, float>(a, grid, s);
-        launch_ex(decode_merge_kernel<64>, mgrid, dim3(256), 0, s, 1, a);
     } else {
         if (a.geom.kv_bf16) launch_split<128, __nv_bfloat16>(a, grid, s);
         else launch_split<128, float>(a, grid, s);
-        launch_ex(decode_merge_kernel<128>, mgrid, dim3(256), 0, s, 1, a);
     }
+}
+
+void launch_decode_merge(const DecodeAttnArgs& a, cudaStream_t s) {
+    if (!decode_attn_splits(a)) return;
+    count_launch();
+    const dim3 mgrid((unsigned)(((int64_t)a.B * a.n_heads + 7) / 8));
+    if (a.geom.head_dim == 64) launch_ex(decode_merge_kernel<64>, mgrid, dim3(256), 0, s, 1, a);
+    else launch_ex(decode_merge_kernel<128>, mgrid, dim3(256), 0, s, 1, a);
+}
+
+void launch_decode_attention(const DecodeAttnArgs& args, int max_ctx, cudaStream_t s) {
+    const DecodeAttnArgs a = plan_decode_attention(args, max_ctx);
+    launch_decode_attention_main(a, s);
+    launch_decode_merge(a, s);
 }
 
 int prefill_attn_query_tile(int head_dim) {

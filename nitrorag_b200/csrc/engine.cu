@@ -407,8 +407,9 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
             a.B = cfg_.max_batch;
             decode_attn_bind_workspace(a, d_attn_ws_, c.max_pages());
             a.B = B_decode;
-            ProfScope ps(this, kKAttn);
-            launch_decode_attention(a, max_ctx, stream_);
+            const DecodeAttnArgs pa = plan_decode_attention(a, max_ctx);
+            { ProfScope ps(this, kKAttn); launch_decode_attention_main(pa, stream_); }
+            if (decode_attn_splits(pa)) { ProfScope ps(this, kKMerge); launch_decode_merge(pa, stream_); }
         }
         // 3. x += Wo . att
         GemmArgs go;

@@ -66,7 +66,7 @@ struct PrefillSeg {
 };
 
 // Kernel classes timed by the engine's optional per-launch CUDA-event profiling.
-enum KernelClass : int { kKEmbed = 0, kKQKV, kKAttn, kKWo, kKW13, kKW2, kKLogits, kKArgmax, kKClasses };
+enum KernelClass : int { kKEmbed = 0, kKQKV, kKAttn, kKWo, kKW13, kKW2, kKLogits, kKArgmax, kKMerge, kKClasses };
 
 class Engine {
 public:

@@ -107,6 +107,12 @@ size_t decode_attn_workspace_bytes(int B, int n_heads, int head_dim, int max_pag
 // Carve part_o/part_ml/counters out of a workspace of decode_attn_workspace_bytes().
 void decode_attn_bind_workspace(DecodeAttnArgs& a, void* ws, int max_pages_capacity);
 void launch_decode_attention(const DecodeAttnArgs& a, int max_ctx, cudaStream_t s);
+// The same in parts: the launch plan (chunk length from the longest context), the attention
+// kernel, and the merge kernel that combines its splits (nothing for small batches).
+DecodeAttnArgs plan_decode_attention(const DecodeAttnArgs& a, int max_ctx);
+bool decode_attn_splits(const DecodeAttnArgs& a);
+void launch_decode_attention_main(const DecodeAttnArgs& a, cudaStream_t s);
+void launch_decode_merge(const DecodeAttnArgs& a, cudaStream_t s);
 
 // Causal prefill attention for T consecutive tokens of one sequence, or (seg != null) for
 // chunks of several sequences whose rows are concatenated in q/out (see attention.cu).

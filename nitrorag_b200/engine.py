@@ -146,8 +146,8 @@ class NitroEngine:
 
     def kernel_times(self) -> dict:
         """{class: (total_ms, launches)} accumulated since profiling was enabled."""
-        ms = (C.c_double * 8)()
-        n = (C.c_int64 * 8)()
+        ms = (C.c_double * len(_lib.KERNEL_CLASSES))()
+        n = (C.c_int64 * len(_lib.KERNEL_CLASSES))()
         self._check(lib().nr_engine_kernel_times(self._h, ms, n), "nr_engine_kernel_times")
         return {name: (ms[i], n[i]) for i, name in enumerate(_lib.KERNEL_CLASSES)}
 
