@@ -140,6 +140,55 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Two fp32 values in one 64-bit register for sm_100's packed f32x2 arithmetic (one
+// instruction for both lanes, each rounded as the scalar operation would be).
+__device__ __forceinline__ unsigned long long pack2(uint32_t lo, uint32_t hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, uint32_t& lo, uint32_t& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// int8 weights to exact floats without a conversion instruction: with u = q + 128 (the
+// byte xor 0x80) in the low byte of 0x4B000000 the float is 2^23 + u, and adding
+// -(2^23 + 128) (bits 0xCB000080) leaves q exactly.  Bytes b and b + 1 (b even) of a word
+// that is already xor 0x80808080:
+__device__ __forceinline__ unsigned long long q8_pair_biased(uint32_t u, int b) {
+    return pack2(__byte_perm(u, 0x4B000000u, 0x7540 + b), __byte_perm(u, 0x4B000000u, 0x7541 + b));
+}
+__device__ __forceinline__ unsigned long long q8_unbias2() { return pack2(0xCB000080u, 0xCB000080u); }
+
+// Release / acquire flags between CTAs of one grid (GPU scope).
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Greedy-sampling key: larger key = larger logit, ties broken towards the smaller index,
 // so an atomicMax over keys reproduces argmax's "first strictly greater" rule
 // (src/model_q8.cpp:559-569).  Only logits > 0 produce candidates; the initial key

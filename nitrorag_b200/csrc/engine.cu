@@ -86,6 +86,7 @@ Engine::~Engine() {
     cudaFree(d_logits_);
     cudaFree(d_keys_);
     cudaFree(d_ss_);
+    cudaFree(d_sk_);
     cudaFree(d_err_);
     cudaFree(d_attn_ws_);
     cudaFree(d_desc_);
@@ -309,9 +310,28 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
             }
             NR_CUDA(cudaStreamSynchronize(stream_));
             NR_CUDA(cudaGetLastError());
+            // batches of up to 64 rows stream the raw tiles with the stream-K kernel
+            if (tc_streamk_enabled()) {
+                int dev = 0, sms = 0;
+                NR_CUDA(cudaGetDevice(&dev));
+                NR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+                sk_capacity_ = std::max(1, sms);
+                const size_t sk_bytes = tc_streamk_scratch_bytes(sk_capacity_);
+                NR_CUDA(cudaMalloc(&d_sk_, sk_bytes));
+                NR_CUDA(cudaMemset(d_sk_, 0, sk_bytes));  // the flags start clear
+                wide_rows_ = 65;
+            }
         }
     }
     return NR_OK;
+}
+
+void Engine::attach_streamk(GemmArgs& g) const {
+    if (!d_sk_) return;
+    g.sk_partial = static_cast<float*>(d_sk_);
+    g.sk_flags = reinterpret_cast<int*>(static_cast<uint8_t*>(d_sk_) + tc_streamk_scratch_bytes(sk_capacity_) -
+                                        (size_t)sk_capacity_ * sizeof(int));
+    g.sk_capacity = sk_capacity_;
 }
 
 int Engine::init_device(const uint8_t* file, size_t size) {
@@ -381,8 +401,9 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g.x = d_x_; g.ldx = D; g.norm_gain = w_.rms_att + (int64_t)l * D;
         g.wq = w_.qkv_q + (int64_t)l * NQKV * D; g.ws = w_.qkv_s + (int64_t)l * NQKV * (D / 32);
         g.M = M; g.N = NQKV; g.K = D; g.kbegin = faithful ? D - 32 : 0;
-        if (w_.qkv_t && !faithful && (!w_.qkv_r || M >= kWideTileRows)) g.wt = w_.qkv_t + l * w_.qkv_t_layer;
+        if (w_.qkv_t && !faithful && (!w_.qkv_r || M >= wide_rows_)) g.wt = w_.qkv_t + l * w_.qkv_t_layer;
         if (w_.qkv_r) g.wr = w_.qkv_r + l * w_.qkv_r_layer;
+        attach_streamk(g);
         if (ss) { g.ss_in = d_ss_; g.ss_parts = ss_parts; g.ss_ld = max_rows_; }
         Epilogue e;
         e.kind = kEpiQKV; e.q_out = d_q_; e.kpool = kpool_; e.vpool = vpool_; e.geom = geom_; e.layer = l;
@@ -416,8 +437,9 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         go.err = d_err_;
         go.x = d_att_; go.ldx = D; go.wq = w_.wo_q + (int64_t)l * D * D; go.ws = w_.wo_s + (int64_t)l * D * (D / 32);
         go.M = M; go.N = D; go.K = D; go.kbegin = faithful ? D - 32 : 0;
-        if (w_.wo_t && !faithful && (!w_.wo_r || M >= kWideTileRows)) go.wt = w_.wo_t + l * w_.wo_t_layer;
+        if (w_.wo_t && !faithful && (!w_.wo_r || M >= wide_rows_)) go.wt = w_.wo_t + l * w_.wo_t_layer;
         if (w_.wo_r) go.wr = w_.wo_r + l * w_.wo_r_layer;
+        attach_streamk(go);
         Epilogue eo;
         eo.kind = kEpiResidual; eo.out = d_x_; eo.ldo = D;
         if (ss) { eo.ss_out = d_ss_; eo.ss_ld = max_rows_; }
@@ -428,8 +450,9 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g13.x = d_x_; g13.ldx = D; g13.norm_gain = w_.rms_ffn + (int64_t)l * D;
         g13.wq = w_.w13_q + (int64_t)l * 2 * H * D; g13.ws = w_.w13_s + (int64_t)l * 2 * H * (D / 32);
         g13.M = M; g13.N = 2 * H; g13.K = D; g13.kbegin = faithful ? D - 32 : 0;
-        if (w_.w13_t && !faithful && (!w_.w13_r || M >= kWideTileRows)) g13.wt = w_.w13_t + l * w_.w13_t_layer;
+        if (w_.w13_t && !faithful && (!w_.w13_r || M >= wide_rows_)) g13.wt = w_.w13_t + l * w_.w13_t_layer;
         if (w_.w13_r) g13.wr = w_.w13_r + l * w_.w13_r_layer;
+        attach_streamk(g13);
         if (ss) { g13.ss_in = d_ss_; g13.ss_parts = ss_parts; g13.ss_ld = max_rows_; }
         Epilogue e13;
         e13.kind = kEpiSwiGLU; e13.out = d_h_; e13.ldo = H;
@@ -439,8 +462,9 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
         g2.err = d_err_;
         g2.x = d_h_; g2.ldx = H; g2.wq = w_.w2_q + (int64_t)l * D * H; g2.ws = w_.w2_s + (int64_t)l * D * (H / 32);
         g2.M = M; g2.N = D; g2.K = H; g2.kbegin = faithful ? H - 32 : 0;
-        if (w_.w2_t && !faithful && (!w_.w2_r || M >= kWideTileRows)) g2.wt = w_.w2_t + l * w_.w2_t_layer;
+        if (w_.w2_t && !faithful && (!w_.w2_r || M >= wide_rows_)) g2.wt = w_.w2_t + l * w_.w2_t_layer;
         if (w_.w2_r) g2.wr = w_.w2_r + l * w_.w2_r_layer;
+        attach_streamk(g2);
         Epilogue e2;
         e2.kind = kEpiResidual; e2.out = d_x_; e2.ldo = D;
         if (ss) { e2.ss_out = d_ss_; e2.ss_ld = max_rows_; }

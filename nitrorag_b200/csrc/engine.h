@@ -154,9 +154,15 @@ private:
     int* d_err_ = nullptr;
     void* d_attn_ws_ = nullptr;
     // large projections have both raw Q8 tiles and hi/lo tiles; batches of at least
-    // kWideTileRows rows read the hi/lo tiles
+    // wide_rows_ rows read the hi/lo tiles: kWideTileRows for the cluster-split kernel,
+    // beyond the stream-K kernel's 64 rows when that takes the raw tiles
     bool wide_tiles_ = false;
     static constexpr int kWideTileRows = 32;
+    int wide_rows_ = kWideTileRows;
+    // stream-K scratch for raw-tile projections (partial tiles + flags), one slot per SM
+    void* d_sk_ = nullptr;
+    int sk_capacity_ = 0;
+    void attach_streamk(GemmArgs& g) const;
     // set while a multi-sequence prefill runs: its segment and tile tables on the device
     const int* d_seg_ = nullptr;
     const int* d_tiles_ = nullptr;

@@ -464,18 +464,11 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     }
     // RMSNorm: a token's 1/rms scales its accumulators in the epilogue (the sum over k is
     // linear), so the sums of squares are needed only after the MMAs.  64-token tiles
-    // request them here, four threads per token, and add them up later.
+    // request them after staging (they would hold up the staging barrier), four threads
+    // per token, and add them up while the MMAs run.
     constexpr int SSP = 8;
     float ssv[SSP];
     const bool ss_pre = NT == 64 && a.norm_gain && a.ss_in && a.ss_parts <= 4 * SSP;
-    if (ss_pre && worker) {
-        const int m = m_base + ur;
-#pragma unroll
-        for (int i = 0; i < SSP; i++) {
-            const int p = ukq + 4 * i;
-            ssv[i] = (m < a.M && p < a.ss_parts) ? __ldcg(a.ss_in + (int64_t)p * a.ss_ld + m) : 0.0f;
-        }
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -590,6 +583,15 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
             __syncwarp();
         }
         if (lane == 0 && nch > 0) umma_commit(&done_bar);  // completes after every MMA above
+    }
+    // the sums of squares are needed only after the MMAs: requested once staging is done
+    if (ss_pre && worker) {
+        const int m = m_base + ur;
+#pragma unroll
+        for (int i = 0; i < SSP; i++) {
+            const int p = ukq + 4 * i;
+            ssv[i] = (m < a.M && p < a.ss_parts) ? __ldcg(a.ss_in + (int64_t)p * a.ss_ld + m) : 0.0f;
+        }
     }
     // 1/rms per token while the MMAs run
     if (a.norm_gain && worker) {
@@ -828,6 +830,353 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     if (warp == 0) tmem_dealloc(tmem, NT);
 }
 
+// ------------------------------------------------------------------ stream-K over raw Q8 tiles
+// Large Q8 projections at decode batches (up to 64 token rows) are HBM-bound, but their
+// 128-row tiles are too few to fill 148 SMs evenly (96 tiles for the 7B shape's q,k,v,
+// 172 for w1/w3), and a cluster K split cannot keep every cluster resident.  So one CTA
+// per SM takes an equal contiguous share of the (tile, 64-wide K chunk) units in
+// tile-major order (the raw tiles' order in memory), streams them through the bulk-copy
+// ring, converts each to bf16 hi/lo and accumulates each tile's run of chunks in TMEM.
+// A share starts inside a tile at most once: the partial sums of that first run go to
+// global scratch and a release flag is set.  The CTA whose share holds the tile's chunk 0
+// (where that run ends its share) waits for the flags of the CTAs after it that cover the
+// rest of the tile, adds their partials in CTA order (a fixed order: the result does not
+// depend on timing), clears the flags for the next launch and runs the epilogue.  A partial
+// is written at the start of its CTA's share and read at the end of an earlier CTA's, so
+// the waits are short; every wait is bounded.
+struct StreamKArgs {
+    int units;      // n_tiles x chunks
+    int chunks;     // K / 64
+    int stages;     // operand stages
+    int raw_slots;  // raw-tile ring slots
+    int raw_off;    // byte offset of the ring in dynamic shared memory
+};
+
+constexpr int SK_NT = 64;        // token columns per tile (the batch, zero-padded)
+constexpr int SK_STAGES = 2;
+constexpr int kSkWorkerBar = 8;  // named barrier of the 256 staging / epilogue threads
+
+__host__ __device__ inline int sk_first_unit(int cta, int grid, int units) { return (int)((int64_t)cta * units / grid); }
+
+// The CTA whose share holds unit u.
+__device__ __forceinline__ int sk_cta_of(int u, int grid, int units) {
+    int c = (int)(((int64_t)u * grid) / units);
+    while (c + 1 < grid && sk_first_unit(c + 1, grid, units) <= u) c++;
+    while (c > 0 && sk_first_unit(c, grid, units) > u) c--;
+    return c;
+}
+
+// Bounded wait for another CTA's release flag.
+__device__ __forceinline__ bool sk_wait_flag(const int* f, int* err) {
+    if (ld_acquire_gpu(f)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; i++) {
+        if (ld_acquire_gpu(f)) return true;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    }
+    if (err) atomicCAS(err, 0, kErrWaitTimeout);
+    return false;
+}
+
+// This thread's 32 weights of one chunk from a raw tile -> bf16 hi/lo core rows: the values
+// of stage_w_raw (w = q * scale rounded once, hi = bf16(w), lo = bf16(w - hi)) in packed
+// f32x2 arithmetic, the int8 -> float step by byte permutes instead of conversions.
+__device__ __forceinline__ void stage_w_raw2(const uint8_t* raw, uint8_t* a_hi, uint8_t* a_lo, int row, int half,
+                                             bool valid) {
+    const uint4 p0 = *reinterpret_cast<const uint4*>(raw + ((half * 2 + 0) * TC_M + row) * 16);
+    const uint4 p1 = *reinterpret_cast<const uint4*>(raw + ((half * 2 + 1) * TC_M + row) * 16);
+    const float sc = reinterpret_cast<const float*>(raw + TC_M * TC_KC)[half * TC_M + row];
+    const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    const unsigned long long sc2 = pack2(__float_as_uint(sc), __float_as_uint(sc)), unb = q8_unbias2();
+#pragma unroll
+    for (int j = 0; j < 4; j++) {  // 8 weights = one 16-byte core-matrix row per half
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t u = words[2 * j + (i >> 1)] ^ 0x80808080u;
+            const unsigned long long w = mul2(add2(q8_pair_biased(u, (i & 1) * 2), unb), sc2);
+            uint32_t w0, w1;
+            unpack2(w, w0, w1);
+            __nv_bfloat162 hb = __floats2bfloat162_rn(__uint_as_float(w0), __uint_as_float(w1));
+            const uint32_t hv = *reinterpret_cast<uint32_t*>(&hb);
+            uint32_t r0, r1;
+            unpack2(sub2(w, pack2(hv << 16, hv & 0xFFFF0000u)), r0, r1);
+            __nv_bfloat162 lb = __floats2bfloat162_rn(__uint_as_float(r0), __uint_as_float(r1));
+            h[i] = valid ? hv : 0u;
+            l[i] = valid ? *reinterpret_cast<uint32_t*>(&lb) : 0u;
+        }
+        *reinterpret_cast<uint4*>(a_hi + core_off(row, half * 4 + j)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(a_lo + core_off(row, half * 4 + j)) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+// Epilogue of one thread's 32 token columns c_base.. of weight row n (tile n_tile); the
+// RESIDUAL kind leaves each column's sum of squares over the warp's 32 rows in red_ss.
+__device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e, float* v, int n, int c_base,
+                                            const float* inv_rms, float* red_ss, int warp, int lane, bool ok) {
+    const int epi = e.kind;
+    if (a.norm_gain) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] *= inv_rms[c_base + j];
+    }
+    const bool nrow = ok && n < a.N;
+    if (epi == kEpiStore) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int m = c_base + j;
+            if (nrow && m < a.M) e.out[(int64_t)m * e.ldo + n] = v[j];
+        }
+    } else if (epi == kEpiResidual) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int m = c_base + j;
+            const bool w = nrow && m < a.M;
+            const float xn = w ? e.out[(int64_t)m * e.ldo + n] + v[j] : 0.0f;
+            if (w) e.out[(int64_t)m * e.ldo + n] = xn;
+            if (e.ss_out) {
+                const float sq = warp_sum(xn * xn);
+                if (lane == 0) red_ss[(warp & 3) * SK_NT + m] = sq;
+            }
+        }
+    } else if (epi == kEpiSwiGLU) {
+        const bool even = (n & 1) == 0;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int m = c_base + j;
+            const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);  // w3 row next to this w1 row
+            if (even && nrow && m < a.M) {
+                const float g = v[j];
+                e.out[(int64_t)m * e.ldo + (n >> 1)] = g * (1.0f / (1.0f + expf(-g))) * other;
+            }
+        }
+    } else if (epi == kEpiQKV) {
+        const int D = e.dim, KV = e.kv_dim, hd = e.head_dim;
+        const int np = n & ~1;
+        const bool even = (n & 1) == 0;
+        int kind = 3, fbase = 0;  // 0 q, 1 k, 2 v, 3 none
+        int64_t row_off = 0;
+        float* pool = nullptr;
+        if (nrow) {
+            if (np < D) {
+                kind = 0;
+                row_off = n;
+                fbase = (np % hd) >> 1;
+            } else {
+                const int cidx = np < D + KV ? n - D : n - D - KV;
+                kind = np < D + KV ? 1 : 2;
+                pool = kind == 1 ? e.kpool : e.vpool;
+                row_off = e.geom.tile_offset(0, e.layer, cidx / hd) + cidx % hd;
+                fbase = ((cidx & ~1) % hd) >> 1;
+            }
+        }
+        const bool rope = kind < 2;
+        const int64_t pf = e.geom.page_floats();
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int m = c_base + j;
+            const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);  // the rotary pair's other row
+            if (m >= a.M || kind == 3) continue;
+            const int pos = e.tok_pos[m];
+            float r = v[j];
+            if (rope) {
+                const int fi = pos * (hd >> 1) + fbase;
+                const float fcr = e.freq_re[fi], fci = e.freq_im[fi];
+                const float v0 = even ? v[j] : other, v1 = even ? other : v[j];
+                r = even ? (v0 * fcr - v1 * fci) : (v0 * fci + v1 * fcr);
+            }
+            if (kind == 0)
+                e.q_out[(int64_t)m * D + row_off] = r;
+            else
+                store_kv(pool, e.geom, (int64_t)e.tok_page[m] * pf + (int64_t)(pos & (kPage - 1)) * hd + row_off, r);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, Epilogue e, StreamKArgs sk) {
+    constexpr int NT = SK_NT;
+    using S = TcSmem<NT>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ uint64_t mma_bar[SK_STAGES];  // the stage's MMAs are done
+    __shared__ uint64_t raw_bar[TC_RAW_MAX];  // the slot's bulk copy has landed
+    __shared__ uint64_t acc_bar;              // a run's MMAs are done: its accumulator is complete
+    __shared__ uint32_t tmem_slot;
+    __shared__ int partners_ok;
+    __shared__ float inv_rms[NT];
+    __shared__ float red_ss[4 * NT];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool worker = warp < kIssuerWarp;
+    const int row = tid & (TC_M - 1), wg = (tid >> 7) & 1;  // weight row / TMEM lane, K half / column half
+    const int G = gridDim.x, cta = blockIdx.x, C = sk.chunks;
+    const int u0 = sk_first_unit(cta, G, sk.units);
+    const int nu = sk_first_unit(cta + 1, G, sk.units) - u0;
+    const int RS = sk.raw_slots;
+    auto stage_ptr = [&](int st, int part) {
+        return smem + st * S::STAGE + (part < 2 ? part * S::A_BYTES : 2 * S::A_BYTES + (part - 2) * S::B_BYTES);
+    };
+    uint8_t* raw_ring = smem + sk.raw_off;
+
+    if (warp == 0) {
+        tmem_alloc(&tmem_slot, NT);
+        tmem_relinquish();
+    }
+    auto fetch_raw = [&](int i) {  // unit u0 + i -> slot i % RS
+        uint64_t* bar = &raw_bar[i % RS];
+        mbar_arrive_expect_tx(bar, TC_RAW_BYTES);
+        bulk_g2s(raw_ring + (size_t)(i % RS) * TC_RAW_BYTES, a.wr + (size_t)(u0 + i) * TC_RAW_BYTES, TC_RAW_BYTES, bar);
+    };
+    if (tid == 0) {
+        for (int st = 0; st < SK_STAGES; st++) mbar_init(&mma_bar[st], 1);
+        for (int r = 0; r < TC_RAW_MAX; r++) mbar_init(&raw_bar[r], 1);
+        mbar_init(&acc_bar, 1);
+        fence_barrier_init();
+        // weights are read-only: the first tiles are requested before the dependency wait
+        for (int i = 0; i < min(nu, RS); i++) fetch_raw(i);
+    }
+    grid_dependency_wait();
+    // 1/rms of every token row; the RMSNorm gain is applied while staging x and the 1/rms
+    // to the sums (linear in x) in the epilogue
+    if (a.norm_gain && worker) {
+        if (a.ss_in) {
+            for (int u = tid; u < NT * 4; u += TC_WORKERS) {
+                const int r = u >> 2, p0 = u & 3;
+                float ss = 0.0f;
+                if (r < a.M)
+                    for (int p = p0; p < a.ss_parts; p += 4) ss += __ldcg(a.ss_in + (int64_t)p * a.ss_ld + r);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                if (p0 == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+            }
+        } else {
+            for (int r = warp; r < NT; r += TC_WORKERS / 32) {
+                float ss = 0.0f;
+                if (r < a.M)
+                    for (int k = lane * 4; k < a.K; k += 128) {
+                        const float4 x4 = *reinterpret_cast<const float4*>(a.x + (int64_t)r * a.ldx + k);
+                        ss += x4.x * x4.x + x4.y * x4.y + x4.z * x4.z + x4.w * x4.w;
+                    }
+                ss = warp_sum(ss);
+                if (lane == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t idesc = umma_idesc_bf16(TC_M, NT);
+    const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+
+    if (worker) {
+        bool ok = true;
+        const int ur = tid >> 2, ukq = tid & 3;  // activation unit: token ur, 16-wide K quarter ukq
+        float4 xn[4], gn[4];
+        auto fetch_x = [&](int i) {  // unit u0 + i's activations (and gain), one unit ahead
+            const int k = ((u0 + i) % C) * TC_KC + ukq * 16;
+            if (ur < a.M) {
+                const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)ur * a.ldx + k);
+#pragma unroll
+                for (int j = 0; j < 4; j++) xn[j] = src[j];
+            }
+            if (a.norm_gain) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) gn[j] = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k) + j);
+            }
+        };
+        if (nu > 0) fetch_x(0);
+        int runs = 0, run_c0 = u0 % C;
+        for (int it = 0; it < nu; it++) {
+            const int u = u0 + it, t = u / C, c = u % C;
+            const int st = it % SK_STAGES, use = it / SK_STAGES;
+            if (c == 0) run_c0 = 0;
+            // the stage was last read by the MMAs of unit it - SK_STAGES
+            if (ok && use > 0 && !mbar_wait(&mma_bar[st], (use - 1) & 1, a.err)) ok = false;
+            if (ok && !mbar_wait(&raw_bar[it % RS], (it / RS) & 1, a.err)) ok = false;
+            if (ok) {
+                stage_w_raw2(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, stage_ptr(st, 0), stage_ptr(st, 1), row, wg,
+                             t * TC_M + row < a.N);
+                stage_x16(xn, a.norm_gain ? reinterpret_cast<const float*>(gn) : nullptr, ur < a.M, stage_ptr(st, 2),
+                          stage_ptr(st, 3), ur, ukq);
+            }
+            if (it + 1 < nu) fetch_x(it + 1);
+            fence_async_smem();
+            named_arrive(1 + st, TC_THREADS);
+            if (it != nu - 1 && c != C - 1) continue;
+
+            // end of a run: its accumulator, then a partial or the tile's epilogue
+            if (ok && !mbar_wait(&acc_bar, runs & 1, a.err)) ok = false;
+            runs++;
+            tc_fence_after();
+            float v[32];
+            tmem_ld32(tl + wg * 32, v);
+            if (it == nu - 1) grid_dependents_launch();
+            if (run_c0 > 0) {
+                // the tile belongs to an earlier CTA: [cta][column][row] partial, then the flag
+                float* dst = a.sk_partial + ((size_t)cta * NT + wg * 32) * TC_M + row;
+#pragma unroll
+                for (int j = 0; j < 32; j++) __stcg(dst + (size_t)j * TC_M, ok ? v[j] : 0.0f);
+                __threadfence();
+                named_sync(kSkWorkerBar, TC_WORKERS);
+                if (tid == 0) st_release_gpu(a.sk_flags + cta, 1);
+            } else {
+                const int last = c == C - 1 ? cta : sk_cta_of(t * C + C - 1, G, sk.units);
+                if (last > cta) {  // the rest of the tile is in the shares of CTAs cta+1..last
+                    if (tid == 0) {
+                        bool all = true;
+                        for (int p = cta + 1; p <= last && all; p++) all = sk_wait_flag(a.sk_flags + p, a.err);
+                        partners_ok = all;
+                    }
+                    named_sync(kSkWorkerBar, TC_WORKERS);
+                    if (partners_ok) {
+                        for (int p = cta + 1; p <= last; p++) {
+                            const float* src = a.sk_partial + ((size_t)p * NT + wg * 32) * TC_M + row;
+#pragma unroll
+                            for (int j = 0; j < 32; j++) v[j] += __ldcg(src + (size_t)j * TC_M);
+                        }
+                        if (tid == 0)
+                            for (int p = cta + 1; p <= last; p++) atomicExch(a.sk_flags + p, 0);
+                    } else {
+                        ok = false;
+                    }
+                }
+                sk_epilogue(a, e, v, t * TC_M + row, wg * 32, inv_rms, red_ss, warp, lane, ok);
+                if (e.kind == kEpiResidual && e.ss_out) {  // this tile's share of the next RMSNorm
+                    named_sync(kSkWorkerBar, TC_WORKERS);
+                    if (tid < NT && tid < a.M)
+                        e.ss_out[(int64_t)t * e.ss_ld + tid] =
+                            red_ss[tid] + red_ss[NT + tid] + red_ss[2 * NT + tid] + red_ss[3 * NT + tid];
+                }
+            }
+            // the accumulator's loads come before the next run's MMAs (ordered by the next
+            // unit's named barrier)
+            tc_fence_before();
+        }
+    } else {
+        // issuer warp: lane 0 refills the raw ring and issues every unit's MMAs
+        for (int it = 0; it < nu; it++) {
+            const int c = (u0 + it) % C;
+            const int st = it % SK_STAGES;
+            // the workers converted unit it - 1 before the barrier this warp passed last
+            // iteration, so its slot takes unit it - 1 + RS
+            if (lane == 0 && it >= 1 && it - 1 + RS < nu) fetch_raw(it - 1 + RS);
+            __syncwarp();
+            named_sync(1 + st, TC_THREADS);
+            if (lane == 0) {
+                tc_fence_after();
+                issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3),
+                                 it == 0 || c == 0);
+                umma_commit(&mma_bar[st]);
+                if (it == nu - 1 || c == C - 1) umma_commit(&acc_bar);
+            }
+            __syncwarp();
+        }
+        grid_dependents_launch();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, NT);
+}
+
 // Allow the kernel the largest dynamic shared memory the device offers next to its static
 // shared memory (per kernel and device, once).
 template <class K>
@@ -1014,14 +1363,68 @@ void tc_tile_weights(const int8_t* q, const float* scales, const float* wf, int 
     tile_weights_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, scales, wf, N, K, out);
 }
 
+bool tc_streamk_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* env = getenv("NITRO_STREAMK");
+        v = (env && env[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+size_t tc_streamk_scratch_bytes(int ctas) {
+    return (size_t)ctas * SK_NT * TC_M * sizeof(float) + (size_t)ctas * sizeof(int);
+}
+
+namespace {
+
+// Smallest batch the stream-K kernel takes (NITRO_STREAMK_MIN_ROWS; 1-2 rows otherwise go
+// to the streamed matvec).
+int streamk_min_rows() {
+    static int v = -1;
+    if (v < 0) {
+        const char* env = getenv("NITRO_STREAMK_MIN_ROWS");
+        v = env ? std::max(1, atoi(env)) : 3;
+    }
+    return v;
+}
+
+bool streamk_takes(const GemmArgs& a) {
+    return tc_streamk_enabled() && a.sk_partial && a.sk_flags && a.sk_capacity > 0 && a.wr && !a.wt && !a.wf &&
+           a.kbegin == 0 && a.M >= streamk_min_rows() && a.M <= SK_NT && a.K % TC_KC == 0 && a.N % 2 == 0;
+}
+
+void tc_launch_streamk(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
+    StreamKArgs sk;
+    sk.chunks = a.K / TC_KC;
+    sk.units = ((a.N + TC_M - 1) / TC_M) * sk.chunks;
+    sk.stages = SK_STAGES;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
+    if (sms <= 0) sms = 148;
+    const int grid = std::max(1, std::min(std::min(sms, sk.units), a.sk_capacity));
+    const int budget = tc_ensure_smem(tc_streamk_kernel);
+    sk.raw_off = SK_STAGES * TcSmem<SK_NT>::STAGE;
+    sk.raw_slots = std::min(TC_RAW_MAX, (budget - sk.raw_off) / (int)TC_RAW_BYTES);
+    launch_ex(tc_streamk_kernel, dim3(grid), dim3(TC_THREADS), sk.raw_off + sk.raw_slots * (int)TC_RAW_BYTES, s, 1, a,
+              e, sk);
+}
+
+}  // namespace
+
 // Raw Q8 tiles send batches of 3-8 tokens here too: for large matrices the tensor-core
-// kernel streams them far better than the matvec (1-2 tokens take the streamed matvec).
+// kernels stream them far better than the matvec (1-2 tokens take the streamed matvec).
 bool tc_gemm_supported(const GemmArgs& a) {
-    return a.K % TC_KC == 0 && a.N % 2 == 0 && (a.M > 8 || (a.wr != nullptr && !a.wf && a.M > 2));
+    return a.K % TC_KC == 0 && a.N % 2 == 0 && (a.M > 8 || (a.wr != nullptr && !a.wf && a.M > 2) || streamk_takes(a));
 }
 
 void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     count_launch();
+    if (streamk_takes(a)) {
+        tc_launch_streamk(a, e, s);
+        return;
+    }
     // 256-token tiles only when they alone fill the GPU (they never split K)
     const int n_tiles = (a.N + TC_M - 1) / TC_M;
     if (a.M <= 64) tc_launch<64>(a, e, s);

@@ -65,7 +65,18 @@ struct GemmArgs {
     // and scales regrouped per 128-row x 64-column tile (9 KB, tc_tile_q8_raw) so the
     // kernel can stream them with bulk copies through a deep shared-memory ring.
     const uint8_t* wr = nullptr;
+    // Optional scratch for the stream-K kernel over raw tiles (batches of 3-64 rows): one
+    // partial tile per CTA, sk_partial [sk_capacity][64][128] fp32, and one flag per CTA,
+    // sk_flags [sk_capacity], zero when no launch is in flight (each launch leaves them so).
+    float* sk_partial = nullptr;
+    int* sk_flags = nullptr;
+    int sk_capacity = 0;
 };
+
+// Bytes of stream-K scratch (partials, then flags) for `ctas` CTAs.
+size_t tc_streamk_scratch_bytes(int ctas);
+// Whether the stream-K kernel may take raw-tile launches (NITRO_STREAMK=0 turns it off).
+bool tc_streamk_enabled();
 
 // M <= 8: CUDA-core matvec; M > 8 with K % 64 == 0: tcgen05 GEMM (gemm_tc.cu); otherwise
 // the CUDA-core tiled kernel.

@@ -252,17 +252,20 @@ def test_ingest_prompt_prefix_cache_hit(ref_fixed, tiny_model):
     ref.close()
 
 
-@pytest.mark.parametrize("B", [1, 5, 24, 40])
+@pytest.mark.parametrize("B", [1, 3, 5, 24, 40, 64])
 def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B):
     """The large-model projection path: with the tile threshold at zero every Q8 projection
-    gets raw Q8 tiles, streamed through the tensor-core kernel's bulk-copy ring by batches
-    of 1-31 tokens (1-8 included: the path the 7B shape takes), and hi/lo tiles beside them,
-    which batches of 32 or more rows read (B = 40 here).  Prefill and two decode steps must
-    match the reference."""
+    gets raw Q8 tiles (and hi/lo tiles beside them, which only batches of more than 64 rows
+    read).  Batches of 3-64 rows take the stream-K kernel: its shares of (tile, K chunk)
+    units cut these small matrices' tiles over up to 12 CTAs each, so the partial-tile
+    hand-over runs on every projection; 1-2 rows take the streamed matvec.  Prefill and two
+    decode steps must match the reference, and a decode step run again on the same inputs
+    must give bit-identical logits (partials are added in a fixed order)."""
     monkeypatch.setenv("NITRO_TILE_MAX_WEIGHTS", "0")
     ref = ref_fixed
-    ref.open(m110_model, 256, 200)
-    eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=200)
+    blocks = 600
+    ref.open(m110_model, 256, blocks)
+    eng = _engine(m110_model, NR_Q8_FIXED, total_blocks=blocks)
     prompts = synth.decode_workload(B, 20, 90, 32000, seed=12 + B)
     rh, eh, toks, pos = [], [], [], []
     for i, p in enumerate(prompts):
@@ -277,6 +280,9 @@ def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B):
         lr = ref.forward_decode(toks, pos, rh)
         le, am = eng.forward_decode_batch(toks, pos, eh)
         assert_close(le, lr, what=f"raw-tile B={B} decode step {step}")
+        if step == 0:  # the same step again: same K/V rows rewritten, same logits bit for bit
+            le2, am2 = eng.forward_decode_batch(toks, pos, eh)
+            assert np.array_equal(le2, le) and np.array_equal(am2, am)
         for i in range(B):
             _check_tokens(int(am[i]), ref.argmax(lr[i]), lr[i], f"raw-tile B={B} step {step} row {i}")
         toks = [int(t) for t in am]
