@@ -994,6 +994,92 @@ def run_quantize(args):
     return line
 
 
+def run_matvec(args):
+    """The Q8_0 matvec alone through nr_q8_matmul (src/model_q8.cpp:92-125) at one token row
+    on the 7B shape's largest projection, w1/w3 interleaved (22016 x 4096), and the other
+    7B projection shapes at one and two rows.  Per shape: `isolated` = one launch after a
+    512 MB write has flushed L2 (CUDA events around the launch alone); `back_to_back` = 32
+    launches over 8 distinct matrices (all of them > L2 together) on one stream, the way the
+    engine chains its projections.  value / roofline = the headline shape's isolated
+    launch; algorithmic bytes = int8 weights + fp32 scales + x + out."""
+    import ctypes as C
+    import torch
+    from nitrorag_b200._lib import NR_Q8_FIXED, lib
+    peak, peak_src = load_peaks()
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    shapes = [(1, 22016, 4096), (1, 12288, 4096), (1, 4096, 4096), (1, 4096, 11008),
+              (2, 22016, 4096), (2, 12288, 4096)]
+    rows, launches = {}, 0
+    for M, N, K in shapes:
+        g = torch.Generator(device="cuda").manual_seed(N + K)
+        mats = [(torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g),
+                 torch.rand((N, K // 32), device="cuda", generator=g) * 1e-3) for _ in range(8)]
+        x = torch.randn((M, K), device="cuda", generator=g)
+        out = torch.empty((M, N), device="cuda")
+
+        def launch(i):
+            q, s = mats[i % 8]
+            rc = lib().nr_q8_matmul(x.data_ptr(), q.data_ptr(), s.data_ptr(), out.data_ptr(), M, N, K, NR_Q8_FIXED,
+                                    C.c_void_p(stream.cuda_stream))
+            assert rc == 0, rc
+
+        for i in range(max(args.warmup, 3) * 2):
+            launch(i)
+        iso = []
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            e0, e1 = _dev_events(torch, stream)
+            e0.record(stream)
+            launch(i)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            iso.append(e0.elapsed_time(e1))
+        e0, e1 = _dev_events(torch, stream)
+        e0.record(stream)
+        for i in range(32):
+            launch(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        launches += args.steps + 32
+        b2b = e0.elapsed_time(e1) / 32
+        iso_ms = sorted(iso)[len(iso) // 2]
+        algo = N * K + N * K // 32 * 4 + M * K * 4 + M * N * 4
+        rows[f"M{M}_{N}x{K}"] = {"isolated_us": round(iso_ms * 1e3, 2), "isolated_GBs": round(algo / iso_ms / 1e6, 1),
+                                  "back_to_back_us": round(b2b * 1e3, 2), "back_to_back_GBs": round(algo / b2b / 1e6, 1),
+                                  "bytes": algo}
+        del mats
+    head = rows["M1_22016x4096"]
+    line = {"workload": "matvec", "metric": "Q8_0 matvec HBM GB/s (nr_q8_matmul, M = 1, 22016 x 4096)",
+            "value": head["isolated_GBs"], "unit": "GB/s", "ms_per_step": round(head["isolated_us"] / 1e3, 5),
+            "higher_is_better": True, "dtype": "q8_0 x f32", "data": "synthetic",
+            "config": {"workload": "matvec", "flush": "512 MB write before each isolated launch"},
+            "shapes": rows,
+            "roofline": {"bound": "hbm", "achieved": head["isolated_GBs"], "peak": peak, "unit": "GB/s",
+                         "frac": round(head["isolated_GBs"] / peak, 4), "peak_source": peak_src,
+                         "back_to_back_frac": round(head["back_to_back_GBs"] / peak, 4)},
+            "gpu_launches": launches, "steps": args.steps, "warmup": args.warmup}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        r = oracle.Restatement()
+        M, N, K = 1, 22016, 4096
+        rng = np.random.default_rng(3)
+        w_aos = synth.quantize_q8((rng.standard_normal(N * K) * 0.02).astype(np.float32))
+        xh = rng.standard_normal((M, K)).astype(np.float32)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 3.0:
+            r.q8_matmul(xh, w_aos, K, N)
+            reps += 1
+        cpu_s = (time.perf_counter() - t0) / reps
+        algo = N * K + N * K // 32 * 4 + M * K * 4 + M * N * 4
+        line["cpu_baseline"] = {"value": round(algo / cpu_s / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                                "sample": f"{reps} calls of orc_q8_matmul (scalar C restatement of the "
+                                          f"reference's matmul) on the headline shape"}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1004,7 +1090,7 @@ def main():
     ap.add_argument("--profile-range", action="store_true",
                     help="mark the timed device-resident replays as the CUDA profiler range")
     ap.add_argument("--workload", choices=["decode64", "config1", "config3", "config4", "config5", "config5_decode",
-                                           "quantize"],
+                                           "quantize", "matvec"],
                     default="decode64", help="decode64 is the headline; the others print their own line")
     ap.add_argument("--batch", type=int, default=0, help="config5: requests per GPU (default 64)")
     args = ap.parse_args()
@@ -1041,7 +1127,7 @@ def main():
         if args.workload != "decode64":
             if rank == 0:
                 fn = {"config1": run_config1, "config4": run_config4, "config5_decode": run_config5_decode,
-                      "quantize": run_quantize}[args.workload]
+                      "quantize": run_quantize, "matvec": run_matvec}[args.workload]
                 print(json.dumps(fn(args)), flush=True)
             return 0
         return engine_arm(args, rank, world, local_rank, comm)

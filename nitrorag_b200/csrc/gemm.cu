@@ -480,6 +480,222 @@ __global__ void __launch_bounds__(256) gemv_stream_kernel(GemmArgs a, Epilogue e
     grid_dependents_launch();
 }
 
+// ------------------------------------------------------------------ ring matvec, M <= 2
+// Large Q8 matrices at one or two token rows (decode at batch 1-2; the 7B shape's
+// projections).  One CTA per SM takes a contiguous range of units of G whole rows: their
+// int8 rows and scales are contiguous in the row-major arrays, so one producer thread
+// streams each unit with two bulk copies into a ring of shared-memory slots, requested
+// before the grid-dependency wait for the first slots.  16 consumer warps read every
+// unit, warp w taking row w % G and K segment w / G of 16 / G; a lane's share of its
+// segment sits at the same K positions in every unit, so the lane keeps those activations
+// (times the RMSNorm gain, as packed pairs) in registers for the whole launch, and the
+// inner loop is one 16-byte shared load per 16 weights, one byte permute per weight
+// (int8 -> exact float, as q8_pair_biased) and packed f32x2 adds and FMAs; the block scale
+// multiplies each 16-weight partial (the products of src/model_q8.cpp:107-111, summed in
+// another order).  A row pair's segment partials meet in shared memory: the last of its
+// warps to arrive (shared-memory counter) adds them in segment order and runs the
+// epilogue, then every warp releases the slot to the producer.
+constexpr int GR_CONSUMERS = 16;
+constexpr int GR_THREADS = (GR_CONSUMERS + 1) * 32;
+constexpr int GR_SLOTS_MAX = 8;
+constexpr int GR_XPAIRS = 32;  // activation pairs a lane may hold: MT x CPL x 8
+
+struct RingPlan {
+    int G;           // rows per unit: 2, 4 or 8
+    int slot_bytes;  // G x (K + K / 8)
+    int slots;
+    int units;       // N / G
+};
+
+template <int MT, int CPL>
+__global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Epilogue e, RingPlan rp) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[GR_SLOTS_MAX], empty[GR_SLOTS_MAX];
+    __shared__ float part[GR_SLOTS_MAX][8][8][MT];  // [slot][row of unit][segment][token]
+    __shared__ int cnt[GR_SLOTS_MAX][4];            // [slot][row pair]: warps done
+    __shared__ float red[GR_CONSUMERS + 1][MT];
+    __shared__ float inv_rms[MT];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int K = a.K, G = rp.G, S = GR_CONSUMERS / G, L = K / S;
+    const int u0 = (int)((int64_t)blockIdx.x * rp.units / gridDim.x);
+    const int nu = (int)((int64_t)(blockIdx.x + 1) * rp.units / gridDim.x) - u0;
+    const bool producer = warp == GR_CONSUMERS;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < rp.slots; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], GR_CONSUMERS);
+        }
+        fence_barrier_init();
+    }
+    for (int i = threadIdx.x; i < GR_SLOTS_MAX * 4; i += blockDim.x) (&cnt[0][0])[i] = 0;
+    __syncthreads();
+    auto fetch = [&](int i) {  // unit u0 + i -> slot i % slots
+        const int s = i % rp.slots;
+        uint8_t* dst = smem + (size_t)s * rp.slot_bytes;
+        const int64_t n = (int64_t)(u0 + i) * G;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(G * (K + K / 8)));
+        bulk_g2s(dst, a.wq + n * K, (uint32_t)(G * K), &full[s]);
+        bulk_g2s(dst + G * K, a.ws + n * (K / 32), (uint32_t)(G * K / 8), &full[s]);
+    };
+    // weights are read-only: the first units are requested before the dependency wait
+    if (producer && lane == 0)
+        for (int i = 0; i < min(nu, rp.slots); i++) fetch(i);
+    grid_dependency_wait();
+
+    // consumer geometry: row r of every unit, K segment sg; the lane's chunks of 16
+    const int r = warp % G, sg = warp / G;
+    const int kseg = sg * L;
+    // the lane's activations (times the gain) as packed pairs, and the RMSNorm sums
+    unsigned long long xp[MT][CPL * 8];
+    float ss[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) ss[m] = 0.0f;
+    if (!producer) {
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            const int k = kseg + (lane + 32 * c) * 16;
+            const bool valid = (lane + 32 * c) * 16 < L;
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (valid && m < a.M) v = *reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k + 4 * j);
+                    ss[m] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    if (valid && a.norm_gain) {
+                        const float4 g = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k + 4 * j));
+                        v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+                    }
+                    xp[m][c * 8 + 2 * j] = pack2(__float_as_uint(v.x), __float_as_uint(v.y));
+                    xp[m][c * 8 + 2 * j + 1] = pack2(__float_as_uint(v.z), __float_as_uint(v.w));
+                }
+            }
+        }
+    }
+    // 1/rms of each token row: the warps of row 0 of the unit hold every K position once
+    if (a.norm_gain) {
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            const float t = warp_sum(ss[m]);
+            if (lane == 0) red[warp][m] = (!producer && r == 0) ? t : 0.0f;
+        }
+    }
+    __syncthreads();
+    if (a.norm_gain && threadIdx.x < MT) {
+        float t = 0.0f;
+        for (int w = 0; w < GR_CONSUMERS; w++) t += red[w][threadIdx.x];
+        inv_rms[threadIdx.x] = 1.0f / sqrtf(t / (float)K + 1e-5f);
+    }
+    __syncthreads();
+
+    if (producer) {
+        // refill each slot once all consumer warps have released it
+        if (lane == 0) {
+            bool ok = true;
+            for (int i = rp.slots; i < nu && ok; i++) {
+                const int s = i % rp.slots;
+                if (!mbar_wait(&empty[s], ((i / rp.slots) - 1) & 1, a.err)) ok = false;
+                else fetch(i);
+            }
+        }
+        grid_dependents_launch();
+        return;
+    }
+    const unsigned long long unb = q8_unbias2();
+    bool ok = true;
+    for (int i = 0; i < nu; i++) {
+        const int s = i % rp.slots;
+        if (ok && !mbar_wait(&full[s], (i / rp.slots) & 1, a.err)) ok = false;
+        const uint8_t* q = smem + (size_t)s * rp.slot_bytes + (size_t)r * K;
+        const float* sc = reinterpret_cast<const float*>(smem + (size_t)s * rp.slot_bytes + (size_t)G * K) + (size_t)r * (K / 32);
+        float acc[MT];
+#pragma unroll
+        for (int m = 0; m < MT; m++) acc[m] = 0.0f;
+        if (ok) {
+#pragma unroll
+            for (int c = 0; c < CPL; c++) {
+                const int kl = (lane + 32 * c) * 16;
+                if (kl < L) {
+                    const uint4 w4 = *reinterpret_cast<const uint4*>(q + kseg + kl);
+                    const float bs = sc[(kseg + kl) >> 5];
+                    const uint32_t u[4] = {w4.x ^ 0x80808080u, w4.y ^ 0x80808080u, w4.z ^ 0x80808080u,
+                                           w4.w ^ 0x80808080u};
+                    unsigned long long d[MT];
+#pragma unroll
+                    for (int m = 0; m < MT; m++) d[m] = 0ull;
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const unsigned long long qv = add2(q8_pair_biased(u[j >> 1], (j & 1) * 2), unb);
+#pragma unroll
+                        for (int m = 0; m < MT; m++) d[m] = fma2(qv, xp[m][c * 8 + j], d[m]);
+                    }
+#pragma unroll
+                    for (int m = 0; m < MT; m++) {
+                        uint32_t lo, hi;
+                        unpack2(d[m], lo, hi);
+                        acc[m] = fmaf(__uint_as_float(lo) + __uint_as_float(hi), bs, acc[m]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) acc[m] = warp_sum(acc[m]);
+        int prev = 0;
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < MT; m++) part[s][r][sg][m] = acc[m];
+            __threadfence_block();
+            prev = atomicAdd(&cnt[s][r >> 1], 1);
+        }
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == 2 * S - 1) {  // the row pair's last warp: segments in order, epilogue
+            __threadfence_block();
+            const int r0 = r & ~1;
+            if (lane < MT && lane < a.M && ok) {
+                float v0 = 0.0f, v1 = 0.0f;
+                for (int t = 0; t < S; t++) {
+                    v0 += part[s][r0][t][lane];
+                    v1 += part[s][r0 + 1][t][lane];
+                }
+                if (a.norm_gain) {
+                    v0 *= inv_rms[lane];
+                    v1 *= inv_rms[lane];
+                }
+                epi_pair(e, lane, (u0 + i) * G + r0, v0, v1);
+            }
+            if (lane == 0) cnt[s][r >> 1] = 0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot and its partials
+    }
+    grid_dependents_launch();
+}
+
+// Whether the ring matvec takes this launch, and its shape: whole-row units of at most
+// 48 KB, the lane's activations in at most GR_XPAIRS packed pairs, at least 3 ring slots.
+bool ring_plan(const GemmArgs& a, RingPlan* rp, int* cpl) {
+    if (a.wf || !a.wq || a.M > 2 || a.kbegin != 0 || a.K % 32 != 0 || a.N % 2 != 0) return false;
+    if (reinterpret_cast<uintptr_t>(a.wq) % 16 || reinterpret_cast<uintptr_t>(a.ws) % 16) return false;
+    if ((int64_t)a.N * a.K < ((int64_t)4 << 20)) return false;  // small matrices: launch latency rules
+    for (int G = 8; G >= 2; G /= 2) {
+        const int S = GR_CONSUMERS / G;
+        if (a.N % G || a.K % (16 * S)) continue;
+        const int slot = G * (a.K + a.K / 8);
+        // every unit's two copies start and end on 16-byte boundaries
+        if (slot > 48 * 1024 || (G * a.K) % 16 || (G * a.K / 8) % 16) continue;
+        const int c = (a.K / S / 16 + 31) / 32;
+        if (c < 1 || a.M * c * 8 > GR_XPAIRS) continue;
+        rp->G = G;
+        rp->slot_bytes = slot;
+        rp->slots = std::min(GR_SLOTS_MAX, (200 * 1024) / slot);
+        rp->units = a.N / G;
+        *cpl = c;
+        return rp->slots >= 3;
+    }
+    return false;
+}
+
 // Whether the streamed matvec takes this launch, and its shape.
 // Measured on B200 (one token row): the streamed kernel wins only for large Q8 matrices
 // with rows short enough for 8 warps' rings (e.g. 22016 x 4096: 2.96 vs 2.61 TB/s); both
@@ -649,6 +865,26 @@ bool gemm_uses_tc(int M, int N, int K) {
     return M > 8 && !tc_disabled() && tc_gemm_supported(g);
 }
 
+template <int MT, int CPL>
+void launch_ring(const GemmArgs& a, const Epilogue& e, const RingPlan& rp, cudaStream_t s) {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
+    if (sms <= 0) sms = 148;
+    const int smem = rp.slots * rp.slot_bytes;
+    cudaFuncSetAttribute(gemv_ring_kernel<MT, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const int grid = std::max(1, std::min(sms, rp.units));
+    launch_ex(gemv_ring_kernel<MT, CPL>, dim3(grid), dim3(GR_THREADS), smem, s, 1, a, e, rp);
+}
+
+template <int MT>
+void dispatch_ring(const GemmArgs& a, const Epilogue& e, const RingPlan& rp, int cpl, cudaStream_t s) {
+    if (cpl <= 1) launch_ring<MT, 1>(a, e, rp, s);
+    else if (cpl <= 2) launch_ring<MT, 2>(a, e, rp, s);
+    else if (MT == 1 && cpl <= 3) launch_ring<MT, (MT == 1 ? 3 : 2)>(a, e, rp, s);
+    else launch_ring<MT, (MT == 1 ? 4 : 2)>(a, e, rp, s);
+}
+
 template <int MT, bool F32W>
 void launch_stream(const GemmArgs& a, const Epilogue& e, const StreamPlan& sp, cudaStream_t s) {
     int dev = 0, sms = 0;
@@ -668,6 +904,13 @@ void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
         return;
     }
     g_launches++;
+    RingPlan rp;
+    int cpl = 0;
+    if (!stream_disabled() && ring_plan(a, &rp, &cpl)) {
+        if (a.M <= 1) dispatch_ring<1>(a, e, rp, cpl, s);
+        else dispatch_ring<2>(a, e, rp, cpl, s);
+        return;
+    }
     StreamPlan sp;
     if (!stream_disabled() && stream_plan(a, &sp)) {
         if (a.M <= 1) launch_stream<1, false>(a, e, sp, s);

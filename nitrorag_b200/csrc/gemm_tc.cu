@@ -878,60 +878,75 @@ __device__ __forceinline__ bool sk_wait_flag(const int* f, int* err) {
     return false;
 }
 
-// This thread's 32 weights of one chunk from a raw tile -> bf16 hi/lo core rows: the values
-// of stage_w_raw (w = q * scale rounded once, hi = bf16(w), lo = bf16(w - hi)) in packed
-// f32x2 arithmetic, the int8 -> float step by byte permutes instead of conversions.
-__device__ __forceinline__ void stage_w_raw2(const uint8_t* raw, uint8_t* a_hi, uint8_t* a_lo, int row, int half,
-                                             bool valid) {
-    const uint4 p0 = *reinterpret_cast<const uint4*>(raw + ((half * 2 + 0) * TC_M + row) * 16);
-    const uint4 p1 = *reinterpret_cast<const uint4*>(raw + ((half * 2 + 1) * TC_M + row) * 16);
-    const float sc = reinterpret_cast<const float*>(raw + TC_M * TC_KC)[half * TC_M + row];
-    const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+constexpr int SK_WORKERS = 512;               // conversion / epilogue threads: 16 warps
+constexpr int SK_THREADS = SK_WORKERS + 32;   // + the warp that refills the ring and issues the MMAs
+constexpr int kSkIssuerWarp = SK_WORKERS / 32;
+constexpr int SK_COLS = SK_NT / (SK_WORKERS / TC_M);  // epilogue columns per thread (16)
+
+// Eight fp32 values -> bf16 hi/lo (hi = bf16(v), lo = bf16(v - hi)), one 16-byte core-matrix
+// row each, in packed f32x2 arithmetic; w[i] holds values 2i, 2i+1.
+__device__ __forceinline__ void split8_store(const unsigned long long w[4], uint8_t* hi_dst, uint8_t* lo_dst) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint32_t w0, w1;
+        unpack2(w[i], w0, w1);
+        __nv_bfloat162 hb = __floats2bfloat162_rn(__uint_as_float(w0), __uint_as_float(w1));
+        h[i] = *reinterpret_cast<uint32_t*>(&hb);
+        uint32_t r0, r1;
+        unpack2(sub2(w[i], pack2(h[i] << 16, h[i] & 0xFFFF0000u)), r0, r1);
+        __nv_bfloat162 lb = __floats2bfloat162_rn(__uint_as_float(r0), __uint_as_float(r1));
+        l[i] = *reinterpret_cast<uint32_t*>(&lb);
+    }
+    *reinterpret_cast<uint4*>(hi_dst) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo_dst) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// This thread's 16 weights of one chunk (16-byte piece kq of row `row` in a raw tile):
+// w = q * scale rounded once, as stage_w_raw, the int8 -> float step by byte permutes
+// (exact), then bf16 hi/lo into K groups 2 kq and 2 kq + 1 of the row.
+__device__ __forceinline__ void stage_w16_raw(const uint8_t* raw, uint8_t* a_hi, uint8_t* a_lo, int row, int kq) {
+    const uint4 p = *reinterpret_cast<const uint4*>(raw + (kq * TC_M + row) * 16);
+    const float sc = reinterpret_cast<const float*>(raw + TC_M * TC_KC)[(kq >> 1) * TC_M + row];
     const unsigned long long sc2 = pack2(__float_as_uint(sc), __float_as_uint(sc)), unb = q8_unbias2();
+    const uint32_t words[4] = {p.x ^ 0x80808080u, p.y ^ 0x80808080u, p.z ^ 0x80808080u, p.w ^ 0x80808080u};
 #pragma unroll
-    for (int j = 0; j < 4; j++) {  // 8 weights = one 16-byte core-matrix row per half
-        uint32_t h[4], l[4];
+    for (int g = 0; g < 2; g++) {
+        unsigned long long w[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t u = words[2 * j + (i >> 1)] ^ 0x80808080u;
-            const unsigned long long w = mul2(add2(q8_pair_biased(u, (i & 1) * 2), unb), sc2);
-            uint32_t w0, w1;
-            unpack2(w, w0, w1);
-            __nv_bfloat162 hb = __floats2bfloat162_rn(__uint_as_float(w0), __uint_as_float(w1));
-            const uint32_t hv = *reinterpret_cast<uint32_t*>(&hb);
-            uint32_t r0, r1;
-            unpack2(sub2(w, pack2(hv << 16, hv & 0xFFFF0000u)), r0, r1);
-            __nv_bfloat162 lb = __floats2bfloat162_rn(__uint_as_float(r0), __uint_as_float(r1));
-            h[i] = valid ? hv : 0u;
-            l[i] = valid ? *reinterpret_cast<uint32_t*>(&lb) : 0u;
-        }
-        *reinterpret_cast<uint4*>(a_hi + core_off(row, half * 4 + j)) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(a_lo + core_off(row, half * 4 + j)) = make_uint4(l[0], l[1], l[2], l[3]);
+        for (int i = 0; i < 4; i++) w[i] = mul2(add2(q8_pair_biased(words[2 * g + (i >> 1)], (i & 1) * 2), unb), sc2);
+        split8_store(w, a_hi + core_off(row, 2 * kq + g), a_lo + core_off(row, 2 * kq + g));
     }
 }
 
-// Epilogue of one thread's 32 token columns c_base.. of weight row n (tile n_tile); the
-// RESIDUAL kind leaves each column's sum of squares over the warp's 32 rows in red_ss.
+// Epilogue of one thread's SK_COLS token columns c_base.. of weight row n; the RESIDUAL
+// kind leaves each column's sum of squares over the warp's 32 rows in red_ss.
 __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e, float* v, int n, int c_base,
                                             const float* inv_rms, float* red_ss, int warp, int lane, bool ok) {
     const int epi = e.kind;
     if (a.norm_gain) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] *= inv_rms[c_base + j];
+        for (int j = 0; j < SK_COLS; j++) v[j] *= inv_rms[c_base + j];
     }
     const bool nrow = ok && n < a.N;
     if (epi == kEpiStore) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < SK_COLS; j++) {
             const int m = c_base + j;
             if (nrow && m < a.M) e.out[(int64_t)m * e.ldo + n] = v[j];
         }
     } else if (epi == kEpiResidual) {
+        float xo[SK_COLS];
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < SK_COLS; j++) {  // every load of the group before its stores
+            const int m = c_base + j;
+            xo[j] = (nrow && m < a.M) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < SK_COLS; j++) {
             const int m = c_base + j;
             const bool w = nrow && m < a.M;
-            const float xn = w ? e.out[(int64_t)m * e.ldo + n] + v[j] : 0.0f;
+            const float xn = w ? xo[j] + v[j] : 0.0f;
             if (w) e.out[(int64_t)m * e.ldo + n] = xn;
             if (e.ss_out) {
                 const float sq = warp_sum(xn * xn);
@@ -941,7 +956,7 @@ __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e
     } else if (epi == kEpiSwiGLU) {
         const bool even = (n & 1) == 0;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < SK_COLS; j++) {
             const int m = c_base + j;
             const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);  // w3 row next to this w1 row
             if (even && nrow && m < a.M) {
@@ -972,7 +987,7 @@ __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e
         const bool rope = kind < 2;
         const int64_t pf = e.geom.page_floats();
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < SK_COLS; j++) {
             const int m = c_base + j;
             const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);  // the rotary pair's other row
             if (m >= a.M || kind == 3) continue;
@@ -992,7 +1007,7 @@ __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e
     }
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, Epilogue e, StreamKArgs sk) {
+__global__ void __launch_bounds__(SK_THREADS, 1) tc_streamk_kernel(GemmArgs a, Epilogue e, StreamKArgs sk) {
     constexpr int NT = SK_NT;
     using S = TcSmem<NT>;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -1005,8 +1020,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
     __shared__ float red_ss[4 * NT];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool worker = warp < kIssuerWarp;
-    const int row = tid & (TC_M - 1), wg = (tid >> 7) & 1;  // weight row / TMEM lane, K half / column half
+    const bool worker = warp < kSkIssuerWarp;
+    // worker roles: weight row / TMEM lane `row` and 16-wide K piece `kq` of every chunk;
+    // activation unit (token xr, 8-wide K group xg); epilogue columns cg * SK_COLS ..
+    const int row = tid & (TC_M - 1), kq = (tid >> 7) & 3;
+    const int xr = tid >> 3, xg = tid & 7;
+    const int cg = (warp >> 2) & 3;
     const int G = gridDim.x, cta = blockIdx.x, C = sk.chunks;
     const int u0 = sk_first_unit(cta, G, sk.units);
     const int nu = sk_first_unit(cta + 1, G, sk.units) - u0;
@@ -1033,13 +1052,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
         // weights are read-only: the first tiles are requested before the dependency wait
         for (int i = 0; i < min(nu, RS); i++) fetch_raw(i);
     }
+    // token rows past the batch stay zero in every stage (staged once, skipped per unit)
+    if (worker && xr >= a.M) {
+        for (int st = 0; st < SK_STAGES; st++) {
+            *reinterpret_cast<uint4*>(stage_ptr(st, 2) + core_off(xr, xg)) = make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(stage_ptr(st, 3) + core_off(xr, xg)) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
     grid_dependency_wait();
     // 1/rms of every token row; the RMSNorm gain is applied while staging x and the 1/rms
     // to the sums (linear in x) in the epilogue
     if (a.norm_gain && worker) {
         if (a.ss_in) {
-            for (int u = tid; u < NT * 4; u += TC_WORKERS) {
-                const int r = u >> 2, p0 = u & 3;
+            if (tid < NT * 4) {
+                const int r = tid >> 2, p0 = tid & 3;
                 float ss = 0.0f;
                 if (r < a.M)
                     for (int p = p0; p < a.ss_parts; p += 4) ss += __ldcg(a.ss_in + (int64_t)p * a.ss_ld + r);
@@ -1048,7 +1074,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
                 if (p0 == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
             }
         } else {
-            for (int r = warp; r < NT; r += TC_WORKERS / 32) {
+            for (int r = warp; r < NT; r += SK_WORKERS / 32) {
                 float ss = 0.0f;
                 if (r < a.M)
                     for (int k = lane * 4; k < a.K; k += 128) {
@@ -1069,69 +1095,86 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
 
     if (worker) {
         bool ok = true;
-        const int ur = tid >> 2, ukq = tid & 3;  // activation unit: token ur, 16-wide K quarter ukq
-        float4 xn[4], gn[4];
-        auto fetch_x = [&](int i) {  // unit u0 + i's activations (and gain), one unit ahead
-            const int k = ((u0 + i) % C) * TC_KC + ukq * 16;
-            if (ur < a.M) {
-                const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)ur * a.ldx + k);
-#pragma unroll
-                for (int j = 0; j < 4; j++) xn[j] = src[j];
-            }
+        const bool xrow = xr < a.M;
+        float4 xn[2], gn[2];
+        auto fetch_x = [&](int c) {  // chunk c's activations (and gain) of this thread's unit
+            const int k = c * TC_KC + xg * 8;
+            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)xr * a.ldx + k);
+            xn[0] = src[0];
+            xn[1] = src[1];
             if (a.norm_gain) {
-#pragma unroll
-                for (int j = 0; j < 4; j++) gn[j] = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k) + j);
+                gn[0] = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k));
+                gn[1] = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k) + 1);
             }
         };
-        if (nu > 0) fetch_x(0);
-        int runs = 0, run_c0 = u0 % C;
+        int t = u0 / C, c = u0 % C;  // tile and chunk of the current unit
+        if (xrow && nu > 0) fetch_x(c);
+        int runs = 0, run_c0 = c;
         for (int it = 0; it < nu; it++) {
-            const int u = u0 + it, t = u / C, c = u % C;
             const int st = it % SK_STAGES, use = it / SK_STAGES;
-            if (c == 0) run_c0 = 0;
             // the stage was last read by the MMAs of unit it - SK_STAGES
             if (ok && use > 0 && !mbar_wait(&mma_bar[st], (use - 1) & 1, a.err)) ok = false;
             if (ok && !mbar_wait(&raw_bar[it % RS], (it / RS) & 1, a.err)) ok = false;
             if (ok) {
-                stage_w_raw2(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, stage_ptr(st, 0), stage_ptr(st, 1), row, wg,
-                             t * TC_M + row < a.N);
-                stage_x16(xn, a.norm_gain ? reinterpret_cast<const float*>(gn) : nullptr, ur < a.M, stage_ptr(st, 2),
-                          stage_ptr(st, 3), ur, ukq);
+                stage_w16_raw(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, stage_ptr(st, 0), stage_ptr(st, 1), row, kq);
+                if (xrow) {
+                    unsigned long long w[4];
+                    if (a.norm_gain) {
+                        w[0] = mul2(pack2(__float_as_uint(xn[0].x), __float_as_uint(xn[0].y)),
+                                    pack2(__float_as_uint(gn[0].x), __float_as_uint(gn[0].y)));
+                        w[1] = mul2(pack2(__float_as_uint(xn[0].z), __float_as_uint(xn[0].w)),
+                                    pack2(__float_as_uint(gn[0].z), __float_as_uint(gn[0].w)));
+                        w[2] = mul2(pack2(__float_as_uint(xn[1].x), __float_as_uint(xn[1].y)),
+                                    pack2(__float_as_uint(gn[1].x), __float_as_uint(gn[1].y)));
+                        w[3] = mul2(pack2(__float_as_uint(xn[1].z), __float_as_uint(xn[1].w)),
+                                    pack2(__float_as_uint(gn[1].z), __float_as_uint(gn[1].w)));
+                    } else {
+                        w[0] = pack2(__float_as_uint(xn[0].x), __float_as_uint(xn[0].y));
+                        w[1] = pack2(__float_as_uint(xn[0].z), __float_as_uint(xn[0].w));
+                        w[2] = pack2(__float_as_uint(xn[1].x), __float_as_uint(xn[1].y));
+                        w[3] = pack2(__float_as_uint(xn[1].z), __float_as_uint(xn[1].w));
+                    }
+                    split8_store(w, stage_ptr(st, 2) + core_off(xr, xg), stage_ptr(st, 3) + core_off(xr, xg));
+                }
             }
-            if (it + 1 < nu) fetch_x(it + 1);
+            // the next unit's tile and chunk; its activations load while this one is multiplied
+            const bool run_end = it == nu - 1 || c == C - 1;
+            const int t_cur = t, c_cur = c;
+            if (++c == C) { c = 0; t++; }
+            if (xrow && it + 1 < nu) fetch_x(c);
             fence_async_smem();
-            named_arrive(1 + st, TC_THREADS);
-            if (it != nu - 1 && c != C - 1) continue;
+            named_arrive(1 + st, SK_THREADS);
+            if (!run_end) continue;
 
             // end of a run: its accumulator, then a partial or the tile's epilogue
             if (ok && !mbar_wait(&acc_bar, runs & 1, a.err)) ok = false;
             runs++;
             tc_fence_after();
-            float v[32];
-            tmem_ld32(tl + wg * 32, v);
+            float v[SK_COLS];
+            tmem_ld16(tl + cg * SK_COLS, v);
             if (it == nu - 1) grid_dependents_launch();
             if (run_c0 > 0) {
                 // the tile belongs to an earlier CTA: [cta][column][row] partial, then the flag
-                float* dst = a.sk_partial + ((size_t)cta * NT + wg * 32) * TC_M + row;
+                float* dst = a.sk_partial + ((size_t)cta * NT + cg * SK_COLS) * TC_M + row;
 #pragma unroll
-                for (int j = 0; j < 32; j++) __stcg(dst + (size_t)j * TC_M, ok ? v[j] : 0.0f);
+                for (int j = 0; j < SK_COLS; j++) __stcg(dst + (size_t)j * TC_M, ok ? v[j] : 0.0f);
                 __threadfence();
-                named_sync(kSkWorkerBar, TC_WORKERS);
+                named_sync(kSkWorkerBar, SK_WORKERS);
                 if (tid == 0) st_release_gpu(a.sk_flags + cta, 1);
             } else {
-                const int last = c == C - 1 ? cta : sk_cta_of(t * C + C - 1, G, sk.units);
+                const int last = c_cur == C - 1 ? cta : sk_cta_of(t_cur * C + C - 1, G, sk.units);
                 if (last > cta) {  // the rest of the tile is in the shares of CTAs cta+1..last
                     if (tid == 0) {
                         bool all = true;
                         for (int p = cta + 1; p <= last && all; p++) all = sk_wait_flag(a.sk_flags + p, a.err);
                         partners_ok = all;
                     }
-                    named_sync(kSkWorkerBar, TC_WORKERS);
+                    named_sync(kSkWorkerBar, SK_WORKERS);
                     if (partners_ok) {
                         for (int p = cta + 1; p <= last; p++) {
-                            const float* src = a.sk_partial + ((size_t)p * NT + wg * 32) * TC_M + row;
+                            const float* src = a.sk_partial + ((size_t)p * NT + cg * SK_COLS) * TC_M + row;
 #pragma unroll
-                            for (int j = 0; j < 32; j++) v[j] += __ldcg(src + (size_t)j * TC_M);
+                            for (int j = 0; j < SK_COLS; j++) v[j] += __ldcg(src + (size_t)j * TC_M);
                         }
                         if (tid == 0)
                             for (int p = cta + 1; p <= last; p++) atomicExch(a.sk_flags + p, 0);
@@ -1139,28 +1182,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
                         ok = false;
                     }
                 }
-                sk_epilogue(a, e, v, t * TC_M + row, wg * 32, inv_rms, red_ss, warp, lane, ok);
+                sk_epilogue(a, e, v, t_cur * TC_M + row, cg * SK_COLS, inv_rms, red_ss, warp, lane, ok);
                 if (e.kind == kEpiResidual && e.ss_out) {  // this tile's share of the next RMSNorm
-                    named_sync(kSkWorkerBar, TC_WORKERS);
+                    named_sync(kSkWorkerBar, SK_WORKERS);
                     if (tid < NT && tid < a.M)
-                        e.ss_out[(int64_t)t * e.ss_ld + tid] =
+                        e.ss_out[(int64_t)t_cur * e.ss_ld + tid] =
                             red_ss[tid] + red_ss[NT + tid] + red_ss[2 * NT + tid] + red_ss[3 * NT + tid];
                 }
             }
+            run_c0 = 0;  // every later run starts at a tile's chunk 0
             // the accumulator's loads come before the next run's MMAs (ordered by the next
             // unit's named barrier)
             tc_fence_before();
         }
     } else {
         // issuer warp: lane 0 refills the raw ring and issues every unit's MMAs
+        int c = u0 % C;
         for (int it = 0; it < nu; it++) {
-            const int c = (u0 + it) % C;
             const int st = it % SK_STAGES;
             // the workers converted unit it - 1 before the barrier this warp passed last
             // iteration, so its slot takes unit it - 1 + RS
             if (lane == 0 && it >= 1 && it - 1 + RS < nu) fetch_raw(it - 1 + RS);
             __syncwarp();
-            named_sync(1 + st, TC_THREADS);
+            named_sync(1 + st, SK_THREADS);
             if (lane == 0) {
                 tc_fence_after();
                 issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3),
@@ -1169,6 +1213,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
                 if (it == nu - 1 || c == C - 1) umma_commit(&acc_bar);
             }
             __syncwarp();
+            if (++c == C) c = 0;
         }
         grid_dependents_launch();
     }
@@ -1407,7 +1452,7 @@ void tc_launch_streamk(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     const int budget = tc_ensure_smem(tc_streamk_kernel);
     sk.raw_off = SK_STAGES * TcSmem<SK_NT>::STAGE;
     sk.raw_slots = std::min(TC_RAW_MAX, (budget - sk.raw_off) / (int)TC_RAW_BYTES);
-    launch_ex(tc_streamk_kernel, dim3(grid), dim3(TC_THREADS), sk.raw_off + sk.raw_slots * (int)TC_RAW_BYTES, s, 1, a,
+    launch_ex(tc_streamk_kernel, dim3(grid), dim3(SK_THREADS), sk.raw_off + sk.raw_slots * (int)TC_RAW_BYTES, s, 1, a,
               e, sk);
 }
 

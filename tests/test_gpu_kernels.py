@@ -60,6 +60,44 @@ def test_q8_matmul(torch_cuda, restatement, M, mode, NK):
             assert_close(got, want, rtol=1e-3, atol=1e-4 * scale, what=f"q8 M={M} mode={mode}")
 
 
+_LARGE = {}
+
+
+def _large_q8(N, K):
+    """Seeded Q8_0 weights of one large shape, made once per session."""
+    if (N, K) not in _LARGE:
+        rng = np.random.default_rng(N + K)
+        w_aos = synth.quantize_q8((rng.standard_normal(N * K) * 0.02).astype(np.float32))
+        _LARGE.clear()
+        _LARGE[(N, K)] = (w_aos, *_aos_to_soa(w_aos, N, K))
+    return _LARGE[(N, K)]
+
+
+@pytest.mark.parametrize("NK", [(12288, 4096), (4096, 11008), (22016, 4096), (12290, 4096), (4098, 2048)])
+@pytest.mark.parametrize("M", [1, 2])
+def test_q8_matvec_large(torch_cuda, restatement, M, NK):
+    """One and two token rows over the 7B shape's projection matrices, a row count that is
+    not a multiple of 4 and one that is only even: the ring matvec (units of 2-8 whole
+    rows streamed through shared memory, activations in registers, row-pair partials
+    joined in shared memory) against the restatement, to the fp32 bar of the matvec."""
+    torch = torch_cuda
+    N, K = NK
+    w_aos, q, s = _large_q8(N, K)
+    x = np.random.default_rng(M + N).standard_normal((M, K)).astype(np.float32)
+    want = restatement.q8_matmul(x, w_aos, K, N)
+    dq, ds, dx = (torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), torch.from_numpy(x).cuda())
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    got = []
+    for _ in range(2):
+        rc = lib().nr_q8_matmul(dx.data_ptr(), dq.data_ptr(), ds.data_ptr(), out.data_ptr(), M, N, K, NR_Q8_FIXED,
+                                C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0
+        torch.cuda.synchronize()
+        got.append(out.cpu().numpy())
+    assert np.array_equal(got[0], got[1])  # a fixed summation order
+    assert_close(got[0], want, rtol=1e-4, atol=1e-5, what=f"q8 matvec M={M} {N}x{K}")
+
+
 def _engine_pools(kref, vref, n_layers, n_kv, hd):
     """[page][layer][16][kv_dim] (reference) -> [page][layer][kv_head][16][hd] (engine)."""
     P = kref.shape[0]
