@@ -310,16 +310,17 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
             }
             NR_CUDA(cudaStreamSynchronize(stream_));
             NR_CUDA(cudaGetLastError());
-            // batches of up to 64 rows stream the raw tiles with the stream-K kernel
+            // batches of 3-64 rows take the stream-K kernel: over the hi/lo tiles where they
+            // exist (no conversion on chip), else over the raw tiles
             if (tc_streamk_enabled()) {
                 int dev = 0, sms = 0;
                 NR_CUDA(cudaGetDevice(&dev));
                 NR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
                 sk_capacity_ = std::max(1, sms);
-                const size_t sk_bytes = tc_streamk_scratch_bytes(sk_capacity_);
+                const size_t sk_bytes = tc_streamk_scratch_bytes(sk_capacity_, std::max(D, H));
                 NR_CUDA(cudaMalloc(&d_sk_, sk_bytes));
                 NR_CUDA(cudaMemset(d_sk_, 0, sk_bytes));  // the flags start clear
-                wide_rows_ = 65;
+                wide_rows_ = 3;
             }
         }
     }
@@ -328,10 +329,7 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
 
 void Engine::attach_streamk(GemmArgs& g) const {
     if (!d_sk_) return;
-    g.sk_partial = static_cast<float*>(d_sk_);
-    g.sk_flags = reinterpret_cast<int*>(static_cast<uint8_t*>(d_sk_) + tc_streamk_scratch_bytes(sk_capacity_) -
-                                        (size_t)sk_capacity_ * sizeof(int));
-    g.sk_capacity = sk_capacity_;
+    tc_streamk_bind(g, d_sk_, sk_capacity_, std::max(shape_.dim, shape_.hidden));
 }
 
 int Engine::init_device(const uint8_t* file, size_t size) {

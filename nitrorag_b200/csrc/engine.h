@@ -155,7 +155,7 @@ private:
     void* d_attn_ws_ = nullptr;
     // large projections have both raw Q8 tiles and hi/lo tiles; batches of at least
     // wide_rows_ rows read the hi/lo tiles: kWideTileRows for the cluster-split kernel,
-    // beyond the stream-K kernel's 64 rows when that takes the raw tiles
+    // 3 when the stream-K kernel takes batches of 3-64 rows (1-2 rows take the matvec)
     bool wide_tiles_ = false;
     static constexpr int kWideTileRows = 32;
     int wide_rows_ = kWideTileRows;

@@ -830,13 +830,17 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     if (warp == 0) tmem_dealloc(tmem, NT);
 }
 
-// ------------------------------------------------------------------ stream-K over raw Q8 tiles
-// Large Q8 projections at decode batches (up to 64 token rows) are HBM-bound, but their
+// ------------------------------------------------------------------ stream-K, batches of up to 64 rows
+// Large Q8 projections at decode batches (3-64 token rows) are HBM-bound, but their
 // 128-row tiles are too few to fill 148 SMs evenly (96 tiles for the 7B shape's q,k,v,
 // 172 for w1/w3), and a cluster K split cannot keep every cluster resident.  So one CTA
 // per SM takes an equal contiguous share of the (tile, 64-wide K chunk) units in
-// tile-major order (the raw tiles' order in memory), streams them through the bulk-copy
-// ring, converts each to bf16 hi/lo and accumulates each tile's run of chunks in TMEM.
+// tile-major order (the weight tiles' order in memory) and accumulates each tile's run of
+// chunks in TMEM.  Operands arrive by bulk copy, issued by one thread several units ahead
+// of the MMAs: the weights as pre-split hi/lo tiles straight into an A slot, or as raw Q8
+// tiles into a ring that 16 worker warps convert into A slots; the activations as bf16
+// hi/lo tiles that tc_split_x_kernel writes once per launch into scratch (the RMSNorm
+// gain applied), so no unit waits on a global-load round trip.
 // A share starts inside a tile at most once: the partial sums of that first run go to
 // global scratch and a release flag is set.  The CTA whose share holds the tile's chunk 0
 // (where that run ends its share) waits for the flags of the CTAs after it that cover the
@@ -847,14 +851,15 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
 struct StreamKArgs {
     int units;      // n_tiles x chunks
     int chunks;     // K / 64
-    int stages;     // operand stages
-    int raw_slots;  // raw-tile ring slots
-    int raw_off;    // byte offset of the ring in dynamic shared memory
+    int raw_slots;  // raw-tile ring slots (raw tiles only)
+    int raw_off;    // byte offset of the raw ring in dynamic shared memory
+    int xrows;      // activation rows copied per unit: the batch rounded up to 8
 };
 
 constexpr int SK_NT = 64;        // token columns per tile (the batch, zero-padded)
-constexpr int SK_STAGES = 2;
-constexpr int kSkWorkerBar = 8;  // named barrier of the 256 staging / epilogue threads
+constexpr int SK_SB = 4;         // activation slots
+constexpr uint32_t SK_XTILE = 2u * SK_NT * TC_KC * 2u;  // hi + lo halves of one 64 x 64 activation tile
+constexpr int kSkWorkerBar = 8;  // named barrier of the worker warps (the stages use 1 and 2)
 
 __host__ __device__ inline int sk_first_unit(int cta, int grid, int units) { return (int)((int64_t)cta * units / grid); }
 
@@ -879,8 +884,10 @@ __device__ __forceinline__ bool sk_wait_flag(const int* f, int* err) {
 }
 
 constexpr int SK_WORKERS = 512;               // conversion / epilogue threads: 16 warps
-constexpr int SK_THREADS = SK_WORKERS + 32;   // + the warp that refills the ring and issues the MMAs
-constexpr int kSkIssuerWarp = SK_WORKERS / 32;
+// + a producer warp (bulk copies) and two warps that issue the MMAs, alternating units
+constexpr int SK_THREADS = SK_WORKERS + 3 * 32;
+constexpr int kSkProducerWarp = SK_WORKERS / 32;
+constexpr int kSkBarThreads = SK_WORKERS + 32;  // a stage barrier: the workers and one issuer warp
 constexpr int SK_COLS = SK_NT / (SK_WORKERS / TC_M);  // epilogue columns per thread (16)
 
 // Eight fp32 values -> bf16 hi/lo (hi = bf16(v), lo = bf16(v - hi)), one 16-byte core-matrix
@@ -919,10 +926,21 @@ __device__ __forceinline__ void stage_w16_raw(const uint8_t* raw, uint8_t* a_hi,
     }
 }
 
-// Epilogue of one thread's SK_COLS token columns c_base.. of weight row n; the RESIDUAL
-// kind leaves each column's sum of squares over the warp's 32 rows in red_ss.
-__device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e, float* v, int n, int c_base,
-                                            const float* inv_rms, float* red_ss, int warp, int lane, bool ok) {
+// The RESIDUAL epilogue's inputs (the residual rows) of one thread's columns, loaded early.
+__device__ __forceinline__ void sk_residual_in(const GemmArgs& a, const Epilogue& e, float* xo, int n, int c_base) {
+#pragma unroll
+    for (int j = 0; j < SK_COLS; j++) {
+        const int m = c_base + j;
+        xo[j] = (e.kind == kEpiResidual && n < a.N && m < a.M) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
+    }
+}
+
+// Epilogue of one thread's SK_COLS token columns c_base.. of weight row n (xo: the residual
+// inputs from sk_residual_in); the RESIDUAL kind leaves each column's sum of squares over
+// the warp's 32 rows in red_ss.
+__device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e, float* v, const float* xo, int n,
+                                            int c_base, const float* inv_rms, float* red_ss, int warp, int lane,
+                                            bool ok) {
     const int epi = e.kind;
     if (a.norm_gain) {
 #pragma unroll
@@ -936,12 +954,6 @@ __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e
             if (nrow && m < a.M) e.out[(int64_t)m * e.ldo + n] = v[j];
         }
     } else if (epi == kEpiResidual) {
-        float xo[SK_COLS];
-#pragma unroll
-        for (int j = 0; j < SK_COLS; j++) {  // every load of the group before its stores
-            const int m = c_base + j;
-            xo[j] = (nrow && m < a.M) ? e.out[(int64_t)m * e.ldo + n] : 0.0f;
-        }
 #pragma unroll
         for (int j = 0; j < SK_COLS; j++) {
             const int m = c_base + j;
@@ -1007,61 +1019,147 @@ __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e
     }
 }
 
+// The activations of one stream-K launch as bf16 hi/lo tiles in the UMMA layout, one
+// 16 KB tile per 64-wide K chunk ([chunk][hi 8 KB][lo 8 KB]), x times the RMSNorm gain;
+// rows from the batch up to the next multiple of 8 are zero.  One thread per (chunk,
+// row, 8-wide K group).
+__global__ void __launch_bounds__(256) tc_split_x_kernel(GemmArgs a, int xrows) {
+    grid_dependency_wait();  // x comes from the previous kernel
+    grid_dependents_launch();
+    const int chunks = a.K / TC_KC;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (int64_t)chunks * xrows * 8) return;
+    const int c = (int)(t / (xrows * 8)), rem = (int)(t % (xrows * 8));
+    const int r = rem >> 3, g = rem & 7;
+    const int k = c * TC_KC + g * 8;
+    unsigned long long w[4] = {0ull, 0ull, 0ull, 0ull};
+    if (r < a.M) {
+        const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)r * a.ldx + k);
+        float4 x0 = src[0], x1 = src[1];
+        if (a.norm_gain) {
+            const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k));
+            const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k) + 1);
+            x0.x *= g0.x; x0.y *= g0.y; x0.z *= g0.z; x0.w *= g0.w;
+            x1.x *= g1.x; x1.y *= g1.y; x1.z *= g1.z; x1.w *= g1.w;
+        }
+        w[0] = pack2(__float_as_uint(x0.x), __float_as_uint(x0.y));
+        w[1] = pack2(__float_as_uint(x0.z), __float_as_uint(x0.w));
+        w[2] = pack2(__float_as_uint(x1.x), __float_as_uint(x1.y));
+        w[3] = pack2(__float_as_uint(x1.z), __float_as_uint(x1.w));
+    }
+    uint8_t* tile = a.sk_xs + (size_t)c * SK_XTILE;
+    split8_store(w, tile + core_off(r, g), tile + SK_XTILE / 2 + core_off(r, g));
+}
+
+// The 12 MMAs of one 64-wide K chunk (hi*hi + hi*lo + lo*hi per 16-wide K step) from
+// descriptors made once per slot (a K step is 256 B further: +16 in the address field).
+__device__ __forceinline__ void issue_unit_mmas(uint32_t d, uint32_t idesc, uint64_t dah, uint64_t dal, uint64_t dbh,
+                                                uint64_t dbl, bool first) {
+#pragma unroll
+    for (int kk = 0; kk < TC_KC / 16; kk++) {
+        const uint64_t o = (uint64_t)kk * 16;
+        umma_bf16(d, dah + o, dbh + o, idesc, (!first || kk > 0) ? 1u : 0u);
+        umma_bf16(d, dah + o, dbl + o, idesc, 1u);
+        umma_bf16(d, dal + o, dbh + o, idesc, 1u);
+    }
+}
+
+// WT: the weights come as pre-split hi/lo tiles (tc_tile_weights), bulk-copied straight
+// into an A slot (no conversion, 4 slots); otherwise as raw Q8 tiles that the workers
+// convert into 2 A slots.  Warps: 0-15 workers (raw conversion, epilogues), 16 producer
+// (every bulk copy), 17-18 MMA issuers: unit it goes to issuer it % 2, which accumulates
+// it into its own TMEM accumulator of the run (4 x 64 columns: 2 runs in flight x 2
+// issuers); the epilogue adds the run's two accumulators in issuer order.
+template <bool WT>
 __global__ void __launch_bounds__(SK_THREADS, 1) tc_streamk_kernel(GemmArgs a, Epilogue e, StreamKArgs sk) {
     constexpr int NT = SK_NT;
-    using S = TcSmem<NT>;
+    constexpr int SA = WT ? 4 : 2;  // weight (A) slots
+    constexpr int SB = SK_SB;       // activation (B) slots
+    constexpr uint32_t A_BYTES = TC_M * TC_KC * 2;  // one bf16 half of a weight tile
+    constexpr uint32_t B_BYTES = NT * TC_KC * 2;    // one bf16 half of an activation tile
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ uint64_t mma_bar[SK_STAGES];  // the stage's MMAs are done
-    __shared__ uint64_t raw_bar[TC_RAW_MAX];  // the slot's bulk copy has landed
-    __shared__ uint64_t acc_bar;              // a run's MMAs are done: its accumulator is complete
+    __shared__ uint64_t full_bar[SB];          // unit in B slot s: its tiles have landed (WT: A and B)
+    __shared__ uint64_t mma_bar[SB];           // unit in B slot s: its MMAs are done
+    __shared__ uint64_t raw_bar[TC_RAW_MAX];   // raw: the ring slot's tile has landed
+    __shared__ uint64_t raw_free[TC_RAW_MAX];  // raw: every worker warp has converted the slot
+    // two runs in flight: full = both issuers' MMAs of the run are done, free = every
+    // worker warp has loaded the run's accumulators
+    __shared__ uint64_t acc_full[2], acc_free[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int partners_ok;
     __shared__ float inv_rms[NT];
     __shared__ float red_ss[4 * NT];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool worker = warp < kSkIssuerWarp;
+    const bool worker = warp < kSkProducerWarp;
     // worker roles: weight row / TMEM lane `row` and 16-wide K piece `kq` of every chunk;
-    // activation unit (token xr, 8-wide K group xg); epilogue columns cg * SK_COLS ..
+    // epilogue columns cg * SK_COLS ..
     const int row = tid & (TC_M - 1), kq = (tid >> 7) & 3;
-    const int xr = tid >> 3, xg = tid & 7;
     const int cg = (warp >> 2) & 3;
     const int G = gridDim.x, cta = blockIdx.x, C = sk.chunks;
     const int u0 = sk_first_unit(cta, G, sk.units);
     const int nu = sk_first_unit(cta + 1, G, sk.units) - u0;
     const int RS = sk.raw_slots;
-    auto stage_ptr = [&](int st, int part) {
-        return smem + st * S::STAGE + (part < 2 ? part * S::A_BYTES : 2 * S::A_BYTES + (part - 2) * S::B_BYTES);
-    };
+    uint8_t* a_slots = smem;                     // [SA][hi | lo]
+    uint8_t* b_slots = smem + SA * 2 * A_BYTES;  // [SB][hi | lo]
     uint8_t* raw_ring = smem + sk.raw_off;
+    auto a_ptr = [&](int s) { return a_slots + (size_t)s * 2 * A_BYTES; };
+    auto b_ptr = [&](int s) { return b_slots + (size_t)s * 2 * B_BYTES; };
 
     if (warp == 0) {
-        tmem_alloc(&tmem_slot, NT);
+        tmem_alloc(&tmem_slot, 4 * NT);
         tmem_relinquish();
     }
-    auto fetch_raw = [&](int i) {  // unit u0 + i -> slot i % RS
-        uint64_t* bar = &raw_bar[i % RS];
-        mbar_arrive_expect_tx(bar, TC_RAW_BYTES);
-        bulk_g2s(raw_ring + (size_t)(i % RS) * TC_RAW_BYTES, a.wr + (size_t)(u0 + i) * TC_RAW_BYTES, TC_RAW_BYTES, bar);
+    auto fetch_w = [&](int i) {  // unit u0 + i's weights: A slot i % SA, or (raw) ring slot i % RS
+        if (WT) {
+            uint64_t* bar = &full_bar[i % SB];
+            mbar_arrive_expect_tx(bar, TC_TILE_BYTES);
+            bulk_g2s(a_ptr(i % SA), a.wt + (size_t)(u0 + i) * TC_TILE_BYTES, TC_TILE_BYTES, bar);
+        } else {
+            mbar_arrive_expect_tx(&raw_bar[i % RS], TC_RAW_BYTES);
+            bulk_g2s(raw_ring + (size_t)(i % RS) * TC_RAW_BYTES, a.wr + (size_t)(u0 + i) * TC_RAW_BYTES, TC_RAW_BYTES,
+                     &raw_bar[i % RS]);
+        }
+    };
+    const uint32_t xbytes = (uint32_t)sk.xrows * 128;  // rows x 64 bf16 of one half
+    auto fetch_x = [&](int i) {  // unit u0 + i's activation tile (chunk (u0 + i) % C): B slot i % SB
+        const uint8_t* src = a.sk_xs + (size_t)((u0 + i) % C) * SK_XTILE;
+        uint64_t* bar = &full_bar[i % SB];
+        mbar_arrive_expect_tx(bar, 2 * xbytes);
+        if (xbytes == B_BYTES) {
+            bulk_g2s(b_ptr(i % SB), src, 2 * B_BYTES, bar);
+        } else {
+            bulk_g2s(b_ptr(i % SB), src, xbytes, bar);
+            bulk_g2s(b_ptr(i % SB) + B_BYTES, src + B_BYTES, xbytes, bar);
+        }
     };
     if (tid == 0) {
-        for (int st = 0; st < SK_STAGES; st++) mbar_init(&mma_bar[st], 1);
-        for (int r = 0; r < TC_RAW_MAX; r++) mbar_init(&raw_bar[r], 1);
-        mbar_init(&acc_bar, 1);
+        for (int s = 0; s < SB; s++) {
+            mbar_init(&full_bar[s], WT ? 2 : 1);  // WT: the weight and the activation copies arrive
+            mbar_init(&mma_bar[s], 1);
+        }
+        for (int r = 0; r < TC_RAW_MAX; r++) {
+            mbar_init(&raw_bar[r], 1);
+            mbar_init(&raw_free[r], SK_WORKERS / 32);
+        }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&acc_full[s], 2);
+            mbar_init(&acc_free[s], SK_WORKERS / 32);
+        }
         fence_barrier_init();
         // weights are read-only: the first tiles are requested before the dependency wait
-        for (int i = 0; i < min(nu, RS); i++) fetch_raw(i);
+        for (int i = 0; i < min(nu, WT ? SA : RS); i++) fetch_w(i);
     }
-    // token rows past the batch stay zero in every stage (staged once, skipped per unit)
-    if (worker && xr >= a.M) {
-        for (int st = 0; st < SK_STAGES; st++) {
-            *reinterpret_cast<uint4*>(stage_ptr(st, 2) + core_off(xr, xg)) = make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(stage_ptr(st, 3) + core_off(xr, xg)) = make_uint4(0u, 0u, 0u, 0u);
+    // activation rows past the copied ones stay zero in every B slot
+    if (worker)
+        for (int i = tid; i < SB * 2 * (NT - sk.xrows) * 8; i += SK_WORKERS) {
+            const int s = i / (2 * (NT - sk.xrows) * 8), rem = i % (2 * (NT - sk.xrows) * 8);
+            const int half = rem / ((NT - sk.xrows) * 8), r = sk.xrows + (rem % ((NT - sk.xrows) * 8)) / 8, g = rem % 8;
+            *reinterpret_cast<uint4*>(b_ptr(s) + half * B_BYTES + core_off(r, g)) = make_uint4(0u, 0u, 0u, 0u);
         }
-    }
     grid_dependency_wait();
-    // 1/rms of every token row; the RMSNorm gain is applied while staging x and the 1/rms
-    // to the sums (linear in x) in the epilogue
+    // 1/rms of every token row; the RMSNorm gain is in the activation tiles and the 1/rms
+    // scales the sums (linear in x) in the epilogue
     if (a.norm_gain && worker) {
         if (a.ss_in) {
             if (tid < NT * 4) {
@@ -1086,6 +1184,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
             }
         }
     }
+    fence_async_smem();  // the zeroed B rows, for the MMAs
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -1095,63 +1194,48 @@ __global__ void __launch_bounds__(SK_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
 
     if (worker) {
         bool ok = true;
-        const bool xrow = xr < a.M;
-        float4 xn[2], gn[2];
-        auto fetch_x = [&](int c) {  // chunk c's activations (and gain) of this thread's unit
-            const int k = c * TC_KC + xg * 8;
-            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)xr * a.ldx + k);
-            xn[0] = src[0];
-            xn[1] = src[1];
-            if (a.norm_gain) {
-                gn[0] = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k));
-                gn[1] = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k) + 1);
-            }
-        };
         int t = u0 / C, c = u0 % C;  // tile and chunk of the current unit
-        if (xrow && nu > 0) fetch_x(c);
-        int runs = 0, run_c0 = c;
+        int runs = 0, run_c0 = c, run_first = 0;
         for (int it = 0; it < nu; it++) {
-            const int st = it % SK_STAGES, use = it / SK_STAGES;
-            // the stage was last read by the MMAs of unit it - SK_STAGES
-            if (ok && use > 0 && !mbar_wait(&mma_bar[st], (use - 1) & 1, a.err)) ok = false;
-            if (ok && !mbar_wait(&raw_bar[it % RS], (it / RS) & 1, a.err)) ok = false;
-            if (ok) {
-                stage_w16_raw(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, stage_ptr(st, 0), stage_ptr(st, 1), row, kq);
-                if (xrow) {
-                    unsigned long long w[4];
-                    if (a.norm_gain) {
-                        w[0] = mul2(pack2(__float_as_uint(xn[0].x), __float_as_uint(xn[0].y)),
-                                    pack2(__float_as_uint(gn[0].x), __float_as_uint(gn[0].y)));
-                        w[1] = mul2(pack2(__float_as_uint(xn[0].z), __float_as_uint(xn[0].w)),
-                                    pack2(__float_as_uint(gn[0].z), __float_as_uint(gn[0].w)));
-                        w[2] = mul2(pack2(__float_as_uint(xn[1].x), __float_as_uint(xn[1].y)),
-                                    pack2(__float_as_uint(gn[1].x), __float_as_uint(gn[1].y)));
-                        w[3] = mul2(pack2(__float_as_uint(xn[1].z), __float_as_uint(xn[1].w)),
-                                    pack2(__float_as_uint(gn[1].z), __float_as_uint(gn[1].w)));
-                    } else {
-                        w[0] = pack2(__float_as_uint(xn[0].x), __float_as_uint(xn[0].y));
-                        w[1] = pack2(__float_as_uint(xn[0].z), __float_as_uint(xn[0].w));
-                        w[2] = pack2(__float_as_uint(xn[1].x), __float_as_uint(xn[1].y));
-                        w[3] = pack2(__float_as_uint(xn[1].z), __float_as_uint(xn[1].w));
-                    }
-                    split8_store(w, stage_ptr(st, 2) + core_off(xr, xg), stage_ptr(st, 3) + core_off(xr, xg));
-                }
+            if (!WT) {
+                // the A slot was last read by the MMAs of unit it - SA
+                const int prev = it - SA;
+                if (ok && prev >= 0 && !mbar_wait(&mma_bar[prev % SB], (prev / SB) & 1, a.err)) ok = false;
+                if (ok && !mbar_wait(&raw_bar[it % RS], (it / RS) & 1, a.err)) ok = false;
+                if (ok)
+                    stage_w16_raw(raw_ring + (size_t)(it % RS) * TC_RAW_BYTES, a_ptr(it % SA), a_ptr(it % SA) + A_BYTES,
+                                  row, kq);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_free[it % RS]);  // the producer may refill the slot
+                named_arrive(1 + it % 2, kSkBarThreads);         // the unit's issuer may start
             }
-            // the next unit's tile and chunk; its activations load while this one is multiplied
             const bool run_end = it == nu - 1 || c == C - 1;
             const int t_cur = t, c_cur = c;
             if (++c == C) { c = 0; t++; }
-            if (xrow && it + 1 < nu) fetch_x(c);
-            fence_async_smem();
-            named_arrive(1 + st, SK_THREADS);
             if (!run_end) continue;
 
-            // end of a run: its accumulator, then a partial or the tile's epilogue
-            if (ok && !mbar_wait(&acc_bar, runs & 1, a.err)) ok = false;
+            // end of a run: load its accumulators (the first unit's issuer, then the other's
+            // when the run has two or more units), hand them back to the issuers, then a
+            // partial or the tile's epilogue
+            const int reg = runs & 1, i0 = run_first & 1;
+            if (ok && !mbar_wait(&acc_full[reg], (runs >> 1) & 1, a.err)) ok = false;
             runs++;
             tc_fence_after();
-            float v[SK_COLS];
-            tmem_ld16(tl + cg * SK_COLS, v);
+            float v[SK_COLS], w2[SK_COLS];
+            tmem_ld16(tl + (reg * 2 + 0) * NT + cg * SK_COLS, v);
+            tmem_ld16(tl + (reg * 2 + 1) * NT + cg * SK_COLS, w2);
+            if (it > run_first) {  // issuer 1-i0 has units in the run too: add in issuer order
+#pragma unroll
+                for (int j = 0; j < SK_COLS; j++) v[j] += w2[j];
+            } else if (i0 == 1) {
+#pragma unroll
+                for (int j = 0; j < SK_COLS; j++) v[j] = w2[j];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_free[reg]);
+            run_first = it + 1;
             if (it == nu - 1) grid_dependents_launch();
             if (run_c0 > 0) {
                 // the tile belongs to an earlier CTA: [cta][column][row] partial, then the flag
@@ -1163,26 +1247,38 @@ __global__ void __launch_bounds__(SK_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
                 if (tid == 0) st_release_gpu(a.sk_flags + cta, 1);
             } else {
                 const int last = c_cur == C - 1 ? cta : sk_cta_of(t_cur * C + C - 1, G, sk.units);
+                float xo[SK_COLS];  // requested before the partners' partials arrive
+                sk_residual_in(a, e, xo, t_cur * TC_M + row, cg * SK_COLS);
                 if (last > cta) {  // the rest of the tile is in the shares of CTAs cta+1..last
-                    if (tid == 0) {
-                        bool all = true;
-                        for (int p = cta + 1; p <= last && all; p++) all = sk_wait_flag(a.sk_flags + p, a.err);
-                        partners_ok = all;
-                    }
+                    // one thread per partner polls its flag (the polls overlap)
+                    if (tid == 0) partners_ok = 1;
+                    named_sync(kSkWorkerBar, SK_WORKERS);
+                    if (tid < last - cta && !sk_wait_flag(a.sk_flags + cta + 1 + tid, a.err)) partners_ok = 0;
                     named_sync(kSkWorkerBar, SK_WORKERS);
                     if (partners_ok) {
-                        for (int p = cta + 1; p <= last; p++) {
-                            const float* src = a.sk_partial + ((size_t)p * NT + cg * SK_COLS) * TC_M + row;
+                        // partials added in CTA order, two partners' loads in flight at a time
+                        for (int p = cta + 1; p <= last; p += 2) {
+                            const bool two = p + 1 <= last;
+                            const float* s0 = a.sk_partial + ((size_t)p * NT + cg * SK_COLS) * TC_M + row;
+                            const float* s1 = s0 + (size_t)NT * TC_M;
+                            float pa[SK_COLS], pb[SK_COLS];
 #pragma unroll
-                            for (int j = 0; j < SK_COLS; j++) v[j] += __ldcg(src + (size_t)j * TC_M);
+                            for (int j = 0; j < SK_COLS; j++) pa[j] = __ldcg(s0 + (size_t)j * TC_M);
+#pragma unroll
+                            for (int j = 0; j < SK_COLS; j++) pb[j] = two ? __ldcg(s1 + (size_t)j * TC_M) : 0.0f;
+#pragma unroll
+                            for (int j = 0; j < SK_COLS; j++) v[j] += pa[j];
+                            if (two) {
+#pragma unroll
+                                for (int j = 0; j < SK_COLS; j++) v[j] += pb[j];
+                            }
                         }
-                        if (tid == 0)
-                            for (int p = cta + 1; p <= last; p++) atomicExch(a.sk_flags + p, 0);
+                        if (tid < last - cta) atomicExch(a.sk_flags + cta + 1 + tid, 0);
                     } else {
                         ok = false;
                     }
                 }
-                sk_epilogue(a, e, v, t_cur * TC_M + row, cg * SK_COLS, inv_rms, red_ss, warp, lane, ok);
+                sk_epilogue(a, e, v, xo, t_cur * TC_M + row, cg * SK_COLS, inv_rms, red_ss, warp, lane, ok);
                 if (e.kind == kEpiResidual && e.ss_out) {  // this tile's share of the next RMSNorm
                     named_sync(kSkWorkerBar, SK_WORKERS);
                     if (tid < NT && tid < a.M)
@@ -1191,35 +1287,80 @@ __global__ void __launch_bounds__(SK_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
                 }
             }
             run_c0 = 0;  // every later run starts at a tile's chunk 0
-            // the accumulator's loads come before the next run's MMAs (ordered by the next
-            // unit's named barrier)
-            tc_fence_before();
         }
-    } else {
-        // issuer warp: lane 0 refills the raw ring and issues every unit's MMAs
-        int c = u0 % C;
-        for (int it = 0; it < nu; it++) {
-            const int st = it % SK_STAGES;
-            // the workers converted unit it - 1 before the barrier this warp passed last
-            // iteration, so its slot takes unit it - 1 + RS
-            if (lane == 0 && it >= 1 && it - 1 + RS < nu) fetch_raw(it - 1 + RS);
-            __syncwarp();
-            named_sync(1 + st, SK_THREADS);
-            if (lane == 0) {
-                tc_fence_after();
-                issue_chunk_mmas(tmem, idesc, stage_ptr(st, 0), stage_ptr(st, 1), stage_ptr(st, 2), stage_ptr(st, 3),
-                                 it == 0 || c == 0);
-                umma_commit(&mma_bar[st]);
-                if (it == nu - 1 || c == C - 1) umma_commit(&acc_bar);
+    } else if (warp == kSkProducerWarp) {
+        // producer: activation tiles (and WT weight tiles) SB units ahead, a slot refilled
+        // once the MMAs of the unit that last read it are done; (raw) the raw ring RS units
+        // ahead, a slot refilled once every worker warp has converted it
+        if (lane == 0) {
+            bool ok = true;
+            for (int i = 0; i < min(nu, SB); i++) fetch_x(i);
+            int next_raw = RS;
+            for (int j = SB; j < nu; j++) {
+                if (!WT)
+                    for (; next_raw < nu && next_raw < j + RS; next_raw++) {  // keep the raw ring full meanwhile
+                        const int done = next_raw - RS;
+                        if (!mbar_try_wait(&raw_free[done % RS], (done / RS) & 1)) break;
+                        fetch_w(next_raw);
+                    }
+                if (ok && !mbar_wait(&mma_bar[(j - SB) % SB], ((j - SB) / SB) & 1, a.err)) ok = false;
+                if (WT) fetch_w(j);
+                fetch_x(j);
             }
-            __syncwarp();
+            if (!WT)
+                for (; next_raw < nu; next_raw++) {
+                    const int done = next_raw - RS;
+                    if (ok && !mbar_wait(&raw_free[done % RS], (done / RS) & 1, a.err)) ok = false;
+                    fetch_w(next_raw);
+                }
+        }
+        grid_dependents_launch();
+    } else {
+        // MMA issuer m (warps 17, 18): units it with it % 2 == m; lane 0 works, the warp
+        // takes the stage barriers
+        const int m = warp - kSkProducerWarp - 1;
+        bool ok = true;
+        int c = u0 % C, run = 0;
+        bool mine = false;  // this issuer has MMAs in the current run
+        // slot descriptors: the address field (bytes >> 4, below 2^14) advances by the
+        // slot stride without carrying into the next field
+        const uint64_t da0 = umma_desc(smem_addr(a_slots)), db0 = umma_desc(smem_addr(b_slots));
+        for (int it = 0; it < nu; it++) {
+            const bool first = it == 0 || c == 0;
+            if (first) {
+                if (it > 0) run++;
+                mine = false;
+                // the run's accumulators are free once the workers loaded run - 2's
+                if (lane == 0 && run >= 2 && ok && !mbar_wait(&acc_free[run & 1], ((run - 2) >> 1) & 1, a.err)) ok = false;
+            }
+            const bool run_end = it == nu - 1 || c == C - 1;
             if (++c == C) c = 0;
+            if ((it & 1) == m) {
+                const int sa = it % SA, sb = it % SB;
+                __syncwarp();
+                if (!WT) named_sync(1 + m, kSkBarThreads);  // the workers converted this unit's weights
+                if (lane == 0) {
+                    if (ok && !mbar_wait(&full_bar[sb], (it / SB) & 1, a.err)) ok = false;
+                    tc_fence_after();
+                    const uint64_t dah = da0 + (uint64_t)sa * (2 * A_BYTES >> 4);
+                    const uint64_t dbh = db0 + (uint64_t)sb * (2 * B_BYTES >> 4);
+                    issue_unit_mmas(tmem + (uint32_t)(((run & 1) * 2 + m) * NT), idesc, dah, dah + (A_BYTES >> 4), dbh,
+                                    dbh + (B_BYTES >> 4), !mine);
+                    umma_commit(&mma_bar[sb]);
+                }
+                mine = true;
+            }
+            if (run_end && lane == 0) {
+                // this issuer's share of the run is complete (or it had none)
+                if (mine) umma_commit(&acc_full[run & 1]);
+                else mbar_arrive(&acc_full[run & 1]);
+            }
         }
         grid_dependents_launch();
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, NT);
+    if (warp == 0) tmem_dealloc(tmem, 4 * NT);
 }
 
 // Allow the kernel the largest dynamic shared memory the device offers next to its static
@@ -1417,8 +1558,21 @@ bool tc_streamk_enabled() {
     return v == 1;
 }
 
-size_t tc_streamk_scratch_bytes(int ctas) {
-    return (size_t)ctas * SK_NT * TC_M * sizeof(float) + (size_t)ctas * sizeof(int);
+// Scratch layout: partial tiles [ctas][64][128] fp32, activation tiles [max_k / 64][16 KB],
+// flags [ctas].
+size_t tc_streamk_scratch_bytes(int ctas, int max_k) {
+    return (size_t)ctas * SK_NT * TC_M * sizeof(float) + (size_t)(max_k / TC_KC) * SK_XTILE + (size_t)ctas * sizeof(int);
+}
+
+void tc_streamk_bind(GemmArgs& g, void* scratch, int ctas, int max_k) {
+    uint8_t* p = static_cast<uint8_t*>(scratch);
+    g.sk_partial = reinterpret_cast<float*>(p);
+    p += (size_t)ctas * SK_NT * TC_M * sizeof(float);
+    g.sk_xs = p;
+    p += (size_t)(max_k / TC_KC) * SK_XTILE;
+    g.sk_flags = reinterpret_cast<int*>(p);
+    g.sk_capacity = ctas;
+    g.sk_max_k = max_k;
 }
 
 namespace {
@@ -1435,25 +1589,38 @@ int streamk_min_rows() {
 }
 
 bool streamk_takes(const GemmArgs& a) {
-    return tc_streamk_enabled() && a.sk_partial && a.sk_flags && a.sk_capacity > 0 && a.wr && !a.wt && !a.wf &&
-           a.kbegin == 0 && a.M >= streamk_min_rows() && a.M <= SK_NT && a.K % TC_KC == 0 && a.N % 2 == 0;
+    return tc_streamk_enabled() && a.sk_partial && a.sk_flags && a.sk_xs && a.sk_capacity > 0 && a.K <= a.sk_max_k &&
+           (a.wr || a.wt) && !a.wf && a.kbegin == 0 && a.M >= streamk_min_rows() && a.M <= SK_NT && a.K % TC_KC == 0 &&
+           a.N % 2 == 0;
 }
 
 void tc_launch_streamk(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     StreamKArgs sk;
     sk.chunks = a.K / TC_KC;
     sk.units = ((a.N + TC_M - 1) / TC_M) * sk.chunks;
-    sk.stages = SK_STAGES;
+    sk.xrows = (a.M + 7) / 8 * 8;
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
     if (sms <= 0) sms = 148;
+    // the activations as hi/lo tiles, once for the launch
+    const int64_t xthreads = (int64_t)sk.chunks * sk.xrows * 8;
+    count_launch();
+    launch_ex(tc_split_x_kernel, dim3((unsigned)((xthreads + 255) / 256)), dim3(256), 0, s, 1, a, sk.xrows);
     const int grid = std::max(1, std::min(std::min(sms, sk.units), a.sk_capacity));
-    const int budget = tc_ensure_smem(tc_streamk_kernel);
-    sk.raw_off = SK_STAGES * TcSmem<SK_NT>::STAGE;
+    constexpr int A_SLOT = 2 * TC_M * TC_KC * 2, B_SLOT = (int)SK_XTILE;
+    if (a.wt) {  // hi/lo tiles: no conversion, 4 A slots
+        sk.raw_off = 4 * A_SLOT + SK_SB * B_SLOT;
+        sk.raw_slots = 0;
+        tc_ensure_smem(tc_streamk_kernel<true>);
+        launch_ex(tc_streamk_kernel<true>, dim3(grid), dim3(SK_THREADS), sk.raw_off, s, 1, a, e, sk);
+        return;
+    }
+    const int budget = tc_ensure_smem(tc_streamk_kernel<false>);
+    sk.raw_off = 2 * A_SLOT + SK_SB * B_SLOT;
     sk.raw_slots = std::min(TC_RAW_MAX, (budget - sk.raw_off) / (int)TC_RAW_BYTES);
-    launch_ex(tc_streamk_kernel, dim3(grid), dim3(SK_THREADS), sk.raw_off + sk.raw_slots * (int)TC_RAW_BYTES, s, 1, a,
-              e, sk);
+    launch_ex(tc_streamk_kernel<false>, dim3(grid), dim3(SK_THREADS), sk.raw_off + sk.raw_slots * (int)TC_RAW_BYTES, s,
+              1, a, e, sk);
 }
 
 }  // namespace

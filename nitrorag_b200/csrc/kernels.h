@@ -65,16 +65,21 @@ struct GemmArgs {
     // and scales regrouped per 128-row x 64-column tile (9 KB, tc_tile_q8_raw) so the
     // kernel can stream them with bulk copies through a deep shared-memory ring.
     const uint8_t* wr = nullptr;
-    // Optional scratch for the stream-K kernel over raw tiles (batches of 3-64 rows): one
-    // partial tile per CTA, sk_partial [sk_capacity][64][128] fp32, and one flag per CTA,
-    // sk_flags [sk_capacity], zero when no launch is in flight (each launch leaves them so).
+    // Optional scratch for the stream-K kernel (batches of 3-64 rows over hi/lo or raw
+    // tiles), laid out by tc_streamk_bind: one partial tile per CTA, the launch's
+    // activations as hi/lo tiles (K up to sk_max_k), and one flag per CTA, zero when no
+    // launch is in flight (each launch leaves them so).
     float* sk_partial = nullptr;
+    uint8_t* sk_xs = nullptr;
     int* sk_flags = nullptr;
     int sk_capacity = 0;
+    int sk_max_k = 0;
 };
 
-// Bytes of stream-K scratch (partials, then flags) for `ctas` CTAs.
-size_t tc_streamk_scratch_bytes(int ctas);
+// Bytes of stream-K scratch for `ctas` CTAs and K up to max_k, and the binding of one
+// such (zeroed) buffer to a GemmArgs.
+size_t tc_streamk_scratch_bytes(int ctas, int max_k);
+void tc_streamk_bind(GemmArgs& g, void* scratch, int ctas, int max_k);
 // Whether the stream-K kernel may take raw-tile launches (NITRO_STREAMK=0 turns it off).
 bool tc_streamk_enabled();
 

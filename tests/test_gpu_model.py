@@ -252,16 +252,19 @@ def test_ingest_prompt_prefix_cache_hit(ref_fixed, tiny_model):
     ref.close()
 
 
+@pytest.mark.parametrize("wide", [True, False], ids=["hilo-tiles", "raw-tiles"])
 @pytest.mark.parametrize("B", [1, 3, 5, 24, 40, 64])
-def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B):
+def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B, wide):
     """The large-model projection path: with the tile threshold at zero every Q8 projection
-    gets raw Q8 tiles (and hi/lo tiles beside them, which only batches of more than 64 rows
-    read).  Batches of 3-64 rows take the stream-K kernel: its shares of (tile, K chunk)
-    units cut these small matrices' tiles over up to 12 CTAs each, so the partial-tile
-    hand-over runs on every projection; 1-2 rows take the streamed matvec.  Prefill and two
-    decode steps must match the reference, and a decode step run again on the same inputs
-    must give bit-identical logits (partials are added in a fixed order)."""
+    gets raw Q8 tiles, and hi/lo tiles beside them unless NITRO_WIDE_TILES=0.  Batches of
+    3-64 rows take the stream-K kernel (over the hi/lo tiles when they exist, else
+    converting the raw ones): its shares of (tile, K chunk) units cut these small
+    matrices' tiles over up to 12 CTAs each, so the partial-tile hand-over runs on every
+    projection; 1-2 rows take the matvec.  Prefill and two decode steps must match the
+    reference, and a decode step run again on the same inputs must give bit-identical
+    logits (partials are added in a fixed order)."""
     monkeypatch.setenv("NITRO_TILE_MAX_WEIGHTS", "0")
+    monkeypatch.setenv("NITRO_WIDE_TILES", "1" if wide else "0")
     ref = ref_fixed
     blocks = 600
     ref.open(m110_model, 256, blocks)
