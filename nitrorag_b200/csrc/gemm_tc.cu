@@ -1363,6 +1363,305 @@ __global__ void __launch_bounds__(SK_THREADS, 1) tc_streamk_kernel(GemmArgs a, E
     if (warp == 0) tmem_dealloc(tmem, 4 * NT);
 }
 
+// ------------------------------------------------------------------ int8 digit-plane matvec, 1-10 rows
+// Small batches over large Q8 matrices (decode at batch 1-10 on the 7B shape).  The int8
+// weights go to the tensor core as they are: the raw tiles' layout ([16-byte K piece][128
+// rows][16 B]) is a K-major UMMA layout (K core matrices 2048 B apart, 8-row groups 128 B
+// apart), so a kind::i8 MMA of K = 32 covers one Q8_0 block with no conversion on chip.
+// The activations are written once per launch (tc_i8_digits_kernel) as three int8 digit
+// planes per token and 32-wide block: with xs = max|x g| / 127 over the block and
+// t = x g / xs, d0 = rint(t), d1 = rint((t - d0) 254), d2 = rint(((t - d0) 254 - d1) 254),
+// so x g = xs (d0 + d1 / 254 + d2 / 254^2) to ~1e-7 of the block's largest value.  One
+// MMA (M = 128 weight rows, N = 16 or 32 columns = 3 digit planes x up to 10 tokens) gives
+// every block's integer dot products exactly (int32); reader warps take them from TMEM and
+// add s[n][block] xs[block][m] (I0 + I1 / 254 + I2 / 254^2) into fp32 sums per row and
+// token: the Q8 products of src/model_q8.cpp:107-111 with the block scale applied once
+// per block.  Units, shares, partials and epilogues are the stream-K kernel's.
+constexpr int I8_RS = 16;         // at most this many ring slots
+constexpr int I8_THREADS = 192;   // 4 reader warps (a row each lane), producer, MMA issuer
+constexpr int kI8ReaderBar = 9;   // named barrier of the 128 reader threads
+constexpr float kI8D1 = 1.0f / 254.0f, kI8D2 = 1.0f / 64516.0f;
+
+__host__ __device__ constexpr int i8_block_tile(int ncol) { return ncol * 32; }  // bytes of one block's digits
+
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version for sm_100; no swizzle
+    return d;
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(0u)
+        : "memory");
+}
+
+// Instruction descriptor of kind::i8: D s32, A and B signed 8-bit, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// The activations' digit planes: thread per (block kb, column c = 3 m + plane); block
+// kb's tile is [16-wide K group][8-column group][8 columns][16 B]; xs[kb][m] after the
+// tiles.  Columns past 3 M are zero.
+template <int NCOL>
+__global__ void __launch_bounds__(256) tc_i8_digits_kernel(GemmArgs a) {
+    grid_dependency_wait();  // x comes from the previous kernel
+    grid_dependents_launch();
+    const int blocks = a.K / 32;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= blocks * NCOL) return;
+    const int kb = t / NCOL, c = t % NCOL, m = c / 3, plane = c % 3;
+    __align__(16) int8_t d[32];
+    float xs = 0.0f;
+    if (m < a.M) {
+        float v[32], amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float4 x4 = *reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + kb * 32 + 4 * j);
+            if (a.norm_gain) {
+                const float4 g4 = __ldg(reinterpret_cast<const float4*>(a.norm_gain + kb * 32) + j);
+                x4.x *= g4.x; x4.y *= g4.y; x4.z *= g4.z; x4.w *= g4.w;
+            }
+            v[4 * j] = x4.x; v[4 * j + 1] = x4.y; v[4 * j + 2] = x4.z; v[4 * j + 3] = x4.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(v[j]));
+        xs = amax / 127.0f;
+        const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const float tt = v[j] * inv;
+            const float d0 = rintf(tt), r1 = (tt - d0) * 254.0f;
+            const float d1 = rintf(r1), d2 = rintf((r1 - d1) * 254.0f);
+            const float dv = plane == 0 ? d0 : (plane == 1 ? d1 : d2);
+            d[j] = (int8_t)fmaxf(-127.0f, fminf(127.0f, dv));
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++) d[j] = 0;
+    }
+    uint8_t* tile = a.sk_xs + (size_t)kb * i8_block_tile(NCOL);
+#pragma unroll
+    for (int g = 0; g < 2; g++)
+        *reinterpret_cast<uint4*>(tile + g * (NCOL / 8) * 128 + (c / 8) * 128 + (c % 8) * 16) =
+            *reinterpret_cast<const uint4*>(d + 16 * g);
+    if (plane == 0 && m < 16) {
+        float* xst = reinterpret_cast<float*>(a.sk_xs + (size_t)blocks * i8_block_tile(NCOL));
+        xst[kb * 16 + m] = xs;
+    }
+}
+
+// UCH consecutive 64-wide chunks of one tile form a unit (their raw tiles are adjacent in
+// memory: one bulk copy), so every wait and copy covers UCH x 9 KB of weights.
+template <int NCOL, int UCH>
+__global__ void __launch_bounds__(I8_THREADS, 1) tc_i8_kernel(GemmArgs a, Epilogue e, StreamKArgs sk) {
+    constexpr int BT = i8_block_tile(NCOL);            // digit bytes of one block
+    constexpr int NB = 2 * UCH;                        // Q8_0 blocks per unit
+    constexpr int UB = UCH * TC_RAW_BYTES + NB * BT;   // one ring slot: raw tiles, then the unit's digit tiles
+    constexpr int R = 512 / (NB * NCOL) < 8 ? 512 / (NB * NCOL) : 8;  // TMEM result regions in flight
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ uint64_t full_bar[I8_RS];      // raw tiles and digits of the slot's unit have landed (2 arrivals)
+    __shared__ uint64_t slot_free[I8_RS];     // the reader warps are done with the slot
+    __shared__ uint64_t mma_done[8];
+    __shared__ uint64_t region_free[8];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int partners_ok;
+    __shared__ float inv_rms[16];
+    __shared__ float red_ss[4 * SK_NT];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, cta = blockIdx.x, C = sk.chunks / UCH;  // units per tile
+    const int RS = sk.raw_slots;
+    const int u0 = sk_first_unit(cta, G, sk.units);
+    const int nu = sk_first_unit(cta + 1, G, sk.units) - u0;
+    const int blocks = a.K / 32;
+    float* xst = reinterpret_cast<float*>(smem + (size_t)RS * UB);  // [blocks][16] block scales of x
+    auto slot_ptr = [&](int s) { return smem + (size_t)s * UB; };
+
+    if (warp == 0) {
+        tmem_alloc(&tmem_slot, R * NB * NCOL);
+        tmem_relinquish();
+    }
+    auto fetch_w = [&](int i) {
+        uint64_t* bar = &full_bar[i % RS];
+        mbar_arrive_expect_tx(bar, UCH * TC_RAW_BYTES);
+        bulk_g2s(slot_ptr(i % RS), a.wr + (size_t)(u0 + i) * UCH * TC_RAW_BYTES, UCH * TC_RAW_BYTES, bar);
+    };
+    auto fetch_d = [&](int i) {  // the unit's blocks NB * ((u0 + i) % C) ..
+        uint64_t* bar = &full_bar[i % RS];
+        mbar_arrive_expect_tx(bar, NB * BT);
+        bulk_g2s(slot_ptr(i % RS) + UCH * TC_RAW_BYTES, a.sk_xs + (size_t)((u0 + i) % C) * NB * BT, NB * BT, bar);
+    };
+    if (tid == 0) {
+        for (int s = 0; s < RS; s++) {
+            mbar_init(&full_bar[s], 2);
+            mbar_init(&slot_free[s], 4);
+        }
+        for (int r = 0; r < R; r++) {
+            mbar_init(&mma_done[r], 1);
+            mbar_init(&region_free[r], 4);
+        }
+        fence_barrier_init();
+        // weights are read-only: the first tiles are requested before the dependency wait
+        for (int i = 0; i < min(nu, RS); i++) fetch_w(i);
+    }
+    grid_dependency_wait();
+    // x block scales into shared memory; 1/rms of each token row
+    const float* xs_g = reinterpret_cast<const float*>(a.sk_xs + (size_t)blocks * BT);
+    for (int i = tid; i < blocks * 16; i += I8_THREADS) xst[i] = xs_g[i];
+    if (a.norm_gain && warp < 4) {
+        for (int r = warp; r < 16; r += 4) {
+            float ss = 0.0f;
+            if (r < a.M)
+                for (int k = lane * 4; k < a.K; k += 128) {
+                    const float4 x4 = *reinterpret_cast<const float4*>(a.x + (int64_t)r * a.ldx + k);
+                    ss += x4.x * x4.x + x4.y * x4.y + x4.z * x4.z + x4.w * x4.w;
+                }
+            ss = warp_sum(ss);
+            if (lane == 0) inv_rms[r] = 1.0f / sqrtf(ss / (float)a.K + 1e-5f);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp < 4) {
+        // readers: thread = weight row `tid` of the tile (TMEM lane)
+        bool ok = true;
+        const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+        float acc[16];
+#pragma unroll
+        for (int m = 0; m < 16; m++) acc[m] = 0.0f;
+        int t = u0 / C, c = u0 % C, run_c0 = c;
+        for (int it = 0; it < nu; it++) {
+            const int s = it % RS, r = it % R;
+            if (ok && !mbar_wait(&mma_done[r], (it / R) & 1, a.err)) ok = false;
+            tc_fence_after();
+#pragma unroll
+            for (int j = 0; j < NB; j++) {
+                float iv[NCOL];
+                if constexpr (NCOL == 16) tmem_ld16(tl + (uint32_t)((r * NB + j) * NCOL), iv);
+                else tmem_ld32(tl + (uint32_t)((r * NB + j) * NCOL), iv);
+                // block j: half j % 2 of raw tile j / 2 ([half][128 rows] scales after its int8)
+                const float ws =
+                    reinterpret_cast<const float*>(slot_ptr(s) + (j >> 1) * TC_RAW_BYTES + TC_M * TC_KC)[(j & 1) * TC_M + tid];
+                const float* xsb = xst + (c * NB + j) * 16;
+#pragma unroll
+                for (int m = 0; m < NCOL / 3; m++) {
+                    const float p = (float)__float_as_int(iv[3 * m]) + (float)__float_as_int(iv[3 * m + 1]) * kI8D1 +
+                                    (float)__float_as_int(iv[3 * m + 2]) * kI8D2;
+                    acc[m] = fmaf(ws, xsb[m] * p, acc[m]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&region_free[r]);
+                mbar_arrive(&slot_free[s]);
+            }
+            const bool run_end = it == nu - 1 || c == C - 1;
+            const int t_cur = t, c_cur = c;
+            if (++c == C) { c = 0; t++; }
+            if (!run_end) continue;
+
+            float v[SK_COLS];
+#pragma unroll
+            for (int m = 0; m < SK_COLS; m++) v[m] = acc[m];
+#pragma unroll
+            for (int m = 0; m < 16; m++) acc[m] = 0.0f;
+            if (it == nu - 1) grid_dependents_launch();
+            if (run_c0 > 0) {
+                // the tile belongs to an earlier CTA: [cta][token][row] partial, then the flag
+                float* dst = a.sk_partial + (size_t)cta * SK_NT * TC_M + tid;
+#pragma unroll
+                for (int m = 0; m < SK_COLS; m++) __stcg(dst + (size_t)m * TC_M, ok ? v[m] : 0.0f);
+                __threadfence();
+                named_sync(kI8ReaderBar, 128);
+                if (tid == 0) st_release_gpu(a.sk_flags + cta, 1);
+            } else {
+                const int last = c_cur == C - 1 ? cta : sk_cta_of(t_cur * C + C - 1, G, sk.units);
+                float xo[SK_COLS];
+                sk_residual_in(a, e, xo, t_cur * TC_M + tid, 0);
+                if (last > cta) {
+                    if (tid == 0) partners_ok = 1;
+                    named_sync(kI8ReaderBar, 128);
+                    if (tid < last - cta && !sk_wait_flag(a.sk_flags + cta + 1 + tid, a.err)) partners_ok = 0;
+                    named_sync(kI8ReaderBar, 128);
+                    if (partners_ok) {
+                        for (int p = cta + 1; p <= last; p++) {
+                            const float* src = a.sk_partial + (size_t)p * SK_NT * TC_M + tid;
+                            float pa[SK_COLS];
+#pragma unroll
+                            for (int m = 0; m < SK_COLS; m++) pa[m] = __ldcg(src + (size_t)m * TC_M);
+#pragma unroll
+                            for (int m = 0; m < SK_COLS; m++) v[m] += pa[m];
+                        }
+                        if (tid < last - cta) atomicExch(a.sk_flags + cta + 1 + tid, 0);
+                    } else {
+                        ok = false;
+                    }
+                }
+                sk_epilogue(a, e, v, xo, t_cur * TC_M + tid, 0, inv_rms, red_ss, warp, lane, ok);
+                if (e.kind == kEpiResidual && e.ss_out) {
+                    named_sync(kI8ReaderBar, 128);
+                    if (tid < a.M)
+                        e.ss_out[(int64_t)t_cur * e.ss_ld + tid] =
+                            red_ss[tid] + red_ss[SK_NT + tid] + red_ss[2 * SK_NT + tid] + red_ss[3 * SK_NT + tid];
+                    named_sync(kI8ReaderBar, 128);
+                }
+            }
+            run_c0 = 0;
+        }
+    } else if (warp == 4) {
+        // producer: digits of the first slots, then every slot refilled (raw tiles and
+        // digits) once the readers are done with its previous unit
+        if (lane == 0) {
+            bool ok = true;
+            for (int i = 0; i < min(nu, RS); i++) fetch_d(i);
+            for (int j = RS; j < nu; j++) {
+                const int done = j - RS;
+                if (ok && !mbar_wait(&slot_free[done % RS], (done / RS) & 1, a.err)) ok = false;
+                fetch_w(j);
+                fetch_d(j);
+            }
+        }
+        grid_dependents_launch();
+    } else {
+        // MMA issuer: one K = 32 MMA per Q8_0 block of the unit into the unit's region
+        if (lane == 0) {
+            bool ok = true;
+            const uint32_t idesc = umma_idesc_i8(TC_M, NCOL);
+            for (int it = 0; it < nu; it++) {
+                const int s = it % RS, r = it % R;
+                if (ok && !mbar_wait(&full_bar[s], (it / RS) & 1, a.err)) ok = false;
+                const int prev = it - R;
+                if (ok && prev >= 0 && !mbar_wait(&region_free[r], (prev / R) & 1, a.err)) ok = false;
+                tc_fence_after();
+                const uint32_t base = smem_addr(slot_ptr(s));
+#pragma unroll
+                for (int j = 0; j < NB; j++) {
+                    const uint64_t da = desc_kmajor(base + (j >> 1) * TC_RAW_BYTES + (j & 1) * 2 * 2048, 2048, 128);
+                    const uint64_t db = desc_kmajor(base + UCH * TC_RAW_BYTES + j * BT, (NCOL / 8) * 128, 128);
+                    umma_i8(tmem + (uint32_t)((r * NB + j) * NCOL), da, db, idesc);
+                }
+                umma_commit(&mma_done[r]);
+            }
+        }
+        grid_dependents_launch();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, R * NB * NCOL);
+}
+
 // Allow the kernel the largest dynamic shared memory the device offers next to its static
 // shared memory (per kernel and device, once).
 template <class K>
@@ -1588,6 +1887,62 @@ int streamk_min_rows() {
     return v;
 }
 
+bool tc_i8_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* env = getenv("NITRO_I8_MATVEC");
+        v = (env && env[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+// Chunks per unit of the digit-plane kernel (4 when the chunk count allows), its ring
+// slots within ~196 KB of shared memory, and the shared memory they take with the x block
+// scales.
+int i8_uch(int K) { return (K / TC_KC) % 4 == 0 ? 4 : ((K / TC_KC) % 2 == 0 ? 2 : 1); }
+int i8_slots(int ncol, int uch) {
+    return std::min(I8_RS, (196 * 1024) / (uch * (int)TC_RAW_BYTES + 2 * uch * i8_block_tile(ncol)));
+}
+int i8_smem(int ncol, int K) {
+    const int uch = i8_uch(K);
+    return i8_slots(ncol, uch) * (uch * (int)TC_RAW_BYTES + 2 * uch * i8_block_tile(ncol)) + (K / 32) * 16 * 4;
+}
+
+bool i8_takes(const GemmArgs& a) {
+    return tc_i8_enabled() && a.sk_partial && a.sk_flags && a.sk_xs && a.sk_capacity > 0 && a.K <= a.sk_max_k &&
+           a.wr && !a.wf && a.kbegin == 0 && a.M >= 1 && a.M <= 10 && a.K % TC_KC == 0 && a.N % 2 == 0 &&
+           i8_smem(32, a.K) <= 224 * 1024 && i8_slots(32, i8_uch(a.K)) >= 3;
+}
+
+template <int NCOL, int UCH>
+void tc_launch_i8_u(const GemmArgs& a, const Epilogue& e, StreamKArgs sk, int grid, cudaStream_t s) {
+    sk.units = ((a.N + TC_M - 1) / TC_M) * (sk.chunks / UCH);
+    sk.raw_slots = i8_slots(NCOL, UCH);
+    grid = std::max(1, std::min(grid, sk.units));
+    tc_ensure_smem(tc_i8_kernel<NCOL, UCH>);
+    launch_ex(tc_i8_kernel<NCOL, UCH>, dim3(grid), dim3(I8_THREADS), i8_smem(NCOL, a.K), s, 1, a, e, sk);
+}
+
+template <int NCOL>
+void tc_launch_i8(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
+    StreamKArgs sk;
+    sk.chunks = a.K / TC_KC;
+    sk.xrows = 0;
+    sk.raw_off = 0;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
+    if (sms <= 0) sms = 148;
+    const int dthreads = (a.K / 32) * NCOL;
+    count_launch();
+    launch_ex(tc_i8_digits_kernel<NCOL>, dim3((unsigned)((dthreads + 255) / 256)), dim3(256), 0, s, 1, a);
+    const int grid = std::min(sms, a.sk_capacity);
+    const int uch = i8_uch(a.K);
+    if (uch == 4) tc_launch_i8_u<NCOL, 4>(a, e, sk, grid, s);
+    else if (uch == 2) tc_launch_i8_u<NCOL, 2>(a, e, sk, grid, s);
+    else tc_launch_i8_u<NCOL, 1>(a, e, sk, grid, s);
+}
+
 bool streamk_takes(const GemmArgs& a) {
     return tc_streamk_enabled() && a.sk_partial && a.sk_flags && a.sk_xs && a.sk_capacity > 0 && a.K <= a.sk_max_k &&
            (a.wr || a.wt) && !a.wf && a.kbegin == 0 && a.M >= streamk_min_rows() && a.M <= SK_NT && a.K % TC_KC == 0 &&
@@ -1628,11 +1983,17 @@ void tc_launch_streamk(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
 // Raw Q8 tiles send batches of 3-8 tokens here too: for large matrices the tensor-core
 // kernels stream them far better than the matvec (1-2 tokens take the streamed matvec).
 bool tc_gemm_supported(const GemmArgs& a) {
-    return a.K % TC_KC == 0 && a.N % 2 == 0 && (a.M > 8 || (a.wr != nullptr && !a.wf && a.M > 2) || streamk_takes(a));
+    return a.K % TC_KC == 0 && a.N % 2 == 0 &&
+           (a.M > 8 || (a.wr != nullptr && !a.wf && a.M > 2) || streamk_takes(a) || i8_takes(a));
 }
 
 void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     count_launch();
+    if (i8_takes(a)) {
+        if (a.M <= 5) tc_launch_i8<16>(a, e, s);
+        else tc_launch_i8<32>(a, e, s);
+        return;
+    }
     if (streamk_takes(a)) {
         tc_launch_streamk(a, e, s);
         return;

@@ -253,14 +253,14 @@ def test_ingest_prompt_prefix_cache_hit(ref_fixed, tiny_model):
 
 
 @pytest.mark.parametrize("wide", [True, False], ids=["hilo-tiles", "raw-tiles"])
-@pytest.mark.parametrize("B", [1, 3, 5, 24, 40, 64])
+@pytest.mark.parametrize("B", [1, 3, 5, 8, 10, 24, 40, 64])
 def test_110m_raw_q8_tiles(ref_fixed, m110_model, monkeypatch, B, wide):
     """The large-model projection path: with the tile threshold at zero every Q8 projection
     gets raw Q8 tiles, and hi/lo tiles beside them unless NITRO_WIDE_TILES=0.  Batches of
-    3-64 rows take the stream-K kernel (over the hi/lo tiles when they exist, else
-    converting the raw ones): its shares of (tile, K chunk) units cut these small
-    matrices' tiles over up to 12 CTAs each, so the partial-tile hand-over runs on every
-    projection; 1-2 rows take the matvec.  Prefill and two decode steps must match the
+    1-10 rows take the int8 digit-plane kernel (the raw tiles straight into kind::i8
+    MMAs, 16 or 32 columns), 11-64 rows the stream-K kernel (over the hi/lo tiles when
+    they exist, else converting the raw ones); both cut these small matrices' tiles over
+    up to 12 CTAs each, so the partial-tile hand-over runs on every projection.  Prefill and two decode steps must match the
     reference, and a decode step run again on the same inputs must give bit-identical
     logits (partials are added in a fixed order)."""
     monkeypatch.setenv("NITRO_TILE_MAX_WEIGHTS", "0")
