@@ -1545,20 +1545,32 @@ __global__ void __launch_bounds__(I8_THREADS, 1) tc_i8_kernel(GemmArgs a, Epilog
             const int s = it % RS, r = it % R;
             if (ok && !mbar_wait(&mma_done[r], (it / R) & 1, a.err)) ok = false;
             tc_fence_after();
+            // the unit's blocks 64 TMEM columns at a time (2 loads in flight, one wait)
+            constexpr int BPL = 32 / NCOL;  // blocks per 32-column load
 #pragma unroll
-            for (int j = 0; j < NB; j++) {
-                float iv[NCOL];
-                if constexpr (NCOL == 16) tmem_ld16(tl + (uint32_t)((r * NB + j) * NCOL), iv);
-                else tmem_ld32(tl + (uint32_t)((r * NB + j) * NCOL), iv);
-                // block j: half j % 2 of raw tile j / 2 ([half][128 rows] scales after its int8)
-                const float ws =
-                    reinterpret_cast<const float*>(slot_ptr(s) + (j >> 1) * TC_RAW_BYTES + TC_M * TC_KC)[(j & 1) * TC_M + tid];
-                const float* xsb = xst + (c * NB + j) * 16;
+            for (int j0 = 0; j0 < NB; j0 += 2 * BPL) {
+                uint32_t iv[2][32];
 #pragma unroll
-                for (int m = 0; m < NCOL / 3; m++) {
-                    const float p = (float)__float_as_int(iv[3 * m]) + (float)__float_as_int(iv[3 * m + 1]) * kI8D1 +
-                                    (float)__float_as_int(iv[3 * m + 2]) * kI8D2;
-                    acc[m] = fmaf(ws, xsb[m] * p, acc[m]);
+                for (int h = 0; h < 2; h++)
+                    if (j0 + h * BPL < NB) tmem_ld32_async(tl + (uint32_t)((r * NB + j0 + h * BPL) * NCOL), iv[h]);
+                tmem_wait_ld();
+                tmem_regs_ready(iv[0]);
+                if (j0 + BPL < NB) tmem_regs_ready(iv[1]);
+#pragma unroll
+                for (int jj = 0; jj < 2 * BPL; jj++) {
+                    const int j = j0 + jj;
+                    if (j >= NB) break;
+                    const uint32_t* col = iv[jj / BPL] + (jj % BPL) * NCOL;
+                    // block j: half j % 2 of raw tile j / 2 ([half][128 rows] scales after its int8)
+                    const float ws = reinterpret_cast<const float*>(slot_ptr(s) + (j >> 1) * TC_RAW_BYTES +
+                                                                    TC_M * TC_KC)[(j & 1) * TC_M + tid];
+                    const float* xsb = xst + (c * NB + j) * 16;
+#pragma unroll
+                    for (int m = 0; m < NCOL / 3; m++) {
+                        const float p = (float)(int)col[3 * m] + (float)(int)col[3 * m + 1] * kI8D1 +
+                                        (float)(int)col[3 * m + 2] * kI8D2;
+                        acc[m] = fmaf(ws, xsb[m] * p, acc[m]);
+                    }
                 }
             }
             tc_fence_before();
