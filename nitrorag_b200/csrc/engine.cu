@@ -86,6 +86,7 @@ Engine::~Engine() {
     cudaFree(d_logits_);
     cudaFree(d_keys_);
     cudaFree(d_ss_);
+    cudaFree(d_xs_);
     cudaFree(d_sk_);
     cudaFree(d_err_);
     cudaFree(d_attn_ws_);
@@ -328,6 +329,9 @@ int Engine::upload_weights(const uint8_t* file, size_t size) {
 }
 
 void Engine::attach_streamk(GemmArgs& g) const {
+    g.xs_tiles = static_cast<uint8_t*>(d_xs_);
+    g.xs_cap_rows = xs_cap_rows_;
+    g.xs_cap_k = xs_cap_k_;
     if (!d_sk_) return;
     tc_streamk_bind(g, d_sk_, sk_capacity_, std::max(shape_.dim, shape_.hidden));
 }
@@ -360,6 +364,10 @@ int Engine::init_device(const uint8_t* file, size_t size) {
     NR_CUDA(cudaMalloc(&d_logits_, (size_t)cfg_.max_batch * c.vocab * 4));
     NR_CUDA(cudaMalloc(&d_keys_, (size_t)R * 8));
     NR_CUDA(cudaMalloc(&d_ss_, (size_t)((c.dim + 127) / 128) * R * 4));
+    // activations pre-split into bf16 hi/lo tiles for the tensor-core GEMM's wide tiles
+    xs_cap_rows_ = (R + 255) / 256 * 256;
+    xs_cap_k_ = std::max(c.dim, c.hidden);
+    NR_CUDA(cudaMalloc(&d_xs_, (size_t)xs_cap_rows_ * xs_cap_k_ * 4));
     NR_CUDA(cudaMalloc(&d_err_, (size_t)(R + 1) * 4));  // [0] error flag, [1..] argmax ids
     d_argmax_ = d_err_ + 1;
     NR_CUDA(cudaMemsetAsync(d_err_, 0, (size_t)(R + 1) * 4, stream_));

@@ -162,6 +162,10 @@ private:
     // stream-K scratch for raw-tile projections (partial tiles + flags), one slot per SM
     void* d_sk_ = nullptr;
     int sk_capacity_ = 0;
+    // activations pre-split into hi/lo tiles for the wide-tile GEMM (rows x K x 4 bytes)
+    void* d_xs_ = nullptr;
+    int xs_cap_rows_ = 0, xs_cap_k_ = 0;
+    // the scratch of the large-matrix and wide-tile projection paths, bound to a GemmArgs
     void attach_streamk(GemmArgs& g) const;
     // set while a multi-sequence prefill runs: its segment and tile tables on the device
     const int* d_seg_ = nullptr;

@@ -314,6 +314,10 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     // every chunk of this CTA has its own stage: all weights are staged before waiting for
     // the previous kernel (weights are read-only; activations are not)
     const bool staged = nch <= stages && !use_raw;
+    // 128/256-token tiles in a ring over hi/lo weight tiles: the activations come pre-split
+    // (tc_split_x_kernel, a.xs_tiles) and are bulk-copied with each weight tile instead of
+    // being converted by every CTA of the launch
+    const bool xs = NT >= 128 && !F32W && a.xs_tiles != nullptr && a.wt != nullptr && !staged && !use_raw;
     const int n = n_base + row;  // this thread's weight row
     auto stage_ptr = [&](int st, int part) { return smem + st * S::STAGE + (part < 2 ? part * S::A_BYTES : 2 * S::A_BYTES + (part - 2) * S::B_BYTES); };
     float* gain_s = reinterpret_cast<float*>(smem + sp.gain_off);  // [nch][64] when staged
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
     if (tid == 0) {
         for (int st = 0; st < TC_MAX_STAGES; st++) {
             mbar_init(&mma_bar[st], 1);
-            mbar_init(&w_bar[st], 1);
+            mbar_init(&w_bar[st], xs ? 2 : 1);  // xs: the weight and the activation copies arrive
         }
         for (int r = 0; r < TC_RAW_MAX; r++) mbar_init(&raw_bar[r], 1);
         mbar_init(&done_bar, 1);
@@ -354,6 +358,12 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
         mbar_arrive_expect_tx(&w_bar[st], TC_TILE_BYTES);
         bulk_g2s(stage_ptr(st, 0), a.wt + ((size_t)n_tile * nchunk_total + c_first + i) * TC_TILE_BYTES, TC_TILE_BYTES,
                  &w_bar[st]);
+    };
+    auto fetch_xtile = [&](int i, int st) {  // xs: chunk c_first + i's activation rows m_base.. (hi, lo)
+        const uint8_t* src = a.xs_tiles + (size_t)(c_first + i) * 2 * a.xs_rows * 128 + (size_t)(m_base / 8) * 1024;
+        mbar_arrive_expect_tx(&w_bar[st], 2u * NT * 128u);
+        bulk_g2s(stage_ptr(st, 2), src, NT * 128, &w_bar[st]);
+        bulk_g2s(stage_ptr(st, 3), src + (size_t)a.xs_rows * 128, NT * 128, &w_bar[st]);
     };
     uint8_t* raw_ring = smem + sp.raw_off;
     auto fetch_raw = [&](int i) {  // chunk i -> slot i % RS
@@ -525,7 +535,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                     for (int j = 0; j < 4; j++) gn[j] = __ldg(g4 + j);
                 }
             };
-            if (XPF && nch > 0) fetch_x(0);
+            if (XPF && !xs && nch > 0) fetch_x(0);
             for (int it = 0; it < nch; it++) {
                 const int st = it % stages, use = it / stages;
                 const int k0 = (c_first + it) * TC_KC;
@@ -540,7 +550,9 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                                     stage_ptr(st, 1), row, wg);
                     else if (!a.wt)
                         stage_w<F32W>(cur, a, n, k0 + wg * 32, stage_ptr(st, 0), stage_ptr(st, 1), row, wg);
-                    if (XPF) {
+                    if (xs) {
+                        // the issuer's bulk copy brings this chunk's activations
+                    } else if (XPF) {
 #pragma unroll
                         for (int u = 0; u < XU; u++)
                             stage_x16(xn[u], a.norm_gain ? reinterpret_cast<const float*>(gn) : nullptr,
@@ -552,7 +564,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                 }
                 // the next chunk's activations (and gain) load while this one goes through
                 // the barrier and the MMAs
-                if (XPF && it + 1 < nch) fetch_x(it + 1);
+                if (XPF && !xs && it + 1 < nch) fetch_x(it + 1);
                 fence_async_smem();
                 named_arrive(1 + st, TC_THREADS);
                 if (!a.wt && !use_raw && it + 1 < nch) cur = nxt;
@@ -560,13 +572,20 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
         }
     } else {
         // issuer warp; with tiled weights in a ring, lane 0 also refills each stage with the
-        // tile of chunk it - 1 + stages once the MMAs of chunk it - 1 are done with it
+        // tile of chunk it - 1 + stages once the MMAs of chunk it - 1 are done with it (xs:
+        // and its activations; the first stages' activations once they exist)
+        if (xs && lane == 0)
+            for (int i = 0; i < min(nch, stages); i++) fetch_xtile(i, i);
         for (int it = 0; it < nch; it++) {
             const int st = staged ? it : it % stages, use = staged ? 0 : it / stages;
             if (!staged && a.wt && lane == 0 && ok && it >= 1 && it - 1 + stages < nch) {
                 const int sp_ = (it - 1) % stages;
-                if (mbar_wait(&mma_bar[sp_], ((it - 1) / stages) & 1, a.err)) fetch_tile(it - 1 + stages, sp_);
-                else ok = false;
+                if (mbar_wait(&mma_bar[sp_], ((it - 1) / stages) & 1, a.err)) {
+                    fetch_tile(it - 1 + stages, sp_);
+                    if (xs) fetch_xtile(it - 1 + stages, sp_);
+                } else {
+                    ok = false;
+                }
             }
             // raw ring: the workers converted chunk it - 1 before the barrier this warp passed
             // last iteration, so its slot takes chunk it - 1 + RS
@@ -1019,11 +1038,12 @@ __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e
     }
 }
 
-// The activations of one stream-K launch as bf16 hi/lo tiles in the UMMA layout, one
-// 16 KB tile per 64-wide K chunk ([chunk][hi 8 KB][lo 8 KB]), x times the RMSNorm gain;
-// rows from the batch up to the next multiple of 8 are zero.  One thread per (chunk,
-// row, 8-wide K group).
-__global__ void __launch_bounds__(256) tc_split_x_kernel(GemmArgs a, int xrows) {
+// The activations of one launch as bf16 hi/lo tiles in the UMMA layout, per 64-wide K
+// chunk [hi: rows_pad x 128 B][lo: rows_pad x 128 B] (8-row core-matrix groups of 1 KB),
+// x times the RMSNorm gain; rows from the batch up to xrows are zero.  One thread per
+// (chunk, row < xrows, 8-wide K group).  The stream-K kernel uses rows_pad = 64 (16 KB
+// per chunk); the cluster kernel's 128/256-token tiles copy rows m_base.. of it.
+__global__ void __launch_bounds__(256) tc_split_x_kernel(GemmArgs a, int xrows, int rows_pad, uint8_t* out) {
     grid_dependency_wait();  // x comes from the previous kernel
     grid_dependents_launch();
     const int chunks = a.K / TC_KC;
@@ -1047,8 +1067,8 @@ __global__ void __launch_bounds__(256) tc_split_x_kernel(GemmArgs a, int xrows) 
         w[2] = pack2(__float_as_uint(x1.x), __float_as_uint(x1.y));
         w[3] = pack2(__float_as_uint(x1.z), __float_as_uint(x1.w));
     }
-    uint8_t* tile = a.sk_xs + (size_t)c * SK_XTILE;
-    split8_store(w, tile + core_off(r, g), tile + SK_XTILE / 2 + core_off(r, g));
+    uint8_t* tile = out + (size_t)c * 2 * rows_pad * 128;
+    split8_store(w, tile + core_off(r, g), tile + (size_t)rows_pad * 128 + core_off(r, g));
 }
 
 // The 12 MMAs of one 64-wide K chunk (hi*hi + hi*lo + lo*hi per 16-wide K step) from
@@ -1789,7 +1809,21 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
         ksplit /= 2;
         smem = plan(ksplit, &sp);
     }
-    launch_ex(kernel, dim3(ksplit, n_tiles, m_tiles), dim3(TC_THREADS), smem, s, ksplit, a, e, sp);
+    // 128/256-token tiles streaming hi/lo weight tiles: the activations split once for the
+    // launch (the kernel's ring path copies them with each weight tile)
+    GemmArgs ax = a;
+    ax.xs_tiles = nullptr;
+    const int rows_pad = m_tiles * NT;
+    if (NT >= 128 && a.xs_tiles && a.wt && !a.wf && !raw && a.kbegin == 0 &&
+        (chunks + ksplit - 1) / ksplit > TcSmem<NT>::MAX_STAGES && rows_pad <= a.xs_cap_rows && a.K <= a.xs_cap_k) {
+        ax.xs_tiles = a.xs_tiles;
+        ax.xs_rows = rows_pad;
+        const int64_t threads = (int64_t)chunks * rows_pad * 8;
+        count_launch();
+        launch_ex(tc_split_x_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, s, 1, ax, rows_pad, rows_pad,
+                  a.xs_tiles);
+    }
+    launch_ex(kernel, dim3(ksplit, n_tiles, m_tiles), dim3(TC_THREADS), smem, s, ksplit, ax, e, sp);
 }
 
 // Pre-split weights: one thread per (row, 8-wide K group) writes the bf16 hi/lo halves of
@@ -1973,7 +2007,8 @@ void tc_launch_streamk(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     // the activations as hi/lo tiles, once for the launch
     const int64_t xthreads = (int64_t)sk.chunks * sk.xrows * 8;
     count_launch();
-    launch_ex(tc_split_x_kernel, dim3((unsigned)((xthreads + 255) / 256)), dim3(256), 0, s, 1, a, sk.xrows);
+    launch_ex(tc_split_x_kernel, dim3((unsigned)((xthreads + 255) / 256)), dim3(256), 0, s, 1, a, sk.xrows, SK_NT,
+              a.sk_xs);
     const int grid = std::max(1, std::min(std::min(sms, sk.units), a.sk_capacity));
     constexpr int A_SLOT = 2 * TC_M * TC_KC * 2, B_SLOT = (int)SK_XTILE;
     if (a.wt) {  // hi/lo tiles: no conversion, 4 A slots

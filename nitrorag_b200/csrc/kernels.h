@@ -69,6 +69,12 @@ struct GemmArgs {
     // tiles), laid out by tc_streamk_bind: one partial tile per CTA, the launch's
     // activations as hi/lo tiles (K up to sk_max_k), and one flag per CTA, zero when no
     // launch is in flight (each launch leaves them so).
+    // Optional scratch for the activations pre-split into bf16 hi/lo tiles, taken by the
+    // tensor-core GEMM's 128/256-token tiles over hi/lo weight tiles: xs_cap_rows x
+    // xs_cap_k x 4 bytes.
+    uint8_t* xs_tiles = nullptr;
+    int xs_rows = 0;  // rows of the launch's tiles (set by the launcher)
+    int xs_cap_rows = 0, xs_cap_k = 0;
     float* sk_partial = nullptr;
     uint8_t* sk_xs = nullptr;
     int* sk_flags = nullptr;
