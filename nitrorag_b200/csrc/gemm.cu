@@ -1,15 +1,17 @@
 // Q8_0 / fp32 projections on CUDA cores with fused prologue and epilogues.
 //
-// Two shapes:
+// Three shapes:
 //   * gemv_kernel, M <= 8 token rows (decode at small batch, the last prefill token):
 //     HBM-bound matvec.  One warp owns an adjacent pair of output rows and streams their
 //     int8 weights with 16-byte loads (16 weights per lane per step, one fp32 scale per
 //     32-wide block), dequantises in registers (w = q * scale, as src/model_q8.cpp:107-111)
 //     and accumulates every token row against them.
+//   * gemv_ring_kernel, M <= 2 over large Q8 matrices: whole-row units streamed through a
+//     shared-memory ring by a producer warp, activations held in registers.
 //   * gemm_tiled_kernel, M > 8: 64x64 output tiles staged through shared memory in
 //     32-wide K chunks (one Q8 block), register double-buffered, 8x4 micro-tile per thread.
 //
-// Both apply, when asked, the RMSNorm of the input rows (src/model_q8.cpp:128-140) while
+// All apply, when asked, the RMSNorm of the input rows (src/model_q8.cpp:128-140) while
 // loading them, and one of the epilogues of kernels.h.  Accumulation is fp32 throughout.
 #include <cuda_runtime.h>
 
@@ -317,169 +319,6 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
     }
 }
 
-// ------------------------------------------------------------------ streamed matvec, M <= 2
-// For large matrices the register-prefetch matvec tops out near 40 % of HBM: its loads
-// go through the SM's L1 miss tracking.  This variant streams each pair of weight rows
-// (int8 row + scale row, or fp32 rows) with bulk copies into a per-warp ring of shared-
-// memory slots, like the decode attention streams pages, and keeps the M activation rows
-// (times the RMSNorm gain) in shared memory for the whole CTA.  Warp g of the grid takes
-// row pairs g, g + total_warps, ...; every pair's slot is refilled with the warp's next
-// pair once its lanes have read it.  Waits are bounded (error flag).
-constexpr int SG_SLOTS = 2;
-
-struct StreamPlan {
-    int warps;       // warps per CTA
-    int slot_bytes;  // one row pair: 2 x (K bytes + K/8 scale bytes), or 2 x 4K for fp32
-    int x_bytes;     // M x K fp32 activations
-};
-
-template <int MT, bool F32W>
-__global__ void __launch_bounds__(256) gemv_stream_kernel(GemmArgs a, Epilogue e, StreamPlan sp) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bars[8][SG_SLOTS];
-    __shared__ float inv_rms[MT];
-    __shared__ float red[8][MT];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int K = a.K;
-    const int row_q = F32W ? K * 4 : K;       // bytes of one row's weights
-    const int row_s = F32W ? 0 : K / 8;       // bytes of one row's scales
-    float* xs = reinterpret_cast<float*>(smem);  // [MT][K]
-    uint8_t* ring = smem + sp.x_bytes + (size_t)warp * SG_SLOTS * sp.slot_bytes;
-    const int n_pairs = a.N / 2;
-    const int total_warps = gridDim.x * sp.warps;
-    const int gw = blockIdx.x * sp.warps + warp;
-    const bool worker = warp < sp.warps;
-
-    if (worker && lane == 0) {
-        for (int i = 0; i < SG_SLOTS; i++) mbar_init(&bars[warp][i], 1);
-        fence_barrier_init();
-    }
-    __syncwarp();
-    auto fetch = [&](int pair, int slot) {  // lane 0
-        uint8_t* dst = ring + (size_t)slot * sp.slot_bytes;
-        const int n = pair * 2;
-        mbar_arrive_expect_tx(&bars[warp][slot], (uint32_t)(2 * (row_q + row_s)));
-        if (F32W) {
-            bulk_g2s(dst, a.wf + (int64_t)n * K, 2 * row_q, &bars[warp][slot]);  // rows n, n+1 are adjacent
-        } else {
-            bulk_g2s(dst, a.wq + (int64_t)n * K, 2 * row_q, &bars[warp][slot]);
-            bulk_g2s(dst + 2 * row_q, a.ws + (int64_t)n * (K / 32), 2 * row_s, &bars[warp][slot]);
-        }
-    };
-    // weights are read-only: the first pairs are requested before the grid-dependency wait
-    int issued = 0;
-    if (worker && lane == 0)
-        for (int i = 0; i < SG_SLOTS && gw + i * total_warps < n_pairs; i++) fetch(gw + i * total_warps, i), issued++;
-    issued = __shfl_sync(0xffffffffu, issued, 0);
-
-    grid_dependency_wait();
-    // activations (times the gain) into shared memory; sums of squares for the RMSNorm
-    for (int m = 0; m < MT; m++) {
-        float ss = 0.0f;
-        for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (m < a.M) v = *reinterpret_cast<const float4*>(a.x + (int64_t)m * a.ldx + k);
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            if (a.norm_gain) {
-                const float4 g = __ldg(reinterpret_cast<const float4*>(a.norm_gain + k));
-                v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
-            }
-            *reinterpret_cast<float4*>(xs + (size_t)m * K + k) = v;
-        }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp][m] = ss;
-    }
-    __syncthreads();
-    if (threadIdx.x < MT) {
-        float ss = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) ss += red[w][threadIdx.x];
-        inv_rms[threadIdx.x] = a.norm_gain ? 1.0f / sqrtf(ss / (float)K + 1e-5f) : 1.0f;
-    }
-    __syncthreads();
-    if (!worker) return;
-
-    bool ok = true;
-    int it = 0;
-    for (int pair = gw; pair < n_pairs; pair += total_warps, it++) {
-        const int slot = it % SG_SLOTS;
-        if (ok && !mbar_wait(&bars[warp][slot], (it / SG_SLOTS) & 1, a.err)) ok = false;
-        float acc0[MT], acc1[MT];
-#pragma unroll
-        for (int m = 0; m < MT; m++) acc0[m] = acc1[m] = 0.0f;
-        if (ok) {
-            const uint8_t* src = ring + (size_t)slot * sp.slot_bytes;
-            for (int k = lane * 16; k < K; k += 512) {
-                float w0[16], w1[16];
-                if (F32W) {
-                    const float4* r0 = reinterpret_cast<const float4*>(src + (size_t)k * 4);
-                    const float4* r1 = reinterpret_cast<const float4*>(src + (size_t)row_q + (size_t)k * 4);
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float4 u = r0[i], v = r1[i];
-                        w0[4 * i] = u.x; w0[4 * i + 1] = u.y; w0[4 * i + 2] = u.z; w0[4 * i + 3] = u.w;
-                        w1[4 * i] = v.x; w1[4 * i + 1] = v.y; w1[4 * i + 2] = v.z; w1[4 * i + 3] = v.w;
-                    }
-                } else {
-                    const uint4 q0 = *reinterpret_cast<const uint4*>(src + k);
-                    const uint4 q1 = *reinterpret_cast<const uint4*>(src + row_q + k);
-                    const float s0 = reinterpret_cast<const float*>(src + 2 * row_q)[k >> 5];
-                    const float s1 = reinterpret_cast<const float*>(src + 2 * row_q + row_s)[k >> 5];
-                    const uint32_t u0[4] = {q0.x, q0.y, q0.z, q0.w}, u1[4] = {q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        q8x4_to_f32(u0[i], w0 + 4 * i);
-                        q8x4_to_f32(u1[i], w1 + 4 * i);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        w0[i] *= s0;  // w = q * scale (src/model_q8.cpp:107-111)
-                        w1[i] *= s1;
-                    }
-                }
-#pragma unroll
-                for (int m = 0; m < MT; m++) {
-                    const float4* x4 = reinterpret_cast<const float4*>(xs + (size_t)m * K + k);
-                    float d0 = 0.0f, d1 = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float4 xv = x4[i];
-                        d0 = fmaf(w0[4 * i], xv.x, d0); d0 = fmaf(w0[4 * i + 1], xv.y, d0);
-                        d0 = fmaf(w0[4 * i + 2], xv.z, d0); d0 = fmaf(w0[4 * i + 3], xv.w, d0);
-                        d1 = fmaf(w1[4 * i], xv.x, d1); d1 = fmaf(w1[4 * i + 1], xv.y, d1);
-                        d1 = fmaf(w1[4 * i + 2], xv.z, d1); d1 = fmaf(w1[4 * i + 3], xv.w, d1);
-                    }
-                    acc0[m] += d0;
-                    acc1[m] += d1;
-                }
-            }
-        }
-        __syncwarp();  // every lane has read the slot
-        if (lane == 0 && ok && pair + SG_SLOTS * total_warps < n_pairs) fetch(pair + SG_SLOTS * total_warps, slot);
-        if (!ok) continue;
-        const int n = pair * 2;
-#pragma unroll
-        for (int m = 0; m < MT; m++) {
-            const float v0 = warp_sum(acc0[m]) * inv_rms[m];
-            const float v1 = warp_sum(acc1[m]) * inv_rms[m];
-            if (m < a.M && lane == 0) {
-                if (e.kind == kEpiLogits) {
-                    if (e.out) {
-                        e.out[(int64_t)m * e.ldo + n] = v0;
-                        e.out[(int64_t)m * e.ldo + n + 1] = v1;
-                    }
-                    float best = v0;
-                    int bi = n;
-                    if (v1 > best) { best = v1; bi = n + 1; }
-                    if (best > 0.0f) argmax_offer(e.argmax_keys + m, argmax_key(best, bi));
-                } else {
-                    epi_pair(e, m, n, v0, v1);
-                }
-            }
-        }
-    }
-    grid_dependents_launch();
-}
-
 // ------------------------------------------------------------------ ring matvec, M <= 2
 // Large Q8 matrices at one or two token rows (decode at batch 1-2; the 7B shape's
 // projections).  One CTA per SM takes a contiguous range of units of G whole rows: their
@@ -696,21 +535,6 @@ bool ring_plan(const GemmArgs& a, RingPlan* rp, int* cpl) {
     return false;
 }
 
-// Whether the streamed matvec takes this launch, and its shape.
-// Measured on B200 (one token row): the streamed kernel wins only for large Q8 matrices
-// with rows short enough for 8 warps' rings (e.g. 22016 x 4096: 2.96 vs 2.61 TB/s); both
-// kernels are then bound by the CUDA-core dequantisation (~4 instructions per weight),
-// near 3 TB/s, not by HBM.  Longer rows and fp32 weights stay on the register matvec.
-bool stream_plan(const GemmArgs& a, StreamPlan* sp) {
-    if (a.wf || a.M > 2 || a.kbegin != 0 || a.K % 128 != 0 || a.N % 2 != 0) return false;
-    if ((int64_t)a.N * a.K < ((int64_t)16 << 20)) return false;  // small matrices: launch latency rules
-    sp->slot_bytes = 2 * (a.K + a.K / 8);
-    sp->x_bytes = ((a.M <= 1 ? 1 : 2) * a.K * 4 + 127) / 128 * 128;
-    const int budget = 200 * 1024 - sp->x_bytes;
-    sp->warps = std::min(8, budget / (SG_SLOTS * sp->slot_bytes));
-    return sp->warps == 8;
-}
-
 // ------------------------------------------------------------------ tiled, M > 8
 constexpr int TN = 64, TM = 64, KC = 32;
 
@@ -885,19 +709,6 @@ void dispatch_ring(const GemmArgs& a, const Epilogue& e, const RingPlan& rp, int
     else launch_ring<MT, (MT == 1 ? 4 : 2)>(a, e, rp, s);
 }
 
-template <int MT, bool F32W>
-void launch_stream(const GemmArgs& a, const Epilogue& e, const StreamPlan& sp, cudaStream_t s) {
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
-    if (sms <= 0) sms = 148;
-    const int smem = sp.x_bytes + sp.warps * SG_SLOTS * sp.slot_bytes;
-    cudaFuncSetAttribute(gemv_stream_kernel<MT, F32W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    const int pairs = a.N / 2;
-    const int grid = std::max(1, std::min(sms, (pairs + sp.warps - 1) / sp.warps));
-    launch_ex(gemv_stream_kernel<MT, F32W>, dim3(grid), dim3(256), smem, s, 1, a, e, sp);
-}
-
 void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     if (!tc_disabled() && tc_gemm_supported(a)) {
         launch_tc_gemm(a, e, s);
@@ -909,12 +720,6 @@ void launch_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     if (!stream_disabled() && ring_plan(a, &rp, &cpl)) {
         if (a.M <= 1) dispatch_ring<1>(a, e, rp, cpl, s);
         else dispatch_ring<2>(a, e, rp, cpl, s);
-        return;
-    }
-    StreamPlan sp;
-    if (!stream_disabled() && stream_plan(a, &sp)) {
-        if (a.M <= 1) launch_stream<1, false>(a, e, sp, s);
-        else launch_stream<2, false>(a, e, sp, s);
         return;
     }
     if (a.M <= 1) gemv_dispatch<1>(a, e, s);
