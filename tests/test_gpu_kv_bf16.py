@@ -132,6 +132,17 @@ def test_bf16_pages_110m(restatement, ref_fixed, m110_model):
     _run(m110_model, restatement, ref_fixed, [24], 3, seed=72, pages=64)
 
 
+@pytest.mark.parametrize("B", [4, 24])
+def test_bf16_pages_large_matrix_paths(restatement, ref_fixed, m110_model, monkeypatch, B):
+    """The 110M model with every projection on the large-matrix paths (tile threshold at
+    zero): prompts of 16-60 tokens prefilled through the stream-K kernel, then decode at
+    B = 4 (int8 digit-plane kernel) or B = 24 (stream-K), K/V appended in bf16 by those
+    kernels' epilogue."""
+    monkeypatch.setenv("NITRO_TILE_MAX_WEIGHTS", "0")
+    lens = [int(n) for n in np.random.default_rng(B).integers(16, 61, B)]
+    _run(m110_model, restatement, ref_fixed, lens, 2, seed=73 + B, pages=512)
+
+
 def test_bf16_pages_packed_scheduler(restatement, tiny_model):
     """NR_SCHED_PACKED with bf16 pages: several prompts in one forward pass (the tensor-core
     prefill attention over a segment table reads bf16 pages), each request's logits
