@@ -235,6 +235,12 @@ int nr_engine_kernel_times(nr_engine* e, double ms[NR_KERNEL_CLASSES], int64_t l
  * append rewrites the same rows; logits written if that step wrote them), without host
  * copies or synchronisation.  For timing the device-resident decode step. */
 int nr_replay_decode(nr_engine* e, int32_t n);
+/* Enqueue only the paged decode attention launches of the engine's last decode step n more
+ * times (every layer in order; with_merge != 0 adds the merge of split contexts after each),
+ * back to back on its stream, without host copies or synchronisation.  The attention output
+ * buffer is rewritten with the values the step computed.  For timing the attention kernel
+ * at the step's shapes without the projections and per-launch events between launches. */
+int nr_replay_decode_attention(nr_engine* e, int32_t n, int32_t with_merge);
 /* Outputs of the most recent decode step or replay: *B_out rows; argmax_out (if not NULL,
  * [B]) the greedy ids, logits_out (if not NULL, [B x vocab]) the logits, which only a step
  * that computed them has (NR_ERR_INVALID otherwise).  Synchronises the engine stream. */

@@ -118,6 +118,7 @@ SIGNATURES = {
     "nr_engine_set_profiling": (C.c_int, [P, I32]),
     "nr_engine_kernel_times": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
     "nr_replay_decode": (C.c_int, [P, I32]),
+    "nr_replay_decode_attention": (C.c_int, [P, I32, I32]),
     "nr_decode_last_outputs": (C.c_int, [P, PI32, PF, PI32]),
     "nr_paged_attention_workspace_size": (C.c_size_t, [I32, I32, I32, I32]),
     "nr_paged_attention_decode": (C.c_int, [P, P, P, P, I32, P, I32, I32, I32, I32, I32, I32, P, P, P, P]),

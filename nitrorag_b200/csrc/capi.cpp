@@ -598,6 +598,11 @@ int nr_replay_decode(nr_engine* e, int32_t n) {
     return e->impl->replay_decode(n);
 }
 
+int nr_replay_decode_attention(nr_engine* e, int32_t n, int32_t with_merge) {
+    if (!e || n < 0) return NR_ERR_INVALID;
+    return e->impl->replay_decode_attention(n, with_merge != 0);
+}
+
 int nr_decode_last_outputs(nr_engine* e, int32_t* argmax_out, float* logits_out, int32_t* B_out) {
     if (!e) return NR_ERR_INVALID;
     return e->impl->last_decode_outputs(argmax_out, logits_out, B_out);

@@ -393,6 +393,21 @@ bool Engine::use_ss(int M) const {
            gemm_uses_tc(M, c.dim + 2 * c.kv_dim(), c.dim) && gemm_uses_tc(M, 2 * c.hidden, c.dim);
 }
 
+// Decode attention of layer l over the step descriptor's B rows (block tables and context
+// lengths in HBM), its split partials in the engine's workspace.
+DecodeAttnArgs Engine::decode_attn_plan(int l, int B, int max_ctx) const {
+    const ModelShape& c = shape_;
+    DecodeAttnArgs a;
+    a.q = d_q_; a.kpool = kpool_; a.vpool = vpool_; a.geom = geom_; a.layer = l;
+    a.block_tables = d_bt_; a.max_pages = c.max_pages(); a.ctx_lens = d_ctx_;
+    a.n_heads = c.n_heads; a.out = d_att_; a.err = d_err_;
+    // partial buffers are laid out for max_batch rows so B may vary per call
+    a.B = cfg_.max_batch;
+    decode_attn_bind_workspace(a, d_attn_ws_, c.max_pages());
+    a.B = B;
+    return plan_decode_attention(a, max_ctx);
+}
+
 void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos, int B_decode, int max_ctx,
                         bool force_fixed) {
     const ModelShape& c = shape_;
@@ -426,15 +441,7 @@ void Engine::run_layers(int M, bool prefill, const Sequence* seq, int start_pos,
             ProfScope ps(this, kKAttn);
             launch_prefill_attention(a, stream_);
         } else {
-            DecodeAttnArgs a;
-            a.q = d_q_; a.kpool = kpool_; a.vpool = vpool_; a.geom = geom_; a.layer = l;
-            a.block_tables = d_bt_; a.max_pages = c.max_pages(); a.ctx_lens = d_ctx_;
-            a.B = B_decode; a.n_heads = c.n_heads; a.out = d_att_; a.err = d_err_;
-            // partial buffers are laid out for max_batch rows so B may vary per call
-            a.B = cfg_.max_batch;
-            decode_attn_bind_workspace(a, d_attn_ws_, c.max_pages());
-            a.B = B_decode;
-            const DecodeAttnArgs pa = plan_decode_attention(a, max_ctx);
+            const DecodeAttnArgs pa = decode_attn_plan(l, B_decode, max_ctx);
             { ProfScope ps(this, kKAttn); launch_decode_attention_main(pa, stream_); }
             if (decode_attn_splits(pa)) { ProfScope ps(this, kKMerge); launch_decode_merge(pa, stream_); }
         }
@@ -757,6 +764,21 @@ int Engine::replay_decode(int n) {
         if (profiling_ && ev_used_ + 512 > ev_pool_.size()) {
             int rc = prof_flush();
             if (rc) return rc;
+        }
+    }
+    NR_CUDA(cudaGetLastError());
+    return NR_OK;
+}
+
+int Engine::replay_decode_attention(int n, bool with_merge) {
+    if (!has_device()) return fail(NR_ERR_NO_DEVICE, "host-only engine");
+    if (!last_valid_) return fail(NR_ERR_INVALID, "no decode step to replay");
+    NR_CUDA(cudaSetDevice(cfg_.device));
+    for (int i = 0; i < n; i++) {
+        for (int l = 0; l < shape_.n_layers; l++) {
+            const DecodeAttnArgs pa = decode_attn_plan(l, last_B_, last_max_ctx_);
+            launch_decode_attention_main(pa, stream_);
+            if (with_merge) launch_decode_merge(pa, stream_);
         }
     }
     NR_CUDA(cudaGetLastError());

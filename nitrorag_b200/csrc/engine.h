@@ -104,6 +104,10 @@ public:
     // Enqueue the kernels of the last decode step again, n times, on the engine stream
     // (its descriptor is still resident); returns without synchronising.
     int replay_decode(int n);
+    // Enqueue only the decode attention launches of the last decode step (every layer in
+    // order, with or without the merge of split contexts), n times, back to back; the
+    // attention output is rewritten with the same values.  For timing the kernel alone.
+    int replay_decode_attention(int n, bool with_merge);
     // Outputs of the most recent decode step or replay: B argmax ids, and the B x vocab
     // logits when that step computed them (synchronises the engine stream).
     int last_decode_outputs(int* argmax_out, float* logits_out, int* B_out);
@@ -129,6 +133,7 @@ private:
     int check_cuda(cudaError_t e, const char* what);
     void run_layers(int M, bool prefill, const Sequence* seq, int start_pos, int B_decode, int max_ctx,
                     bool force_fixed);
+    DecodeAttnArgs decode_attn_plan(int l, int B, int max_ctx) const;
 
     nr_config cfg_;
     ModelShape shape_;

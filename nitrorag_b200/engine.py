@@ -154,6 +154,10 @@ class NitroEngine:
     def replay_decode(self, n: int) -> None:
         self._check(lib().nr_replay_decode(self._h, n), "nr_replay_decode")
 
+    def replay_decode_attention(self, n: int, with_merge: bool = False) -> None:
+        """Enqueue the last decode step's attention launches (all layers) n more times."""
+        self._check(lib().nr_replay_decode_attention(self._h, n, int(with_merge)), "nr_replay_decode_attention")
+
     def last_decode_outputs(self, want_logits: bool = False):
         """(argmax ids, logits or None) of the most recent decode step or replay."""
         cap = self.config.max_batch

@@ -329,5 +329,12 @@ def test_decode64_bench_workload_and_replay(ref_fixed, m110_model):
     am, lg = eng.last_decode_outputs(want_logits=True)
     assert np.array_equal(am, step_tokens)
     assert_close(lg, step_logits, rtol=1e-6, atol=1e-7, what="replayed decode step")
+    # the attention launches alone (the bench's roofline pass) leave the state as it was
+    eng.replay_decode_attention(2, with_merge=False)
+    eng.replay_decode_attention(2, with_merge=True)
+    eng.replay_decode(1)
+    am, lg = eng.last_decode_outputs(want_logits=True)
+    assert np.array_equal(am, step_tokens)
+    assert_close(lg, step_logits, rtol=1e-6, atol=1e-7, what="decode step after attention replays")
     eng.close()
     ref.close()
