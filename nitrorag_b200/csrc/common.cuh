@@ -22,18 +22,28 @@ constexpr int kErrBadContext = 2;
 // sets the kernel's error flag; the kernel then skips the work that needed the data.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
-// Page layout of the device K and V pools: [page][layer][kv_head][16][head_dim] elements
-// (fp32, or bf16 with kv_bf16 = 1), so the 16 rows of one (page, layer, kv_head) form one
-// contiguous tile of 16*head_dim elements.  Offsets below count elements.
+// Page layout of the device K and V pools, in elements (fp32, or bf16 with kv_bf16 = 1).
+// Page-major (pages == 0): [page][layer][kv_head][16][head_dim], a page's layers together.
+// Layer-major (pages = the pool's page count): [layer][page][kv_head][16][head_dim], so the
+// tiles one layer's attention reads lie in one region of 1/n_layers of the pool.  Either way
+// the 16 rows of one (page, layer, kv_head) form one contiguous tile of 16*head_dim elements.
+// Offsets below count elements.
 struct PoolGeom {
     int n_layers;
     int n_kv_heads;
     int head_dim;
     int kv_bf16 = 0;
+    int64_t pages = 0;
     __host__ __device__ int elem_bytes() const { return kv_bf16 ? 2 : 4; }
+    // elements of one page over all layers
     __host__ __device__ int64_t page_floats() const { return (int64_t)n_layers * n_kv_heads * kPage * head_dim; }
+    // elements of one (page, layer): all kv heads' tiles, contiguous in both layouts
+    __host__ __device__ int64_t layer_floats() const { return (int64_t)n_kv_heads * kPage * head_dim; }
+    // distance between the same (layer, kv_head) tile of consecutive pages
+    __host__ __device__ int64_t page_stride() const { return pages ? layer_floats() : page_floats(); }
     __host__ __device__ int64_t tile_offset(int64_t page, int layer, int kvh) const {
-        return page * page_floats() + ((int64_t)layer * n_kv_heads + kvh) * kPage * head_dim;
+        const int64_t slab = pages ? (int64_t)layer * pages + page : page * n_layers + layer;
+        return slab * layer_floats() + (int64_t)kvh * kPage * head_dim;
     }
 };
 

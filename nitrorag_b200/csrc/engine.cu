@@ -349,6 +349,9 @@ int Engine::init_device(const uint8_t* file, size_t size) {
     if (rc != NR_OK) return rc;
 
     geom_ = PoolGeom{c.n_layers, c.n_kv_heads, c.head_dim(), cfg_.kv_dtype == NR_KV_BF16 ? 1 : 0};
+    // layer-major pools (NITRO_KV_PAGE_MAJOR=1 keeps every page's layers together)
+    const char* pm_env = getenv("NITRO_KV_PAGE_MAJOR");
+    if (!(pm_env && pm_env[0] == '1')) geom_.pages = cfg_.total_blocks;
     const size_t pool_bytes = (size_t)cfg_.total_blocks * geom_.page_floats() * geom_.elem_bytes();
     NR_CUDA(cudaMalloc(&kpool_, pool_bytes));
     NR_CUDA(cudaMalloc(&vpool_, pool_bytes));
@@ -864,7 +867,7 @@ int Engine::read_page(int block, float* k_out, float* v_out) {
     if (block < 0 || block >= cfg_.total_blocks) return fail(NR_ERR_INVALID, "block id out of range");
     const ModelShape& c = shape_;
     const int hd = c.head_dim(), KV = c.kv_dim();
-    const size_t pf = (size_t)geom_.page_floats();
+    const size_t pf = (size_t)geom_.page_floats(), lf = (size_t)geom_.layer_floats();
     const size_t eb = (size_t)geom_.elem_bytes();
     std::vector<float> tmp(pf);
     std::vector<uint16_t> raw16(geom_.kv_bf16 ? pf : 0);
@@ -872,9 +875,11 @@ int Engine::read_page(int block, float* k_out, float* v_out) {
     for (int which = 0; which < 2; which++) {
         float* dst = which == 0 ? k_out : v_out;
         if (!dst) continue;
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(which == 0 ? kpool_ : vpool_) + (size_t)block * pf * eb;
-        NR_CUDA(cudaMemcpyAsync(geom_.kv_bf16 ? (void*)raw16.data() : (void*)tmp.data(), src, pf * eb,
-                                cudaMemcpyDeviceToHost, stream_));
+        const uint8_t* pool = reinterpret_cast<const uint8_t*>(which == 0 ? kpool_ : vpool_);
+        uint8_t* host = geom_.kv_bf16 ? reinterpret_cast<uint8_t*>(raw16.data()) : reinterpret_cast<uint8_t*>(tmp.data());
+        for (int l = 0; l < c.n_layers; l++)  // the page's tiles of layer l: lf contiguous elements
+            NR_CUDA(cudaMemcpyAsync(host + (size_t)l * lf * eb, pool + (size_t)geom_.tile_offset(block, l, 0) * eb,
+                                    lf * eb, cudaMemcpyDeviceToHost, stream_));
         NR_CUDA(cudaStreamSynchronize(stream_));
         if (geom_.kv_bf16)  // bf16 is the upper half of an fp32
             for (size_t i = 0; i < pf; i++) {

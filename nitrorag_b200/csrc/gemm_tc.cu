@@ -810,7 +810,7 @@ __global__ void __launch_bounds__(TC_THREADS, EPI == kEpiLogits ? 2 : 1) tc_gemm
                         }
                     }
                 }
-                const int64_t pf = e.geom.page_floats();
+                const int64_t pf = e.geom.page_stride();
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int m = m_base + c0 + j;
@@ -1016,7 +1016,7 @@ __device__ __forceinline__ void sk_epilogue(const GemmArgs& a, const Epilogue& e
             }
         }
         const bool rope = kind < 2;
-        const int64_t pf = e.geom.page_floats();
+        const int64_t pf = e.geom.page_stride();
 #pragma unroll
         for (int j = 0; j < SK_COLS; j++) {
             const int m = c_base + j;
