@@ -331,9 +331,9 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
 // inner loop is one 16-byte shared load per 16 weights, one byte permute per weight
 // (int8 -> exact float, as q8_pair_biased) and packed f32x2 adds and FMAs; the block scale
 // multiplies each 16-weight partial (the products of src/model_q8.cpp:107-111, summed in
-// another order).  A row pair's segment partials meet in shared memory: the last of its
-// warps to arrive (shared-memory counter) adds them in segment order and runs the
-// epilogue, then every warp releases the slot to the producer.
+// another order).  Segment partials meet in shared memory: after one named barrier of the
+// consumer warps per unit, warp w < G / 2 adds row pair (2w, 2w + 1)'s partials in segment
+// order and runs the epilogue, and every warp releases the slot to the producer.
 constexpr int GR_CONSUMERS = 16;
 constexpr int GR_THREADS = (GR_CONSUMERS + 1) * 32;
 constexpr int GR_SLOTS_MAX = 8;
@@ -346,12 +346,16 @@ struct RingPlan {
     int units;       // N / G
 };
 
+// Named barrier 1 over the consumer warps of the ring matvec (the producer warp is not in it).
+__device__ __forceinline__ void gr_consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(GR_CONSUMERS * 32) : "memory");
+}
+
 template <int MT, int CPL>
 __global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Epilogue e, RingPlan rp) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[GR_SLOTS_MAX], empty[GR_SLOTS_MAX];
     __shared__ float part[GR_SLOTS_MAX][8][8][MT];  // [slot][row of unit][segment][token]
-    __shared__ int cnt[GR_SLOTS_MAX][4];            // [slot][row pair]: warps done
     __shared__ float red[GR_CONSUMERS + 1][MT];
     __shared__ float inv_rms[MT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -367,7 +371,6 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Ep
         }
         fence_barrier_init();
     }
-    for (int i = threadIdx.x; i < GR_SLOTS_MAX * 4; i += blockDim.x) (&cnt[0][0])[i] = 0;
     __syncthreads();
     auto fetch = [&](int i) {  // unit u0 + i -> slot i % slots
         const int s = i % rp.slots;
@@ -443,11 +446,13 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Ep
     }
     const unsigned long long unb = q8_unbias2();
     bool ok = true;
+    int s = 0;         // slot of unit i
+    uint32_t ph = 0;   // its fill parity
+    const uint8_t* slot_base = smem;
     for (int i = 0; i < nu; i++) {
-        const int s = i % rp.slots;
-        if (ok && !mbar_wait(&full[s], (i / rp.slots) & 1, a.err)) ok = false;
-        const uint8_t* q = smem + (size_t)s * rp.slot_bytes + (size_t)r * K;
-        const float* sc = reinterpret_cast<const float*>(smem + (size_t)s * rp.slot_bytes + (size_t)G * K) + (size_t)r * (K / 32);
+        if (ok && !mbar_wait(&full[s], ph, a.err)) ok = false;
+        const uint8_t* q = slot_base + (size_t)r * K + kseg;
+        const float* sc = reinterpret_cast<const float*>(slot_base + (size_t)G * K) + (size_t)r * (K / 32) + (kseg >> 5);
         float acc[MT];
 #pragma unroll
         for (int m = 0; m < MT; m++) acc[m] = 0.0f;
@@ -456,8 +461,8 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Ep
             for (int c = 0; c < CPL; c++) {
                 const int kl = (lane + 32 * c) * 16;
                 if (kl < L) {
-                    const uint4 w4 = *reinterpret_cast<const uint4*>(q + kseg + kl);
-                    const float bs = sc[(kseg + kl) >> 5];
+                    const uint4 w4 = *reinterpret_cast<const uint4*>(q + kl);
+                    const float bs = sc[kl >> 5];
                     const uint32_t u[4] = {w4.x ^ 0x80808080u, w4.y ^ 0x80808080u, w4.z ^ 0x80808080u,
                                            w4.w ^ 0x80808080u};
                     unsigned long long d[MT];
@@ -480,33 +485,36 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Ep
         }
 #pragma unroll
         for (int m = 0; m < MT; m++) acc[m] = warp_sum(acc[m]);
-        int prev = 0;
         if (lane == 0) {
 #pragma unroll
             for (int m = 0; m < MT; m++) part[s][r][sg][m] = acc[m];
-            __threadfence_block();
-            prev = atomicAdd(&cnt[s][r >> 1], 1);
         }
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == 2 * S - 1) {  // the row pair's last warp: segments in order, epilogue
-            __threadfence_block();
-            const int r0 = r & ~1;
-            if (lane < MT && lane < a.M && ok) {
-                float v0 = 0.0f, v1 = 0.0f;
-                for (int t = 0; t < S; t++) {
-                    v0 += part[s][r0][t][lane];
-                    v1 += part[s][r0 + 1][t][lane];
-                }
-                if (a.norm_gain) {
-                    v0 *= inv_rms[lane];
-                    v1 *= inv_rms[lane];
-                }
-                epi_pair(e, lane, (u0 + i) * G + r0, v0, v1);
+        // every consumer warp passes this barrier once per unit, so the counts match; the
+        // unit's partials are then complete, and part[s] is next written `slots` units later,
+        // after the readers below have passed the following units' barriers
+        gr_consumer_sync();
+        if (warp < G / 2 && lane < MT && lane < a.M && ok) {  // row pair (2 warp, 2 warp + 1)
+            const int r0 = 2 * warp;
+            float v0 = 0.0f, v1 = 0.0f;
+            for (int t = 0; t < S; t++) {
+                v0 += part[s][r0][t][lane];
+                v1 += part[s][r0 + 1][t][lane];
             }
-            if (lane == 0) cnt[s][r >> 1] = 0;
+            if (a.norm_gain) {
+                v0 *= inv_rms[lane];
+                v1 *= inv_rms[lane];
+            }
+            epi_pair(e, lane, (u0 + i) * G + r0, v0, v1);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot and its partials
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot
+        if (++s == rp.slots) {
+            s = 0;
+            ph ^= 1u;
+            slot_base = smem;
+        } else {
+            slot_base += rp.slot_bytes;
+        }
     }
     grid_dependents_launch();
 }
