@@ -53,16 +53,27 @@ struct QState {
     }
 };
 
+// The lane's half of the query (pre-scaled, in shared memory at qs) as attend_page reads
+// it, in registers: float4 j of the lane's half is float4 (j + lane) mod HD/8 of it.
+template <int HD>
+__device__ __forceinline__ void load_query(float4* qr, const float* qs, int lane) {
+    constexpr int HALF4 = HD / 8;
+    const float4* qrow = reinterpret_cast<const float4*>(qs + (lane & 1) * (HD / 2));
+#pragma unroll
+    for (int j = 0; j < HALF4; j++) qr[j] = qrow[(j + lane) & (HALF4 - 1)];
+}
+
 // Fold the 16 rows of one K/V page tile (in shared memory) into a query's state.
-// qs: the query (head_dim floats, shared memory, pre-scaled by log2(e)/sqrt(head_dim));
-// n_valid: how many leading rows of the page are attended (1..16).
+// qr: the query from load_query (pre-scaled by log2(e)/sqrt(head_dim)); pbuf: 16 floats of
+// this warp's shared memory for the page's probabilities (free again once the caller's
+// __syncwarp after the page has passed); n_valid: how many leading rows of the page are
+// attended (1..16).
 template <int HD, typename KT>
-__device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, const KT* Kt, const KT* Vt,
-                                            int n_valid, int lane) {
+__device__ __forceinline__ void attend_page(QState<HD>& st, const float4* qr, float* pbuf, const KT* Kt,
+                                            const KT* Vt, int n_valid, int lane) {
     constexpr int HALF4 = HD / 8;  // groups of 4 values per half row
     const int t = lane >> 1, half = lane & 1;
     const KT* krow = Kt + t * HD + half * (HD / 2);
-    const float4* qrow = reinterpret_cast<const float4*>(qs + half * (HD / 2));
     float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;  // four short FMA chains
 #pragma unroll
     for (int j = 0; j < HALF4; j++) {
@@ -70,14 +81,14 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
         // phase hit 8 different bank groups
         const int jj = (j + lane) & (HALF4 - 1);
         float4 kv = ldkv4(krow + 4 * jj);
-        float4 qv = qrow[jj];
+        const float4 qv = qr[j];
         s0 = fmaf(qv.x, kv.x, s0);
         s1 = fmaf(qv.y, kv.y, s1);
         s2 = fmaf(qv.z, kv.z, s2);
         s3 = fmaf(qv.w, kv.w, s3);
     }
     float s = (s0 + s1) + (s2 + s3);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);  // both lanes of a key row hold its score
     if (t >= n_valid) s = -INFINITY;
     float mp = s;
 #pragma unroll
@@ -85,27 +96,37 @@ __device__ __forceinline__ void attend_page(QState<HD>& st, const float* qs, con
     const float m_new = fmaxf(st.m, mp);
     const float corr = exp2f(st.m - m_new);
     const float p = exp2f(s - m_new);
-    float ps = half == 0 ? p : 0.0f;
+    if (half == 0) pbuf[t] = p;
+    // the 16 lanes of one half hold the 16 keys' probabilities once each
+    float ps = p;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    for (int o = 2; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
     st.l = st.l * corr + ps;
     st.m = m_new;
 #pragma unroll
     for (int i = 0; i < QState<HD>::DPL; i++) st.o[i] *= corr;
+    __syncwarp();  // pbuf written
+    const float4* pb = reinterpret_cast<const float4*>(pbuf);
     const KT* vbase = Vt + lane * QState<HD>::DPL;
 #pragma unroll
-    for (int tt = 0; tt < kPage; tt++) {
-        const float pt = __shfl_sync(0xffffffffu, p, 2 * tt);
-        if (QState<HD>::DPL == 2) {
-            float2 v = ldkv2(vbase + tt * HD);
-            st.o[0] = fmaf(pt, v.x, st.o[0]);
-            st.o[1] = fmaf(pt, v.y, st.o[1]);
-        } else {
-            float4 v = ldkv4(vbase + tt * HD);
-            st.o[0] = fmaf(pt, v.x, st.o[0]);
-            st.o[1] = fmaf(pt, v.y, st.o[1]);
-            st.o[2] = fmaf(pt, v.z, st.o[2]);
-            st.o[3] = fmaf(pt, v.w, st.o[3]);
+    for (int t4 = 0; t4 < kPage / 4; t4++) {
+        const float4 pp = pb[t4];  // broadcast read
+        const float pv[4] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+        for (int i4 = 0; i4 < 4; i4++) {
+            const int tt = 4 * t4 + i4;
+            const float pt = pv[i4];
+            if (QState<HD>::DPL == 2) {
+                float2 v = ldkv2(vbase + tt * HD);
+                st.o[0] = fmaf(pt, v.x, st.o[0]);
+                st.o[1] = fmaf(pt, v.y, st.o[1]);
+            } else {
+                float4 v = ldkv4(vbase + tt * HD);
+                st.o[0] = fmaf(pt, v.x, st.o[0]);
+                st.o[1] = fmaf(pt, v.y, st.o[1]);
+                st.o[2] = fmaf(pt, v.z, st.o[2]);
+                st.o[3] = fmaf(pt, v.w, st.o[3]);
+            }
         }
     }
 }
@@ -133,7 +154,7 @@ struct DecCfg {
     static constexpr int TILE = kPage * HD;                              // elements per K or V tile
     static constexpr int TILE_BYTES = TILE * (int)sizeof(KT);
     static constexpr int RING_BYTES = WARPS * kDecStages * 2 * TILE_BYTES;
-    static constexpr int SMEM = RING_BYTES + WARPS * HD * 4;             // + one query per warp
+    static constexpr int SMEM = RING_BYTES + WARPS * (HD + kPage) * 4;   // + a query and a page's p per warp
 };
 
 struct DecItem {
@@ -301,6 +322,7 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
 
     KT* ring = reinterpret_cast<KT*>(smem_raw + warp * kDecStages * 2 * C::TILE_BYTES);
     float* qs = reinterpret_cast<float*>(smem_raw + C::RING_BYTES) + warp * HD;
+    float* pbuf = reinterpret_cast<float*>(smem_raw + C::RING_BYTES) + C::WARPS * HD + warp * kPage;
     uint64_t* wb = bars[warp];
     if (lane == 0) {
         for (int s = 0; s < kDecStages; s++) mbar_init(&wb[s], 1);
@@ -348,6 +370,8 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
 #pragma unroll
         for (int j = 0; j < HD / 32; j++) qs[lane + 32 * j] = cur.q[j];
         __syncwarp();
+        float4 qr[HD / 8];
+        load_query<HD>(qr, qs, lane);
         QState<HD> st;
         st.init();
         for (int pg = 0; pg < cur.np; pg++) {
@@ -356,7 +380,7 @@ __global__ void __launch_bounds__(DecCfg<HD>::WARPS * 32, 1) decode_attn_kernel(
             if (ok && !mbar_wait(&wb[slot], (consumed / kDecStages) & 1, a.err)) ok = false;
             if (ok) {
                 const int first = (cur.p0 + pg) * kPage;
-                attend_page<HD, KT>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
+                attend_page<HD, KT>(st, qr, pbuf, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
                                     min(kPage, cur.ctx - first), lane);
             }
             __syncwarp();  // every lane is done with the slot before it is refilled
@@ -412,7 +436,7 @@ struct DecSmall {
     static constexpr int TILE = kPage * HD;
     static constexpr int TILE_BYTES = TILE * (int)sizeof(KT);
     static constexpr int RING_BYTES = WARPS * STAGES * 2 * TILE_BYTES;
-    static constexpr int SMEM = RING_BYTES + HD * 4 + WARPS * (HD + 2) * 4;
+    static constexpr int SMEM = RING_BYTES + HD * 4 + WARPS * (HD + 2 + kPage) * 4;
 };
 
 template <int HD, typename KT>
@@ -430,6 +454,7 @@ __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small
     KT* ring = reinterpret_cast<KT*>(smem_raw + warp * S * 2 * C::TILE_BYTES);
     float* qs = reinterpret_cast<float*>(smem_raw + C::RING_BYTES);
     float* part = qs + HD;  // [W][HD + 2]: o, then m, l
+    float* pbuf = part + W * (HD + 2) + warp * kPage;  // this warp's page probabilities
 
     // page ids of this warp's pages (descriptor data: read before the wait)
     const int ctx = checked_ctx(a, b, h == 0 && threadIdx.x == 0);
@@ -454,6 +479,8 @@ __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small
         for (int j = 0; j < S && j < mine; j++) issue(j);
     __syncthreads();  // q in shared memory
 
+    float4 qr[HD / 8];
+    load_query<HD>(qr, qs, lane);
     QState<HD> st;
     st.init();
     bool ok = true;
@@ -462,7 +489,7 @@ __global__ void __launch_bounds__(DecSmall<HD>::WARPS * 32, 1) decode_attn_small
         if (ok && !mbar_wait(&bars[warp][slot], (j / S) & 1, a.err)) ok = false;
         if (ok) {
             const int first = (warp + j * W) * kPage;
-            attend_page<HD, KT>(st, qs, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
+            attend_page<HD, KT>(st, qr, pbuf, ring + (2 * slot) * C::TILE, ring + (2 * slot + 1) * C::TILE,
                                 min(kPage, ctx - first), lane);
         }
         __syncwarp();  // every lane is done with the slot before it is refilled
