@@ -333,7 +333,8 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemmArgs a, Epilogue e) {
 // multiplies each 16-weight partial (the products of src/model_q8.cpp:107-111, summed in
 // another order).  Segment partials meet in shared memory: after one named barrier of the
 // consumer warps per unit, warp w < G / 2 adds row pair (2w, 2w + 1)'s partials in segment
-// order and runs the epilogue, and every warp releases the slot to the producer.
+// order and runs the epilogue.  Each warp releases the slot to the producer as soon as its
+// lanes have read their weights, before the reduction.
 constexpr int GR_CONSUMERS = 16;
 constexpr int GR_THREADS = (GR_CONSUMERS + 1) * 32;
 constexpr int GR_SLOTS_MAX = 8;
@@ -483,6 +484,8 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Ep
                 }
             }
         }
+        __syncwarp();  // every lane has read its weights and scales from the slot
+        if (lane == 0) mbar_arrive(&empty[s]);  // the refill may start during the reduction
 #pragma unroll
         for (int m = 0; m < MT; m++) acc[m] = warp_sum(acc[m]);
         if (lane == 0) {
@@ -506,8 +509,6 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_ring_kernel(GemmArgs a, Ep
             }
             epi_pair(e, lane, (u0 + i) * G + r0, v0, v1);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot
         if (++s == rp.slots) {
             s = 0;
             ph ^= 1u;
