@@ -1,10 +1,11 @@
 // Paged attention over the fp32 KV pools, decode and causal prefill.
 //
-// The pools are laid out [page][layer][kv_head][16][head_dim], so one (page, layer,
-// kv_head) is a contiguous 16 x head_dim tile (4 KB at head_dim 64).  Every tile a CTA
-// needs is fetched with one bulk asynchronous copy (cp.async.bulk, the TMA engine's
-// non-tensor form) into shared memory and signalled on an mbarrier, so the SMs issue a
-// handful of instructions per 4 KB and keep many tiles in flight.
+// The pools are laid out [layer][page][kv_head][16][head_dim] in the engine and
+// [page][layer][kv_head][16][head_dim] for the standalone entry points (PoolGeom), so one
+// (page, layer, kv_head) is a contiguous 16 x head_dim tile (4 KB at head_dim 64).  Every
+// tile a CTA needs is fetched with one bulk asynchronous copy (cp.async.bulk, the TMA
+// engine's non-tensor form) into shared memory and signalled on an mbarrier, so the SMs
+// issue a handful of instructions per 4 KB and keep many tiles in flight.
 //
 // Scores and the softmax are fp32.  Inside a warp two lanes share one key row (each takes
 // half of head_dim; their partial dots are joined with one shuffle), the 16 keys of a page
