@@ -186,4 +186,11 @@ def test_invalid_arguments(tmp_path):
     with pytest.raises(NrError) as ei:
         eng.forward_prefill_chunk(eng.seq_create(0), [1, 2], 0)
     assert ei.value.code == -6  # host-only engine has no device
+    for replay in (lambda: eng.replay_decode(1), lambda: eng.replay_decode_attention(1, True)):
+        with pytest.raises(NrError) as ei:
+            replay()
+        assert ei.value.code == -6
+    from nitrorag_b200._lib import lib
+    assert lib().nr_replay_decode_attention(None, 1, 0) == -1
+    assert lib().nr_replay_decode_attention(eng._h, -1, 0) == -1
     eng.close()
