@@ -1749,6 +1749,14 @@ int tc_max_clusters(TcKernel kernel, int ks, int smem, int n_tiles, int m_tiles)
     return n;
 }
 
+// SMs of the current device (the runtime caches the attribute).
+int device_sms() {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms > 0 ? sms : 148;
+}
+
 template <int NT>
 void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     const int n_tiles = (a.N + TC_M - 1) / TC_M;
@@ -1802,7 +1810,9 @@ void tc_launch(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     int ksplit = 1;
     const int tiles = n_tiles * m_tiles;
     if (a.kbegin == 0 && NT <= 128)
-        while (ksplit < NITRO_TC_MAX_KSPLIT && tiles * ksplit < 148 && ksplit * 2 <= chunks && NT / (ksplit * 2) >= 8) ksplit *= 2;
+        while (ksplit < NITRO_TC_MAX_KSPLIT && tiles * ksplit < device_sms() && ksplit * 2 <= chunks &&
+               NT / (ksplit * 2) >= 8)
+            ksplit *= 2;
     SplitArgs sp;
     int smem = plan(ksplit, &sp);
     while (ksplit > 1 && tc_max_clusters(kernel, ksplit, smem, n_tiles, m_tiles) < tiles) {
@@ -1975,10 +1985,7 @@ void tc_launch_i8(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     sk.chunks = a.K / TC_KC;
     sk.xrows = 0;
     sk.raw_off = 0;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
-    if (sms <= 0) sms = 148;
+    const int sms = device_sms();
     const int dthreads = (a.K / 32) * NCOL;
     count_launch();
     launch_ex(tc_i8_digits_kernel<NCOL>, dim3((unsigned)((dthreads + 255) / 256)), dim3(256), 0, s, 1, a);
@@ -2000,10 +2007,7 @@ void tc_launch_streamk(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     sk.chunks = a.K / TC_KC;
     sk.units = ((a.N + TC_M - 1) / TC_M) * sk.chunks;
     sk.xrows = (a.M + 7) / 8 * 8;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);  // cached by the runtime
-    if (sms <= 0) sms = 148;
+    const int sms = device_sms();
     // the activations as hi/lo tiles, once for the launch
     const int64_t xthreads = (int64_t)sk.chunks * sk.xrows * 8;
     count_launch();
@@ -2048,7 +2052,7 @@ void launch_tc_gemm(const GemmArgs& a, const Epilogue& e, cudaStream_t s) {
     // 256-token tiles only when they alone fill the GPU (they never split K)
     const int n_tiles = (a.N + TC_M - 1) / TC_M;
     if (a.M <= 64) tc_launch<64>(a, e, s);
-    else if (a.M <= 128 || n_tiles * ((a.M + 255) / 256) < 148) tc_launch<128>(a, e, s);
+    else if (a.M <= 128 || n_tiles * ((a.M + 255) / 256) < device_sms()) tc_launch<128>(a, e, s);
     else tc_launch<256>(a, e, s);
 }
 
