@@ -311,8 +311,9 @@ def workload_config(ctx):
 
 
 # ------------------------------------------------------------------ other configs
-# The survey's other workloads, one JSON line each (`--workload config1|config3|config4|
-# config5`); the default `decode64` line above is the headline.  All run on one GPU.
+# The reference's other benchmark configurations, one JSON line each (`--workload
+# config1|config3|config4|config5`); the default `decode64` line above is the headline.
+# All run on one GPU.
 W110_BYTES = 193_932_288          # Q8 projections + fp32 classifier + RMS gains, 110M
 KV110_PER_TOKEN = 12 * 2 * 768 * 4  # K and V of every layer, 110M
 
